@@ -1,0 +1,382 @@
+// Persistent, warp-specialised bf16 GEMM on the 5th-generation tensor cores (sm_100a).
+//
+//   C[M, N] = A[M, K] @ B[N, K]^T      (both operands K-major, i.e. nn.Linear layout)
+//
+// One CTA per SM, 128x256 output tiles, 64-deep K blocks:
+//   warp 0      TMA producer: A and B tiles into a 4-stage shared-memory ring
+//               (128-byte swizzle), completion counted by mbarrier transaction bytes.
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128, N=256, K=16)
+//               into a TMEM accumulator; tcgen05.commit frees each smem stage and
+//               signals a finished accumulator. Two accumulators (2 x 256 TMEM columns)
+//               so the epilogue of tile i overlaps the main loop of tile i+1.
+//   warps 2-5   epilogue: tcgen05.ld 32x32b.x32 (thread = output row), fused math, store.
+//
+// Fused epilogues (the elementwise work that follows each DiT GEMM in the reference's
+// block forward, src/models/ops/fused_block.py:41-90):
+//   EPI_STORE      C = acc (+ bias)
+//   EPI_RESIDUAL   X += gate[adaln_idx[row]] * (acc + bias)       (the gated residual)
+//   EPI_SWIGLU     H = (acc_v + b_v) * silu(acc_g + b_g); the weight rows are interleaved
+//                  per 256-row tile as [128 value rows | 128 gate rows]
+//   EPI_ADD        C += acc (+ bias)                               (accumulate into C)
+//
+// Every wait is bounded (common.cuh): a protocol failure records an error code, unwinds
+// the CTA, drains its own copies and MMAs and frees its TMEM instead of hanging the GPU.
+#include "common.cuh"
+#include "tma.cuh"
+#include "launchers.h"
+
+namespace vdn {
+
+constexpr int GM_BM = 128;
+constexpr int GM_BN = 256;
+constexpr int GM_BK = 64;
+constexpr int GM_STAGES = 4;
+constexpr int GM_A_BYTES = GM_BM * GM_BK * 2;  // 16 KB
+constexpr int GM_B_BYTES = GM_BN * GM_BK * 2;  // 32 KB
+constexpr int GM_STAGE_BYTES = GM_A_BYTES + GM_B_BYTES;
+constexpr int GM_THREADS = 192;
+constexpr int GM_GROUP_N = 16;  // n-blocks per raster band (weights of one band stay in L2)
+constexpr int GM_SMEM = GM_STAGES * GM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+enum EpiMode : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ADD = 3 };
+
+struct EpiParams {
+  __nv_bfloat16* out;        // C / X / H
+  int64_t ldo;               // row stride of `out` (elements)
+  const float* bias;         // [N] fp32 or null
+  const __nv_bfloat16* gate; // EPI_RESIDUAL: gate table [rows, ldg]
+  int64_t ldg;
+  const int* gate_idx;       // EPI_RESIDUAL: per-row table index
+  int* err;                  // device error word
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  // n-band major raster: a band of GM_GROUP_N n-blocks sweeps all of M.
+  int band_size = GM_GROUP_N * num_m;
+  int band = tile / band_size;
+  int in_band = tile - band * band_size;
+  int n0 = band * GM_GROUP_N;
+  int gn = min(GM_GROUP_N, num_n - n0);
+  mb = in_band / gn;
+  nb = n0 + (in_band - mb * gn);
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile(const EpiParams& p, uint32_t tacc, int quarter,
+                                              int m0, int n0, int M, int N) {
+  const int lane = lane_id();
+  const int row = m0 + quarter * 32 + lane;
+  const uint32_t lane_base = tacc + ((uint32_t)(quarter * 32) << 16);
+  const bool row_ok = row < M;
+  if constexpr (EPI == EPI_SWIGLU) {
+    // columns [0,128) value, [128,256) gate -> 128 outputs at n0/2.
+    const int out_c0 = n0 >> 1;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+      uint32_t v[32], g[32];
+      tmem_ld32(lane_base + c, v);
+      tmem_ld32(lane_base + 128 + c, g);
+      tmem_wait_ld();
+      if (!row_ok) continue;
+      const int oc = out_c0 + c;
+      if (oc >= (N >> 1)) continue;
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        float a0 = __uint_as_float(v[j]), a1 = __uint_as_float(v[j + 1]);
+        float g0 = __uint_as_float(g[j]), g1 = __uint_as_float(g[j + 1]);
+        if (p.bias) {
+          a0 += p.bias[n0 + c + j];
+          a1 += p.bias[n0 + c + j + 1];
+          g0 += p.bias[n0 + 128 + c + j];
+          g1 += p.bias[n0 + 128 + c + j + 1];
+        }
+        packed[j >> 1] = pack_bf16(a0 * siluf_(g0), a1 * siluf_(g1));
+      }
+      uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t)row * p.ldo + oc);
+      if (oc + 32 <= (N >> 1)) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      } else {
+        __nv_bfloat16* d = p.out + (int64_t)row * p.ldo + oc;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (oc + j < (N >> 1)) {
+            uint32_t w = packed[j >> 1];
+            d[j] = __ushort_as_bfloat16((unsigned short)((j & 1) ? (w >> 16) : (w & 0xFFFF)));
+          }
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int c = 0; c < GM_BN; c += 32) {
+    uint32_t v[32];
+    tmem_ld32(lane_base + c, v);
+    tmem_wait_ld();
+    const int col0 = n0 + c;
+    if (!row_ok || col0 >= N) continue;
+    const bool full = col0 + 32 <= N;
+    float f[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+    if (p.bias) {
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] += p.bias[col0 + j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) f[j] += p.bias[col0 + j];
+      }
+    }
+    __nv_bfloat16* orow = p.out + (int64_t)row * p.ldo + col0;
+    if constexpr (EPI == EPI_RESIDUAL || EPI == EPI_ADD) {
+      const __nv_bfloat16* grow =
+          EPI == EPI_RESIDUAL ? p.gate + (int64_t)p.gate_idx[row] * p.ldg + col0 : nullptr;
+      if (full) {
+        uint4 xr[4], gr[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xr[q] = reinterpret_cast<const uint4*>(orow)[q];
+        if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) gr[q] = reinterpret_cast<const uint4*>(grow)[q];
+        }
+        const uint32_t* xw = reinterpret_cast<const uint32_t*>(xr);
+        const uint32_t* gw = reinterpret_cast<const uint32_t*>(gr);
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float y0 = f[2 * j], y1 = f[2 * j + 1];
+          if constexpr (EPI == EPI_RESIDUAL) {
+            y0 *= bf16_lo(gw[j]);
+            y1 *= bf16_hi(gw[j]);
+          }
+          packed[j] = pack_bf16(bf16_lo(xw[j]) + y0, bf16_hi(xw[j]) + y1);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<uint4*>(orow)[q] =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (col0 + j < N) {
+            float y = f[j];
+            if constexpr (EPI == EPI_RESIDUAL) y *= __bfloat162float(grow[j]);
+            orow[j] = __float2bfloat16(__bfloat162float(orow[j]) + y);
+          }
+        }
+      }
+    } else {  // EPI_STORE
+      if (full) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) packed[j] = pack_bf16(f[2 * j], f[2 * j + 1]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<uint4*>(orow)[q] =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) orow[j] = __float2bfloat16(f[j]);
+      }
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, EpiParams p, int M, int N,
+                     int K) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GM_STAGES * GM_STAGE_BYTES);
+  uint64_t* empty = full + GM_STAGES;
+  uint64_t* tfull = empty + GM_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int num_m = (M + GM_BM - 1) / GM_BM;
+  const int num_n = (N + GM_BN - 1) / GM_BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + GM_BK - 1) / GM_BK;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < GM_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued_mask = 0, issued_par = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * GM_STAGE_BYTES;
+          uint8_t* sB = sA + GM_A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], GM_STAGE_BYTES);
+          tma_load_2d(sA, &tmA, &full[stage], kb * GM_BK, mb * GM_BM);
+          tma_load_2d(sB, &tmB, &full[stage], kb * GM_BK, nb * GM_BN);
+          issued_mask |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == GM_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: every load this thread issued must land before the CTA exits.
+        for (int s = 0; s < GM_STAGES; ++s) {
+          if (!(issued_mask >> s & 1)) continue;
+          uint32_t par = (issued_par >> s) & 1;
+          long long t0 = clock64();
+          while (!mbar_try_wait(&full[s], par) && clock64() - t0 < kWaitBudgetCycles) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(GM_BM, GM_BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tacc = tmem_base + buf * GM_BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aaddr = smem_u32(smem + stage * GM_STAGE_BYTES);
+          const uint32_t baddr = aaddr + GM_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < GM_BK / 16; ++k) {
+            umma_f16_ss(tacc, umma_desc_kmajor_sw128(aaddr + k * 32),
+                        umma_desc_kmajor_sw128(baddr + k * 32), idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == GM_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma_commit(&tfull[buf]);
+      }
+      // All MMAs issued by this thread complete before TMEM is released.
+      umma_commit(mma_done);
+      long long t0 = clock64();
+      while (!mbar_try_wait(mma_done, 0) && clock64() - t0 < kWaitBudgetCycles) {
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int buf = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1);
+      if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      epilogue_tile<EPI>(p, tmem_base + buf * GM_BN, quarter, mb * GM_BM, nb * GM_BN, M, N);
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------- host
+template <int EPI>
+static void launch_gemm(const GemmArgs& a, EpiParams p, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GM_SMEM);
+    attr_set = true;
+  }
+  CUtensorMap ta = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M,
+                                a.lda * 2, GM_BK, GM_BM);
+  CUtensorMap tb = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N,
+                                a.ldb * 2, GM_BK, GM_BN);
+  const int tiles = ((a.M + GM_BM - 1) / GM_BM) * ((a.N + GM_BN - 1) / GM_BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_bf16_kernel<EPI><<<grid, GM_THREADS, GM_SMEM, stream>>>(ta, tb, p, a.M, a.N, a.K);
+}
+
+void launch_gemm_bf16(const GemmArgs& a, int mode, void* out, int64_t ldo, const float* bias,
+                      const void* gate, int64_t ldg, const int* gate_idx, int* err,
+                      cudaStream_t stream) {
+  if (a.M == 0 || a.N == 0) return;
+  EpiParams p{};
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.bias = bias;
+  p.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
+  p.ldg = ldg;
+  p.gate_idx = gate_idx;
+  p.err = err;
+  switch (mode) {
+    case EPI_STORE: launch_gemm<EPI_STORE>(a, p, stream); break;
+    case EPI_RESIDUAL: launch_gemm<EPI_RESIDUAL>(a, p, stream); break;
+    case EPI_SWIGLU: launch_gemm<EPI_SWIGLU>(a, p, stream); break;
+    case EPI_ADD: launch_gemm<EPI_ADD>(a, p, stream); break;
+    default: throw std::runtime_error("unknown GEMM epilogue mode");
+  }
+}
+
+}  // namespace vdn

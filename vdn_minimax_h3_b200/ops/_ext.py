@@ -1,0 +1,73 @@
+"""Loader for the package's compiled sm_100a extension (`vdn_minimax_h3_b200._C`).
+
+The extension is built in place (`python setup.py build_ext --inplace`, or
+`__graft_entry__.build()`), so the `.so` lives inside the package directory. CUDA tensors
+always go through it: if it is missing on a machine that has a GPU, `ext()` raises instead
+of quietly running some other implementation. CPU tensors never reach it -- the CPU path
+of every op is the fp32 PyTorch oracle the kernels are tested against.
+"""
+import importlib
+
+import torch
+
+_EXT = None
+_ERR = {}
+
+
+class KernelError(RuntimeError):
+    """A kernel reported a failure through its device error word."""
+
+
+ERROR_NAMES = {
+    1: "TMA producer wait timed out",
+    2: "MMA issuer wait timed out",
+    3: "epilogue wait timed out",
+    4: "peer flag wait timed out",
+    5: "bad argument",
+    6: "softmax wait timed out",
+}
+
+
+def ext():
+    """The compiled module. Raises ImportError with the build command when absent."""
+    global _EXT
+    if _EXT is None:
+        try:
+            _EXT = importlib.import_module("vdn_minimax_h3_b200._C")
+        except ImportError as exc:  # pragma: no cover - depends on the build
+            raise ImportError(
+                "vdn_minimax_h3_b200._C is not built; run `python setup.py build_ext --inplace` "
+                "(or __graft_entry__.build()). CUDA tensors have no other implementation."
+            ) from exc
+    return _EXT
+
+
+def available():
+    try:
+        ext()
+        return True
+    except ImportError:
+        return False
+
+
+def error_word(device):
+    """The per-device int32 word the kernels write a failure code into."""
+    device = torch.device(device)
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    word = _ERR.get(key)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+        _ERR[key] = word
+    return word
+
+
+def check_device_error(device=None, reset=True):
+    """Synchronise and raise KernelError if any kernel on `device` recorded a failure."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    word = error_word(device)
+    code = int(word.item())
+    if code:
+        if reset:
+            word.zero_()
+        raise KernelError(f"device kernel error {code}: {ERROR_NAMES.get(code, 'unknown')}")
