@@ -9,7 +9,7 @@ from vdn_minimax_h3_b200.ops._ext import check_device_error
 pytestmark = pytest.mark.gpu
 
 SHAPES = [(128, 256, 64), (256, 512, 128), (300, 200, 136), (1000, 768, 1024),
-          (129, 257, 72), (4096, 5376, 512)]
+          (129, 264, 72), (4096, 5376, 512)]
 
 
 def _rel(a, b):

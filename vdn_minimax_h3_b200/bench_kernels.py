@@ -1,0 +1,75 @@
+"""Kernel micro-benchmarks on the VDN-H3 shapes (one GPU, CUDA-event timing).
+
+    python -m vdn_minimax_h3_b200.bench_kernels --gemm
+    python -m vdn_minimax_h3_b200.bench_kernels --attention
+    python -m vdn_minimax_h3_b200.bench_kernels --linear
+
+Each case runs 3 warm-up launches and times 10 with CUDA events on the launching stream;
+operands are larger than the 126 MB L2 for the full-size shapes. Library baselines
+(cuBLAS through torch.matmul, cuDNN/flash SDPA) run beside the package's kernels.
+"""
+import argparse
+import json
+
+import torch
+
+M_ROWS = 104766  # packed rows of a 14.4 s T2VA clip (800 text + 1150 audio + 102*1008 video)
+
+
+def timed(fn, iters=10, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(True), torch.cuda.Event(True)
+    start.record()
+    for _ in range(iters):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def bench_gemm():
+    from vdn_minimax_h3_b200.ops import gemm
+    from vdn_minimax_h3_b200.ops._ext import check_device_error
+    rows = []
+    for name, n, k in [("qkv", 21504, 5376), ("o_proj", 5376, 7168), ("ff_up", 28672, 5376),
+                       ("ff_down", 5376, 14336), ("square", 8192, 8192)]:
+        m = 8192 if name == "square" else M_ROWS
+        x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) / k ** 0.5
+        out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        ours = timed(lambda: gemm.linear(x, w, out=out))
+        check_device_error()
+        lib = timed(lambda: torch.matmul(x, w.t(), out=out))
+        flop = 2.0 * m * n * k
+        row = dict(case=name, M=m, N=n, K=k, ours_ms=ours, ours_tflops=flop / ours / 1e9,
+                   cublas_ms=lib, cublas_tflops=flop / lib / 1e9)
+        if name == "ff_up":
+            wi, _ = gemm.interleave_swiglu_rows(w)
+            row["swiglu_ms"] = timed(lambda: gemm.linear_swiglu(x, wi))
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+        del x, w, out
+        torch.cuda.empty_cache()
+    return rows
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--gemm", action="store_true")
+    p.add_argument("--attention", action="store_true")
+    p.add_argument("--linear", action="store_true")
+    a = p.parse_args(argv)
+    if a.gemm:
+        bench_gemm()
+    if a.attention:
+        from vdn_minimax_h3_b200.ops.attention import bench_attention
+        bench_attention(timed)
+    if a.linear:
+        from vdn_minimax_h3_b200.ops.linear_branch import bench_linear
+        bench_linear(timed)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,301 @@
+"""The inference engine: one DiT block as a short sequence of fused sm_100a kernels.
+
+Per block (T packed rows, D = 5376, inner = 56 x 128):
+
+    n1   = adaln_rmsnorm(x)                          norm.cu (+ per-frame sums of n1)
+    qkvg = n1 @ [Wq; Wk; Wv; Wsgate; Wbeta; Wgdown]^T  gemm.cu, ONE GEMM for the three
+                                                     projections and the three gate inputs
+    q, k = qk_prep(qkvg)                             norm.cu (QK RMSNorm + 3D RoPE)
+    cat[:, :inner] = window_attention(q, k, v) * sigmoid(sgate)   attention.cu
+    cat[video, inner:] = linear branch readout       linear_branch.cu chain
+    x   += gate_msa[idx] * (cat @ [Wo | Wo_lin]^T + bo)  gemm.cu, K-concatenated O-proj and
+                                                     to_out_linear, gated residual epilogue
+    n2   = adaln_rmsnorm(x)
+    h    = swiglu(n2 @ Wup^T + bup)                  gemm.cu, SwiGLU epilogue
+    x   += gate_mlp[idx] * (h @ Wdown^T + bdown)     gemm.cu, gated residual epilogue
+
+This is the arithmetic of the reference's fast_block_forward + HybridAttention
+(src/models/ops/fused_block.py:93-111, src/models/hybrid_attention.py:178-255) with the
+pointwise stretches folded into the GEMM epilogues. Packing the weights is one-way and
+allocation-neutral: the packed buffers are built block by block and every original
+parameter is re-pointed at a view of them, so the module tree (and LoRA/state-dict names)
+keeps working and nothing is held twice.
+"""
+import torch
+import torch.nn.functional as F
+
+from vdn_minimax_h3_b200.models.h3 import H3Transformer
+from vdn_minimax_h3_b200.models.hybrid_attention import HybridAttention
+from vdn_minimax_h3_b200.models.layout import SequenceLayout
+from vdn_minimax_h3_b200.models.window import AttentionPlan, full_cover
+from vdn_minimax_h3_b200.ops import attention as attn_ops
+from vdn_minimax_h3_b200.ops import gemm
+from vdn_minimax_h3_b200.ops import linear_branch as lb
+from vdn_minimax_h3_b200.ops import norm as norm_ops
+
+
+def _f32(t):
+    return None if t is None else t.detach().float().contiguous()
+
+
+class PackedBlock:
+    """Concatenated / interleaved weights of one hybrid DiT block."""
+
+    def __init__(self, block, cfg):
+        attn = block.attn
+        hybrid = isinstance(attn, HybridAttention)
+        orig = attn.orig if hybrid else attn
+        D, H, d = cfg.hidden_size, cfg.num_attention_heads, cfg.attention_head_dim
+        inner = H * d
+        self.hybrid = hybrid
+        self.heads, self.head_dim, self.inner = H, d, inner
+        dev = orig.to_q.weight.device
+        dt = orig.to_q.weight.dtype
+        # ---- QKV + gate inputs: one weight, one GEMM
+        parts = [orig.to_q, orig.to_k, orig.to_v]
+        extra = []
+        self.has_sgate = hybrid and attn.enable_softmax_gate
+        if self.has_sgate:
+            extra.append(("sgate", attn.softmax_gate.up.weight, attn.softmax_gate.up.bias))
+        if hybrid:
+            br = attn.linear_attention
+            extra.append(("beta", br.beta_proj.weight, None))
+            extra.append(("ghid", br.output_gate.down.weight, None))
+        rows = 3 * inner + sum(w.shape[0] for _, w, _ in extra)
+        rows_pad = (rows + 7) // 8 * 8
+        W = torch.zeros(rows_pad, D, device=dev, dtype=dt)
+        b = torch.zeros(rows_pad, device=dev, dtype=torch.float32)
+        off = 0
+        self.cols = {}
+        for name, lin in zip(("q", "k", "v"), parts):
+            W[off:off + inner].copy_(lin.weight)
+            if lin.bias is not None:
+                b[off:off + inner].copy_(lin.bias.float())
+            self.cols[name] = (off, off + inner)
+            lin.weight.data = W[off:off + inner]
+            off += inner
+        for name, w, bias in extra:
+            n = w.shape[0]
+            W[off:off + n].copy_(w)
+            if bias is not None:
+                b[off:off + n].copy_(bias.float())
+            self.cols[name] = (off, off + n)
+            w.data = W[off:off + n]
+            off += n
+        self.w_qkvg, self.b_qkvg = W, b
+        self.norm_q = _f32(orig.norm_q.weight)
+        self.norm_k = _f32(orig.norm_k.weight)
+        self.qk_eps = orig.norm_q.eps
+        # ---- O-projection, K-concatenated with to_out_linear
+        wo = orig.to_out[0].weight
+        if hybrid:
+            wl = attn.to_out_linear.weight
+            Wo = torch.empty(D, inner + wl.shape[1], device=dev, dtype=dt)
+            Wo[:, :inner].copy_(wo)
+            Wo[:, inner:].copy_(wl)
+            orig.to_out[0].weight.data = Wo[:, :inner]
+            attn.to_out_linear.weight.data = Wo[:, inner:]
+        else:
+            Wo = wo.contiguous()
+        self.w_o, self.b_o = Wo, _f32(orig.to_out[0].bias)
+        # ---- feed-forward
+        ff = block.ff
+        self.ff_act = ff.activation
+        up = ff.net[0].proj
+        if self.ff_act == "swiglu":
+            wi, bi = gemm.interleave_swiglu_rows(up.weight.data, up.bias)
+            up.weight.data = wi   # NOTE: the module now holds the interleaved layout
+            self.ff_interleaved = True
+            self.w_up, self.b_up = wi, _f32(bi)
+        else:
+            self.ff_interleaved = False
+            self.w_up, self.b_up = up.weight.data, _f32(up.bias)
+        self.w_down, self.b_down = ff.net[2].weight.data, _f32(ff.net[2].bias)
+        # ---- norms / modulation
+        self.norm1 = _f32(block.norm1.weight)
+        self.norm2 = _f32(block.norm2.weight)
+        self.eps = block.norm1.eps
+        self.adaln_w = block.adaln_proj.linear.weight.data
+        self.adaln_b = _f32(block.adaln_proj.linear.bias)
+        if hybrid:
+            br = attn.linear_attention
+            self.gate_up_w = br.output_gate.up.weight.data
+            self.gate_up_b = _f32(br.output_gate.up.bias)
+
+
+class InferenceEngine:
+    """Runs an H3Transformer (dense or hybrid) forward through the fused kernels."""
+
+    def __init__(self, model: H3Transformer):
+        self.model = model
+        self.cfg = model.config
+        self.blocks = []
+        with torch.no_grad():
+            for block in model.transformer_blocks:
+                self.blocks.append(PackedBlock(block, self.cfg))
+                if block.ff.activation == "swiglu":
+                    block.ff.net[0].interleaved = 256
+        self._plan_key = None
+        self.plan = None
+        self.dense_plan = None
+        self._buffers = {}
+        self._cat_dirty = False
+
+    # --------------------------------------------------------------------- helpers
+    def _plans(self, attn, layout, T):
+        key = (layout, attn.radius, attn.chunk, attn.anchor_frames) if attn is not None else (T,)
+        if key != self._plan_key:
+            dev = self.blocks[0].w_qkvg.device
+            if attn is None or layout is None:
+                from vdn_minimax_h3_b200.models.layout import SequenceLayout as SL
+                lay = SL(seq_len=T, video_start=T, num_frames=0, tokens_per_frame=1)
+                self.plan = AttentionPlan(lay, [], "none", device=dev, dense=True)
+                self.covered = True
+            else:
+                bounds = attn.bounds(layout)
+                self.covered = full_cover(bounds, layout.num_frames)
+                self.plan = AttentionPlan(layout, bounds, attn.anchor_frames, device=dev,
+                                          dense=self.covered)
+                self.bounds = bounds
+            self._plan_key = key
+        return self.plan
+
+    def _buf(self, name, shape, dtype, device, zero=False):
+        b = self._buffers.get(name)
+        if b is None or tuple(b.shape) != tuple(shape) or b.dtype != dtype or b.device != device:
+            b = (torch.zeros if zero else torch.empty)(shape, dtype=dtype, device=device)
+            self._buffers[name] = b
+            if name == "cat":
+                self._cat_dirty = False
+        return b
+
+    # ----------------------------------------------------------------------- block
+    def block_forward(self, i, x, temb_act, adaln_idx, rope, layout):
+        """x [T, D] bf16 updated in place."""
+        pb = self.blocks[i]
+        block = self.model.transformer_blocks[i]
+        attn = block.attn
+        cfg = self.cfg
+        T, D = x.shape
+        dev = x.device
+        H, d, inner = pb.heads, pb.head_dim, pb.inner
+        # AdaLN table for this block: [n_t * MOD, 6D]
+        table = gemm.linear(temb_act, pb.adaln_w, pb.adaln_b).view(-1, 6 * D)
+        linear_on = (pb.hybrid and layout is not None and attn.linear_attention_enabled
+                     and not attn.teacher_mode)
+        plan = self._plans(attn if pb.hybrid and not attn.teacher_mode else None, layout, T)
+        linear_on = linear_on and not self.covered
+        Fr = layout.num_frames if linear_on else 0
+        S = layout.tokens_per_frame if linear_on else 1
+        vs = layout.video_start if linear_on else 0
+        frame_sums = torch.zeros(Fr, D, dtype=torch.float32, device=dev) if linear_on else None
+        n1 = self._buf("normed", (T, D), x.dtype, dev)
+        norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1,
+                               frame_sums=frame_sums, video_start=vs, tokens_per_frame=S,
+                               num_frames=Fr)
+        qkvg = self._buf("qkvg", (T, pb.w_qkvg.shape[0]), x.dtype, dev)
+        gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
+        c = pb.cols
+        q_raw = qkvg[:, c["q"][0]:c["q"][1]]
+        k_raw = qkvg[:, c["k"][0]:c["k"][1]]
+        v = qkvg[:, c["v"][0]:c["v"][1]]
+        cos, sin = rope
+        q = self._buf("q", (T, inner), x.dtype, dev)
+        k = self._buf("k", (T, inner), x.dtype, dev)
+        norm_ops.qk_prep(q_raw, H, pb.norm_q, pb.qk_eps, cos, sin, out=q)
+        norm_ops.qk_prep(k_raw, H, pb.norm_k, pb.qk_eps, cos, sin, out=k)
+        kcat = pb.w_o.shape[1]
+        cat = self._buf("cat", (T, kcat), x.dtype, dev, zero=True)
+        sgate = qkvg[:, c["sgate"][0]:c["sgate"][1]] if pb.has_sgate else None
+        attn_ops.window_attention(q.view(T, H, d), k.view(T, H, d), v.view(T, H, d), plan,
+                                  d ** -0.5, gate_logits=sgate, out=cat[:, :inner])
+        if pb.hybrid:
+            if linear_on:
+                self._linear_branch(pb, attn, layout, n1, qkvg, frame_sums, cat[:, inner:])
+            elif self._cat_dirty:
+                cat[:, inner:].zero_()
+                self._cat_dirty = False
+        gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D], adaln_idx)
+        n2 = n1
+        norm_ops.adaln_rmsnorm(x, pb.norm2, pb.eps, table, 3 * D, 4 * D, adaln_idx, out=n2)
+        if pb.ff_interleaved:
+            h = gemm.linear_swiglu(n2, pb.w_up, pb.b_up)
+        else:
+            h = F.gelu(gemm.linear(n2, pb.w_up, pb.b_up).float(), approximate="tanh").to(x.dtype)
+        gemm.linear_gated_residual(h, pb.w_down, pb.b_down, x, table[:, 5 * D:6 * D], adaln_idx)
+        return x
+
+    def _linear_branch(self, pb, attn, layout, n1, qkvg, frame_sums, out):
+        """The linear branch over the video rows; writes token-major readout into `out`
+        (video rows; anchor frames zero under anchors 'both')."""
+        br = attn.linear_attention
+        c = pb.cols
+        H, d = pb.heads, pb.head_dim
+        Fr, S = layout.num_frames, layout.tokens_per_frame
+        vs, ve = layout.video_start, layout.video_end
+        skip = attn.anchor_frames == "both"
+        f0, f1 = (1, Fr - 1) if skip else (0, Fr)
+        if f1 - f0 <= 0:
+            out[vs:ve].zero_()
+            return
+        r0, r1 = vs + f0 * S, vs + f1 * S
+        nF = f1 - f0
+        q_raw = qkvg[r0:r1, c["q"][0]:c["q"][1]].view(-1, H, d)
+        k_raw = qkvg[r0:r1, c["k"][0]:c["k"][1]].view(-1, H, d)
+        v_raw = qkvg[r0:r1, c["v"][0]:c["v"][1]].view(-1, H, d)
+        conv = br.short_conv
+        fs = layout.frame_size if conv is not None else None
+        feats = []
+        for t, proj in ((q_raw, "q"), (k_raw, "k"), (v_raw, "v")):
+            if conv is not None and proj in conv.projs:
+                w_sp, w_tm = conv.weights(proj)
+                feats.append(lb.conv_features(t, w_sp, w_tm, nF, fs, proj != "v"))
+            else:
+                feats.append(lb.activate(t, proj != "v"))
+        qf, kf, vf = feats
+        beta = torch.sigmoid(qkvg[r0:r1, c["beta"][0]:c["beta"][1]].float())
+        A, B = lb.frame_statistics(kf.view(nF, S, H, d), vf.view(nF, S, H, d),
+                                   beta.view(nF, S, H), a_fp32=br.a_fp32)
+        del kf, vf
+        frame_mean = frame_sums[f0:f1] / S
+        alpha = br.alpha(frame_mean)
+        text_state = None
+        if attn.enable_text_state:
+            ts, te = layout.text_range
+            text_raw = tuple(qkvg[ts:te, c[n][0]:c[n][1]].view(-1, H, d) for n in "qkv")
+            text_beta = torch.sigmoid(qkvg[ts:te, c["beta"][0]:c["beta"][1]].float())
+            text_state = br.text_state(None, text_raw, text_beta=text_beta)
+        trans, inj = lb.factor_apply(br.backend(S), alpha, A, B)
+        prefix, suffix = lb.run_scans(trans, inj, text_state)
+        bounds = self.bounds[f0:f1]
+        if skip:
+            bounds = [(lo - 1, hi - 1) for lo, hi in bounds]
+        state = lb.gather(prefix, suffix, alpha, bounds, br.bridge, text_state, out_dtype=n1.dtype)
+        del prefix, suffix, trans, inj
+        ghid = qkvg[r0:r1, c["ghid"][0]:c["ghid"][1]]
+        gate_logits = gemm.linear(ghid, pb.gate_up_w, pb.gate_up_b)
+        lb.readout(qf.view(nF, S, H, d), state, br.norm.weight, gate_logits.view(-1, H, d),
+                   br.norm.eps, out=out[r0:r1], gate_logits=True)
+        self._cat_dirty = True
+
+    # --------------------------------------------------------------------- forward
+    @torch.no_grad()
+    def forward(self, hidden_states, audio_hidden_states, encoder_hidden_states, timestep,
+                timestep_indices, token_tags, position_ids, video_indices, audio_indices,
+                text_indices, layout: SequenceLayout = None, return_dict=False):
+        m = self.model
+        packed, temb, adaln_idx, rope = m.embed(
+            hidden_states, audio_hidden_states, encoder_hidden_states, timestep,
+            timestep_indices, token_tags, position_ids, video_indices, audio_indices, text_indices)
+        x = packed[0].contiguous()
+        adaln_idx = adaln_idx.to(torch.int32).contiguous()
+        temb_act = F.silu(temb.float()).to(x.dtype).contiguous()
+        rope = (rope[0].contiguous(), rope[1].contiguous())
+        if layout is None:
+            first = next((b.attn for b in m.transformer_blocks if isinstance(b.attn, HybridAttention)), None)
+            layout = None if first is None else first.layout
+        for i in range(len(self.blocks)):
+            self.block_forward(i, x, temb_act, adaln_idx, rope, layout)
+        return m.head(x.unsqueeze(0), temb, timestep_indices, video_indices, audio_indices)
+
+    __call__ = forward

@@ -1,0 +1,65 @@
+"""Window softmax attention over an AttentionPlan (models/window.py).
+
+CUDA tensors run the sm_100a flash-attention kernel of csrc/attention.cu: tcgen05 MMAs for
+S = Q K^T and O += P V with both accumulators in TMEM, Q/K/V tiles by TMA (no multicast),
+online softmax in registers, K/V walked over the plan's contiguous row ranges in place (no
+gather, no mask tensor), the per-head softmax gate applied in the epilogue. CPU tensors run
+the dense-segment oracle below.
+
+Reference parity: the window softmax of src/models/softmax_attention/{window,decomposed,
+flex_attention}.py and the gate of kernels.py:51-67.
+"""
+import torch
+import torch.nn.functional as F
+
+from vdn_minimax_h3_b200.ops._ext import error_word, ext
+
+
+def window_attention_reference(q, k, v, plan, scale, gate_logits=None):
+    """q, k, v [T, H, d]; returns [T, H*d] (gated when gate_logits [T, H] is given)."""
+    T, H, d = q.shape
+    out = torch.empty(T, H, d, dtype=torch.float32, device=q.device)
+    for seg in plan.segments:
+        kv_rows = torch.cat([torch.arange(a, b, device=q.device) for a, b in seg.kv])
+        qs = q[seg.q_start:seg.q_end].float().transpose(0, 1)
+        ks = k[kv_rows].float().transpose(0, 1)
+        vs = v[kv_rows].float().transpose(0, 1)
+        o = F.scaled_dot_product_attention(qs[None], ks[None], vs[None], scale=scale)[0]
+        out[seg.q_start:seg.q_end] = o.transpose(0, 1)
+    if gate_logits is not None:
+        out = out * torch.sigmoid(gate_logits.float())[..., None]
+    return out.reshape(T, H * d).to(q.dtype)
+
+
+def window_attention(q, k, v, plan, scale, gate_logits=None, out=None):
+    """q, k, v: [T, H, d] views (row stride allowed, d contiguous). out: [T, H*d] view."""
+    if not q.is_cuda:
+        y = window_attention_reference(q, k, v, plan, scale, gate_logits)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    T, H, d = q.shape
+    if out is None:
+        out = torch.empty(T, H * d, dtype=q.dtype, device=q.device)
+    ext().window_attention(q, k, v, plan.tiles, plan.kv, gate_logits, out, float(scale),
+                           error_word(q.device))
+    return out
+
+
+def bench_attention(timed):  # pragma: no cover - GPU tool
+    import json
+    from vdn_minimax_h3_b200.models.layout import SequenceLayout
+    from vdn_minimax_h3_b200.models.window import AttentionPlan, window_bounds
+    T_text, T_audio, Fr, S, H, d = 800, 1150, 102, 1008, 56, 128
+    layout = SequenceLayout(seq_len=T_text + T_audio + Fr * S, video_start=T_text + T_audio,
+                            num_frames=Fr, tokens_per_frame=S, frame_height=24, frame_width=42,
+                            text_start=0, text_len=T_text)
+    plan = AttentionPlan(layout, window_bounds(Fr, 1, 5), "both", device="cuda")
+    T = layout.seq_len
+    q = torch.randn(T, H, d, device="cuda", dtype=torch.bfloat16)
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    ms = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
+    fl = plan.flops(H, d)
+    print(json.dumps(dict(case="window_attention_c1_both", T=T, ms=ms,
+                          tflops=fl / ms / 1e9)), flush=True)

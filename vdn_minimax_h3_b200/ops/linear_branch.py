@@ -1,0 +1,133 @@
+"""The linear branch's inference stages.
+
+Each function is one stage of the forward-only body
+(models/linear_branch.py: BidirectionalLinearBranch._readout_inference). On CUDA tensors a
+stage runs its sm_100a kernel from csrc/linear_branch.cu; on CPU it runs the fp32 PyTorch
+oracle the kernel is tested against (reference src/models/linear_attention/{features,scan,
+delta_rule,kernels}.py).
+"""
+import torch
+import torch.nn.functional as F
+
+from vdn_minimax_h3_b200.models import scan as scan_ref
+from vdn_minimax_h3_b200.models.delta_rule import SanaDelta, VdnDelta
+from vdn_minimax_h3_b200.models.linear_branch import activate as activate_ref
+from vdn_minimax_h3_b200.models.linear_branch import conv_features_reference
+from vdn_minimax_h3_b200.ops._ext import error_word, ext
+
+
+def _native(t):
+    return t.is_cuda
+
+
+# ---------------------------------------------------------------------------- features
+def activate(tokens, l2norm):
+    """SiLU [+ L2 over d]: [N, H, d] -> same shape, same dtype."""
+    if not _native(tokens):
+        return activate_ref(tokens, l2norm)
+    out = torch.empty(tokens.shape, dtype=tokens.dtype, device=tokens.device)
+    ext().lb_activate(tokens, out, bool(l2norm))
+    return out
+
+
+def conv_features(tokens, w_sp, w_tm, num_frames, frame_size, l2norm):
+    """5x5 depthwise spatial conv, 5-tap temporal conv, SiLU [, L2] in one pass."""
+    if not _native(tokens):
+        return conv_features_reference(tokens, w_sp, w_tm, num_frames, frame_size, l2norm)
+    gh, gw = frame_size
+    out = torch.empty(tokens.shape, dtype=tokens.dtype, device=tokens.device)
+    ext().lb_conv_features(tokens, w_sp.float().contiguous(), w_tm.float().contiguous(), out,
+                           num_frames, gh, gw, bool(l2norm))
+    return out
+
+
+# -------------------------------------------------------------------------- statistics
+def frame_statistics(k, v, beta, a_fp32=True):
+    """k, v [F, S, n, d] (token-major views of the projections); beta [F, S, n].
+    -> A [F, n, d, d] fp32 symmetric, B [F, n, d, d] fp32."""
+    if not _native(k):
+        return scan_ref.frame_statistics(k.permute(0, 2, 1, 3), v.permute(0, 2, 1, 3),
+                                         beta.permute(0, 2, 1), a_fp32=a_fp32)
+    Fr, S, n, d = k.shape
+    A = torch.empty(Fr, n, d, d, dtype=torch.float32, device=k.device)
+    B = torch.empty_like(A)
+    ext().lb_frame_stats(k, v, beta.float().contiguous(), A, B, error_word(k.device))
+    return A, B
+
+
+def factor_apply(backend, alpha, A, B):
+    """transition = diag(alpha) * M^-1 (row scale), injection = (b B) M^-1 for the vdn
+    rules; the sana rule is elementwise."""
+    if not _native(A) or isinstance(backend, SanaDelta):
+        return backend.factor_apply(alpha, A, B)
+    assert isinstance(backend, VdnDelta)
+    trans = torch.empty_like(A)
+    inj = torch.empty_like(B)
+    ext().lb_spd_factor(A.contiguous(), B.contiguous(), alpha.float().contiguous(), trans, inj,
+                        float(backend.a_scale), float(backend.b_scale), error_word(A.device))
+    return trans, inj
+
+
+def run_scans(trans, inj, text_state=None):
+    """prefix/suffix banks of the two serial recurrences. [F, n, d, d] fp32."""
+    if not _native(trans):
+        return scan_ref.run_scans(trans, inj, text_state)
+    prefix = torch.empty_like(inj)
+    suffix = torch.empty_like(inj)
+    start = None if text_state is None else text_state.float().contiguous()
+    ext().lb_scan(trans.contiguous(), inj.contiguous(), start, prefix, suffix, error_word(trans.device))
+    return prefix, suffix
+
+
+def gather(prefix, suffix, alpha, bounds, bridge, text_state, out_dtype=torch.bfloat16):
+    """The complement of each frame's window, bridged into the frame. [F, n, d, d]."""
+    if not _native(prefix):
+        return scan_ref.gather_linear_state(prefix, suffix, alpha, bounds, bridge=bridge,
+                                            text_state=text_state, out_dtype=out_dtype)
+    Fr = prefix.shape[0]
+    lo = torch.tensor([b[0] for b in bounds], dtype=torch.int32)
+    hi = torch.tensor([b[1] for b in bounds], dtype=torch.int32)
+    bnd = torch.stack([lo, hi], dim=1).to(prefix.device)
+    out = torch.empty(prefix.shape, dtype=out_dtype, device=prefix.device)
+    start = None if text_state is None else text_state.float().contiguous()
+    ext().lb_gather(prefix, suffix, alpha.float().contiguous(), bnd, start, out,
+                    bridge == "alpha")
+    return out
+
+
+# --------------------------------------------------------------------------- readout
+def readout_reference(q, state, norm_w, gate, eps, gate_logits=False):
+    Fr, S, n, d = q.shape
+    if gate_logits:
+        gate = torch.sigmoid(gate.float())
+    r = torch.einsum("fhvk,fshk->fshv", state.float(), q.float())
+    ms = r.pow(2).mean(-1, keepdim=True)
+    r = r * torch.rsqrt(ms + eps) * norm_w.float()
+    return (r.reshape(Fr * S, n, d) * gate.float()).reshape(Fr * S, n * d).to(q.dtype)
+
+
+def readout(q, state, norm_w, gate, eps, out=None, gate_logits=False):
+    """RMSNorm(q . state^T) * w * gate, token-major [F*S, n*d]. `out` may be a strided view
+    (the right half of the O-projection input). With gate_logits the gate is sigmoid(gate)."""
+    if not _native(q):
+        r = readout_reference(q, state, norm_w, gate, eps, gate_logits)
+        if out is not None:
+            out.copy_(r)
+            return out
+        return r
+    Fr, S, n, d = q.shape
+    if out is None:
+        out = torch.empty(Fr * S, n * d, dtype=q.dtype, device=q.device)
+    ext().lb_readout(q, state.contiguous(), norm_w.float().contiguous(), gate, out, float(eps),
+                     bool(gate_logits), error_word(q.device))
+    return out
+
+
+def bench_linear(timed):  # pragma: no cover - GPU tool
+    import json
+    Fr, S, n, d = 100, 1008, 56, 128
+    k = torch.randn(Fr, S, n, d, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn_like(k)
+    beta = torch.rand(Fr, S, n, device="cuda")
+    ms = timed(lambda: frame_statistics(k, v, beta))
+    print(json.dumps(dict(case="frame_stats", ms=ms)), flush=True)
