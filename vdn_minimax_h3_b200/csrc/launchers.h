@@ -18,4 +18,18 @@ void launch_gemm_bf16(const GemmArgs& a, int mode, void* out, int64_t ldo, const
                       const void* gate, int64_t ldg, const int* gate_idx, int* err,
                       cudaStream_t stream);
 
+void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps, const void* table,
+                          int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
+                          int64_t ldo, int T, int D, cudaStream_t stream);
+void launch_frame_sums(const void* x, int64_t ldx, int F, int S, int D, float* out,
+                       cudaStream_t stream);
+void launch_qk_prep(const void* src, int64_t lds, int T, int H, int d, const float* w, float eps,
+                    const float* cosv, const float* sinv, int rot, void* out, int64_t ldo,
+                    cudaStream_t stream);
+
+void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                             int64_t ldv, int T, int H, const int* tiles, int n_tiles,
+                             const int* kv, const void* gate, int64_t ldg, void* out,
+                             int64_t ldo, float scale, int* err, cudaStream_t stream);
+
 }  // namespace vdn

@@ -1,0 +1,191 @@
+// Row-wise normalisation kernels of the DiT block (sm_100a).
+//
+//   adaln_rmsnorm   out = RMSNorm(x) * w * (1 + table[idx[r], scale]) + table[idx[r], shift]
+//                   (reference src/models/ops/fused_block.py:41-44, fused: one read of x,
+//                   one write, the per-row AdaLN gather done in registers)
+//   frame_sums      per-frame column sums of the video rows (fp32), for the linear branch's
+//                   alpha (reference linear_attention/branch.py:440-442)
+//   qk_prep         per-head RMSNorm then rotate-half RoPE (softmax_attention/kernels.py:27-30)
+#include "common.cuh"
+#include "launchers.h"
+
+namespace vdn {
+
+// One warp per row; VPL 16-byte vectors per lane held in registers.
+template <int VPL>
+__global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const float* __restrict__ w, float eps,
+    const __nv_bfloat16* __restrict__ table, int64_t ldt, int shift_col, int scale_col,
+    const int* __restrict__ idx, __nv_bfloat16* __restrict__ out, int64_t ldo, int T, int D) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const int nvec = D >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * ldx);
+  uint4 v[VPL];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+      v[i] = xr[c];
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float a = bf16_lo(u[j]), b = bf16_hi(u[j]);
+        ss += a * a + b * b;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / (float)D + eps);
+  const int ti = idx[row];
+  const __nv_bfloat16* trow = table + (int64_t)ti * ldt;
+  uint4* orow = reinterpret_cast<uint4*>(out + (int64_t)row * ldo);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+      const uint4 sh = *reinterpret_cast<const uint4*>(trow + shift_col + c * 8);
+      const uint4 sc = *reinterpret_cast<const uint4*>(trow + scale_col + c * 8);
+      const uint32_t* shu = reinterpret_cast<const uint32_t*>(&sh);
+      const uint32_t* scu = reinterpret_cast<const uint32_t*>(&sc);
+      uint32_t res[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = c * 8 + 2 * j;
+        float w0 = w ? w[col] : 1.f, w1 = w ? w[col + 1] : 1.f;
+        float a = bf16_lo(u[j]) * rstd * w0, b = bf16_hi(u[j]) * rstd * w1;
+        a = a * (1.f + bf16_lo(scu[j])) + bf16_lo(shu[j]);
+        b = b * (1.f + bf16_hi(scu[j])) + bf16_hi(shu[j]);
+        res[j] = pack_bf16(a, b);
+      }
+      orow[c] = make_uint4(res[0], res[1], res[2], res[3]);
+    }
+  }
+}
+
+void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps, const void* table,
+                          int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
+                          int64_t ldo, int T, int D, cudaStream_t stream) {
+  if (T == 0) return;
+  const int nvec = D / 8;
+  const int need = (nvec + 31) / 32;
+  dim3 grid((T + 7) / 8), block(256);
+  auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto tb = reinterpret_cast<const __nv_bfloat16*>(table);
+  auto ob = reinterpret_cast<__nv_bfloat16*>(out);
+#define VDN_ADALN(N)                                                                          \
+  adaln_rmsnorm_kernel<N><<<grid, block, 0, stream>>>(xb, ldx, w, eps, tb, ldt, shift_col,    \
+                                                       scale_col, idx, ob, ldo, T, D)
+  if (need <= 1) VDN_ADALN(1);
+  else if (need <= 2) VDN_ADALN(2);
+  else if (need <= 4) VDN_ADALN(4);
+  else if (need <= 8) VDN_ADALN(8);
+  else if (need <= 16) VDN_ADALN(16);
+  else if (need <= 24) VDN_ADALN(24);
+  else VDN_ADALN(48);
+#undef VDN_ADALN
+}
+
+// Column sums of `rows` video rows grouped by frame: out[f, c] = sum_s x[vs + f*S + s, c].
+// grid (F, ceil(D/256)), 256 threads; lane owns 8 consecutive columns, warps stride rows.
+__global__ void __launch_bounds__(256) frame_sums_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         int64_t ldx, int S, int D,
+                                                         float* __restrict__ out) {
+  __shared__ float red[8][256];
+  const int f = blockIdx.x;
+  const int c0 = blockIdx.y * 256;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col = c0 + lane * 8;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (col < D) {
+    for (int s = warp; s < S; s += 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + ((int64_t)f * S + s) * ldx + col);
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] += bf16_lo(u[j]);
+        acc[2 * j + 1] += bf16_hi(u[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = acc[j];
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (c0 + t < D) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += red[w][t];
+    out[(int64_t)f * D + c0 + t] = s;
+  }
+}
+
+void launch_frame_sums(const void* x, int64_t ldx, int F, int S, int D, float* out,
+                       cudaStream_t stream) {
+  if (F == 0) return;
+  dim3 grid(F, (D + 255) / 256);
+  frame_sums_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, S,
+                                              D, out);
+}
+
+// One warp per (row, head). Generic head_dim <= 256 (multiple of 2), rotary_dim <= head_dim.
+__global__ void __launch_bounds__(256) qk_prep_kernel(
+    const __nv_bfloat16* __restrict__ src, int64_t lds, int T, int H, int d,
+    const float* __restrict__ w, float eps, const float* __restrict__ cosv,
+    const float* __restrict__ sinv, int rot, __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  __shared__ float buf[8][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * 8 + warp;
+  if (item >= (int64_t)T * H) return;
+  const int row = (int)(item / H), h = (int)(item % H);
+  const __nv_bfloat16* s = src + (int64_t)row * lds + h * d;
+  float* b = buf[warp];
+  float ss = 0.f;
+  for (int i = lane * 2; i < d; i += 64) {
+    const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(s + i);
+    const float a = __bfloat162float(p.x), c = __bfloat162float(p.y);
+    b[i] = a;
+    b[i + 1] = c;
+    ss += a * a + c * c;
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / (float)d + eps);
+  for (int i = lane * 2; i < d; i += 64) {
+    b[i] *= rstd * w[i];
+    b[i + 1] *= rstd * w[i + 1];
+  }
+  __syncwarp();
+  const float* cr = cosv + (int64_t)row * rot;
+  const float* sr = sinv + (int64_t)row * rot;
+  const int half = rot >> 1;
+  __nv_bfloat16* o = out + (int64_t)row * ldo + h * d;
+  for (int i = lane * 2; i < d; i += 64) {
+    float r[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int e = i + j;
+      if (e < rot) {
+        const float rotated = e < half ? -b[e + half] : b[e - half];
+        r[j] = b[e] * cr[e] + rotated * sr[e];
+      } else {
+        r[j] = b[e];
+      }
+    }
+    *reinterpret_cast<__nv_bfloat162*>(o + i) = __floats2bfloat162_rn(r[0], r[1]);
+  }
+}
+
+void launch_qk_prep(const void* src, int64_t lds, int T, int H, int d, const float* w, float eps,
+                    const float* cosv, const float* sinv, int rot, void* out, int64_t ldo,
+                    cudaStream_t stream) {
+  const int64_t items = (int64_t)T * H;
+  if (items == 0) return;
+  qk_prep_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(src), lds, T, H, d, w, eps, cosv, sinv, rot,
+      reinterpret_cast<__nv_bfloat16*>(out), ldo);
+}
+
+}  // namespace vdn

@@ -94,6 +94,105 @@ void gemm_bf16_swiglu(torch::Tensor A, torch::Tensor B, torch::Tensor H,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+
+void adaln_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, torch::Tensor table,
+                   int64_t shift_col, int64_t scale_col, torch::Tensor idx, torch::Tensor out) {
+  check_2d_bf16(x, "x");
+  check_2d_bf16(table, "table");
+  check_2d_bf16(out, "out");
+  const int T = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % 8 == 0, "hidden size must be a multiple of 8");
+  TORCH_CHECK(out.size(0) == T && out.size(1) == D, "out shape mismatch");
+  TORCH_CHECK(shift_col % 8 == 0 && scale_col % 8 == 0, "table columns must be 8-aligned");
+  TORCH_CHECK(shift_col + D <= table.size(1) && scale_col + D <= table.size(1), "table too narrow");
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.is_contiguous() &&
+                  idx.numel() >= T, "idx must be contiguous int32 [T]");
+  c10::cuda::CUDAGuard g(x.device());
+  launch_adaln_rmsnorm(x.data_ptr(), x.stride(0), opt_f32(w, D, "w"), (float)eps, table.data_ptr(),
+                       table.stride(0), (int)shift_col, (int)scale_col, idx.data_ptr<int>(),
+                       out.data_ptr(), out.stride(0), T, D, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void frame_sums(torch::Tensor x, int64_t F, int64_t S, torch::Tensor out) {
+  check_2d_bf16(x, "x");
+  const int D = x.size(1);
+  TORCH_CHECK(x.size(0) >= F * S, "x has fewer than F*S rows");
+  TORCH_CHECK(D % 8 == 0, "D must be a multiple of 8");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() &&
+                  out.numel() == F * D, "out must be contiguous fp32 [F, D]");
+  c10::cuda::CUDAGuard g(x.device());
+  launch_frame_sums(x.data_ptr(), x.stride(0), (int)F, (int)S, D, out.data_ptr<float>(),
+                    at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void qk_prep(torch::Tensor src, int64_t H, torch::Tensor w, double eps, torch::Tensor cosv,
+             torch::Tensor sinv, torch::Tensor out) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16 && src.dim() == 2 &&
+                  src.stride(1) == 1, "src must be bf16 [T, H*d] with contiguous rows");
+  check_2d_bf16(out, "out");
+  const int T = src.size(0);
+  const int d = src.size(1) / H;
+  TORCH_CHECK(d * H == src.size(1) && d % 2 == 0 && d <= 256, "bad head_dim");
+  TORCH_CHECK(src.stride(0) % 2 == 0, "src row stride must be even");
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kFloat && w.numel() == d, "w fp32 [d]");
+  TORCH_CHECK(cosv.scalar_type() == at::kFloat && sinv.scalar_type() == at::kFloat &&
+                  cosv.is_contiguous() && sinv.is_contiguous() && cosv.size(0) >= T,
+              "cos/sin must be contiguous fp32 [T, rot]");
+  const int rot = cosv.size(1);
+  TORCH_CHECK(rot <= d && rot % 2 == 0, "rotary dim must be even and <= head_dim");
+  c10::cuda::CUDAGuard g(src.device());
+  launch_qk_prep(src.data_ptr(), src.stride(0), T, (int)H, d, w.data_ptr<float>(), (float)eps,
+                 cosv.data_ptr<float>(), sinv.data_ptr<float>(), rot, out.data_ptr(),
+                 out.stride(0), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+
+namespace {
+void check_heads(const torch::Tensor& t, const char* name, int64_t T, int64_t H) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 3, name,
+              " must be a bf16 CUDA [T, H, d] tensor");
+  TORCH_CHECK(t.size(0) == T && t.size(1) == H && t.size(2) == 128, name,
+              " must be [T, H, 128], got ", t.sizes());
+  TORCH_CHECK(t.stride(2) == 1 && t.stride(1) == 128, name,
+              " must have contiguous heads (stride(1)=128, stride(2)=1)");
+  TORCH_CHECK((t.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              name, " row stride / base must be 16-byte aligned");
+}
+}  // namespace
+
+void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles,
+                      torch::Tensor kv, c10::optional<torch::Tensor> gate, torch::Tensor out,
+                      double scale, torch::Tensor err) {
+  const int64_t T = q.size(0), H = q.size(1);
+  check_heads(q, "q", T, H);
+  check_heads(k, "k", T, H);
+  check_heads(v, "v", T, H);
+  check_2d_bf16(out, "out");
+  TORCH_CHECK(out.size(0) == T && out.size(1) == H * 128, "out must be [T, H*128]");
+  TORCH_CHECK(tiles.is_cuda() && tiles.scalar_type() == at::kInt && tiles.is_contiguous() &&
+                  tiles.dim() == 2 && tiles.size(1) == 4, "tiles must be int32 [n, 4]");
+  TORCH_CHECK(kv.is_cuda() && kv.scalar_type() == at::kInt && kv.is_contiguous() &&
+                  kv.dim() == 2 && kv.size(1) == 8, "kv must be int32 [n_seg, 8]");
+  const void* gp = nullptr;
+  int64_t ldg = 0;
+  if (gate) {
+    TORCH_CHECK(gate->is_cuda() && gate->scalar_type() == at::kBFloat16 && gate->dim() == 2 &&
+                    gate->size(0) == T && gate->size(1) == H && gate->stride(1) == 1,
+                "gate logits must be bf16 [T, H] with contiguous heads");
+    gp = gate->data_ptr();
+    ldg = gate->stride(0);
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  launch_window_attention(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(),
+                          v.stride(0), (int)T, (int)H, tiles.data_ptr<int>(), (int)tiles.size(0),
+                          kv.data_ptr<int>(), gp, ldg, out.data_ptr(), out.stride(0),
+                          (float)scale, err_ptr(err), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace vdn
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -103,4 +202,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "bf16 tcgen05 GEMM with gated-residual epilogue: X += gate[idx] * (A @ B^T + bias)");
   m.def("gemm_bf16_swiglu", &vdn::gemm_bf16_swiglu,
         "bf16 tcgen05 GEMM with SwiGLU epilogue over interleaved value|gate weight tiles");
+  m.def("adaln_rmsnorm", &vdn::adaln_rmsnorm, "RMSNorm * w * (1 + scale[idx]) + shift[idx]");
+  m.def("frame_sums", &vdn::frame_sums, "per-frame fp32 column sums of video rows");
+  m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");
+  m.def("window_attention", &vdn::window_attention,
+        "tcgen05 window softmax attention over an AttentionPlan (gated epilogue)");
 }

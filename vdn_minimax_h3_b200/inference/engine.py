@@ -188,11 +188,9 @@ class InferenceEngine:
         Fr = layout.num_frames if linear_on else 0
         S = layout.tokens_per_frame if linear_on else 1
         vs = layout.video_start if linear_on else 0
-        frame_sums = torch.zeros(Fr, D, dtype=torch.float32, device=dev) if linear_on else None
         n1 = self._buf("normed", (T, D), x.dtype, dev)
-        norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1,
-                               frame_sums=frame_sums, video_start=vs, tokens_per_frame=S,
-                               num_frames=Fr)
+        norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1)
+        frame_sums = norm_ops.frame_sums(n1[vs:vs + Fr * S], Fr, S) if linear_on else None
         qkvg = self._buf("qkvg", (T, pb.w_qkvg.shape[0]), x.dtype, dev)
         gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
         c = pb.cols

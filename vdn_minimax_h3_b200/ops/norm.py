@@ -20,19 +20,10 @@ def adaln_rmsnorm_reference(x, weight, eps, table, shift_col, scale_col, idx):
     return (n * (1.0 + scale) + shift).to(x.dtype)
 
 
-def adaln_rmsnorm(x, weight, eps, table, shift_col, scale_col, idx, out=None,
-                  frame_sums=None, video_start=0, tokens_per_frame=1, num_frames=0):
-    """out = RMSNorm(x) * w * (1 + table[idx, scale]) + table[idx, shift]; [T, D] bf16.
-
-    With `frame_sums` (fp32 [F, D], zeroed by the caller) the kernel also accumulates the
-    per-frame sums of the OUTPUT over the video rows -- the frame means the linear branch's
-    alpha needs, without a second pass over the tensor."""
+def adaln_rmsnorm(x, weight, eps, table, shift_col, scale_col, idx, out=None):
+    """out = RMSNorm(x) * w * (1 + table[idx, scale]) + table[idx, shift]; [T, D] bf16."""
     if not x.is_cuda:
         y = adaln_rmsnorm_reference(x, weight, eps, table, shift_col, scale_col, idx)
-        if frame_sums is not None and num_frames:
-            vs = video_start
-            frame_sums += y[vs:vs + num_frames * tokens_per_frame].float().view(
-                num_frames, tokens_per_frame, -1).sum(1)
         if out is not None:
             out.copy_(y)
             return out
@@ -40,8 +31,16 @@ def adaln_rmsnorm(x, weight, eps, table, shift_col, scale_col, idx, out=None,
     if out is None:
         out = torch.empty_like(x)
     w = None if weight is None else weight.float().contiguous()
-    ext().adaln_rmsnorm(x, w, float(eps), table, int(shift_col), int(scale_col), idx, out,
-                        frame_sums, int(video_start), int(tokens_per_frame), int(num_frames))
+    ext().adaln_rmsnorm(x, w, float(eps), table, int(shift_col), int(scale_col), idx, out)
+    return out
+
+
+def frame_sums(rows, num_frames, tokens_per_frame):
+    """fp32 [F, D] column sums of F consecutive frames of S rows each ([F*S, D] view)."""
+    if not rows.is_cuda:
+        return rows.float().view(num_frames, tokens_per_frame, -1).sum(1)
+    out = torch.empty(num_frames, rows.shape[1], dtype=torch.float32, device=rows.device)
+    ext().frame_sums(rows, int(num_frames), int(tokens_per_frame), out)
     return out
 
 
