@@ -32,4 +32,23 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              const int* kv, const void* gate, int64_t ldg, void* out,
                              int64_t ldo, float scale, int* err, cudaStream_t stream);
 
+void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, int64_t ldo, int l2,
+                        cudaStream_t stream);
+void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,
+                    int64_t ldo, int F, int gh, int gw, int H, int l2, cudaStream_t stream);
+void launch_lb_frame_stats(const void* k, int64_t ldk, const void* v, int64_t ldv, int F, int S,
+                           int H, const float* beta, float* A, float* B, int* err,
+                           cudaStream_t stream);
+void launch_lb_spd_factor(const float* A, const float* B, const float* alpha, float* trans,
+                          float* inj, int n_mats, float a_scale, float b_scale,
+                          cudaStream_t stream);
+void launch_lb_scan(const float* trans, const float* inj, const float* start, int F, int H,
+                    float* prefix, float* suffix, cudaStream_t stream);
+void launch_lb_gather(const float* prefix, const float* suffix, const int* idx, const float* ab,
+                      const float* aa, const float* start, int F, int H, void* out,
+                      cudaStream_t stream);
+void launch_lb_readout(const void* q, int64_t ldq, const void* state, int F, int S, int H,
+                       const float* w, const void* gate, int64_t ldg, int gate_logits, void* out,
+                       int64_t ldo, float eps, int* err, cudaStream_t stream);
+
 }  // namespace vdn

@@ -1,0 +1,678 @@
+// The linear branch's kernels (sm_100a). Reference parity, per kernel:
+//
+//   lb_activate       SiLU [+ L2 over the head dim]     linear_attention/features.py:47-67
+//   lb_conv_features  5x5 depthwise spatial conv, 5-tap temporal conv, SiLU [+ L2], one
+//                     pass (features.py:133-209 + ops/temporal_conv.py; the reference runs
+//                     cuDNN for the spatial half and a Triton kernel for the rest)
+//   lb_frame_stats    A = sum_s beta k k^T, B = sum_s beta v k^T per (frame, head) on
+//                     tcgen05 (scan.py:79-167). A needs fp32 accuracy: beta*k is split into
+//                     bf16 hi + lo and both halves accumulate into one fp32 TMEM tile, so A
+//                     carries ~16 mantissa bits of the products (the reference: TF32, 10).
+//   lb_spd_factor     (I + a A)^-1 by Gauss-Jordan in fp32 shared memory (SPD: no pivoting),
+//                     transition = diag(alpha) inv, injection = (b B) inv (delta_rule.py:31-89)
+//   lb_scan           both serial recurrences S_t = S_{t-1} T_t + inj_t (scan.py:170-255)
+//   lb_gather         window complement + alpha bridge (scan.py:261-396)
+//   lb_readout        q . S^T on tcgen05, then RMSNorm * w * sigmoid(gate) and the store in
+//                     token order (branch.py:440-458, kernels.py:8-57)
+#include "common.cuh"
+#include "launchers.h"
+#include "tma.cuh"
+
+namespace vdn {
+
+// ------------------------------------------------------------------------- activation
+__global__ void __launch_bounds__(256) lb_activate_kernel(const __nv_bfloat16* __restrict__ in,
+                                                          int64_t ldi, int N, int H,
+                                                          __nv_bfloat16* __restrict__ out,
+                                                          int64_t ldo, int l2) {
+  const int64_t item = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (item >= (int64_t)N * H) return;
+  const int row = (int)(item / H), h = (int)(item % H);
+  const uint2 v = *reinterpret_cast<const uint2*>(in + (int64_t)row * ldi + h * 128 + lane * 4);
+  float y[4] = {siluf_(bf16_lo(v.x)), siluf_(bf16_hi(v.x)), siluf_(bf16_lo(v.y)), siluf_(bf16_hi(v.y))};
+  if (l2) {
+    float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
+    const float inv = 1.f / fmaxf(sqrtf(ss), 1e-6f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) y[i] *= inv;
+  }
+  *reinterpret_cast<uint2*>(out + (int64_t)row * ldo + h * 128 + lane * 4) =
+      make_uint2(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
+}
+
+void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, int64_t ldo, int l2,
+                        cudaStream_t stream) {
+  const int64_t items = (int64_t)N * H;
+  if (!items) return;
+  lb_activate_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(in), ldi, N, H, reinterpret_cast<__nv_bfloat16*>(out),
+      ldo, l2);
+}
+
+// --------------------------------------------------------------- separable short conv
+// Block = 8 warps = 8 grid positions of one head; a warp walks a chunk of LB_FC frames
+// (plus a 2-frame halo each side) keeping the last five spatial results in a shift register.
+constexpr int LB_FC = 16;
+
+__global__ void __launch_bounds__(256) lb_conv_kernel(const __nv_bfloat16* __restrict__ in,
+                                                      int64_t ldi, const float* __restrict__ wsp,
+                                                      const float* __restrict__ wtm,
+                                                      __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                                      int F, int gh, int gw, int H, int l2) {
+  __shared__ float s_wsp[25][128];
+  __shared__ float s_wtm[5][128];
+  const int h = blockIdx.y;
+  const int S = gh * gw;
+  for (int i = threadIdx.x; i < 25 * 128; i += 256) {
+    const int tap = i / 128, c = i % 128;
+    s_wsp[tap][c] = wsp[(int64_t)(h * 128 + c) * 25 + tap];
+  }
+  for (int i = threadIdx.x; i < 5 * 128; i += 256) {
+    const int tap = i / 128, c = i % 128;
+    s_wtm[tap][c] = wtm[(int64_t)(h * 128 + c) * 5 + tap];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = blockIdx.x * 8 + warp;
+  const int f0 = blockIdx.z * LB_FC;
+  if (pos >= S || f0 >= F) return;
+  const int y = pos / gw, x = pos % gw;
+  const int c0 = lane * 4;
+  const int64_t col = (int64_t)h * 128 + c0;
+  float r[5][4];
+#pragma unroll
+  for (int a = 0; a < 5; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) r[a][b] = 0.f;
+  const int f_end = min(F, f0 + LB_FC);
+  // spatial results for frames f0-2 .. f_end+1; output frame fo = f - 2
+  for (int f = f0 - 2; f < f_end + 2; ++f) {
+    float sp[4] = {0.f, 0.f, 0.f, 0.f};
+    if (f >= 0 && f < F) {
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        const int yy = y + i - 2;
+        if (yy < 0 || yy >= gh) continue;
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+          const int xx = x + j - 2;
+          if (xx < 0 || xx >= gw) continue;
+          const uint2 v = *reinterpret_cast<const uint2*>(in + ((int64_t)f * S + yy * gw + xx) * ldi + col);
+          const float* w = &s_wsp[i * 5 + j][c0];
+          sp[0] += w[0] * bf16_lo(v.x);
+          sp[1] += w[1] * bf16_hi(v.x);
+          sp[2] += w[2] * bf16_lo(v.y);
+          sp[3] += w[3] * bf16_hi(v.y);
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      r[0][b] = r[1][b];
+      r[1][b] = r[2][b];
+      r[2][b] = r[3][b];
+      r[3][b] = r[4][b];
+      r[4][b] = sp[b];
+    }
+    const int fo = f - 2;
+    if (fo < f0) continue;
+    float o[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      float t = 0.f;
+#pragma unroll
+      for (int dt = 0; dt < 5; ++dt) t += s_wtm[dt][c0 + b] * r[dt][b];
+      o[b] = siluf_(t);
+    }
+    if (l2) {
+      const float ss = warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+      const float inv = 1.f / fmaxf(sqrtf(ss), 1e-6f);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) o[b] *= inv;
+    }
+    *reinterpret_cast<uint2*>(out + ((int64_t)fo * S + pos) * ldo + col) =
+        make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
+  }
+}
+
+void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,
+                    int64_t ldo, int F, int gh, int gw, int H, int l2, cudaStream_t stream) {
+  const int S = gh * gw;
+  if (!F || !S) return;
+  dim3 grid((S + 7) / 8, H, (F + LB_FC - 1) / LB_FC);
+  lb_conv_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(in), ldi, wsp,
+                                           wtm, reinterpret_cast<__nv_bfloat16*>(out), ldo, F,
+                                           gh, gw, H, l2);
+}
+
+// ------------------------------------------------------------------ frame statistics
+// CTA = (frame, head). 64-token chunks through a 2-stage ring: k and v by TMA (MN-major,
+// 128B swizzle); the 128 threads write beta*k (hi, lo) and beta*v in the same layout; one
+// thread issues MMAs into two TMEM accumulators (A: cols 0-127, B: cols 128-255).
+constexpr int FS_CHUNK = 64;
+constexpr int FS_TILE = FS_CHUNK * 128 * 2;              // 16 KB
+constexpr int FS_STAGE = 5 * FS_TILE;                    // k, v, hi, lo, bv
+constexpr int FS_SMEM = 2 * FS_STAGE + 1024 + 256;
+
+__global__ void __launch_bounds__(128, 1)
+    lb_frame_stats_kernel(const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const float* __restrict__ beta,
+                          int S, int H, float* __restrict__ Aout, float* __restrict__ Bout,
+                          int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * FS_STAGE);
+  uint64_t* mma_bar = full + 2;
+  uint64_t* done = full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int f = blockIdx.x / H, h = blockIdx.x % H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nchunks = (S + FS_CHUNK - 1) / FS_CHUNK;
+
+  if (tid == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(&mma_bar[0], 1);
+    mbar_init(&mma_bar[1], 1);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto issue = [&](int c) {
+    uint8_t* st = smem + (c & 1) * FS_STAGE;
+    const int row = f * S + c * FS_CHUNK;
+    mbar_arrive_expect_tx(&full[c & 1], 2 * FS_TILE);  // k and v, two boxes each
+    tma_load_2d(st, &tmK, &full[c & 1], h * 128, row);
+    tma_load_2d(st + FS_TILE / 2, &tmK, &full[c & 1], h * 128 + 64, row);
+    tma_load_2d(st + FS_TILE, &tmV, &full[c & 1], h * 128, row);
+    tma_load_2d(st + FS_TILE + FS_TILE / 2, &tmV, &full[c & 1], h * 128 + 64, row);
+  };
+  if (tid == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    issue(0);
+    if (nchunks > 1) issue(1);
+  }
+  constexpr uint32_t idesc = umma_idesc_bf16(128, 128, true, true);
+  bool ok = true;
+  int last_issued[2] = {0, nchunks > 1 ? 1 : -1};
+  for (int c = 0; c < nchunks; ++c) {
+    const int s = c & 1;
+    uint8_t* st = smem + s * FS_STAGE;
+    const bool got = mbar_wait(&full[s], (c >> 1) & 1, abort_flag, err, kErrTimeoutEpilogue);
+    if (__syncthreads_or(!got)) {     // block-uniform: every thread leaves together
+      ok = false;
+      break;
+    }
+    // beta-weighted operands, 16 bytes (8 channels of one token) at a time, written at the
+    // same swizzled offsets the TMA used for k and v
+    const int ntok = min(FS_CHUNK, S - c * FS_CHUNK);
+    for (int i = tid; i < FS_CHUNK * 16; i += 128) {
+      const int o = i * 16;
+      const int t = (o % (FS_TILE / 2)) / 128;
+      const float b = t < ntok ? beta[((int64_t)f * S + c * FS_CHUNK + t) * H + h] : 0.f;
+      const uint4 kk = *reinterpret_cast<const uint4*>(st + o);
+      const uint4 vv = *reinterpret_cast<const uint4*>(st + FS_TILE + o);
+      const uint32_t* ku = reinterpret_cast<const uint32_t*>(&kk);
+      const uint32_t* vu = reinterpret_cast<const uint32_t*>(&vv);
+      uint32_t hi[4], lo[4], bv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float k0 = bf16_lo(ku[j]) * b, k1 = bf16_hi(ku[j]) * b;
+        const __nv_bfloat162 hh = __floats2bfloat162_rn(k0, k1);
+        hi[j] = *reinterpret_cast<const uint32_t*>(&hh);
+        lo[j] = pack_bf16(k0 - __bfloat162float(hh.x), k1 - __bfloat162float(hh.y));
+        const __nv_bfloat162 vb = *reinterpret_cast<const __nv_bfloat162*>(&vu[j]);
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(b, b);
+        const __nv_bfloat162 pr = __hmul2(vb, bb);  // bf16 product, as the reference's v*beta
+        bv[j] = *reinterpret_cast<const uint32_t*>(&pr);
+      }
+      *reinterpret_cast<uint4*>(st + 2 * FS_TILE + o) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(st + 3 * FS_TILE + o) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      *reinterpret_cast<uint4*>(st + 4 * FS_TILE + o) = make_uint4(bv[0], bv[1], bv[2], bv[3]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    bool fail = false;
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t aK = smem_u32(st), aHi = smem_u32(st + 2 * FS_TILE),
+                     aLo = smem_u32(st + 3 * FS_TILE), aBv = smem_u32(st + 4 * FS_TILE);
+#pragma unroll
+      for (int k = 0; k < FS_CHUNK / 16; ++k) {
+        const uint32_t off = k * 2048;
+        const uint64_t dk = umma_desc_mnmajor_sw128(aK + off, FS_TILE / 2);
+        umma_f16_ss(tmem, umma_desc_mnmajor_sw128(aHi + off, FS_TILE / 2), dk, idesc, (c | k) != 0);
+        umma_f16_ss(tmem, umma_desc_mnmajor_sw128(aLo + off, FS_TILE / 2), dk, idesc, 1u);
+        umma_f16_ss(tmem + 128, umma_desc_mnmajor_sw128(aBv + off, FS_TILE / 2), dk, idesc, (c | k) != 0);
+      }
+      umma_commit(&mma_bar[s]);
+      if (c + 2 < nchunks) {
+        // stage s is rewritten only after the MMAs reading it are done
+        if (mbar_wait(&mma_bar[s], (c >> 1) & 1, abort_flag, err, kErrTimeoutMma)) {
+          issue(c + 2);
+          last_issued[s] = c + 2;
+        } else {
+          fail = true;
+        }
+      }
+    }
+    if (__syncthreads_or(fail)) {
+      ok = false;
+      break;
+    }
+  }
+  if (!ok && tid == 0) {
+    // let the copies this thread issued land before the CTA exits
+    long long t0 = clock64();
+    for (int st = 0; st < 2; ++st) {
+      if (last_issued[st] < 0) continue;
+      while (!mbar_try_wait(&full[st], (last_issued[st] >> 1) & 1) &&
+             clock64() - t0 < kWaitBudgetCycles) {
+      }
+    }
+  }
+  if (tid == 0) {
+    umma_commit(done);
+  }
+  if (mbar_wait(done, 0, abort_flag, err, kErrTimeoutEpilogue) && ok) {
+    tc_fence_after();
+    const int row = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float* arow = Aout + (((int64_t)f * H + h) * 128 + row) * 128;
+    float* brow = Bout + (((int64_t)f * H + h) * 128 + row) * 128;
+#pragma unroll 1
+    for (int cc = 0; cc < 128; cc += 32) {
+      uint32_t u[32];
+      tmem_ld32(tmem + lane_off + cc, u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(arow + cc)[q] =
+            make_float4(__uint_as_float(u[4 * q]), __uint_as_float(u[4 * q + 1]),
+                        __uint_as_float(u[4 * q + 2]), __uint_as_float(u[4 * q + 3]));
+      tmem_ld32(tmem + lane_off + 128 + cc, u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(brow + cc)[q] =
+            make_float4(__uint_as_float(u[4 * q]), __uint_as_float(u[4 * q + 1]),
+                        __uint_as_float(u[4 * q + 2]), __uint_as_float(u[4 * q + 3]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+void launch_lb_frame_stats(const void* k, int64_t ldk, const void* v, int64_t ldv, int F, int S,
+                           int H, const float* beta, float* A, float* B, int* err,
+                           cudaStream_t stream) {
+  if (!F || !S || !H) return;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(lb_frame_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FS_SMEM);
+    attr = true;
+  }
+  const uint64_t cols = (uint64_t)H * 128, rows = (uint64_t)F * S;
+  CUtensorMap tk = make_tmap_2d(k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, ldk * 2, 64, FS_CHUNK);
+  CUtensorMap tv = make_tmap_2d(v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, ldv * 2, 64, FS_CHUNK);
+  lb_frame_stats_kernel<<<F * H, 128, FS_SMEM, stream>>>(tk, tv, beta, S, H, A, B, err);
+}
+
+// ---------------------------------------------------------------------- SPD factor
+constexpr int SPD_PITCH = 129;
+constexpr int SPD_SMEM = (128 * SPD_PITCH + 2 * 128) * 4;
+
+__global__ void __launch_bounds__(256) lb_spd_factor_kernel(
+    const float* __restrict__ A, const float* __restrict__ B, const float* __restrict__ alpha,
+    float* __restrict__ trans, float* __restrict__ inj, float a_scale, float b_scale) {
+  extern __shared__ float sm[];
+  float* M = sm;
+  float* colk = sm + 128 * SPD_PITCH;
+  float* rowk = colk + 128;
+  const int64_t mat = blockIdx.x;
+  const float* a = A + mat * 16384;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < 16384; i += 256) {
+    const int r = i >> 7, c = i & 127;
+    const float sym = 0.5f * (a[r * 128 + c] + a[c * 128 + r]);
+    M[r * SPD_PITCH + c] = a_scale * sym + (r == c ? 1.f : 0.f);
+  }
+  __syncthreads();
+  // Gauss-Jordan inversion in place (SPD: pivots stay positive without row exchanges).
+  for (int k = 0; k < 128; ++k) {
+    const float inv_p = 1.f / M[k * SPD_PITCH + k];
+    if (tid < 128) {
+      colk[tid] = M[tid * SPD_PITCH + k];
+      rowk[tid] = M[k * SPD_PITCH + tid] * inv_p;
+    }
+    __syncthreads();
+    for (int i = tid; i < 16384; i += 256) {
+      const int r = i >> 7, c = i & 127;
+      float val;
+      if (r == k) {
+        val = (c == k) ? inv_p : rowk[c];
+      } else if (c == k) {
+        val = -colk[r] * inv_p;
+      } else {
+        val = M[r * SPD_PITCH + c] - colk[r] * rowk[c];
+      }
+      M[r * SPD_PITCH + c] = val;
+    }
+    __syncthreads();
+  }
+  // symmetrise, then transition = diag(alpha) * inv (row scale)
+  const float* al = alpha + mat * 128;
+  float* tr = trans + mat * 16384;
+  for (int i = tid; i < 16384; i += 256) {
+    const int r = i >> 7, c = i & 127;
+    if (c < r) continue;
+    const float s = 0.5f * (M[r * SPD_PITCH + c] + M[c * SPD_PITCH + r]);
+    M[r * SPD_PITCH + c] = s;
+    M[c * SPD_PITCH + r] = s;
+  }
+  __syncthreads();
+  for (int i = tid; i < 16384; i += 256) {
+    const int r = i >> 7, c = i & 127;
+    tr[i] = al[r] * M[r * SPD_PITCH + c];
+  }
+  // injection = (b_scale * B) @ inv, 8x8 register tile per thread
+  const float* bm = B + mat * 16384;
+  float* out = inj + mat * 16384;
+  const int ti = tid >> 4, tj = tid & 15;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  for (int kk = 0; kk < 128; ++kk) {
+    float bi[8], mj[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) bi[i] = bm[(ti * 8 + i) * 128 + kk];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mj[j] = M[kk * SPD_PITCH + tj * 8 + j];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] += bi[i] * mj[j];
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[(ti * 8 + i) * 128 + tj * 8 + j] = b_scale * acc[i][j];
+}
+
+void launch_lb_spd_factor(const float* A, const float* B, const float* alpha, float* trans,
+                          float* inj, int n_mats, float a_scale, float b_scale,
+                          cudaStream_t stream) {
+  if (!n_mats) return;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(lb_spd_factor_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SPD_SMEM);
+    attr = true;
+  }
+  lb_spd_factor_kernel<<<n_mats, 256, SPD_SMEM, stream>>>(A, B, alpha, trans, inj, a_scale, b_scale);
+}
+
+// ------------------------------------------------------------------------------ scans
+constexpr int SC_PITCH = 132;
+constexpr int SC_SMEM = 2 * 128 * SC_PITCH * 4;
+
+__global__ void __launch_bounds__(256) lb_scan_kernel(const float* __restrict__ trans,
+                                                      const float* __restrict__ inj,
+                                                      const float* __restrict__ start, int F,
+                                                      int H, float* __restrict__ prefix,
+                                                      float* __restrict__ suffix) {
+  extern __shared__ float sm[];
+  float* St = sm;                       // state [128][SC_PITCH]
+  float* Tm = sm + 128 * SC_PITCH;      // transition
+  const int h = blockIdx.x, dir = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int ti = tid >> 4, tj = tid & 15;
+  for (int i = tid; i < 16384; i += 256) {
+    const int r = i >> 7, c = i & 127;
+    St[r * SC_PITCH + c] = start ? start[(int64_t)h * 16384 + i] : 0.f;
+  }
+  float* bank = dir == 0 ? prefix : suffix;
+  for (int step = 0; step < F; ++step) {
+    const int f = dir == 0 ? step : F - 1 - step;
+    const int64_t base = ((int64_t)f * H + h) * 16384;
+    const float4* t4 = reinterpret_cast<const float4*>(trans + base);
+    for (int i = tid; i < 4096; i += 256) {
+      const int r = i >> 5, c4 = i & 31;
+      *reinterpret_cast<float4*>(&Tm[r * SC_PITCH + c4 * 4]) = t4[i];
+    }
+    __syncthreads();
+    float acc[8][8];
+    const float* ij = inj + base;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 a0 = *reinterpret_cast<const float4*>(ij + (ti * 8 + i) * 128 + tj * 8);
+      const float4 a1 = *reinterpret_cast<const float4*>(ij + (ti * 8 + i) * 128 + tj * 8 + 4);
+      acc[i][0] = a0.x; acc[i][1] = a0.y; acc[i][2] = a0.z; acc[i][3] = a0.w;
+      acc[i][4] = a1.x; acc[i][5] = a1.y; acc[i][6] = a1.z; acc[i][7] = a1.w;
+    }
+#pragma unroll 4
+    for (int k = 0; k < 128; ++k) {
+      float si[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) si[i] = St[(ti * 8 + i) * SC_PITCH + k];
+      const float4 m0 = *reinterpret_cast<const float4*>(&Tm[k * SC_PITCH + tj * 8]);
+      const float4 m1 = *reinterpret_cast<const float4*>(&Tm[k * SC_PITCH + tj * 8 + 4]);
+      const float mj[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] += si[i] * mj[j];
+    }
+    __syncthreads();
+    float* ob = bank + base;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = ti * 8 + i;
+      *reinterpret_cast<float4*>(&St[r * SC_PITCH + tj * 8]) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      *reinterpret_cast<float4*>(&St[r * SC_PITCH + tj * 8 + 4]) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+      *reinterpret_cast<float4*>(ob + r * 128 + tj * 8) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      *reinterpret_cast<float4*>(ob + r * 128 + tj * 8 + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+    }
+    __syncthreads();
+  }
+}
+
+void launch_lb_scan(const float* trans, const float* inj, const float* start, int F, int H,
+                    float* prefix, float* suffix, cudaStream_t stream) {
+  if (!F || !H) return;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(lb_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM);
+    attr = true;
+  }
+  lb_scan_kernel<<<dim3(H, 2), 256, SC_SMEM, stream>>>(trans, inj, start, F, H, prefix, suffix);
+}
+
+// ----------------------------------------------------------------------------- gather
+// out[t,h,v,k] = before(t)[v,k] * ab[t,h,k] + after(t)[v,k] * aa[t,h,k]; a missing side
+// reads the scan start (text state) or zero.
+__global__ void __launch_bounds__(256) lb_gather_kernel(
+    const float* __restrict__ prefix, const float* __restrict__ suffix,
+    const int* __restrict__ idx /*[F,4]: bi, ai, has_b, has_a*/, const float* __restrict__ ab,
+    const float* __restrict__ aa, const float* __restrict__ start, int F, int H,
+    __nv_bfloat16* __restrict__ out) {
+  const int64_t i4 = (int64_t)blockIdx.x * 256 + threadIdx.x;   // one float4 per thread
+  const int64_t total4 = (int64_t)F * H * 4096;
+  if (i4 >= total4) return;
+  const int64_t e = i4 * 4;
+  const int t = (int)(e / ((int64_t)H * 16384));
+  const int h = (int)((e / 16384) % H);
+  const int vk = (int)(e % 16384);
+  const int kcol = vk & 127;
+  const int* ix = idx + 4 * t;
+  float4 b, a;
+  const int64_t off_b = ((int64_t)ix[0] * H + h) * 16384 + vk;
+  const int64_t off_a = ((int64_t)ix[1] * H + h) * 16384 + vk;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 st = start ? *reinterpret_cast<const float4*>(start + (int64_t)h * 16384 + vk) : zero;
+  b = ix[2] ? *reinterpret_cast<const float4*>(prefix + off_b) : st;
+  a = ix[3] ? *reinterpret_cast<const float4*>(suffix + off_a) : st;
+  const float* fb = ab + ((int64_t)t * H + h) * 128 + kcol;
+  const float* fa = aa + ((int64_t)t * H + h) * 128 + kcol;
+  const float o0 = b.x * fb[0] + a.x * fa[0], o1 = b.y * fb[1] + a.y * fa[1];
+  const float o2 = b.z * fb[2] + a.z * fa[2], o3 = b.w * fb[3] + a.w * fa[3];
+  *reinterpret_cast<uint2*>(out + e) = make_uint2(pack_bf16(o0, o1), pack_bf16(o2, o3));
+}
+
+void launch_lb_gather(const float* prefix, const float* suffix, const int* idx, const float* ab,
+                      const float* aa, const float* start, int F, int H, void* out,
+                      cudaStream_t stream) {
+  const int64_t total4 = (int64_t)F * H * 4096;
+  if (!total4) return;
+  lb_gather_kernel<<<(unsigned)((total4 + 255) / 256), 256, 0, stream>>>(
+      prefix, suffix, idx, ab, aa, start, F, H, reinterpret_cast<__nv_bfloat16*>(out));
+}
+
+// ---------------------------------------------------------------------------- readout
+// CTA = (frame, head, 128-token tile). R = Q_tile . S^T on tcgen05 (both K-major), then
+// thread = token: RMSNorm over the 128 outputs, * w * sigmoid(gate), bf16 store in token
+// order into the O-projection input.
+constexpr int RO_TILE = 128 * 128 * 2;
+constexpr int RO_SMEM = 2 * RO_TILE + 1024 + 64;
+
+__global__ void __launch_bounds__(128) lb_readout_kernel(
+    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmS, int S,
+    int H, const float* __restrict__ w, const __nv_bfloat16* __restrict__ gate, int64_t ldg,
+    int gate_logits, __nv_bfloat16* __restrict__ out, int64_t ldo, float eps, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * RO_TILE);
+  uint64_t* done = full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int tiles_per_frame = (S + 127) / 128;
+  const int mt = blockIdx.x % tiles_per_frame;
+  const int fh = blockIdx.x / tiles_per_frame;
+  const int f = fh / H, h = fh % H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    mbar_init(full, 1);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int row0 = f * S + mt * 128;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(full, 2 * RO_TILE);
+    tma_load_2d(smem, &tmQ, full, h * 128, row0);
+    tma_load_2d(smem + RO_TILE / 2, &tmQ, full, h * 128 + 64, row0);
+    tma_load_2d(smem + RO_TILE, &tmS, full, 0, fh * 128);
+    tma_load_2d(smem + RO_TILE + RO_TILE / 2, &tmS, full, 64, fh * 128);
+    if (mbar_wait(full, 0, abort_flag, err, kErrTimeoutMma)) {
+      tc_fence_after();
+      constexpr uint32_t idesc = umma_idesc_bf16(128, 128, false, false);
+      const uint32_t aQ = smem_u32(smem), aS = smem_u32(smem + RO_TILE);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t off = (k >> 2) * (RO_TILE / 2) + (k & 3) * 32;
+        umma_f16_ss(tmem, umma_desc_kmajor_sw128(aQ + off), umma_desc_kmajor_sw128(aS + off),
+                    idesc, k != 0);
+      }
+    }
+    umma_commit(done);
+  }
+  const bool ok = mbar_wait(done, 0, abort_flag, err, kErrTimeoutEpilogue) && !*abort_flag;
+  if (ok) {
+    tc_fence_after();
+    const int r = warp * 32 + lane;
+    const int tok = mt * 128 + r;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float v[128];
+#pragma unroll
+    for (int c = 0; c < 128; c += 32) {
+      uint32_t u[32];
+      tmem_ld32(tmem + lane_off + c, u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[c + i] = __uint_as_float(u[i]);
+    }
+    if (tok < S) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) ss += v[i] * v[i];
+      const float rstd = rsqrtf(ss / 128.f + eps);
+      const int64_t row = (int64_t)f * S + tok;
+      const __nv_bfloat16* g = gate + row * ldg + h * 128;
+      __nv_bfloat16* o = out + row * ldo + h * 128;
+#pragma unroll
+      for (int c = 0; c < 128; c += 8) {
+        const uint4 gv = *reinterpret_cast<const uint4*>(g + c);
+        const uint32_t* gu = reinterpret_cast<const uint32_t*>(&gv);
+        uint32_t pk[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float g0 = bf16_lo(gu[j]), g1 = bf16_hi(gu[j]);
+          if (gate_logits) {
+            g0 = sigmoidf_(g0);
+            g1 = sigmoidf_(g1);
+          }
+          pk[j] = pack_bf16(v[c + 2 * j] * rstd * w[c + 2 * j] * g0,
+                            v[c + 2 * j + 1] * rstd * w[c + 2 * j + 1] * g1);
+        }
+        *reinterpret_cast<uint4*>(o + c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+void launch_lb_readout(const void* q, int64_t ldq, const void* state, int F, int S, int H,
+                       const float* w, const void* gate, int64_t ldg, int gate_logits, void* out,
+                       int64_t ldo, float eps, int* err, cudaStream_t stream) {
+  if (!F || !S || !H) return;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(lb_readout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RO_SMEM);
+    attr = true;
+  }
+  CUtensorMap tq = make_tmap_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * 128,
+                                (uint64_t)F * S, ldq * 2, 64, 128);
+  CUtensorMap ts = make_tmap_2d(state, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128,
+                                (uint64_t)F * H * 128, 256, 64, 128);
+  const int tiles = F * H * ((S + 127) / 128);
+  lb_readout_kernel<<<tiles, 128, RO_SMEM, stream>>>(
+      tq, ts, S, H, w, reinterpret_cast<const __nv_bfloat16*>(gate), ldg, gate_logits,
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, eps, err);
+}
+
+}  // namespace vdn

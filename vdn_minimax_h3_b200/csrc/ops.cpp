@@ -193,6 +193,144 @@ void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+
+namespace {
+// [N, H, 128] bf16 view with contiguous heads -> (base, row stride)
+void check_rows_heads(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, " must be bf16 CUDA");
+  TORCH_CHECK(t.dim() == 3 && t.size(2) == 128 && t.stride(2) == 1 && t.stride(1) == 128, name,
+              " must be [N, H, 128] with contiguous heads");
+  TORCH_CHECK((t.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              name, " row stride / base must be 16-byte aligned");
+}
+void check_f32(const torch::Tensor& t, const char* name, int64_t numel) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous() && t.numel() == numel,
+              name, " must be a contiguous fp32 CUDA tensor of ", numel, " elements, got ", t.sizes());
+}
+cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
+}  // namespace
+
+void lb_activate(torch::Tensor in, torch::Tensor out, bool l2) {
+  check_rows_heads(in, "in");
+  check_rows_heads(out, "out");
+  TORCH_CHECK(in.sizes() == out.sizes(), "shape mismatch");
+  c10::cuda::CUDAGuard g(in.device());
+  launch_lb_activate(in.data_ptr(), in.stride(0), in.size(0), in.size(1), out.data_ptr(),
+                     out.stride(0), l2, cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void lb_conv_features(torch::Tensor in, torch::Tensor wsp, torch::Tensor wtm, torch::Tensor out,
+                      int64_t F, int64_t gh, int64_t gw, bool l2) {
+  check_rows_heads(in, "in");
+  check_rows_heads(out, "out");
+  const int64_t H = in.size(1);
+  TORCH_CHECK(in.size(0) == F * gh * gw, "rows != F * gh * gw");
+  check_f32(wsp, "w_spatial", H * 128 * 25);
+  check_f32(wtm, "w_temporal", H * 128 * 5);
+  c10::cuda::CUDAGuard g(in.device());
+  launch_lb_conv(in.data_ptr(), in.stride(0), wsp.data_ptr<float>(), wtm.data_ptr<float>(),
+                 out.data_ptr(), out.stride(0), (int)F, (int)gh, (int)gw, (int)H, l2, cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void lb_frame_stats(torch::Tensor k, torch::Tensor v, torch::Tensor beta, torch::Tensor A,
+                    torch::Tensor B, torch::Tensor err) {
+  // k, v: [F, S, H, 128] views whose (F, S) rows are one row stride apart
+  TORCH_CHECK(k.dim() == 4 && v.dim() == 4 && k.sizes() == v.sizes(), "k, v must be [F, S, H, 128]");
+  const int64_t F = k.size(0), S = k.size(1), H = k.size(2);
+  TORCH_CHECK(k.stride(0) == S * k.stride(1) && v.stride(0) == S * v.stride(1),
+              "frames must be consecutive rows");
+  check_rows_heads(k.view({F * S, H, 128}), "k");
+  check_rows_heads(v.view({F * S, H, 128}), "v");
+  check_f32(beta, "beta", F * S * H);
+  check_f32(A, "A", F * H * 16384);
+  check_f32(B, "B", F * H * 16384);
+  c10::cuda::CUDAGuard g(k.device());
+  launch_lb_frame_stats(k.data_ptr(), k.stride(1), v.data_ptr(), v.stride(1), (int)F, (int)S,
+                        (int)H, beta.data_ptr<float>(), A.data_ptr<float>(), B.data_ptr<float>(),
+                        err_ptr(err), cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void lb_spd_factor(torch::Tensor A, torch::Tensor B, torch::Tensor alpha, torch::Tensor trans,
+                   torch::Tensor inj, double a_scale, double b_scale, torch::Tensor err) {
+  const int64_t n = A.numel() / 16384;
+  TORCH_CHECK(A.size(-1) == 128 && A.size(-2) == 128, "A must be [..., 128, 128]");
+  check_f32(A, "A", n * 16384);
+  check_f32(B, "B", n * 16384);
+  check_f32(alpha, "alpha", n * 128);
+  check_f32(trans, "trans", n * 16384);
+  check_f32(inj, "inj", n * 16384);
+  c10::cuda::CUDAGuard g(A.device());
+  launch_lb_spd_factor(A.data_ptr<float>(), B.data_ptr<float>(), alpha.data_ptr<float>(),
+                       trans.data_ptr<float>(), inj.data_ptr<float>(), (int)n, (float)a_scale,
+                       (float)b_scale, cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void lb_scan(torch::Tensor trans, torch::Tensor inj, c10::optional<torch::Tensor> start,
+             torch::Tensor prefix, torch::Tensor suffix, torch::Tensor err) {
+  TORCH_CHECK(trans.dim() == 4 && trans.size(2) == 128 && trans.size(3) == 128, "trans [F,H,128,128]");
+  const int64_t F = trans.size(0), H = trans.size(1);
+  check_f32(trans, "trans", F * H * 16384);
+  check_f32(inj, "inj", F * H * 16384);
+  check_f32(prefix, "prefix", F * H * 16384);
+  check_f32(suffix, "suffix", F * H * 16384);
+  const float* sp = nullptr;
+  if (start) {
+    check_f32(*start, "start", H * 16384);
+    sp = start->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(trans.device());
+  launch_lb_scan(trans.data_ptr<float>(), inj.data_ptr<float>(), sp, (int)F, (int)H,
+                 prefix.data_ptr<float>(), suffix.data_ptr<float>(), cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void lb_gather(torch::Tensor prefix, torch::Tensor suffix, torch::Tensor idx, torch::Tensor ab,
+               torch::Tensor aa, c10::optional<torch::Tensor> start, torch::Tensor out) {
+  const int64_t F = prefix.size(0), H = prefix.size(1);
+  check_f32(prefix, "prefix", F * H * 16384);
+  check_f32(suffix, "suffix", F * H * 16384);
+  check_f32(ab, "alpha_before", F * H * 128);
+  check_f32(aa, "alpha_after", F * H * 128);
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.is_contiguous() &&
+                  idx.numel() == F * 4, "idx must be int32 [F, 4]");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.is_contiguous() &&
+                  out.numel() == F * H * 16384, "out must be contiguous bf16 [F, H, 128, 128]");
+  const float* sp = nullptr;
+  if (start) {
+    check_f32(*start, "start", H * 16384);
+    sp = start->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(prefix.device());
+  launch_lb_gather(prefix.data_ptr<float>(), suffix.data_ptr<float>(), idx.data_ptr<int>(),
+                   ab.data_ptr<float>(), aa.data_ptr<float>(), sp, (int)F, (int)H, out.data_ptr(),
+                   cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void lb_readout(torch::Tensor q, torch::Tensor state, torch::Tensor w, torch::Tensor gate,
+                torch::Tensor out, double eps, bool gate_logits, torch::Tensor err) {
+  TORCH_CHECK(q.dim() == 4, "q must be [F, S, H, 128]");
+  const int64_t F = q.size(0), S = q.size(1), H = q.size(2);
+  TORCH_CHECK(q.stride(0) == S * q.stride(1), "q frames must be consecutive rows");
+  check_rows_heads(q.view({F * S, H, 128}), "q");
+  TORCH_CHECK(state.is_cuda() && state.scalar_type() == at::kBFloat16 && state.is_contiguous() &&
+                  state.numel() == F * H * 16384, "state must be contiguous bf16 [F, H, 128, 128]");
+  check_f32(w, "norm weight", 128);
+  TORCH_CHECK(gate.dim() == 3 && gate.size(0) == F * S && gate.size(1) == H, "gate [F*S, H, 128]");
+  check_rows_heads(gate, "gate");
+  check_2d_bf16(out, "out");
+  TORCH_CHECK(out.size(0) == F * S && out.size(1) == H * 128, "out must be [F*S, H*128]");
+  c10::cuda::CUDAGuard g(q.device());
+  launch_lb_readout(q.data_ptr(), q.stride(1), state.data_ptr(), (int)F, (int)S, (int)H,
+                    w.data_ptr<float>(), gate.data_ptr(), gate.stride(0), gate_logits,
+                    out.data_ptr(), out.stride(0), (float)eps, err_ptr(err), cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace vdn
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -207,4 +345,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");
   m.def("window_attention", &vdn::window_attention,
         "tcgen05 window softmax attention over an AttentionPlan (gated epilogue)");
+  m.def("lb_activate", &vdn::lb_activate, "SiLU [+ L2] over 128-wide heads");
+  m.def("lb_conv_features", &vdn::lb_conv_features, "separable 5x5x5 depthwise conv + SiLU [+ L2]");
+  m.def("lb_frame_stats", &vdn::lb_frame_stats, "tcgen05 per-frame delta-rule statistics A, B");
+  m.def("lb_spd_factor", &vdn::lb_spd_factor, "batched (I + aA)^-1, transition and injection");
+  m.def("lb_scan", &vdn::lb_scan, "bidirectional serial state recurrences");
+  m.def("lb_gather", &vdn::lb_gather, "window-complement state gather with alpha bridge");
+  m.def("lb_readout", &vdn::lb_readout, "tcgen05 readout q.S^T + RMSNorm * w * gate");
 }

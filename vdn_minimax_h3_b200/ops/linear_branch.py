@@ -36,8 +36,9 @@ def conv_features(tokens, w_sp, w_tm, num_frames, frame_size, l2norm):
         return conv_features_reference(tokens, w_sp, w_tm, num_frames, frame_size, l2norm)
     gh, gw = frame_size
     out = torch.empty(tokens.shape, dtype=tokens.dtype, device=tokens.device)
-    ext().lb_conv_features(tokens, w_sp.float().contiguous(), w_tm.float().contiguous(), out,
-                           num_frames, gh, gw, bool(l2norm))
+    ext().lb_conv_features(tokens, w_sp.float().reshape(-1).contiguous(),
+                           w_tm.float().reshape(-1).contiguous(), out, num_frames, gh, gw,
+                           bool(l2norm))
     return out
 
 
@@ -51,7 +52,7 @@ def frame_statistics(k, v, beta, a_fp32=True):
     Fr, S, n, d = k.shape
     A = torch.empty(Fr, n, d, d, dtype=torch.float32, device=k.device)
     B = torch.empty_like(A)
-    ext().lb_frame_stats(k, v, beta.float().contiguous(), A, B, error_word(k.device))
+    ext().lb_frame_stats(k, v, beta.float().reshape(-1).contiguous(), A, B, error_word(k.device))
     return A, B
 
 
@@ -63,8 +64,8 @@ def factor_apply(backend, alpha, A, B):
     assert isinstance(backend, VdnDelta)
     trans = torch.empty_like(A)
     inj = torch.empty_like(B)
-    ext().lb_spd_factor(A.contiguous(), B.contiguous(), alpha.float().contiguous(), trans, inj,
-                        float(backend.a_scale), float(backend.b_scale), error_word(A.device))
+    ext().lb_spd_factor(A.contiguous(), B.float().contiguous(), alpha.float().contiguous(), trans,
+                        inj, float(backend.a_scale), float(backend.b_scale), error_word(A.device))
     return trans, inj
 
 
@@ -79,20 +80,35 @@ def run_scans(trans, inj, text_state=None):
     return prefix, suffix
 
 
+def gather_tables(alpha, bounds, bridge):
+    """Per-frame gather indices [F, 4] (before, after, has_before, has_after) and the bridge
+    factors prod(alpha) over the skipped frames, [F, H, d] each (fp32, from log-prefix sums)."""
+    F_ = alpha.shape[0]
+    idx = scan_ref.gather_indices(bounds, F_, alpha.device)
+    table = torch.stack([idx["before_idx"], idx["after_idx"], idx["has_before"].long(),
+                         idx["has_after"].long()], dim=1).to(torch.int32).contiguous()
+    if bridge == "alpha":
+        log_a = torch.log(alpha.float().clamp_min(1e-12))
+        pre = torch.cat([torch.zeros_like(log_a[:1]), log_a.cumsum(0)])
+        fr = idx["frames"]
+        ab = torch.exp(pre[fr + 1] - pre[idx["bridge_before"]])
+        aa = torch.exp(pre[idx["bridge_after"]] - pre[fr])
+    else:
+        ab = torch.ones_like(alpha, dtype=torch.float32)
+        aa = torch.ones_like(alpha, dtype=torch.float32)
+    return table, ab.contiguous(), aa.contiguous()
+
+
 def gather(prefix, suffix, alpha, bounds, bridge, text_state, out_dtype=torch.bfloat16):
     """The complement of each frame's window, bridged into the frame. [F, n, d, d]."""
     if not _native(prefix):
         return scan_ref.gather_linear_state(prefix, suffix, alpha, bounds, bridge=bridge,
                                             text_state=text_state, out_dtype=out_dtype)
-    Fr = prefix.shape[0]
-    lo = torch.tensor([b[0] for b in bounds], dtype=torch.int32)
-    hi = torch.tensor([b[1] for b in bounds], dtype=torch.int32)
-    bnd = torch.stack([lo, hi], dim=1).to(prefix.device)
-    out = torch.empty(prefix.shape, dtype=out_dtype, device=prefix.device)
+    table, ab, aa = gather_tables(alpha, bounds, bridge)
+    out = torch.empty(prefix.shape, dtype=torch.bfloat16, device=prefix.device)
     start = None if text_state is None else text_state.float().contiguous()
-    ext().lb_gather(prefix, suffix, alpha.float().contiguous(), bnd, start, out,
-                    bridge == "alpha")
-    return out
+    ext().lb_gather(prefix.contiguous(), suffix.contiguous(), table, ab, aa, start, out)
+    return out if out_dtype in (None, torch.bfloat16) else out.to(out_dtype)
 
 
 # --------------------------------------------------------------------------- readout
