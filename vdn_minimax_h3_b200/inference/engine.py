@@ -61,8 +61,10 @@ class PackedBlock:
             br = attn.linear_attention
             extra.append(("beta", br.beta_proj.weight, None))
             extra.append(("ghid", br.output_gate.down.weight, None))
-        rows = 3 * inner + sum(w.shape[0] for _, w, _ in extra)
-        rows_pad = (rows + 7) // 8 * 8
+        def pad8(n):
+            return (n + 7) // 8 * 8
+        # every column group starts 16-byte aligned (a TMA / vector-load requirement)
+        rows_pad = 3 * pad8(inner) + sum(pad8(w.shape[0]) for _, w, _ in extra)
         W = torch.zeros(rows_pad, D, device=dev, dtype=dt)
         b = torch.zeros(rows_pad, device=dev, dtype=torch.float32)
         off = 0
@@ -73,7 +75,7 @@ class PackedBlock:
                 b[off:off + inner].copy_(lin.bias.float())
             self.cols[name] = (off, off + inner)
             lin.weight.data = W[off:off + inner]
-            off += inner
+            off += pad8(inner)
         for name, w, bias in extra:
             n = w.shape[0]
             W[off:off + n].copy_(w)
@@ -81,7 +83,7 @@ class PackedBlock:
                 b[off:off + n].copy_(bias.float())
             self.cols[name] = (off, off + n)
             w.data = W[off:off + n]
-            off += n
+            off += pad8(n)
         self.w_qkvg, self.b_qkvg = W, b
         self.norm_q = _f32(orig.norm_q.weight)
         self.norm_k = _f32(orig.norm_k.weight)
