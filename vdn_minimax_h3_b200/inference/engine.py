@@ -32,6 +32,7 @@ from vdn_minimax_h3_b200.ops import attention as attn_ops
 from vdn_minimax_h3_b200.ops import gemm
 from vdn_minimax_h3_b200.ops import linear_branch as lb
 from vdn_minimax_h3_b200.ops import norm as norm_ops
+from vdn_minimax_h3_b200.utils.profiling import SectionTimer
 
 
 def _f32(t):
@@ -142,6 +143,7 @@ class InferenceEngine:
         self.dense_plan = None
         self._buffers = {}
         self._cat_dirty = False
+        self.timer = SectionTimer(False)
 
     # --------------------------------------------------------------------- helpers
     def _plans(self, attn, layout, T):
@@ -181,8 +183,10 @@ class InferenceEngine:
         T, D = x.shape
         dev = x.device
         H, d, inner = pb.heads, pb.head_dim, pb.inner
+        sec = self.timer.section
         # AdaLN table for this block: [n_t * MOD, 6D]
-        table = gemm.linear(temb_act, pb.adaln_w, pb.adaln_b).view(-1, 6 * D)
+        with sec("adaln_table"):
+            table = gemm.linear(temb_act, pb.adaln_w, pb.adaln_b).view(-1, 6 * D)
         linear_on = (pb.hybrid and layout is not None and attn.linear_attention_enabled
                      and not attn.teacher_mode)
         plan = self._plans(attn if pb.hybrid and not attn.teacher_mode else None, layout, T)
@@ -191,10 +195,12 @@ class InferenceEngine:
         S = layout.tokens_per_frame if linear_on else 1
         vs = layout.video_start if linear_on else 0
         n1 = self._buf("normed", (T, D), x.dtype, dev)
-        norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1)
-        frame_sums = norm_ops.frame_sums(n1[vs:vs + Fr * S], Fr, S) if linear_on else None
+        with sec("norm"):
+            norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1)
+            frame_sums = norm_ops.frame_sums(n1[vs:vs + Fr * S], Fr, S) if linear_on else None
         qkvg = self._buf("qkvg", (T, pb.w_qkvg.shape[0]), x.dtype, dev)
-        gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
+        with sec("gemm_qkv"):
+            gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
         c = pb.cols
         q_raw = qkvg[:, c["q"][0]:c["q"][1]]
         k_raw = qkvg[:, c["k"][0]:c["k"][1]]
@@ -202,27 +208,34 @@ class InferenceEngine:
         cos, sin = rope
         q = self._buf("q", (T, inner), x.dtype, dev)
         k = self._buf("k", (T, inner), x.dtype, dev)
-        norm_ops.qk_prep(q_raw, H, pb.norm_q, pb.qk_eps, cos, sin, out=q)
-        norm_ops.qk_prep(k_raw, H, pb.norm_k, pb.qk_eps, cos, sin, out=k)
+        with sec("qk_prep"):
+            norm_ops.qk_prep(q_raw, H, pb.norm_q, pb.qk_eps, cos, sin, out=q)
+            norm_ops.qk_prep(k_raw, H, pb.norm_k, pb.qk_eps, cos, sin, out=k)
         kcat = pb.w_o.shape[1]
         cat = self._buf("cat", (T, kcat), x.dtype, dev, zero=True)
         sgate = qkvg[:, c["sgate"][0]:c["sgate"][1]] if pb.has_sgate else None
-        attn_ops.window_attention(q.view(T, H, d), k.view(T, H, d), v.view(T, H, d), plan,
-                                  d ** -0.5, gate_logits=sgate, out=cat[:, :inner])
+        with sec("attention"):
+            attn_ops.window_attention(q.view(T, H, d), k.view(T, H, d), v.view(T, H, d), plan,
+                                      d ** -0.5, gate_logits=sgate, out=cat[:, :inner])
         if pb.hybrid:
             if linear_on:
-                self._linear_branch(pb, attn, layout, n1, qkvg, frame_sums, cat[:, inner:])
+                with sec("linear_branch"):
+                    self._linear_branch(pb, attn, layout, n1, qkvg, frame_sums, cat[:, inner:])
             elif self._cat_dirty:
                 cat[:, inner:].zero_()
                 self._cat_dirty = False
-        gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D], adaln_idx)
+        with sec("gemm_o"):
+            gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D], adaln_idx)
         n2 = n1
-        norm_ops.adaln_rmsnorm(x, pb.norm2, pb.eps, table, 3 * D, 4 * D, adaln_idx, out=n2)
-        if pb.ff_interleaved:
-            h = gemm.linear_swiglu(n2, pb.w_up, pb.b_up)
-        else:
-            h = F.gelu(gemm.linear(n2, pb.w_up, pb.b_up).float(), approximate="tanh").to(x.dtype)
-        gemm.linear_gated_residual(h, pb.w_down, pb.b_down, x, table[:, 5 * D:6 * D], adaln_idx)
+        with sec("norm"):
+            norm_ops.adaln_rmsnorm(x, pb.norm2, pb.eps, table, 3 * D, 4 * D, adaln_idx, out=n2)
+        with sec("gemm_ff_up"):
+            if pb.ff_interleaved:
+                h = gemm.linear_swiglu(n2, pb.w_up, pb.b_up)
+            else:
+                h = F.gelu(gemm.linear(n2, pb.w_up, pb.b_up).float(), approximate="tanh").to(x.dtype)
+        with sec("gemm_ff_down"):
+            gemm.linear_gated_residual(h, pb.w_down, pb.b_down, x, table[:, 5 * D:6 * D], adaln_idx)
         return x
 
     def _linear_branch(self, pb, attn, layout, n1, qkvg, frame_sums, out):

@@ -12,6 +12,26 @@ import torch
 
 _EXT = None
 _ERR = {}
+LAUNCHES = [0]   # kernel launches issued through the extension (bench.py reads this)
+
+
+class _Counted:
+    """The extension module, counting every kernel-launching call made through it."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self._cache = {}
+
+    def __getattr__(self, name):
+        fn = self._cache.get(name)
+        if fn is None:
+            raw = getattr(self._mod, name)
+
+            def fn(*args, _raw=raw):
+                LAUNCHES[0] += 1
+                return _raw(*args)
+            self._cache[name] = fn
+        return fn
 
 
 class KernelError(RuntimeError):
@@ -33,7 +53,7 @@ def ext():
     global _EXT
     if _EXT is None:
         try:
-            _EXT = importlib.import_module("vdn_minimax_h3_b200._C")
+            _EXT = _Counted(importlib.import_module("vdn_minimax_h3_b200._C"))
         except ImportError as exc:  # pragma: no cover - depends on the build
             raise ImportError(
                 "vdn_minimax_h3_b200._C is not built; run `python setup.py build_ext --inplace` "
