@@ -239,56 +239,15 @@ class InferenceEngine:
         return x
 
     def _linear_branch(self, pb, attn, layout, n1, qkvg, frame_sums, out):
-        """The linear branch over the video rows; writes token-major readout into `out`
-        (video rows; anchor frames zero under anchors 'both')."""
-        br = attn.linear_attention
+        """The linear branch over the video rows, all heads; readout into `out` (video rows;
+        anchor frames stay zero under anchors 'both')."""
         c = pb.cols
         H, d = pb.heads, pb.head_dim
-        Fr, S = layout.num_frames, layout.tokens_per_frame
-        vs, ve = layout.video_start, layout.video_end
-        skip = attn.anchor_frames == "both"
-        f0, f1 = (1, Fr - 1) if skip else (0, Fr)
-        if f1 - f0 <= 0:
-            out[vs:ve].zero_()
-            return
-        r0, r1 = vs + f0 * S, vs + f1 * S
-        nF = f1 - f0
-        q_raw = qkvg[r0:r1, c["q"][0]:c["q"][1]].view(-1, H, d)
-        k_raw = qkvg[r0:r1, c["k"][0]:c["k"][1]].view(-1, H, d)
-        v_raw = qkvg[r0:r1, c["v"][0]:c["v"][1]].view(-1, H, d)
-        conv = br.short_conv
-        fs = layout.frame_size if conv is not None else None
-        feats = []
-        for t, proj in ((q_raw, "q"), (k_raw, "k"), (v_raw, "v")):
-            if conv is not None and proj in conv.projs:
-                w_sp, w_tm = conv.weights(proj)
-                feats.append(lb.conv_features(t, w_sp, w_tm, nF, fs, proj != "v"))
-            else:
-                feats.append(lb.activate(t, proj != "v"))
-        qf, kf, vf = feats
-        beta = torch.sigmoid(qkvg[r0:r1, c["beta"][0]:c["beta"][1]].float())
-        A, B = lb.frame_statistics(kf.view(nF, S, H, d), vf.view(nF, S, H, d),
-                                   beta.view(nF, S, H), a_fp32=br.a_fp32)
-        del kf, vf
-        frame_mean = frame_sums[f0:f1] / S
-        alpha = br.alpha(frame_mean)
-        text_state = None
-        if attn.enable_text_state:
-            ts, te = layout.text_range
-            text_raw = tuple(qkvg[ts:te, c[n][0]:c[n][1]].view(-1, H, d) for n in "qkv")
-            text_beta = torch.sigmoid(qkvg[ts:te, c["beta"][0]:c["beta"][1]].float())
-            text_state = br.text_state(None, text_raw, text_beta=text_beta)
-        trans, inj = lb.factor_apply(br.backend(S), alpha, A, B)
-        prefix, suffix = lb.run_scans(trans, inj, text_state)
-        bounds = self.bounds[f0:f1]
-        if skip:
-            bounds = [(lo - 1, hi - 1) for lo, hi in bounds]
-        state = lb.gather(prefix, suffix, alpha, bounds, br.bridge, text_state, out_dtype=n1.dtype)
-        del prefix, suffix, trans, inj
-        ghid = qkvg[r0:r1, c["ghid"][0]:c["ghid"][1]]
-        gate_logits = gemm.linear(ghid, pb.gate_up_w, pb.gate_up_b)
-        lb.readout(qf.view(nF, S, H, d), state, br.norm.weight, gate_logits.view(-1, H, d),
-                   br.norm.eps, out=out[r0:r1], gate_logits=True)
+        view = lambda name: qkvg[:, c[name][0]:c[name][1]]  # noqa: E731
+        linear_branch_core(pb, attn, layout, self.bounds,
+                           view("q").view(-1, H, d), view("k").view(-1, H, d),
+                           view("v").view(-1, H, d), view("beta"), view("ghid"), frame_sums,
+                           slice(0, H), out, n1.dtype)
         self._cat_dirty = True
 
     # --------------------------------------------------------------------- forward
@@ -312,3 +271,59 @@ class InferenceEngine:
         return m.head(x.unsqueeze(0), temb, timestep_indices, video_indices, audio_indices)
 
     __call__ = forward
+
+
+def linear_branch_core(pb, attn, layout, bounds, q_raw, k_raw, v_raw, beta_logits, ghid,
+                       frame_sums, heads, out, dtype):
+    """The forward-only linear branch for a head range over every video row.
+
+    q_raw/k_raw/v_raw [T, n, d] and beta_logits [T, n] cover the packed sequence (rows of
+    the whole sequence, this head range); ghid [T, rank] is the output gate's low-rank
+    hidden; frame_sums [F, D] fp32 are the per-frame sums of the attention input over the
+    whole clip. Writes the gated, normalised readout of the generated frames into
+    out[video rows] ([T, n*d] view); other rows are left untouched (zero)."""
+    br = attn.linear_attention
+    n, d = heads.stop - heads.start, pb.head_dim
+    ch = slice(heads.start * d, heads.stop * d)
+    Fr, S = layout.num_frames, layout.tokens_per_frame
+    vs = layout.video_start
+    skip = attn.anchor_frames == "both"
+    f0, f1 = (1, Fr - 1) if skip else (0, Fr)
+    if f1 - f0 <= 0:
+        return
+    r0, r1 = vs + f0 * S, vs + f1 * S
+    nF = f1 - f0
+    conv = br.short_conv
+    fs = layout.frame_size if conv is not None else None
+    feats = []
+    for t, proj in ((q_raw, "q"), (k_raw, "k"), (v_raw, "v")):
+        t = t[r0:r1]
+        if conv is not None and proj in conv.projs:
+            w_sp, w_tm = conv.weights(proj, ch)
+            feats.append(lb.conv_features(t, w_sp, w_tm, nF, fs, proj != "v"))
+        else:
+            feats.append(lb.activate(t, proj != "v"))
+    qf, kf, vf = feats
+    beta = torch.sigmoid(beta_logits[r0:r1].float())
+    A, B = lb.frame_statistics(kf.view(nF, S, n, d), vf.view(nF, S, n, d), beta.view(nF, S, n),
+                               a_fp32=br.a_fp32)
+    del kf, vf
+    alpha = br.alpha(frame_sums[f0:f1] / S, heads=None if n == pb.heads else heads)
+    text_state = None
+    if attn.enable_text_state:
+        ts, te = layout.text_range
+        text_raw = (q_raw[ts:te], k_raw[ts:te], v_raw[ts:te])
+        text_beta = torch.sigmoid(beta_logits[ts:te].float())
+        text_state = lb.text_state(br, text_raw, text_beta)
+    trans, inj = lb.factor_apply(br.backend(S), alpha, A, B)
+    prefix, suffix = lb.run_scans(trans, inj, text_state)
+    bnd = bounds[f0:f1]
+    if skip:
+        bnd = [(lo - 1, hi - 1) for lo, hi in bnd]
+    state = lb.gather(prefix, suffix, alpha, bnd, br.bridge, text_state, out_dtype=dtype)
+    del prefix, suffix, trans, inj
+    up_w = pb.gate_up_w[ch]
+    up_b = None if pb.gate_up_b is None else pb.gate_up_b[ch]
+    gate_logits = gemm.linear(ghid[r0:r1], up_w, up_b)
+    lb.readout(qf.view(nF, S, n, d), state, br.norm.weight, gate_logits.view(-1, n, d),
+               br.norm.eps, out=out[r0:r1], gate_logits=True)

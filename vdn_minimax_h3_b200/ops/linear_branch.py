@@ -139,6 +139,21 @@ def readout(q, state, norm_w, gate, eps, out=None, gate_logits=False):
     return out
 
 
+def text_state(branch, text_raw, text_beta):
+    """TEXT_STATE_SCALE * S_text for a head range: the prompt written into a zero state as one
+    delta-rule chunk of L rows (reference branch.py:178-216). text_raw = (q, k, v) [L, n, d]
+    views; text_beta [L, n] fp32. [n, d, d] fp32."""
+    q, k, v = text_raw
+    L, n, d = k.shape
+    kf = activate(k, True)
+    vf = activate(v, False)
+    A, B = frame_statistics(kf.view(1, L, n, d), vf.view(1, L, n, d), text_beta.reshape(1, L, n),
+                            a_fp32=branch.a_fp32)
+    ones = torch.ones(1, n, d, device=A.device, dtype=torch.float32)
+    _, inj = factor_apply(branch.backend(L), ones, A, B)
+    return branch.TEXT_STATE_SCALE * inj[0]
+
+
 def bench_linear(timed):  # pragma: no cover - GPU tool
     import json
     Fr, S, n, d = 100, 1008, 56, 128
