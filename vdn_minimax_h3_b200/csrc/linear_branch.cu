@@ -51,99 +51,152 @@ void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, in
 }
 
 // --------------------------------------------------------------- separable short conv
-// Block = 8 warps = 8 grid positions of one head; a warp walks a chunk of LB_FC frames
-// (plus a 2-frame halo each side) keeping the last five spatial results in a shift register.
+// Block = one grid row of one head for a chunk of LB_FC frames. Per frame, the 5 grid rows
+// around it (2-row halo each side) are staged in shared memory once; warp w computes
+// positions {w, w+14, w+28} of the row, lane = 4 channels. The last five spatial results
+// per output live in a register shift ring, so each input frame is read from global memory
+// (L2) five times in total instead of 25 times per output.
 constexpr int LB_FC = 16;
+constexpr int LB_WARPS = 14;
+constexpr int LB_PPW = 3;           // positions per warp (grid width <= 42)
+constexpr int LB_MAXW = LB_WARPS * LB_PPW;
 
-__global__ void __launch_bounds__(256) lb_conv_kernel(const __nv_bfloat16* __restrict__ in,
-                                                      int64_t ldi, const float* __restrict__ wsp,
-                                                      const float* __restrict__ wtm,
-                                                      __nv_bfloat16* __restrict__ out, int64_t ldo,
-                                                      int F, int gh, int gw, int H, int l2) {
+__global__ void __launch_bounds__(LB_WARPS * 32) lb_conv_kernel(
+    const __nv_bfloat16* __restrict__ in, int64_t ldi, const float* __restrict__ wsp,
+    const float* __restrict__ wtm, __nv_bfloat16* __restrict__ out, int64_t ldo, int F, int gh,
+    int gw, int H, int l2) {
   __shared__ float s_wsp[25][128];
   __shared__ float s_wtm[5][128];
-  const int h = blockIdx.y;
+  // rows y-2..y+2, cols -2..gw+1 of the frame (dynamic shared memory)
+  extern __shared__ __align__(16) uint8_t lb_conv_dyn[];
+  auto s_in = reinterpret_cast<__nv_bfloat16 (*)[LB_MAXW + 4][128]>(lb_conv_dyn);
+  const int y = blockIdx.x, h = blockIdx.y;
+  const int f0 = blockIdx.z * LB_FC;
   const int S = gh * gw;
-  for (int i = threadIdx.x; i < 25 * 128; i += 256) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < 25 * 128; i += blockDim.x) {
     const int tap = i / 128, c = i % 128;
     s_wsp[tap][c] = wsp[(int64_t)(h * 128 + c) * 25 + tap];
   }
-  for (int i = threadIdx.x; i < 5 * 128; i += 256) {
+  for (int i = tid; i < 5 * 128; i += blockDim.x) {
     const int tap = i / 128, c = i % 128;
     s_wtm[tap][c] = wtm[(int64_t)(h * 128 + c) * 5 + tap];
   }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pos = blockIdx.x * 8 + warp;
-  const int f0 = blockIdx.z * LB_FC;
-  if (pos >= S || f0 >= F) return;
-  const int y = pos / gw, x = pos % gw;
+  // zero the padded border columns once (they stay zero)
+  for (int i = tid; i < 5 * 4 * 16; i += blockDim.x) {
+    const int r = i / 64, rest = i % 64, side = rest / 32, c8 = rest % 16, half = (rest / 16) & 1;
+    const int col = side == 0 ? half : gw + 2 + half;
+    reinterpret_cast<uint4*>(&s_in[r][col][0])[c8] = make_uint4(0, 0, 0, 0);
+  }
   const int c0 = lane * 4;
-  const int64_t col = (int64_t)h * 128 + c0;
-  float r[5][4];
+  const int64_t chan = (int64_t)h * 128;
+  float ring[5][LB_PPW][4];
 #pragma unroll
   for (int a = 0; a < 5; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) r[a][b] = 0.f;
+    for (int q = 0; q < LB_PPW; ++q)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) ring[a][q][b] = 0.f;
   const int f_end = min(F, f0 + LB_FC);
-  // spatial results for frames f0-2 .. f_end+1; output frame fo = f - 2
   for (int f = f0 - 2; f < f_end + 2; ++f) {
-    float sp[4] = {0.f, 0.f, 0.f, 0.f};
-    if (f >= 0 && f < F) {
+    const bool live = f >= 0 && f < F;
+    __syncthreads();   // previous frame's smem reads are done
+    if (live) {
+      // stage rows y-2..y+2 of frame f, 16 bytes per thread-iteration
+      const int per_row = gw * 16;
+      for (int i = tid; i < 5 * per_row; i += blockDim.x) {
+        const int r = i / per_row, rem = i % per_row, x = rem / 16, c8 = rem % 16;
+        const int yy = y + r - 2;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (yy >= 0 && yy < gh)
+          v = *reinterpret_cast<const uint4*>(in + ((int64_t)f * S + yy * gw + x) * ldi + chan + c8 * 8);
+        reinterpret_cast<uint4*>(&s_in[r][x + 2][0])[c8] = v;
+      }
+    }
+    __syncthreads();
+    float sp[LB_PPW][4];
+#pragma unroll
+    for (int q = 0; q < LB_PPW; ++q)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) sp[q][b] = 0.f;
+    if (live) {
 #pragma unroll
       for (int i = 0; i < 5; ++i) {
-        const int yy = y + i - 2;
-        if (yy < 0 || yy >= gh) continue;
 #pragma unroll
         for (int j = 0; j < 5; ++j) {
-          const int xx = x + j - 2;
-          if (xx < 0 || xx >= gw) continue;
-          const uint2 v = *reinterpret_cast<const uint2*>(in + ((int64_t)f * S + yy * gw + xx) * ldi + col);
-          const float* w = &s_wsp[i * 5 + j][c0];
-          sp[0] += w[0] * bf16_lo(v.x);
-          sp[1] += w[1] * bf16_hi(v.x);
-          sp[2] += w[2] * bf16_lo(v.y);
-          sp[3] += w[3] * bf16_hi(v.y);
+          const float4 w = *reinterpret_cast<const float4*>(&s_wsp[i * 5 + j][c0]);
+#pragma unroll
+          for (int q = 0; q < LB_PPW; ++q) {
+            const int x = warp + q * LB_WARPS;
+            if (x < gw) {
+              const uint2 v = *reinterpret_cast<const uint2*>(&s_in[i][x + j][c0]);
+              sp[q][0] += w.x * bf16_lo(v.x);
+              sp[q][1] += w.y * bf16_hi(v.x);
+              sp[q][2] += w.z * bf16_lo(v.y);
+              sp[q][3] += w.w * bf16_hi(v.y);
+            }
+          }
         }
       }
     }
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      r[0][b] = r[1][b];
-      r[1][b] = r[2][b];
-      r[2][b] = r[3][b];
-      r[3][b] = r[4][b];
-      r[4][b] = sp[b];
-    }
+    for (int q = 0; q < LB_PPW; ++q)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        ring[0][q][b] = ring[1][q][b];
+        ring[1][q][b] = ring[2][q][b];
+        ring[2][q][b] = ring[3][q][b];
+        ring[3][q][b] = ring[4][q][b];
+        ring[4][q][b] = sp[q][b];
+      }
     const int fo = f - 2;
     if (fo < f0) continue;
-    float o[4];
+    const float4 t0 = *reinterpret_cast<const float4*>(&s_wtm[0][c0]);
+    const float4 t1 = *reinterpret_cast<const float4*>(&s_wtm[1][c0]);
+    const float4 t2 = *reinterpret_cast<const float4*>(&s_wtm[2][c0]);
+    const float4 t3 = *reinterpret_cast<const float4*>(&s_wtm[3][c0]);
+    const float4 t4 = *reinterpret_cast<const float4*>(&s_wtm[4][c0]);
+    const float tw[5][4] = {{t0.x, t0.y, t0.z, t0.w}, {t1.x, t1.y, t1.z, t1.w},
+                            {t2.x, t2.y, t2.z, t2.w}, {t3.x, t3.y, t3.z, t3.w},
+                            {t4.x, t4.y, t4.z, t4.w}};
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      float t = 0.f;
+    for (int q = 0; q < LB_PPW; ++q) {
+      const int x = warp + q * LB_WARPS;
+      float o[4];
 #pragma unroll
-      for (int dt = 0; dt < 5; ++dt) t += s_wtm[dt][c0 + b] * r[dt][b];
-      o[b] = siluf_(t);
+      for (int b = 0; b < 4; ++b) {
+        float t = 0.f;
+#pragma unroll
+        for (int dt = 0; dt < 5; ++dt) t += tw[dt][b] * ring[dt][q][b];
+        o[b] = siluf_(t);
+      }
+      if (l2) {
+        const float ss = warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+        const float inv = 1.f / fmaxf(sqrtf(ss), 1e-6f);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) o[b] *= inv;
+      }
+      if (x < gw)
+        *reinterpret_cast<uint2*>(out + ((int64_t)fo * S + y * gw + x) * ldo + chan + c0) =
+            make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
     }
-    if (l2) {
-      const float ss = warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
-      const float inv = 1.f / fmaxf(sqrtf(ss), 1e-6f);
-#pragma unroll
-      for (int b = 0; b < 4; ++b) o[b] *= inv;
-    }
-    *reinterpret_cast<uint2*>(out + ((int64_t)fo * S + pos) * ldo + col) =
-        make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
   }
 }
 
 void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,
                     int64_t ldo, int F, int gh, int gw, int H, int l2, cudaStream_t stream) {
-  const int S = gh * gw;
-  if (!F || !S) return;
-  dim3 grid((S + 7) / 8, H, (F + LB_FC - 1) / LB_FC);
-  lb_conv_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(in), ldi, wsp,
-                                           wtm, reinterpret_cast<__nv_bfloat16*>(out), ldo, F,
-                                           gh, gw, H, l2);
+  if (!F || !gh || !gw) return;
+  if (gw > LB_MAXW) throw std::runtime_error("short conv: grid width above 42 is not supported");
+  dim3 grid(gh, H, (F + LB_FC - 1) / LB_FC);
+  constexpr int smem = 5 * (LB_MAXW + 4) * 128 * 2;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(lb_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr = true;
+  }
+  lb_conv_kernel<<<grid, LB_WARPS * 32, smem, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(in), ldi, wsp, wtm,
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, F, gh, gw, H, l2);
 }
 
 // ------------------------------------------------------------------ frame statistics
@@ -338,86 +391,123 @@ void launch_lb_frame_stats(const void* k, int64_t ldk, const void* v, int64_t ld
 }
 
 // ---------------------------------------------------------------------- SPD factor
-constexpr int SPD_PITCH = 129;
-constexpr int SPD_SMEM = (128 * SPD_PITCH + 2 * 128) * 4;
+// Gauss-Jordan inversion with the matrix held in registers: thread (ti, tj) of 16 x 16 owns
+// the 8 x 8 block rows 8ti.., cols 8tj..; step k broadcasts only pivot column k and pivot
+// row k through shared memory. SPD (I + aA): no row exchanges needed.
+constexpr int SPD_SMEM = (128 * 129 + 2 * 128) * 4;
 
 __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
     const float* __restrict__ A, const float* __restrict__ B, const float* __restrict__ alpha,
     float* __restrict__ trans, float* __restrict__ inj, float a_scale, float b_scale) {
   extern __shared__ float sm[];
-  float* M = sm;
-  float* colk = sm + 128 * SPD_PITCH;
-  float* rowk = colk + 128;
+  float* colk = sm;            // [128]
+  float* rowk = sm + 128;      // [128]
+  float* Ms = sm + 256;        // [128][129] final inverse, for the injection product
   const int64_t mat = blockIdx.x;
   const float* a = A + mat * 16384;
-  const int tid = threadIdx.x;
-  for (int i = tid; i < 16384; i += 256) {
-    const int r = i >> 7, c = i & 127;
-    const float sym = 0.5f * (a[r * 128 + c] + a[c * 128 + r]);
-    M[r * SPD_PITCH + c] = a_scale * sym + (r == c ? 1.f : 0.f);
+  const int tid = threadIdx.x, ti = tid >> 4, tj = tid & 15;
+  float m[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = ti * 8 + i;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = tj * 8 + j;
+      m[i][j] = a_scale * 0.5f * (a[r * 128 + c] + a[c * 128 + r]) + (r == c ? 1.f : 0.f);
+    }
   }
-  __syncthreads();
-  // Gauss-Jordan inversion in place (SPD: pivots stay positive without row exchanges).
   for (int k = 0; k < 128; ++k) {
-    const float inv_p = 1.f / M[k * SPD_PITCH + k];
-    if (tid < 128) {
-      colk[tid] = M[tid * SPD_PITCH + k];
-      rowk[tid] = M[k * SPD_PITCH + tid] * inv_p;
-    }
-    __syncthreads();
-    for (int i = tid; i < 16384; i += 256) {
-      const int r = i >> 7, c = i & 127;
-      float val;
-      if (r == k) {
-        val = (c == k) ? inv_p : rowk[c];
-      } else if (c == k) {
-        val = -colk[r] * inv_p;
-      } else {
-        val = M[r * SPD_PITCH + c] - colk[r] * rowk[c];
+    const int kb = k >> 3, kk = k & 7;
+    if (tj == kb) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float v = m[i][0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) v = (j == kk) ? m[i][j] : v;
+        colk[ti * 8 + i] = v;
       }
-      M[r * SPD_PITCH + c] = val;
+    }
+    if (ti == kb) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v = m[0][j];
+#pragma unroll
+        for (int i = 1; i < 8; ++i) v = (i == kk) ? m[i][j] : v;
+        rowk[tj * 8 + j] = v;
+      }
+    }
+    __syncthreads();
+    const float inv_p = 1.f / colk[k];
+    float cr[8], rr[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cr[i] = colk[ti * 8 + i];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) rr[j] = rowk[tj * 8 + j] * inv_p;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const bool rk = (ti * 8 + i) == k;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool ck = (tj * 8 + j) == k;
+        const float upd = m[i][j] - cr[i] * rr[j];
+        m[i][j] = rk ? (ck ? inv_p : rr[j]) : (ck ? -cr[i] * inv_p : upd);
+      }
     }
     __syncthreads();
   }
-  // symmetrise, then transition = diag(alpha) * inv (row scale)
-  const float* al = alpha + mat * 128;
-  float* tr = trans + mat * 16384;
-  for (int i = tid; i < 16384; i += 256) {
-    const int r = i >> 7, c = i & 127;
-    if (c < r) continue;
-    const float s = 0.5f * (M[r * SPD_PITCH + c] + M[c * SPD_PITCH + r]);
-    M[r * SPD_PITCH + c] = s;
-    M[c * SPD_PITCH + r] = s;
-  }
-  __syncthreads();
-  for (int i = tid; i < 16384; i += 256) {
-    const int r = i >> 7, c = i & 127;
-    tr[i] = al[r] * M[r * SPD_PITCH + c];
-  }
-  // injection = (b_scale * B) @ inv, 8x8 register tile per thread
-  const float* bm = B + mat * 16384;
-  float* out = inj + mat * 16384;
-  const int ti = tid >> 4, tj = tid & 15;
-  float acc[8][8];
+  // symmetrise through shared memory, transition = diag(alpha) inv
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 8; ++j) Ms[(ti * 8 + i) * 129 + tj * 8 + j] = m[i][j];
+  __syncthreads();
+  const float* al = alpha + mat * 128;
+  float* tr = trans + mat * 16384;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = ti * 8 + i;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = tj * 8 + j;
+      m[i][j] = 0.5f * (Ms[r * 129 + c] + Ms[c * 129 + r]);
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = ti * 8 + i;
+    const float ar = al[r];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) Ms[r * 129 + tj * 8 + j] = m[i][j];
+    float4* dst = reinterpret_cast<float4*>(tr + r * 128 + tj * 8);
+    dst[0] = make_float4(ar * m[i][0], ar * m[i][1], ar * m[i][2], ar * m[i][3]);
+    dst[1] = make_float4(ar * m[i][4], ar * m[i][5], ar * m[i][6], ar * m[i][7]);
+  }
+  __syncthreads();
+  // injection = (b_scale * B) @ inv
+  const float* bm = B + mat * 16384;
+  float* out = inj + mat * 16384;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m[i][j] = 0.f;
   for (int kk = 0; kk < 128; ++kk) {
     float bi[8], mj[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) bi[i] = bm[(ti * 8 + i) * 128 + kk];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) mj[j] = M[kk * SPD_PITCH + tj * 8 + j];
+    for (int j = 0; j < 8; ++j) mj[j] = Ms[kk * 129 + tj * 8 + j];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] += bi[i] * mj[j];
+      for (int j = 0; j < 8; ++j) m[i][j] += bi[i] * mj[j];
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) out[(ti * 8 + i) * 128 + tj * 8 + j] = b_scale * acc[i][j];
+  for (int i = 0; i < 8; ++i) {
+    float4* dst = reinterpret_cast<float4*>(out + (ti * 8 + i) * 128 + tj * 8);
+    dst[0] = make_float4(b_scale * m[i][0], b_scale * m[i][1], b_scale * m[i][2], b_scale * m[i][3]);
+    dst[1] = make_float4(b_scale * m[i][4], b_scale * m[i][5], b_scale * m[i][6], b_scale * m[i][7]);
+  }
 }
 
 void launch_lb_spd_factor(const float* A, const float* B, const float* alpha, float* trans,

@@ -155,10 +155,39 @@ def text_state(branch, text_raw, text_beta):
 
 
 def bench_linear(timed):  # pragma: no cover - GPU tool
+    """Each linear-branch stage at the full geometry: 100 inner frames x 1008 tokens x 56
+    heads (anchors both), 800 prompt rows."""
     import json
-    Fr, S, n, d = 100, 1008, 56, 128
-    k = torch.randn(Fr, S, n, d, device="cuda", dtype=torch.bfloat16)
-    v = torch.randn_like(k)
-    beta = torch.rand(Fr, S, n, device="cuda")
-    ms = timed(lambda: frame_statistics(k, v, beta))
-    print(json.dumps(dict(case="frame_stats", ms=ms)), flush=True)
+    from vdn_minimax_h3_b200.models.delta_rule import VdnDelta
+    from vdn_minimax_h3_b200.models.window import window_bounds
+    Fr, S, n, d, gh, gw = 100, 1008, 56, 128, 24, 42
+    dev = "cuda"
+    raw = torch.randn(Fr * S, 3 * n * d + 8, device=dev, dtype=torch.bfloat16)
+    q_raw = raw[:, :n * d].view(-1, n, d)
+    k_raw = raw[:, n * d:2 * n * d].view(-1, n, d)
+    w_sp = torch.randn(n * d, 5, 5, device=dev) / 5
+    w_tm = torch.randn(n * d, 5, device=dev) / 2
+    res = {}
+    res["activate_q"] = timed(lambda: activate(q_raw, True))
+    res["conv_features_k"] = timed(lambda: conv_features(k_raw, w_sp, w_tm, Fr, (gh, gw), True))
+    kf = conv_features(k_raw, w_sp, w_tm, Fr, (gh, gw), True)
+    vf = conv_features(k_raw, w_sp, w_tm, Fr, (gh, gw), False)
+    beta = torch.rand(Fr, S, n, device=dev)
+    res["frame_stats"] = timed(lambda: frame_statistics(kf.view(Fr, S, n, d), vf.view(Fr, S, n, d), beta))
+    A, B = frame_statistics(kf.view(Fr, S, n, d), vf.view(Fr, S, n, d), beta)
+    alpha = torch.rand(Fr, n, d, device=dev) * 0.5 + 0.5
+    res["spd_factor"] = timed(lambda: factor_apply(VdnDelta(S), alpha, A, B))
+    trans, inj = factor_apply(VdnDelta(S), alpha, A, B)
+    trans = trans * 0.05
+    res["scan"] = timed(lambda: run_scans(trans, inj, None))
+    pre, suf = run_scans(trans, inj, None)
+    bounds = [(lo - 1, hi - 1) for lo, hi in window_bounds(Fr + 2, 1, 5)[1:-1]]
+    res["gather"] = timed(lambda: gather(pre, suf, alpha, bounds, "alpha", None))
+    state = gather(pre, suf, alpha, bounds, "alpha", None)
+    qf = activate(q_raw, True)
+    gate = torch.randn(Fr * S, n, d, device=dev, dtype=torch.bfloat16)
+    w = torch.ones(d, device=dev)
+    out = torch.empty(Fr * S, n * d, device=dev, dtype=torch.bfloat16)
+    res["readout"] = timed(lambda: readout(qf.view(Fr, S, n, d), state, w, gate, 1e-6, out=out,
+                                           gate_logits=True))
+    print(json.dumps({"linear_branch_ms": {k: round(v, 3) for k, v in res.items()}}), flush=True)
