@@ -1,23 +1,27 @@
 // Window softmax attention on the 5th-generation tensor cores (sm_100a).
 //
-// One work item = (head, 128-row query tile). The tile belongs to a plan segment whose kept
-// K/V rows are at most four CONTIGUOUS row ranges of the packed sequence (globals, the
-// window frames, the anchor frames; models/window.py: AttentionPlan). The kernel walks
-// those ranges in 128-key blocks straight out of the [T, H, d] projections -- no gather,
-// no mask tensor; only the ragged tail of each range is masked.
+// One work item = (head, 256 query rows) of one plan segment, processed as TWO 128-row
+// tiles that share every K/V block. The segment's kept K/V rows are at most four CONTIGUOUS
+// row ranges of the packed sequence (globals, the window frames, the anchor frames;
+// models/window.py: AttentionPlan); the kernel walks them in 64-key blocks straight out of
+// the [T, H, d] projections -- no gather, no mask tensor; only the ragged tail of a range
+// is masked.
 //
-// Roles (192 threads, one CTA per SM, persistent over head-major work items so the CTAs
-// in flight share one head's K/V in L2):
-//   warp 0     TMA producer: Q tile once per item, K/V blocks into a 2-stage ring.
-//   warp 1     MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S buffers
-//              (kind::f16, M=128, N=128, K=16 x 8), then O += P_{j-1} V_{j-1} with P from
-//              shared memory (K-major) and V as an MN-major operand; commits free K/V
-//              stages and signal the softmax warps.
-//   warps 2-5  softmax (thread = query row): S row from TMEM (tcgen05.ld), online softmax
-//              in the exp2 domain with a lazy rescale (O in TMEM is rescaled only when the
-//              running max grows by more than 2^8), P (bf16) written into the 128B-swizzled
-//              shared-memory operand, and the epilogue O / l * sigmoid(gate) -> bf16.
-// TMEM: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+// Roles (320 threads, one CTA per SM, persistent over head-major work items so the CTAs in
+// flight share one head's K/V in L2):
+//   warp 0      TMA producer: both Q tiles once per item, K/V blocks into a 3-stage ring.
+//   warp 1      MMA issuer (one thread): per block, S_t = Q_t K^T for both tiles into
+//               double-buffered TMEM S (kind::f16, M=128, N=64), then O_t += P_t V for
+//               the previous block (P from shared memory, V as an MN-major operand).
+//   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1 (thread = query row): S row
+//               from TMEM, online softmax in the exp2 domain with a lazy rescale (O in TMEM
+//               is rescaled only when the running max grows by more than 2^8), P written as
+//               bf16 into the 128B-swizzled shared operand, epilogue O / l * sigmoid(gate).
+//               While one tile's softmax runs, the tensor core works on the other tile.
+//               A quarter of the exponentials run as a cubic polynomial on the FMA pipe
+//               (2^x = 2^n * p(f), Cody-Waite split, p fitted for minimax relative error
+//               8.6e-5 on [0,1)) so the MUFU unit is not the bottleneck.
+// TMEM (512 columns): S[tile][buf] at (2*tile + buf) * 64, O[tile] at 256 + 128 * tile.
 //
 // Every wait is bounded; a protocol failure unwinds, drains and frees TMEM (common.cuh).
 // Reference parity: the window softmax of src/models/softmax_attention/ (decomposed.py's
@@ -28,17 +32,19 @@
 
 namespace vdn {
 
-constexpr int AT_BM = 128;      // query rows per tile
-constexpr int AT_BN = 128;      // keys per block
-constexpr int AT_D = 128;       // head dim
-constexpr int AT_STAGES = 2;
-constexpr int AT_TILE_BYTES = AT_BM * AT_D * 2;  // 32 KB (two 64-column swizzle atoms)
-constexpr int AT_THREADS = 192;
-constexpr int AT_SMEM = AT_TILE_BYTES * (1 /*Q*/ + 2 * AT_STAGES /*K,V*/ + 1 /*P*/) + 1024 + 512;
+constexpr int AT_BM = 128;                         // query rows per tile (2 tiles per item)
+constexpr int AT_BN = 64;                          // keys per block
+constexpr int AT_D = 128;                          // head dim
+constexpr int AT_STAGES = 3;
+constexpr int AT_Q_BYTES = AT_BM * AT_D * 2;       // 32 KB per Q tile (2 atoms of 16 KB)
+constexpr int AT_KV_BYTES = AT_BN * AT_D * 2;      // 16 KB per K or V block (2 atoms of 8 KB)
+constexpr int AT_P_BYTES = AT_BM * AT_BN * 2;      // 16 KB per P tile (1 atom column)
+constexpr int AT_THREADS = 320;
+constexpr int AT_SMEM = 2 * AT_Q_BYTES + 2 * AT_STAGES * AT_KV_BYTES + 2 * AT_P_BYTES + 1024 + 512;
 constexpr int AT_MAX_RANGES = 4;
 
 struct AttnParams {
-  const int* tiles;          // [n_tiles, 4] (q0, q1, segment, kv_len)
+  const int* tiles;          // [n_items_per_head, 4] (q0, q_end, segment, kv_len), q_end-q0 <= 256
   const int* kv;             // [n_seg, 8] (start, end) x 4
   int n_tiles, H, T;
   const __nv_bfloat16* gate; // [T, ldg] logits per head, or null
@@ -55,7 +61,17 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Iterates the 128-key blocks of a segment's K/V ranges.
+// 2^x on the FMA pipe: x = n + f, n = floor(x), 2^f by a cubic fitted for minimax relative
+// error (8.6e-5 on [0,1)), 2^n by adding n to the exponent field. Valid for x >= -126.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float n = floorf(x);
+  const float f = x - n;
+  const float p = fmaf(fmaf(fmaf(0.07706641f, f, 0.2276457f), f, 0.69511664f), f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
+}
+
+// Iterates the 64-key blocks of a segment's K/V ranges.
 struct KvWalk {
   int r[2 * AT_MAX_RANGES];
   int range, pos;
@@ -93,24 +109,24 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + AT_TILE_BYTES;
-  uint8_t* sV = sK + AT_STAGES * AT_TILE_BYTES;
-  uint8_t* sP = sV + AT_STAGES * AT_TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + AT_TILE_BYTES);
+  uint8_t* sQ = smem;                                   // [2][32 KB]
+  uint8_t* sK = sQ + 2 * AT_Q_BYTES;                    // [3][16 KB]
+  uint8_t* sV = sK + AT_STAGES * AT_KV_BYTES;           // [3][16 KB]
+  uint8_t* sP = sV + AT_STAGES * AT_KV_BYTES;           // [2][16 KB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * AT_P_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;    // [2]
-  uint64_t* k_empty = bars + 4;   // [2]
-  uint64_t* v_full = bars + 6;    // [2]
-  uint64_t* v_empty = bars + 8;   // [2]
-  uint64_t* s_full = bars + 10;   // [2]
-  uint64_t* s_empty = bars + 12;  // [2]
-  uint64_t* p_full = bars + 14;
-  uint64_t* pv_done = bars + 15;
-  uint64_t* o_empty = bars + 16;
-  uint64_t* mma_done = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* k_full = bars + 2;             // [3]
+  uint64_t* k_empty = bars + 5;            // [3]
+  uint64_t* v_full = bars + 8;             // [3]
+  uint64_t* v_empty = bars + 11;           // [3]
+  uint64_t* s_full = bars + 14;            // [tile*2 + buf]
+  uint64_t* s_empty = bars + 18;           // [tile*2 + buf]
+  uint64_t* p_full = bars + 22;            // [tile]
+  uint64_t* pv_done = bars + 24;           // [tile]
+  uint64_t* o_empty = bars + 26;           // [tile]
+  uint64_t* mma_done = bars + 28;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 29);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -125,13 +141,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 128);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
-    mbar_init(o_empty, 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&p_full[t], 128);
+      mbar_init(&pv_done[t], 1);
+      mbar_init(&o_empty[t], 128);
+    }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -166,9 +184,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           break;
         }
         last_phase[2 * AT_STAGES] = local & 1;
-        mbar_arrive_expect_tx(q_full, AT_TILE_BYTES);
-        tma_load_2d(sQ, &tmQ, q_full, head * AT_D, t[0]);
-        tma_load_2d(sQ + AT_TILE_BYTES / 2, &tmQ, q_full, head * AT_D + 64, t[0]);
+        mbar_arrive_expect_tx(q_full, 2 * AT_Q_BYTES);
+#pragma unroll
+        for (int qt = 0; qt < 2; ++qt) {
+          tma_load_2d(sQ + qt * AT_Q_BYTES, &tmQ, q_full, head * AT_D, t[0] + qt * AT_BM);
+          tma_load_2d(sQ + qt * AT_Q_BYTES + AT_Q_BYTES / 2, &tmQ, q_full, head * AT_D + 64,
+                      t[0] + qt * AT_BM);
+        }
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         for (; !w.done(); w.next()) {
@@ -176,34 +198,34 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             ok = false;
             break;
           }
-          uint8_t* k = sK + stage * AT_TILE_BYTES;
+          uint8_t* k = sK + stage * AT_KV_BYTES;
           last_phase[stage] = (int)phase;
-          mbar_arrive_expect_tx(&k_full[stage], AT_TILE_BYTES);
+          mbar_arrive_expect_tx(&k_full[stage], AT_KV_BYTES);
           tma_load_2d(k, &tmK, &k_full[stage], head * AT_D, w.start());
-          tma_load_2d(k + AT_TILE_BYTES / 2, &tmK, &k_full[stage], head * AT_D + 64, w.start());
+          tma_load_2d(k + AT_KV_BYTES / 2, &tmK, &k_full[stage], head * AT_D + 64, w.start());
           if (!mbar_wait(&v_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
-          uint8_t* v = sV + stage * AT_TILE_BYTES;
+          uint8_t* v = sV + stage * AT_KV_BYTES;
           last_phase[AT_STAGES + stage] = (int)phase;
-          mbar_arrive_expect_tx(&v_full[stage], AT_TILE_BYTES);
+          mbar_arrive_expect_tx(&v_full[stage], AT_KV_BYTES);
           tma_load_2d(v, &tmV, &v_full[stage], head * AT_D, w.start());
-          tma_load_2d(v + AT_TILE_BYTES / 2, &tmV, &v_full[stage], head * AT_D + 64, w.start());
+          tma_load_2d(v + AT_KV_BYTES / 2, &tmV, &v_full[stage], head * AT_D + 64, w.start());
           if (++stage == AT_STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      // On abort, let every copy this thread issued land before the CTA exits.
       if (!ok || *abort_flag) {
+        // let every copy this thread issued land before the CTA exits
         long long t0 = clock64();
         for (int i = 0; i < 2 * AT_STAGES + 1; ++i) {
-          uint64_t* bar = i < AT_STAGES ? &k_full[i] : (i < 2 * AT_STAGES ? &v_full[i - AT_STAGES] : q_full);
-          const int par = last_phase[i];
-          if (par < 0) continue;
-          while (!mbar_try_wait(bar, (uint32_t)par) && clock64() - t0 < kWaitBudgetCycles) {
+          uint64_t* bar = i < AT_STAGES ? &k_full[i]
+                                        : (i < 2 * AT_STAGES ? &v_full[i - AT_STAGES] : q_full);
+          if (last_phase[i] < 0) continue;
+          while (!mbar_try_wait(bar, (uint32_t)last_phase[i]) && clock64() - t0 < kWaitBudgetCycles) {
           }
         }
       }
@@ -233,47 +255,58 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         while (true) {
           const bool have = !w.done();
           if (have) {
-            // S_j = Q K_j^T into S buffer (g & 1)
             const uint32_t b = g & 1;
-            if (!mbar_wait(&k_full[stage], phase, abort_flag, p.err, kErrTimeoutMma) ||
-                !mbar_wait(&s_empty[b], ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
+            if (!mbar_wait(&k_full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint32_t aK = smem_u32(sK + stage * AT_TILE_BYTES);
+            const uint32_t aK = smem_u32(sK + stage * AT_KV_BYTES);
+            for (int qt = 0; qt < 2 && ok; ++qt) {
+              if (!mbar_wait(&s_empty[qt * 2 + b], ((g >> 1) & 1) ^ 1, abort_flag, p.err,
+                             kErrTimeoutMma)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t tS = tmem + (qt * 2 + b) * AT_BN;
 #pragma unroll
-            for (int k = 0; k < AT_D / 16; ++k) {
-              const uint32_t off = (k >> 2) * (AT_TILE_BYTES / 2) + (k & 3) * 32;
-              umma_f16_ss(tmem + b * 128, umma_desc_kmajor_sw128(aQ + off),
-                          umma_desc_kmajor_sw128(aK + off), idesc_s, k != 0);
+              for (int k = 0; k < AT_D / 16; ++k) {
+                const uint32_t offQ = qt * AT_Q_BYTES + (k >> 2) * (AT_Q_BYTES / 2) + (k & 3) * 32;
+                const uint32_t offK = (k >> 2) * (AT_KV_BYTES / 2) + (k & 3) * 32;
+                umma_f16_ss(tS, umma_desc_kmajor_sw128(aQ + offQ),
+                            umma_desc_kmajor_sw128(aK + offK), idesc_s, k != 0);
+              }
+              umma_commit(&s_full[qt * 2 + b]);
             }
+            if (!ok) break;
             umma_commit(&k_empty[stage]);
-            umma_commit(&s_full[b]);
           }
           if (j > 0) {
-            // O += P_{j-1} V_{j-1}
-            if (!mbar_wait(p_full, g_prev & 1, abort_flag, p.err, kErrTimeoutMma) ||
-                !mbar_wait(&v_full[prev_stage], prev_phase, abort_flag, p.err, kErrTimeoutMma)) {
+            // O_t += P_t V for the previous block
+            if (!mbar_wait(&v_full[prev_stage], prev_phase, abort_flag, p.err, kErrTimeoutMma)) {
               ok = false;
               break;
             }
-            if (j == 1 && local > 0 &&
-                !mbar_wait(o_empty, (local - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t aV = smem_u32(sV + prev_stage * AT_TILE_BYTES);
+            const uint32_t aV = smem_u32(sV + prev_stage * AT_KV_BYTES);
+            for (int qt = 0; qt < 2 && ok; ++qt) {
+              if (!mbar_wait(&p_full[qt], g_prev & 1, abort_flag, p.err, kErrTimeoutMma) ||
+                  (j == 1 && local > 0 &&
+                   !mbar_wait(&o_empty[qt], (local - 1) & 1, abort_flag, p.err, kErrTimeoutMma))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t tO = tmem + 256 + qt * 128;
 #pragma unroll
-            for (int k = 0; k < AT_BN / 16; ++k) {
-              const uint32_t offP = (k >> 2) * (AT_TILE_BYTES / 2) + (k & 3) * 32;
-              umma_f16_ss(tmem + 256, umma_desc_kmajor_sw128(aP + offP),
-                          umma_desc_mnmajor_sw128(aV + k * 2048, AT_TILE_BYTES / 2), idesc_o,
-                          (j > 1 || k > 0) ? 1u : 0u);
+              for (int k = 0; k < AT_BN / 16; ++k) {
+                umma_f16_ss(tO, umma_desc_kmajor_sw128(aP + qt * AT_P_BYTES + k * 32),
+                            umma_desc_mnmajor_sw128(aV + k * 2048, AT_KV_BYTES / 2), idesc_o,
+                            (j > 1 || k > 0) ? 1u : 0u);
+              }
+              umma_commit(&pv_done[qt]);
             }
+            if (!ok) break;
             umma_commit(&v_empty[prev_stage]);
-            umma_commit(pv_done);
           }
           if (!have) break;
           prev_stage = stage;
@@ -297,9 +330,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------- softmax + epilogue warps
+    const int qt = (warp - 2) >> 2;           // which query tile
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // row within the tile
+    const int r = quarter * 32 + lane;        // row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tO = tmem + lane_off + 256 + qt * 128;
+    uint8_t* prow = sP + qt * AT_P_BYTES + r * 128;
     uint32_t g = 0;
     int local = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++local) {
@@ -313,7 +349,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       bool ok = true;
       for (; !w.done(); w.next(), ++j, ++g) {
         const uint32_t b = g & 1;
-        if (!mbar_wait(&s_full[b], (g >> 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+        if (!mbar_wait(&s_full[qt * 2 + b], (g >> 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
           ok = false;
           break;
         }
@@ -322,13 +358,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < AT_BN; c += 32) {
           uint32_t u[32];
-          tmem_ld32(tmem + lane_off + b * 128 + c, u);
+          tmem_ld32(tmem + lane_off + (qt * 2 + b) * AT_BN + c, u);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(u[i]);
         }
         tc_fence_before();
-        mbar_arrive(&s_empty[b]);
+        mbar_arrive(&s_empty[qt * 2 + b]);
         const int valid = w.valid();
         float mx = -INFINITY;
 #pragma unroll
@@ -339,9 +375,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         const float m_new = fmaxf(m_ref, mx);
         const bool need = m_new > m_ref + 8.0f;
         const bool warp_need = __any_sync(0xffffffffu, need);
-        // PV_{j-1} must finish before O is touched or the P buffer is rewritten.
+        // PV of the previous block must finish before O or the P buffer is touched.
         if (j > 0) {
-          if (!mbar_wait(pv_done, (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+          if (!mbar_wait(&pv_done[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
             ok = false;
             break;
           }
@@ -357,48 +393,46 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll 1
           for (int c = 0; c < AT_D; c += 32) {
             uint32_t u[32];
-            tmem_ld32(tmem + lane_off + 256 + c, u);
+            tmem_ld32(tO + c, u);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
-            tmem_st32(tmem + lane_off + 256 + c, u);
+            tmem_st32(tO + c, u);
           }
           tmem_wait_st();
         }
         const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;
         float sum = 0.f;
-        uint8_t* prow = sP + r * 128;
 #pragma unroll
         for (int c = 0; c < AT_BN; c += 8) {
           float e[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            e[i] = ex2(s[c + i] - mref);
+            const float x = s[c + i] - mref;
+            e[i] = (i & 3) == 3 ? ex2_poly(x) : ex2(x);
             sum += e[i];
           }
           const uint4 pk = make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]),
                                       pack_bf16(e[4], e[5]), pack_bf16(e[6], e[7]));
-          const int chunk = c >> 3;                  // 16-byte chunk along the keys
-          const int atom = chunk >> 3, jj = chunk & 7;
-          *reinterpret_cast<uint4*>(prow + atom * (AT_TILE_BYTES / 2) + ((jj ^ (r & 7)) << 4)) = pk;
+          *reinterpret_cast<uint4*>(prow + (((c >> 3) ^ (r & 7)) << 4)) = pk;
         }
         l += sum;
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[qt]);
       }
       if (!ok) break;
       // Epilogue: wait for the last PV, O / l * gate -> bf16.
-      if (!mbar_wait(pv_done, (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
+      if (!mbar_wait(&pv_done[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
       tc_fence_after();
-      const int row = t[0] + r;
+      const int row = t[0] + qt * AT_BM + r;
       const bool row_ok = row < t[1];
       float gscale = 1.f / l;
       if (p.gate && row_ok) gscale *= sigmoidf_(__bfloat162float(p.gate[(int64_t)row * p.ldg + head]));
 #pragma unroll 1
       for (int c = 0; c < AT_D; c += 32) {
         uint32_t u[32];
-        tmem_ld32(tmem + lane_off + 256 + c, u);
+        tmem_ld32(tO + c, u);
         tmem_wait_ld();
         if (row_ok) {
           uint32_t pk[16];
@@ -411,7 +445,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(o_empty);
+      mbar_arrive(&o_empty[qt]);
     }
   }
 

@@ -134,12 +134,13 @@ def plan_segments(layout: SequenceLayout, bounds, anchor_frames="none", dense=Fa
 class AttentionPlan:
     """Device tables for the window-attention kernel, built once per (layout, bounds).
 
-    tiles:  int32 [n_tiles, 4]  (q_start, q_end, segment, 0) for each 128-row query tile,
-            longest K/V first so the persistent schedule ends balanced.
+    tiles:  int32 [n_tiles, 4]  (q_start, q_end, segment, kv_rows) for each work item of up
+            to `block_q` (256) query rows -- the kernel runs it as two 128-row tiles sharing
+            every K/V block -- longest K/V first so the persistent schedule ends balanced.
     kv:     int32 [n_segments, 2 * MAX_KV_RANGES] (start, end) pairs, empty ranges (0, 0).
     """
 
-    def __init__(self, layout, bounds, anchor_frames="none", device="cpu", block_q=128,
+    def __init__(self, layout, bounds, anchor_frames="none", device="cpu", block_q=256,
                  dense=False):
         self.segments = plan_segments(layout, bounds, anchor_frames, dense=dense)
         kv = torch.zeros(len(self.segments), 2 * MAX_KV_RANGES, dtype=torch.int32)

@@ -154,13 +154,13 @@ def text_state(branch, text_raw, text_beta):
     return branch.TEXT_STATE_SCALE * inj[0]
 
 
-def bench_linear(timed):  # pragma: no cover - GPU tool
+def bench_linear(timed, frames=100):  # pragma: no cover - GPU tool
     """Each linear-branch stage at the full geometry: 100 inner frames x 1008 tokens x 56
-    heads (anchors both), 800 prompt rows."""
+    heads (anchors both)."""
     import json
     from vdn_minimax_h3_b200.models.delta_rule import VdnDelta
     from vdn_minimax_h3_b200.models.window import window_bounds
-    Fr, S, n, d, gh, gw = 100, 1008, 56, 128, 24, 42
+    Fr, S, n, d, gh, gw = frames, 1008, 56, 128, 24, 42
     dev = "cuda"
     raw = torch.randn(Fr * S, 3 * n * d + 8, device=dev, dtype=torch.bfloat16)
     q_raw = raw[:, :n * d].view(-1, n, d)
