@@ -31,9 +31,13 @@ def test_adaln_rmsnorm(T, D):
 def test_frame_sums():
     torch.manual_seed(0)
     x = torch.randn(7 * 100 + 13, 512, device="cuda", dtype=torch.bfloat16)
-    out = norm_ops.frame_sums(x[13:], 7, 100)
+    out = norm_ops.frame_sums(x, 7, 100, 0, 13)
     ref = x[13:].float().view(7, 100, 512).sum(1)
     assert _rel(out, ref) < 1e-5
+    # a shard holding packed rows [250, 480) of the same sequence
+    part = norm_ops.frame_sums(x[250:480], 7, 100, 250, 13)
+    ref_part = norm_ops.frame_sums(x[250:480].cpu(), 7, 100, 250, 13)
+    assert _rel(part, ref_part) < 1e-5
 
 
 @pytest.mark.parametrize("T,H,d,rot,ld_extra", [(257, 4, 128, 128, 0), (100, 3, 64, 48, 64)])

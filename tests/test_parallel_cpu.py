@@ -1,0 +1,79 @@
+"""Ulysses sequence parallelism on CPU ranks (gloo, world 2): the sharded engine forward
+equals the single-process engine forward, and the split helpers match the reference's rules."""
+import copy
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from vdn_minimax_h3_b200.parallel.ulysses import balanced_splits, sequence_splits
+
+
+def test_sequence_splits():
+    assert sequence_splits(10, 1) == (10,)
+    assert sequence_splits(104766, 8) == (13096,) * 7 + (104766 - 7 * 13096,)
+    assert sum(sequence_splits(17, 5)) == 17
+    assert balanced_splits(56, 3) == (19, 19, 18)
+    with pytest.raises(ValueError):
+        balanced_splits(2, 3)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from tests.test_model_cpu import _forward_inputs, tiny_model
+        from vdn_minimax_h3_b200.inference.engine import InferenceEngine
+        from vdn_minimax_h3_b200.inference.render import render_geometry
+        from vdn_minimax_h3_b200.models.factory import RELEASED_HYBRID
+        from vdn_minimax_h3_b200.models.h3 import H3Config
+        from vdn_minimax_h3_b200.models.hybrid_transform import set_layout
+        from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
+        cfg = H3Config(hidden_size=128, num_layers=2, num_attention_heads=2, attention_head_dim=64,
+                       in_channels=8, text_dim=96, time_embed_dim=64, time_freq_dim=32,
+                       ff_inner_dim=256, num_refiner_layers=1, rope_axes_dim=(16, 24, 24))
+        model = tiny_model(RELEASED_HYBRID, cfg)
+        geo = render_geometry(cfg, 5, latent_h=8, latent_w=12, audio=True, num_latent_frames=17)
+        geo.num_audio_latents = 6
+        kw, layout = _forward_inputs(cfg, geo, 11)
+        set_layout(model, layout)
+        with torch.no_grad():
+            ref_v, ref_a = InferenceEngine(copy.deepcopy(model))(**kw, layout=layout)
+            eng = UlyssesEngine(InferenceEngine(model), init_ulysses())
+            out_v, out_a = eng(**kw, layout=layout)
+        err = max(((out_v - ref_v).norm() / ref_v.norm()).item(),
+                  ((out_a - ref_a).norm() / ref_a.norm()).item())
+        q.put((rank, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_ulysses_matches_single_process():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=280)
+    results = {}
+    while not q.empty():
+        r, e = q.get()
+        results[r] = e
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert len(results) == world
+    assert max(results.values()) < 1e-4, results

@@ -60,6 +60,8 @@ def main(argv=None):
     p.add_argument("--gemm", action="store_true")
     p.add_argument("--attention", action="store_true")
     p.add_argument("--linear", action="store_true")
+    p.add_argument("--attention-small", action="store_true",
+                   help="window attention on 20 frames x 8 heads (an ncu-sized case)")
     p.add_argument("--linear-small", action="store_true",
                    help="conv features + SPD inverse on 8 frames (an ncu-sized case)")
     a = p.parse_args(argv)
@@ -71,6 +73,9 @@ def main(argv=None):
     if a.linear:
         from vdn_minimax_h3_b200.ops.linear_branch import bench_linear
         bench_linear(timed)
+    if a.attention_small:
+        from vdn_minimax_h3_b200.ops.attention import bench_attention
+        bench_attention(timed, frames=20, heads=8)
     if a.linear_small:
         from vdn_minimax_h3_b200.ops.linear_branch import bench_linear
         bench_linear(lambda fn: (fn(), torch.cuda.synchronize(), 0.0)[2], frames=8)

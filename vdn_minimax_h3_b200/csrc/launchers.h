@@ -21,8 +21,8 @@ void launch_gemm_bf16(const GemmArgs& a, int mode, void* out, int64_t ldo, const
 void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps, const void* table,
                           int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
                           int64_t ldo, int T, int D, cudaStream_t stream);
-void launch_frame_sums(const void* x, int64_t ldx, int F, int S, int D, float* out,
-                       cudaStream_t stream);
+void launch_frame_sums(const void* x, int64_t ldx, int64_t row0, int64_t nrows, int64_t vs,
+                       int F, int S, int D, float* out, cudaStream_t stream);
 void launch_qk_prep(const void* src, int64_t lds, int T, int H, int d, const float* w, float eps,
                     const float* cosv, const float* sinv, int rot, void* out, int64_t ldo,
                     cudaStream_t stream);

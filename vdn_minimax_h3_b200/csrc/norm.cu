@@ -89,10 +89,12 @@ void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps,
 #undef VDN_ADALN
 }
 
-// Column sums of `rows` video rows grouped by frame: out[f, c] = sum_s x[vs + f*S + s, c].
-// grid (F, ceil(D/256)), 256 threads; lane owns 8 consecutive columns, warps stride rows.
+// Column sums of video rows grouped by frame: out[f, c] = sum over the rows of frame f that
+// lie in x (x[0] is packed row `row0`, x holds `nrows` rows; frame f is packed rows
+// [vs + f*S, vs + (f+1)*S)). grid (F, ceil(D/256)); lane = 8 columns, warps stride rows.
 __global__ void __launch_bounds__(256) frame_sums_kernel(const __nv_bfloat16* __restrict__ x,
-                                                         int64_t ldx, int S, int D,
+                                                         int64_t ldx, int64_t row0, int64_t nrows,
+                                                         int64_t vs, int S, int D,
                                                          float* __restrict__ out) {
   __shared__ float red[8][256];
   const int f = blockIdx.x;
@@ -100,9 +102,11 @@ __global__ void __launch_bounds__(256) frame_sums_kernel(const __nv_bfloat16* __
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = c0 + lane * 8;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int64_t a = max(vs + (int64_t)f * S, row0) - row0;
+  const int64_t b = min(vs + (int64_t)(f + 1) * S, row0 + nrows) - row0;
   if (col < D) {
-    for (int s = warp; s < S; s += 8) {
-      const uint4 v = *reinterpret_cast<const uint4*>(x + ((int64_t)f * S + s) * ldx + col);
+    for (int64_t s = a + warp; s < b; s += 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + s * ldx + col);
       const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -123,12 +127,12 @@ __global__ void __launch_bounds__(256) frame_sums_kernel(const __nv_bfloat16* __
   }
 }
 
-void launch_frame_sums(const void* x, int64_t ldx, int F, int S, int D, float* out,
-                       cudaStream_t stream) {
+void launch_frame_sums(const void* x, int64_t ldx, int64_t row0, int64_t nrows, int64_t vs,
+                       int F, int S, int D, float* out, cudaStream_t stream) {
   if (F == 0) return;
   dim3 grid(F, (D + 255) / 256);
-  frame_sums_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, S,
-                                              D, out);
+  frame_sums_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                                              row0, nrows, vs, S, D, out);
 }
 
 // One warp per (row, head). Generic head_dim <= 256 (multiple of 2), rotary_dim <= head_dim.

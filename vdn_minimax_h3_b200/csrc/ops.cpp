@@ -114,16 +114,16 @@ void adaln_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void frame_sums(torch::Tensor x, int64_t F, int64_t S, torch::Tensor out) {
+void frame_sums(torch::Tensor x, int64_t row0, int64_t video_start, int64_t F, int64_t S,
+                torch::Tensor out) {
   check_2d_bf16(x, "x");
   const int D = x.size(1);
-  TORCH_CHECK(x.size(0) >= F * S, "x has fewer than F*S rows");
   TORCH_CHECK(D % 8 == 0, "D must be a multiple of 8");
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() &&
                   out.numel() == F * D, "out must be contiguous fp32 [F, D]");
   c10::cuda::CUDAGuard g(x.device());
-  launch_frame_sums(x.data_ptr(), x.stride(0), (int)F, (int)S, D, out.data_ptr<float>(),
-                    at::cuda::getCurrentCUDAStream());
+  launch_frame_sums(x.data_ptr(), x.stride(0), row0, x.size(0), video_start, (int)F, (int)S, D,
+                    out.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -197,7 +197,7 @@ class InferenceEngine:
         n1 = self._buf("normed", (T, D), x.dtype, dev)
         with sec("norm"):
             norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1)
-            frame_sums = norm_ops.frame_sums(n1[vs:vs + Fr * S], Fr, S) if linear_on else None
+            frame_sums = norm_ops.frame_sums(n1, Fr, S, 0, vs) if linear_on else None
         qkvg = self._buf("qkvg", (T, pb.w_qkvg.shape[0]), x.dtype, dev)
         with sec("gemm_qkv"):
             gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)

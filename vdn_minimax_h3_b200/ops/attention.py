@@ -47,11 +47,11 @@ def window_attention(q, k, v, plan, scale, gate_logits=None, out=None):
     return out
 
 
-def bench_attention(timed):  # pragma: no cover - GPU tool
+def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
     import json
     from vdn_minimax_h3_b200.models.layout import SequenceLayout
     from vdn_minimax_h3_b200.models.window import AttentionPlan, window_bounds
-    T_text, T_audio, Fr, S, H, d = 800, 1150, 102, 1008, 56, 128
+    T_text, T_audio, Fr, S, H, d = 800, 1150, frames, 1008, heads, 128
     layout = SequenceLayout(seq_len=T_text + T_audio + Fr * S, video_start=T_text + T_audio,
                             num_frames=Fr, tokens_per_frame=S, frame_height=24, frame_width=42,
                             text_start=0, text_len=T_text)

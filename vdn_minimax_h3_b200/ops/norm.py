@@ -35,12 +35,22 @@ def adaln_rmsnorm(x, weight, eps, table, shift_col, scale_col, idx, out=None):
     return out
 
 
-def frame_sums(rows, num_frames, tokens_per_frame):
-    """fp32 [F, D] column sums of F consecutive frames of S rows each ([F*S, D] view)."""
+def frame_sums(rows, num_frames, tokens_per_frame, row0=0, video_start=0):
+    """fp32 [F, D] per-frame column sums of the video rows found in `rows`.
+
+    rows[0] is packed row `row0`; frame f spans packed rows [video_start + f*S, ... + S).
+    A shard that holds part of a frame contributes its part (sum the shards' results)."""
+    F_, S = num_frames, tokens_per_frame
     if not rows.is_cuda:
-        return rows.float().view(num_frames, tokens_per_frame, -1).sum(1)
-    out = torch.empty(num_frames, rows.shape[1], dtype=torch.float32, device=rows.device)
-    ext().frame_sums(rows, int(num_frames), int(tokens_per_frame), out)
+        out = torch.zeros(F_, rows.shape[1], dtype=torch.float32)
+        for f in range(F_):
+            a = max(video_start + f * S, row0) - row0
+            b = min(video_start + (f + 1) * S, row0 + rows.shape[0]) - row0
+            if b > a:
+                out[f] = rows[a:b].float().sum(0)
+        return out
+    out = torch.empty(F_, rows.shape[1], dtype=torch.float32, device=rows.device)
+    ext().frame_sums(rows, int(row0), int(video_start), int(F_), int(S), out)
     return out
 
 
