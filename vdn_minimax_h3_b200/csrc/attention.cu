@@ -18,7 +18,7 @@
 //               is rescaled only when the running max grows by more than 2^8), P written as
 //               bf16 into the 128B-swizzled shared operand, epilogue O / l * sigmoid(gate).
 //               While one tile's softmax runs, the tensor core works on the other tile.
-//               A quarter of the exponentials run as a cubic polynomial on the FMA pipe
+//               A fraction of the exponentials run as a cubic polynomial on the FMA pipe
 //               (2^x = 2^n * p(f), Cody-Waite split, p fitted for minimax relative error
 //               8.6e-5 on [0,1)) so the MUFU unit is not the bottleneck.
 // TMEM (512 columns): S[tile][buf] at (2*tile + buf) * 64, O[tile] at 256 + 128 * tile.
@@ -42,6 +42,9 @@ constexpr int AT_P_BYTES = AT_BM * AT_BN * 2;      // 16 KB per P tile (1 atom c
 constexpr int AT_THREADS = 320;
 constexpr int AT_SMEM = 2 * AT_Q_BYTES + 2 * AT_STAGES * AT_KV_BYTES + 2 * AT_P_BYTES + 1024 + 512;
 constexpr int AT_MAX_RANGES = 4;
+// One exponential in every 8 * POLY_EVERY runs on the FMA pipe (0: all on MUFU); the
+// launcher picks the instance (attention_set_poly_every, default 2).
+static int g_poly_every = 2;
 
 struct AttnParams {
   const int* tiles;          // [n_items_per_head, 4] (q0, q_end, segment, kv_len), q_end-q0 <= 256
@@ -102,6 +105,7 @@ __device__ __forceinline__ void item_coords(const AttnParams& p, int item, int& 
   tile = item - head * p.n_tiles;
 }
 
+template <int AT_POLY_EVERY>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                             const __grid_constant__ CUtensorMap tmK,
@@ -365,13 +369,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         tc_fence_before();
         mbar_arrive(&s_empty[qt * 2 + b]);
+        // Row max on the raw scores (8 independent chains), masking only a ragged block.
         const int valid = w.valid();
-        float mx = -INFINITY;
+        if (valid < AT_BN) {
 #pragma unroll
-        for (int c = 0; c < AT_BN; ++c) {
-          s[c] = c < valid ? s[c] * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[c]);
+          for (int c = 0; c < AT_BN; ++c) s[c] = c < valid ? s[c] : -INFINITY;
         }
+        float mxv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mxv[i] = s[i];
+#pragma unroll
+        for (int c = 8; c < AT_BN; c += 8)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mxv[i] = fmaxf(mxv[i], s[c + i]);
+        const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
+                               fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * p.scale_log2;
         const float m_new = fmaxf(m_ref, mx);
         const bool need = m_new > m_ref + 8.0f;
         const bool warp_need = __any_sync(0xffffffffu, need);
@@ -401,21 +413,23 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           }
           tmem_wait_st();
         }
-        const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;
-        float sum = 0.f;
+        // p = 2^(s * scale_log2 - m): one FFMA per score, exp on MUFU (a fraction on FMA).
+        const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < AT_BN; c += 8) {
           float e[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float x = s[c + i] - mref;
-            e[i] = (i & 3) == 3 ? ex2_poly(x) : ex2(x);
-            sum += e[i];
+            const float x = fmaf(s[c + i], p.scale_log2, neg_m);
+            e[i] = (AT_POLY_EVERY > 0 && (i % 8) == 7 && ((c / 8) % AT_POLY_EVERY) == 0) ? ex2_poly(x) : ex2(x);
+            sums[i] += e[i];
           }
           const uint4 pk = make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]),
                                       pack_bf16(e[4], e[5]), pack_bf16(e[6], e[7]));
           *reinterpret_cast<uint4*>(prow + (((c >> 3) ^ (r & 7)) << 4)) = pk;
         }
+        const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
         l += sum;
         fence_proxy_async_smem();
         tc_fence_before();
@@ -464,8 +478,10 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
   if (n_tiles == 0 || H == 0) return;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(window_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         AT_SMEM);
+    cudaFuncSetAttribute(window_attention_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
+    cudaFuncSetAttribute(window_attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
+    cudaFuncSetAttribute(window_attention_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
+    cudaFuncSetAttribute(window_attention_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
     attr = true;
   }
   const uint64_t cols = (uint64_t)H * AT_D;
@@ -486,7 +502,14 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
   p.err = err;
   const int items = n_tiles * H;
   const int grid = items < num_sms() ? items : num_sms();
-  window_attention_kernel<<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p);
+  switch (g_poly_every) {
+    case 0: window_attention_kernel<0><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
+    case 1: window_attention_kernel<1><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
+    case 4: window_attention_kernel<4><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
+    default: window_attention_kernel<2><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
+  }
 }
+
+void attention_set_poly_every(int n) { g_poly_every = n; }
 
 }  // namespace vdn

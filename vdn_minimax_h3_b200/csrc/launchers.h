@@ -32,6 +32,7 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              const int* kv, const void* gate, int64_t ldg, void* out,
                              int64_t ldo, float scale, int* err, cudaStream_t stream);
 
+void attention_set_poly_every(int n);
 void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, int64_t ldo, int l2,
                         cudaStream_t stream);
 void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,

@@ -59,7 +59,10 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
     T = layout.seq_len
     q = torch.randn(T, H, d, device="cuda", dtype=torch.bfloat16)
     k, v = torch.randn_like(q), torch.randn_like(q)
-    ms = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
     fl = plan.flops(H, d)
-    print(json.dumps(dict(case="window_attention_c1_both", T=T, ms=ms,
-                          tflops=fl / ms / 1e9)), flush=True)
+    for pe in (0, 1, 2, 4):
+        ext().attention_set_poly_every(pe)
+        ms = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
+        print(json.dumps(dict(case="window_attention_c1_both", T=T, heads=H, poly_every=pe, ms=ms,
+                              tflops=fl / ms / 1e9)), flush=True)
+    ext().attention_set_poly_every(2)
