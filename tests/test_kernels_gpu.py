@@ -12,7 +12,7 @@ pytestmark = pytest.mark.gpu
 
 
 def _rel(a, b):
-    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+    return ((a.float().cpu() - b.float().cpu()).norm() / b.float().cpu().norm().clamp_min(1e-12)).item()
 
 
 @pytest.mark.parametrize("T,D", [(300, 256), (1000, 5376), (77, 1024)])

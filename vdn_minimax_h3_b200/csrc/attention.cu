@@ -3,16 +3,18 @@
 // One work item = (head, 256 query rows) of one plan segment, processed as TWO 128-row
 // tiles that share every K/V block. The segment's kept K/V rows are at most four CONTIGUOUS
 // row ranges of the packed sequence (globals, the window frames, the anchor frames;
-// models/window.py: AttentionPlan); the kernel walks them in 64-key blocks straight out of
+// models/window.py: AttentionPlan); the kernel walks them in 128-key blocks straight out of
 // the [T, H, d] projections -- no gather, no mask tensor; only the ragged tail of a range
 // is masked.
 //
 // Roles (320 threads, one CTA per SM, persistent over head-major work items so the CTAs in
 // flight share one head's K/V in L2):
-//   warp 0      TMA producer: both Q tiles once per item, K/V blocks into a 3-stage ring.
-//   warp 1      MMA issuer (one thread): per block, S_t = Q_t K^T for both tiles into
-//               double-buffered TMEM S (kind::f16, M=128, N=64), then O_t += P_t V for
-//               the previous block (P from shared memory, V as an MN-major operand).
+//   warp 0      TMA producers: lane 0 both Q tiles once per item and K blocks into a
+//               2-stage ring, lane 1 V blocks (single buffer, refilled while the softmax
+//               of the block runs).
+//   warp 1      MMA issuer (one thread): per block, S_t = Q_t K^T for both tiles into TMEM
+//               (kind::f16, M=128, N=128), then O_t += P_t V for the previous block (P from
+//               shared memory, V as an MN-major operand).
 //   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1 (thread = query row): S row
 //               from TMEM, online softmax in the exp2 domain with a lazy rescale (O in TMEM
 //               is rescaled only when the running max grows by more than 2^8), P written as
@@ -21,7 +23,8 @@
 //               A fraction of the exponentials run as a cubic polynomial on the FMA pipe
 //               (2^x = 2^n * p(f), Cody-Waite split, p fitted for minimax relative error
 //               8.6e-5 on [0,1)) so the MUFU unit is not the bottleneck.
-// TMEM (512 columns): S[tile][buf] at (2*tile + buf) * 64, O[tile] at 256 + 128 * tile.
+// TMEM (512 columns): S[tile] at 128 * tile, O[tile] at 256 + 128 * tile. The softmax warps
+// copy S to registers first thing, so the next block's S MMA can start while they work.
 //
 // Every wait is bounded; a protocol failure unwinds, drains and frees TMEM (common.cuh).
 // Reference parity: the window softmax of src/models/softmax_attention/ (decomposed.py's
@@ -33,14 +36,14 @@
 namespace vdn {
 
 constexpr int AT_BM = 128;                         // query rows per tile (2 tiles per item)
-constexpr int AT_BN = 64;                          // keys per block
+constexpr int AT_BN = 128;                         // keys per block
 constexpr int AT_D = 128;                          // head dim
-constexpr int AT_STAGES = 3;
+constexpr int AT_KSTAGES = 2;                      // K ring; V is single-buffered
 constexpr int AT_Q_BYTES = AT_BM * AT_D * 2;       // 32 KB per Q tile (2 atoms of 16 KB)
-constexpr int AT_KV_BYTES = AT_BN * AT_D * 2;      // 16 KB per K or V block (2 atoms of 8 KB)
-constexpr int AT_P_BYTES = AT_BM * AT_BN * 2;      // 16 KB per P tile (1 atom column)
+constexpr int AT_KV_BYTES = AT_BN * AT_D * 2;      // 32 KB per K or V block (2 atoms of 16 KB)
+constexpr int AT_P_BYTES = AT_BM * AT_BN * 2;      // 32 KB per P tile (2 atom columns)
 constexpr int AT_THREADS = 320;
-constexpr int AT_SMEM = 2 * AT_Q_BYTES + 2 * AT_STAGES * AT_KV_BYTES + 2 * AT_P_BYTES + 1024 + 512;
+constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + 1) * AT_KV_BYTES + 2 * AT_P_BYTES + 1024 + 384;
 constexpr int AT_MAX_RANGES = 4;
 // One exponential in every 8 * POLY_EVERY runs on the FMA pipe (0: all on MUFU); the
 // launcher picks the instance (attention_set_poly_every, default 2).
@@ -113,24 +116,24 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                   // [2][32 KB]
-  uint8_t* sK = sQ + 2 * AT_Q_BYTES;                    // [3][16 KB]
-  uint8_t* sV = sK + AT_STAGES * AT_KV_BYTES;           // [3][16 KB]
-  uint8_t* sP = sV + AT_STAGES * AT_KV_BYTES;           // [2][16 KB]
+  uint8_t* sQ = smem;                                   // [2 tiles][32 KB]
+  uint8_t* sK = sQ + 2 * AT_Q_BYTES;                    // [2 stages][32 KB]
+  uint8_t* sV = sK + AT_KSTAGES * AT_KV_BYTES;          // [32 KB]
+  uint8_t* sP = sV + AT_KV_BYTES;                       // [2 tiles][32 KB]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * AT_P_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;             // [3]
-  uint64_t* k_empty = bars + 5;            // [3]
-  uint64_t* v_full = bars + 8;             // [3]
-  uint64_t* v_empty = bars + 11;           // [3]
-  uint64_t* s_full = bars + 14;            // [tile*2 + buf]
-  uint64_t* s_empty = bars + 18;           // [tile*2 + buf]
-  uint64_t* p_full = bars + 22;            // [tile]
-  uint64_t* pv_done = bars + 24;           // [tile]
-  uint64_t* o_empty = bars + 26;           // [tile]
-  uint64_t* mma_done = bars + 28;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 29);
+  uint64_t* k_full = bars + 2;             // [2]
+  uint64_t* k_empty = bars + 4;            // [2]
+  uint64_t* v_full = bars + 6;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 8;             // [tile]
+  uint64_t* s_empty = bars + 10;           // [tile]
+  uint64_t* p_full = bars + 12;            // [tile]
+  uint64_t* pv_done = bars + 14;           // [tile]
+  uint64_t* o_empty = bars + 16;           // [tile]
+  uint64_t* mma_done = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -139,17 +142,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int s = 0; s < AT_STAGES; ++s) {
+    for (int s = 0; s < AT_KSTAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
-    }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
     for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 128);
       mbar_init(&p_full[t], 128);
       mbar_init(&pv_done[t], 1);
       mbar_init(&o_empty[t], 128);
@@ -168,17 +169,16 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+    // --------------------------------------------- TMA producers: lane 0 Q + K, lane 1 V
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      int last_phase[2 * AT_STAGES + 1];
-      for (int i = 0; i < 2 * AT_STAGES + 1; ++i) last_phase[i] = -1;
+      int last_phase[AT_KSTAGES + 1];
+      for (int i = 0; i < AT_KSTAGES + 1; ++i) last_phase[i] = -1;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++local) {
         int head, tile;
         item_coords(p, item, head, tile);
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           ok = false;
           break;
         }
-        last_phase[2 * AT_STAGES] = local & 1;
+        last_phase[AT_KSTAGES] = local & 1;
         mbar_arrive_expect_tx(q_full, 2 * AT_Q_BYTES);
 #pragma unroll
         for (int qt = 0; qt < 2; ++qt) {
@@ -207,30 +207,47 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           mbar_arrive_expect_tx(&k_full[stage], AT_KV_BYTES);
           tma_load_2d(k, &tmK, &k_full[stage], head * AT_D, w.start());
           tma_load_2d(k + AT_KV_BYTES / 2, &tmK, &k_full[stage], head * AT_D + 64, w.start());
-          if (!mbar_wait(&v_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          uint8_t* v = sV + stage * AT_KV_BYTES;
-          last_phase[AT_STAGES + stage] = (int)phase;
-          mbar_arrive_expect_tx(&v_full[stage], AT_KV_BYTES);
-          tma_load_2d(v, &tmV, &v_full[stage], head * AT_D, w.start());
-          tma_load_2d(v + AT_KV_BYTES / 2, &tmV, &v_full[stage], head * AT_D + 64, w.start());
-          if (++stage == AT_STAGES) {
+          if (++stage == AT_KSTAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
       if (!ok || *abort_flag) {
-        // let every copy this thread issued land before the CTA exits
         long long t0 = clock64();
-        for (int i = 0; i < 2 * AT_STAGES + 1; ++i) {
-          uint64_t* bar = i < AT_STAGES ? &k_full[i]
-                                        : (i < 2 * AT_STAGES ? &v_full[i - AT_STAGES] : q_full);
+        for (int i = 0; i < AT_KSTAGES + 1; ++i) {
+          uint64_t* bar = i < AT_KSTAGES ? &k_full[i] : q_full;
           if (last_phase[i] < 0) continue;
           while (!mbar_try_wait(bar, (uint32_t)last_phase[i]) && clock64() - t0 < kWaitBudgetCycles) {
           }
+        }
+      }
+    } else if (lane == 1) {
+      tma_prefetch_desc(&tmV);
+      uint32_t phase = 0;
+      int last = -1;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        int head, tile;
+        item_coords(p, item, head, tile);
+        const int* t = p.tiles + 4 * tile;
+        KvWalk w;
+        w.init(p.kv + 8 * t[2]);
+        for (; !w.done(); w.next()) {
+          if (!mbar_wait(v_empty, phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          last = (int)phase;
+          mbar_arrive_expect_tx(v_full, AT_KV_BYTES);
+          tma_load_2d(sV, &tmV, v_full, head * AT_D, w.start());
+          tma_load_2d(sV + AT_KV_BYTES / 2, &tmV, v_full, head * AT_D + 64, w.start());
+          phase ^= 1;
+        }
+      }
+      if ((!ok || *abort_flag) && last >= 0) {
+        long long t0 = clock64();
+        while (!mbar_try_wait(v_full, (uint32_t)last) && clock64() - t0 < kWaitBudgetCycles) {
         }
       }
     }
@@ -239,10 +256,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(AT_BM, AT_BN, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(AT_BM, AT_D, false, true);
-      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP), aV = smem_u32(sV);
       int stage = 0;
-      uint32_t phase = 0;
-      uint32_t g = 0;  // global block counter (S buffer = g & 1)
+      uint32_t phase = 0, vphase = 0;
+      uint32_t g = 0;  // global block counter: S_t / P_t / PV_t phases are g & 1
       int local = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++local) {
@@ -254,44 +271,39 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         int j = 0;
-        int prev_stage = 0;
-        uint32_t prev_phase = 0, g_prev = 0;
+        uint32_t g_prev = 0;
         while (true) {
           const bool have = !w.done();
           if (have) {
-            const uint32_t b = g & 1;
             if (!mbar_wait(&k_full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
               ok = false;
               break;
             }
             const uint32_t aK = smem_u32(sK + stage * AT_KV_BYTES);
             for (int qt = 0; qt < 2 && ok; ++qt) {
-              if (!mbar_wait(&s_empty[qt * 2 + b], ((g >> 1) & 1) ^ 1, abort_flag, p.err,
-                             kErrTimeoutMma)) {
+              // S_t is free once the softmax warps copied the previous S_t to registers
+              if (!mbar_wait(&s_empty[qt], (g & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint32_t tS = tmem + (qt * 2 + b) * AT_BN;
 #pragma unroll
               for (int k = 0; k < AT_D / 16; ++k) {
-                const uint32_t offQ = qt * AT_Q_BYTES + (k >> 2) * (AT_Q_BYTES / 2) + (k & 3) * 32;
-                const uint32_t offK = (k >> 2) * (AT_KV_BYTES / 2) + (k & 3) * 32;
-                umma_f16_ss(tS, umma_desc_kmajor_sw128(aQ + offQ),
-                            umma_desc_kmajor_sw128(aK + offK), idesc_s, k != 0);
+                const uint32_t off = (k >> 2) * (AT_Q_BYTES / 2) + (k & 3) * 32;
+                umma_f16_ss(tmem + qt * AT_BN, umma_desc_kmajor_sw128(aQ + qt * AT_Q_BYTES + off),
+                            umma_desc_kmajor_sw128(aK + off), idesc_s, k != 0);
               }
-              umma_commit(&s_full[qt * 2 + b]);
+              umma_commit(&s_full[qt]);
             }
             if (!ok) break;
             umma_commit(&k_empty[stage]);
           }
           if (j > 0) {
             // O_t += P_t V for the previous block
-            if (!mbar_wait(&v_full[prev_stage], prev_phase, abort_flag, p.err, kErrTimeoutMma)) {
+            if (!mbar_wait(v_full, vphase, abort_flag, p.err, kErrTimeoutMma)) {
               ok = false;
               break;
             }
-            const uint32_t aV = smem_u32(sV + prev_stage * AT_KV_BYTES);
             for (int qt = 0; qt < 2 && ok; ++qt) {
               if (!mbar_wait(&p_full[qt], g_prev & 1, abort_flag, p.err, kErrTimeoutMma) ||
                   (j == 1 && local > 0 &&
@@ -300,23 +312,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 break;
               }
               tc_fence_after();
-              const uint32_t tO = tmem + 256 + qt * 128;
 #pragma unroll
               for (int k = 0; k < AT_BN / 16; ++k) {
-                umma_f16_ss(tO, umma_desc_kmajor_sw128(aP + qt * AT_P_BYTES + k * 32),
+                const uint32_t offP = (k >> 2) * (AT_P_BYTES / 2) + (k & 3) * 32;
+                umma_f16_ss(tmem + 256 + qt * 128, umma_desc_kmajor_sw128(aP + qt * AT_P_BYTES + offP),
                             umma_desc_mnmajor_sw128(aV + k * 2048, AT_KV_BYTES / 2), idesc_o,
                             (j > 1 || k > 0) ? 1u : 0u);
               }
               umma_commit(&pv_done[qt]);
             }
             if (!ok) break;
-            umma_commit(&v_empty[prev_stage]);
+            umma_commit(v_empty);
+            vphase ^= 1;
           }
           if (!have) break;
-          prev_stage = stage;
-          prev_phase = phase;
           g_prev = g;
-          if (++stage == AT_STAGES) {
+          if (++stage == AT_KSTAGES) {
             stage = 0;
             phase ^= 1;
           }
@@ -338,6 +349,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;        // row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_off + qt * AT_BN;
     const uint32_t tO = tmem + lane_off + 256 + qt * 128;
     uint8_t* prow = sP + qt * AT_P_BYTES + r * 128;
     uint32_t g = 0;
@@ -352,8 +364,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       int j = 0;
       bool ok = true;
       for (; !w.done(); w.next(), ++j, ++g) {
-        const uint32_t b = g & 1;
-        if (!mbar_wait(&s_full[qt * 2 + b], (g >> 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+        if (!mbar_wait(&s_full[qt], g & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
           ok = false;
           break;
         }
@@ -362,14 +373,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < AT_BN; c += 32) {
           uint32_t u[32];
-          tmem_ld32(tmem + lane_off + (qt * 2 + b) * AT_BN + c, u);
-          tmem_wait_ld();
+          tmem_ld32(tS + c, u);
 #pragma unroll
           for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(u[i]);
         }
+        tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&s_empty[qt * 2 + b]);
-        // Row max on the raw scores (8 independent chains), masking only a ragged block.
+        mbar_arrive(&s_empty[qt]);
+        // row max on the raw scores (8 independent chains); only a ragged block is masked
         const int valid = w.valid();
         if (valid < AT_BN) {
 #pragma unroll
@@ -387,56 +398,62 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         const float m_new = fmaxf(m_ref, mx);
         const bool need = m_new > m_ref + 8.0f;
         const bool warp_need = __any_sync(0xffffffffu, need);
-        // PV of the previous block must finish before O or the P buffer is touched.
-        if (j > 0) {
-          if (!mbar_wait(&pv_done[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-        }
         float factor = 1.f;
         if (need) {
           factor = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - m_new);
           m_ref = m_new;
           l *= factor;
         }
-        if (warp_need && j > 0) {
-#pragma unroll 1
-          for (int c = 0; c < AT_D; c += 32) {
-            uint32_t u[32];
-            tmem_ld32(tO + c, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
-            tmem_st32(tO + c, u);
-          }
-          tmem_wait_st();
-        }
-        // p = 2^(s * scale_log2 - m): one FFMA per score, exp on MUFU (a fraction on FMA).
+        // p = 2^(s * scale_log2 - m) into packed bf16 registers (the exps overlap the
+        // previous block's P.V on the tensor core)
         const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
         float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[AT_BN / 2];
 #pragma unroll
         for (int c = 0; c < AT_BN; c += 8) {
           float e[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float x = fmaf(s[c + i], p.scale_log2, neg_m);
-            e[i] = (AT_POLY_EVERY > 0 && (i % 8) == 7 && ((c / 8) % AT_POLY_EVERY) == 0) ? ex2_poly(x) : ex2(x);
+            e[i] = (AT_POLY_EVERY > 0 && i == 7 && ((c / 8) % AT_POLY_EVERY) == 0) ? ex2_poly(x) : ex2(x);
             sums[i] += e[i];
           }
-          const uint4 pk = make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]),
-                                      pack_bf16(e[4], e[5]), pack_bf16(e[6], e[7]));
-          *reinterpret_cast<uint4*>(prow + (((c >> 3) ^ (r & 7)) << 4)) = pk;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) pk[c / 2 + i] = pack_bf16(e[2 * i], e[2 * i + 1]);
         }
-        const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
-        l += sum;
+        l += ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
+        // P.V of the previous block must finish before O or the P buffer is touched.
+        if (j > 0) {
+          if (!mbar_wait(&pv_done[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (warp_need) {
+#pragma unroll 1
+            for (int c = 0; c < AT_D; c += 32) {
+              uint32_t u[32];
+              tmem_ld32(tO + c, u);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
+              tmem_st32(tO + c, u);
+            }
+            tmem_wait_st();
+          }
+        }
+#pragma unroll
+        for (int c8 = 0; c8 < AT_BN / 8; ++c8) {
+          const int atom = c8 >> 3, jj = c8 & 7;
+          *reinterpret_cast<uint4*>(prow + atom * (AT_P_BYTES / 2) + ((jj ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+        }
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&p_full[qt]);
       }
       if (!ok) break;
-      // Epilogue: wait for the last PV, O / l * gate -> bf16.
+      // Epilogue: wait for the last P.V, O / l * gate -> bf16.
       if (!mbar_wait(&pv_done[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
       tc_fence_after();
       const int row = t[0] + qt * AT_BM + r;
@@ -449,13 +466,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tmem_ld32(tO + c, u);
         tmem_wait_ld();
         if (row_ok) {
-          uint32_t pk[16];
+          uint32_t o[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            pk[i] = pack_bf16(__uint_as_float(u[2 * i]) * gscale, __uint_as_float(u[2 * i + 1]) * gscale);
+            o[i] = pack_bf16(__uint_as_float(u[2 * i]) * gscale, __uint_as_float(u[2 * i + 1]) * gscale);
           uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t)row * p.ldo + head * AT_D + c);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          for (int q = 0; q < 4; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
         }
       }
       tc_fence_before();

@@ -51,25 +51,21 @@ void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, in
 }
 
 // --------------------------------------------------------------- separable short conv
-// Block = one grid row of one head for a chunk of LB_FC frames. Per frame, the 5 grid rows
-// around it (2-row halo each side) are staged in shared memory once; warp w computes
-// positions {w, w+14, w+28} of the row, lane = 4 channels. The last five spatial results
-// per output live in a register shift ring, so each input frame is read from global memory
-// (L2) five times in total instead of 25 times per output.
+// Block = (grid row y, head h, chunk of LB_FC frames); warp w owns positions 4w..4w+3 of the
+// row, lane owns 4 channels, so a warp covers the head's 128 channels and the L2 norm is a
+// warp reduction. Per frame and tap row, one 8-position input window (8 loads) feeds all
+// 20 (position, tap) products of the row; the five latest spatial results per output sit
+// in a register ring for the temporal taps. Frames are chunked (2-frame halo each side).
 constexpr int LB_FC = 16;
-constexpr int LB_WARPS = 14;
-constexpr int LB_PPW = 3;           // positions per warp (grid width <= 42)
-constexpr int LB_MAXW = LB_WARPS * LB_PPW;
+constexpr int LB_PPW = 4;                 // positions per warp
+constexpr int LB_MAXW = 48;               // widest supported grid row
 
-__global__ void __launch_bounds__(LB_WARPS * 32) lb_conv_kernel(
+__global__ void __launch_bounds__(384) lb_conv_kernel(
     const __nv_bfloat16* __restrict__ in, int64_t ldi, const float* __restrict__ wsp,
     const float* __restrict__ wtm, __nv_bfloat16* __restrict__ out, int64_t ldo, int F, int gh,
     int gw, int H, int l2) {
-  __shared__ float s_wsp[25][128];
-  __shared__ float s_wtm[5][128];
-  // rows y-2..y+2, cols -2..gw+1 of the frame (dynamic shared memory)
-  extern __shared__ __align__(16) uint8_t lb_conv_dyn[];
-  auto s_in = reinterpret_cast<__nv_bfloat16 (*)[LB_MAXW + 4][128]>(lb_conv_dyn);
+  __shared__ __align__(16) float s_wsp[25][128];
+  __shared__ __align__(16) float s_wtm[5][128];
   const int y = blockIdx.x, h = blockIdx.y;
   const int f0 = blockIdx.z * LB_FC;
   const int S = gh * gw;
@@ -82,14 +78,11 @@ __global__ void __launch_bounds__(LB_WARPS * 32) lb_conv_kernel(
     const int tap = i / 128, c = i % 128;
     s_wtm[tap][c] = wtm[(int64_t)(h * 128 + c) * 5 + tap];
   }
-  // zero the padded border columns once (they stay zero)
-  for (int i = tid; i < 5 * 4 * 16; i += blockDim.x) {
-    const int r = i / 64, rest = i % 64, side = rest / 32, c8 = rest % 16, half = (rest / 16) & 1;
-    const int col = side == 0 ? half : gw + 2 + half;
-    reinterpret_cast<uint4*>(&s_in[r][col][0])[c8] = make_uint4(0, 0, 0, 0);
-  }
+  __syncthreads();
+  const int x0 = warp * LB_PPW;
+  if (x0 >= gw) return;
   const int c0 = lane * 4;
-  const int64_t chan = (int64_t)h * 128;
+  const int64_t chan = (int64_t)h * 128 + c0;
   float ring[5][LB_PPW][4];
 #pragma unroll
   for (int a = 0; a < 5; ++a)
@@ -97,44 +90,50 @@ __global__ void __launch_bounds__(LB_WARPS * 32) lb_conv_kernel(
     for (int q = 0; q < LB_PPW; ++q)
 #pragma unroll
       for (int b = 0; b < 4; ++b) ring[a][q][b] = 0.f;
+  const float4 t0 = *reinterpret_cast<const float4*>(&s_wtm[0][c0]);
+  const float4 t1 = *reinterpret_cast<const float4*>(&s_wtm[1][c0]);
+  const float4 t2 = *reinterpret_cast<const float4*>(&s_wtm[2][c0]);
+  const float4 t3 = *reinterpret_cast<const float4*>(&s_wtm[3][c0]);
+  const float4 t4 = *reinterpret_cast<const float4*>(&s_wtm[4][c0]);
+  const float tw[5][4] = {{t0.x, t0.y, t0.z, t0.w}, {t1.x, t1.y, t1.z, t1.w},
+                          {t2.x, t2.y, t2.z, t2.w}, {t3.x, t3.y, t3.z, t3.w},
+                          {t4.x, t4.y, t4.z, t4.w}};
   const int f_end = min(F, f0 + LB_FC);
   for (int f = f0 - 2; f < f_end + 2; ++f) {
-    const bool live = f >= 0 && f < F;
-    __syncthreads();   // previous frame's smem reads are done
-    if (live) {
-      // stage rows y-2..y+2 of frame f, 16 bytes per thread-iteration
-      const int per_row = gw * 16;
-      for (int i = tid; i < 5 * per_row; i += blockDim.x) {
-        const int r = i / per_row, rem = i % per_row, x = rem / 16, c8 = rem % 16;
-        const int yy = y + r - 2;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (yy >= 0 && yy < gh)
-          v = *reinterpret_cast<const uint4*>(in + ((int64_t)f * S + yy * gw + x) * ldi + chan + c8 * 8);
-        reinterpret_cast<uint4*>(&s_in[r][x + 2][0])[c8] = v;
-      }
-    }
-    __syncthreads();
     float sp[LB_PPW][4];
 #pragma unroll
     for (int q = 0; q < LB_PPW; ++q)
 #pragma unroll
       for (int b = 0; b < 4; ++b) sp[q][b] = 0.f;
-    if (live) {
+    if (f >= 0 && f < F) {
 #pragma unroll
       for (int i = 0; i < 5; ++i) {
+        const int yy = y + i - 2;
+        if (yy < 0 || yy >= gh) continue;
+        const __nv_bfloat16* rowp = in + ((int64_t)f * S + (int64_t)yy * gw) * ldi + chan;
+        float win[LB_PPW + 4][4];
+#pragma unroll
+        for (int u = 0; u < LB_PPW + 4; ++u) {
+          const int xx = x0 + u - 2;
+          if (xx >= 0 && xx < gw) {
+            const uint2 v = *reinterpret_cast<const uint2*>(rowp + (int64_t)xx * ldi);
+            win[u][0] = bf16_lo(v.x);
+            win[u][1] = bf16_hi(v.x);
+            win[u][2] = bf16_lo(v.y);
+            win[u][3] = bf16_hi(v.y);
+          } else {
+            win[u][0] = win[u][1] = win[u][2] = win[u][3] = 0.f;
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 5; ++j) {
           const float4 w = *reinterpret_cast<const float4*>(&s_wsp[i * 5 + j][c0]);
 #pragma unroll
           for (int q = 0; q < LB_PPW; ++q) {
-            const int x = warp + q * LB_WARPS;
-            if (x < gw) {
-              const uint2 v = *reinterpret_cast<const uint2*>(&s_in[i][x + j][c0]);
-              sp[q][0] += w.x * bf16_lo(v.x);
-              sp[q][1] += w.y * bf16_hi(v.x);
-              sp[q][2] += w.z * bf16_lo(v.y);
-              sp[q][3] += w.w * bf16_hi(v.y);
-            }
+            sp[q][0] = fmaf(w.x, win[q + j][0], sp[q][0]);
+            sp[q][1] = fmaf(w.y, win[q + j][1], sp[q][1]);
+            sp[q][2] = fmaf(w.z, win[q + j][2], sp[q][2]);
+            sp[q][3] = fmaf(w.w, win[q + j][3], sp[q][3]);
           }
         }
       }
@@ -151,23 +150,15 @@ __global__ void __launch_bounds__(LB_WARPS * 32) lb_conv_kernel(
       }
     const int fo = f - 2;
     if (fo < f0) continue;
-    const float4 t0 = *reinterpret_cast<const float4*>(&s_wtm[0][c0]);
-    const float4 t1 = *reinterpret_cast<const float4*>(&s_wtm[1][c0]);
-    const float4 t2 = *reinterpret_cast<const float4*>(&s_wtm[2][c0]);
-    const float4 t3 = *reinterpret_cast<const float4*>(&s_wtm[3][c0]);
-    const float4 t4 = *reinterpret_cast<const float4*>(&s_wtm[4][c0]);
-    const float tw[5][4] = {{t0.x, t0.y, t0.z, t0.w}, {t1.x, t1.y, t1.z, t1.w},
-                            {t2.x, t2.y, t2.z, t2.w}, {t3.x, t3.y, t3.z, t3.w},
-                            {t4.x, t4.y, t4.z, t4.w}};
 #pragma unroll
     for (int q = 0; q < LB_PPW; ++q) {
-      const int x = warp + q * LB_WARPS;
+      const int x = x0 + q;
       float o[4];
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
         float t = 0.f;
 #pragma unroll
-        for (int dt = 0; dt < 5; ++dt) t += tw[dt][b] * ring[dt][q][b];
+        for (int dt = 0; dt < 5; ++dt) t = fmaf(tw[dt][b], ring[dt][q][b], t);
         o[b] = siluf_(t);
       }
       if (l2) {
@@ -177,7 +168,7 @@ __global__ void __launch_bounds__(LB_WARPS * 32) lb_conv_kernel(
         for (int b = 0; b < 4; ++b) o[b] *= inv;
       }
       if (x < gw)
-        *reinterpret_cast<uint2*>(out + ((int64_t)fo * S + y * gw + x) * ldo + chan + c0) =
+        *reinterpret_cast<uint2*>(out + ((int64_t)fo * S + (int64_t)y * gw + x) * ldo + chan) =
             make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
     }
   }
@@ -186,15 +177,10 @@ __global__ void __launch_bounds__(LB_WARPS * 32) lb_conv_kernel(
 void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,
                     int64_t ldo, int F, int gh, int gw, int H, int l2, cudaStream_t stream) {
   if (!F || !gh || !gw) return;
-  if (gw > LB_MAXW) throw std::runtime_error("short conv: grid width above 42 is not supported");
+  if (gw > LB_MAXW) throw std::runtime_error("short conv: grid width above 48 is not supported");
+  const int warps = (gw + LB_PPW - 1) / LB_PPW;
   dim3 grid(gh, H, (F + LB_FC - 1) / LB_FC);
-  constexpr int smem = 5 * (LB_MAXW + 4) * 128 * 2;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(lb_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
-  lb_conv_kernel<<<grid, LB_WARPS * 32, smem, stream>>>(
+  lb_conv_kernel<<<grid, warps * 32, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(in), ldi, wsp, wtm,
       reinterpret_cast<__nv_bfloat16*>(out), ldo, F, gh, gw, H, l2);
 }
