@@ -1,0 +1,58 @@
+"""Multi-GPU render entry point (one process per GPU, Ulysses sequence parallel).
+
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m vdn_minimax_h3_b200.inference.infer_ulysses \
+        --config configs/inference/8nfe_ulysses_b200.yaml render.prompt_file=... render.out=...
+
+init NCCL -> assemble on every rank -> UlyssesEngine -> barrier -> warm-up -> timed render
+(device-synchronised, max over ranks) -> rank-0 decode + save -> timing line.
+Reference parity: src/inference/infer_ulysses.py:43-184.
+"""
+import datetime
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+from vdn_minimax_h3_b200.config import load_config
+from vdn_minimax_h3_b200.config.schemas import (InferenceConfig, validate_ablation, validate_kernels,
+                                                validate_parallel)
+
+
+def main(argv=None):
+    t_start = time.perf_counter()
+    cfg = load_config(InferenceConfig, argv, (validate_kernels, validate_ablation, validate_parallel))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    from vdn_minimax_h3_b200.inference.infer import assemble, render
+    from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
+    model, engine = assemble(cfg, device)
+    runtime = init_ulysses(profile=cfg.parallel.profile)
+    sp = UlyssesEngine(engine, runtime, exchange=cfg.parallel.exchange)
+    runtime.barrier()
+    t_setup = time.perf_counter() - t_start
+    lat, aud, steps, denoise = render(cfg, model, engine, device, runtime=runtime, transformer=sp)
+    d = torch.tensor([denoise], device=device)
+    dist.all_reduce(d, op=dist.ReduceOp.MAX)
+    t_decode = 0.0
+    if dist.get_rank() == 0:
+        from vdn_minimax_h3_b200.inference.vae import decode_and_save
+        t0 = time.perf_counter()
+        decode_and_save(lat, aud, cfg.render.out)
+        t_decode = time.perf_counter() - t0
+    runtime.barrier()
+    if dist.get_rank() == 0:
+        prof = runtime.timer.report() if cfg.parallel.profile else {}
+        print(f"Ulysses timing ({dist.get_world_size()} GPUs): setup {t_setup:.1f}s, denoise "
+              f"{float(d.item()):.2f}s ({cfg.render.num_steps} NFE), decode+encode {t_decode:.1f}s, "
+              f"E2E {time.perf_counter() - t_start:.1f}s" + (f", sections {prof}" if prof else ""),
+              flush=True)
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
