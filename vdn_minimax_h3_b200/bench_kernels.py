@@ -55,11 +55,39 @@ def bench_gemm():
     return rows
 
 
+def profile_small():
+    """Single launches on small inputs, for a one-pass-per-kernel profiler capture."""
+    from vdn_minimax_h3_b200.models.delta_rule import VdnDelta
+    from vdn_minimax_h3_b200.models.layout import SequenceLayout
+    from vdn_minimax_h3_b200.models.window import AttentionPlan, window_bounds
+    from vdn_minimax_h3_b200.ops import attention, linear_branch as lb
+    from vdn_minimax_h3_b200.ops._ext import check_device_error
+    Fr, S, H = 20, 1008, 8
+    lay = SequenceLayout(seq_len=1950 + Fr * S, video_start=1950, num_frames=Fr, tokens_per_frame=S,
+                         frame_height=24, frame_width=42, text_start=0, text_len=800)
+    plan = AttentionPlan(lay, window_bounds(Fr, 1, 5), "both", device="cuda")
+    q = torch.randn(lay.seq_len, H, 128, device="cuda", dtype=torch.bfloat16)
+    attention.window_attention(q, q, q, plan, 128 ** -0.5)
+    A = torch.randn(256, 128, 128, device="cuda") * 0.01
+    A = A @ A.transpose(-1, -2)
+    lb.factor_apply(VdnDelta(S), torch.rand(256, 128, device="cuda"), A.view(16, 16, 128, 128),
+                    torch.randn(16, 16, 128, 128, device="cuda"))
+    x = torch.randn(8 * S, H, 128, device="cuda", dtype=torch.bfloat16)
+    lb.conv_features(x, torch.randn(H * 128, 5, 5, device="cuda"), torch.randn(H * 128, 5, device="cuda"),
+                     8, (24, 42), True)
+    torch.cuda.synchronize()
+    check_device_error()
+    print("profile-small ok", flush=True)
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gemm", action="store_true")
     p.add_argument("--attention", action="store_true")
     p.add_argument("--linear", action="store_true")
+    p.add_argument("--profile-small", action="store_true",
+                   help="one launch each of window attention, SPD inverse and conv features on "
+                        "small inputs (an ncu-sized driver)")
     p.add_argument("--attention-small", action="store_true",
                    help="window attention on 20 frames x 8 heads (an ncu-sized case)")
     p.add_argument("--linear-small", action="store_true",
@@ -73,6 +101,8 @@ def main(argv=None):
     if a.linear:
         from vdn_minimax_h3_b200.ops.linear_branch import bench_linear
         bench_linear(timed)
+    if a.profile_small:
+        profile_small()
     if a.attention_small:
         from vdn_minimax_h3_b200.ops.attention import bench_attention
         bench_attention(timed, frames=20, heads=8)

@@ -46,8 +46,9 @@ constexpr int AT_THREADS = 320;
 constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + 1) * AT_KV_BYTES + 2 * AT_P_BYTES + 1024 + 384;
 constexpr int AT_MAX_RANGES = 4;
 // One exponential in every 8 * POLY_EVERY runs on the FMA pipe (0: all on MUFU); the
-// launcher picks the instance (attention_set_poly_every, default 2).
-static int g_poly_every = 2;
+// launcher picks the instance (attention_set_poly_every, default 0: measured fastest,
+// the kernel is issue-bound rather than MUFU-bound).
+static int g_poly_every = 0;
 
 struct AttnParams {
   const int* tiles;          // [n_items_per_head, 4] (q0, q_end, segment, kv_len), q_end-q0 <= 256

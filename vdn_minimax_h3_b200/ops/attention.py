@@ -65,4 +65,4 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
         ms = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
         print(json.dumps(dict(case="window_attention_c1_both", T=T, heads=H, poly_every=pe, ms=ms,
                               tflops=fl / ms / 1e9)), flush=True)
-    ext().attention_set_poly_every(2)
+    ext().attention_set_poly_every(0)
