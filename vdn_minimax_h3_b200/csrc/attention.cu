@@ -78,26 +78,37 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
 }
 
-// Iterates the 64-key blocks of a segment's K/V ranges.
+// Iterates the 128-key blocks of a segment's K/V ranges (at most four). The ranges are
+// held in scalars and selected with a switch, so nothing is indexed dynamically (no local
+// memory traffic in the per-block loops).
 struct KvWalk {
-  int r[2 * AT_MAX_RANGES];
-  int range, pos;
+  int a0, b0, a1, b1, a2, b2, a3, b3;
+  int range, pos, end;
   __device__ void init(const int* kv_row) {
-#pragma unroll
-    for (int i = 0; i < 2 * AT_MAX_RANGES; ++i) r[i] = kv_row[i];
+    a0 = kv_row[0]; b0 = kv_row[1]; a1 = kv_row[2]; b1 = kv_row[3];
+    a2 = kv_row[4]; b2 = kv_row[5]; a3 = kv_row[6]; b3 = kv_row[7];
     range = 0;
-    pos = r[0];
+    pos = a0;
+    end = b0;
     skip_empty();
   }
+  __device__ void select(int rg) {
+    switch (rg) {
+      case 0: pos = a0; end = b0; break;
+      case 1: pos = a1; end = b1; break;
+      case 2: pos = a2; end = b2; break;
+      default: pos = a3; end = b3; break;
+    }
+  }
   __device__ void skip_empty() {
-    while (range < AT_MAX_RANGES && pos >= r[2 * range + 1]) {
+    while (range < AT_MAX_RANGES && pos >= end) {
       ++range;
-      if (range < AT_MAX_RANGES) pos = r[2 * range];
+      if (range < AT_MAX_RANGES) select(range);
     }
   }
   __device__ bool done() const { return range >= AT_MAX_RANGES; }
   __device__ int start() const { return pos; }
-  __device__ int valid() const { return min(AT_BN, r[2 * range + 1] - pos); }
+  __device__ int valid() const { return min(AT_BN, end - pos); }
   __device__ void next() {
     pos += AT_BN;
     skip_empty();

@@ -402,43 +402,48 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
       m[i][j] = a_scale * 0.5f * (a[r * 128 + c] + a[c * 128 + r]) + (r == c ? 1.f : 0.f);
     }
   }
+  // Step k of Gauss-Jordan as ONE uniform rank-1 update: with c the pivot column, r the
+  // pivot row and p = M[k][k], set c'_k = p - 1 and r'_k = p + 1; then
+  // M -= c' r'^T / p gives the eliminated entries, the scaled pivot row r/p, the column
+  // -c/p and the new pivot 1/p at once -- one FFMA per element, no per-element branches.
   for (int k = 0; k < 128; ++k) {
     const int kb = k >> 3, kk = k & 7;
     if (tj == kb) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float v = m[i][0];
+      for (int c = 0; c < 8; ++c) {
+        if (c == kk) {
 #pragma unroll
-        for (int j = 1; j < 8; ++j) v = (j == kk) ? m[i][j] : v;
-        colk[ti * 8 + i] = v;
+          for (int i = 0; i < 8; ++i) colk[ti * 8 + i] = m[i][c];
+        }
       }
     }
     if (ti == kb) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float v = m[0][j];
+      for (int rr0 = 0; rr0 < 8; ++rr0) {
+        if (rr0 == kk) {
 #pragma unroll
-        for (int i = 1; i < 8; ++i) v = (i == kk) ? m[i][j] : v;
-        rowk[tj * 8 + j] = v;
+          for (int j = 0; j < 8; ++j) rowk[tj * 8 + j] = m[rr0][j];
+        }
       }
     }
     __syncthreads();
-    const float inv_p = 1.f / colk[k];
+    const float piv = colk[k];
+    const float inv_p = 1.f / piv;
     float cr[8], rr[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) cr[i] = colk[ti * 8 + i];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) rr[j] = rowk[tj * 8 + j] * inv_p;
-#pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const bool rk = (ti * 8 + i) == k;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const bool ck = (tj * 8 + j) == k;
-        const float upd = m[i][j] - cr[i] * rr[j];
-        m[i][j] = rk ? (ck ? inv_p : rr[j]) : (ck ? -cr[i] * inv_p : upd);
-      }
+      const float v = colk[ti * 8 + i];
+      cr[i] = (ti * 8 + i == k) ? piv - 1.f : v;
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = rowk[tj * 8 + j];
+      rr[j] = ((tj * 8 + j == k) ? piv + 1.f : v) * inv_p;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m[i][j] = fmaf(-cr[i], rr[j], m[i][j]);
     __syncthreads();
   }
   // symmetrise through shared memory, transition = diag(alpha) inv
