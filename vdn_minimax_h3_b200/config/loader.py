@@ -75,6 +75,11 @@ def _coerce(value, tp, path):
             raise ConfigError(f"{path}: expected an int, got {value!r}")
         return value
     if tp is float:
+        if isinstance(value, str):
+            try:                      # YAML 1.1 reads "1e-6" (no dot) as a string
+                return float(value)
+            except ValueError:
+                pass
         if isinstance(value, bool) or not isinstance(value, (int, float)):
             raise ConfigError(f"{path}: expected a float, got {value!r}")
         return float(value)

@@ -69,6 +69,9 @@ class H3Config:
     @staticmethod
     def from_dict(d):
         d = {k: v for k, v in d.items() if k in H3Config.__dataclass_fields__}
+        for k, f in H3Config.__dataclass_fields__.items():
+            if k in d and f.type in (float, "float") and isinstance(d[k], str):
+                d[k] = float(d[k])
         if "patch_size" in d:
             d["patch_size"] = tuple(d["patch_size"])
         if "rope_axes_dim" in d:

@@ -90,10 +90,10 @@ def _load_dataset(cfg, video_shape=None, text_only=False):
     from vdn_minimax_h3_b200.training.dataset import H3LatentT2VADataset, SyntheticLatentDataset
     idx = cfg.data.index_file
     if idx.startswith("synthetic:"):
-        # synthetic:<n>:<F>x<h>x<w>:<audio>:<text_len>:<text_dim>
+        # synthetic:<n>:<C>x<F>x<h>x<w>:<audio latents>:<text_len>:<text_dim>
         _, n, geo, na, tl, td = idx.split(":")
-        F_, h, w = (int(v) for v in geo.split("x"))
-        return SyntheticLatentDataset(int(n), (24, F_, h, w), int(na), int(tl), int(td),
+        C, F_, h, w = (int(v) for v in geo.split("x"))
+        return SyntheticLatentDataset(int(n), (C, F_, h, w), int(na), int(tl), int(td),
                                       text_only=text_only)
     return H3LatentT2VADataset(idx, text_only=text_only)
 
@@ -271,7 +271,9 @@ def run_stage_a1(cfg):
     from vdn_minimax_h3_b200.models.factory import h3_config_from_resolved
     from vdn_minimax_h3_b200.models.h3 import h3_full_config
     base = cfg.model.base
-    loaded = dict(cfg.model.base.config_overrides) if cfg.model.base.config_overrides else h3_full_config().to_dict()
+    from vdn_minimax_h3_b200.models.h3 import H3Config
+    loaded = (H3Config.from_dict(dict(cfg.model.base.config_overrides)).to_dict()
+              if cfg.model.base.config_overrides else h3_full_config().to_dict())
     section = {"base": dict(library=base.library, class_name=base.class_name, source=base.source,
                             subfolder=base.subfolder, revision=base.revision, dtype=base.dtype),
                "architecture": resolved_dict(cfg)["model"]["architecture"]}
@@ -305,11 +307,9 @@ def run_stage_a1(cfg):
         if idx % world != rank:
             continue
         params = [p for _, p in named if p.requires_grad]
-        sub = SimpleNamespace(parameters=lambda ps=params: ps)
-        groups = fs.build_param_groups(attn, opt_cfg.lr, big_scale=opt_cfg.big_lr_scale,
+        groups = fs.build_param_groups(model, opt_cfg.lr, big_scale=opt_cfg.big_lr_scale,
                                        small_scale=opt_cfg.small_lr_scale, small_eps=opt_cfg.small_eps,
                                        select=lambda n, p, ok={id(q) for q in params}: id(p) in ok)
-        del sub
         optimizers[idx] = torch.optim.AdamW(groups, lr=opt_cfg.lr, weight_decay=opt_cfg.weight_decay)
     sched = _sched_args(opt_cfg, cfg.training.max_steps)
     gens = fs.make_generators(cfg.training.seed, rank, device)
