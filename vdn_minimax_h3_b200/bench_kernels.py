@@ -61,7 +61,11 @@ def profile_small():
     from vdn_minimax_h3_b200.models.layout import SequenceLayout
     from vdn_minimax_h3_b200.models.window import AttentionPlan, window_bounds
     from vdn_minimax_h3_b200.ops import attention, linear_branch as lb
+    from vdn_minimax_h3_b200.ops import gemm
     from vdn_minimax_h3_b200.ops._ext import check_device_error
+    xa = torch.randn(16384, 5376, device="cuda", dtype=torch.bfloat16)
+    wa = torch.randn(5376, 5376, device="cuda", dtype=torch.bfloat16) / 70
+    gemm.linear(xa, wa)
     Fr, S, H = 20, 1008, 8
     lay = SequenceLayout(seq_len=1950 + Fr * S, video_start=1950, num_frames=Fr, tokens_per_frame=S,
                          frame_height=24, frame_width=42, text_start=0, text_len=800)
