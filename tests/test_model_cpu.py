@@ -118,3 +118,26 @@ def test_tiny_golden_two_euler_steps():
                                audio=False, num_latent_frames=4,
                                on_layout=lambda lay: set_layout(eng.model, lay))
     assert _rel(lat3, lat1) < 1e-4
+
+
+def test_column_route_cpu_semantics():
+    """ColumnRoute on CPU: raw planes copy columns, plane 1 of q/k heads gets QK-prep."""
+    from vdn_minimax_h3_b200.ops import gemm
+    from vdn_minimax_h3_b200.ops.norm import qk_prep_reference
+    from vdn_minimax_h3_b200.models.h3 import RotaryEmbedding3D
+    torch.manual_seed(0)
+    M, K, N = 40, 64, 272
+    x, w = torch.randn(M, K), torch.randn(N, K) / 8
+    pos = torch.stack([torch.arange(M) // 10, torch.arange(M) % 5, torch.arange(M) % 3], 1)
+    cos, sin = RotaryEmbedding3D((32, 48, 48))(pos)
+    raw, q, rep = torch.zeros(M, N), torch.zeros(M, 128), torch.zeros(M, 16)
+    route = gemm.ColumnRoute(N, planes=3)
+    route.place(0, raw).place(0, q, plane=1).place(256, rep, plane=2)
+    nq = torch.rand(128) + 0.5
+    gemm.linear_routed(x, w, None, route, (0, 128), (0, 0), nq, None, 1e-6, cos, sin)
+    y = x @ w.t()
+    assert torch.allclose(raw, y, atol=1e-5)
+    assert torch.allclose(rep, y[:, 256:272], atol=1e-5)
+    assert torch.allclose(q, qk_prep_reference(y[:, :128], 1, nq, 1e-6, cos, sin), atol=1e-5)
+    with pytest.raises(ValueError):
+        route.place(4, raw[:, :8])

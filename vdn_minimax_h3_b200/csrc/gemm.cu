@@ -18,6 +18,14 @@
 //   EPI_SWIGLU     H = (acc_v + b_v) * silu(acc_g + b_g); the weight rows are interleaved
 //                  per 256-row tile as [128 value rows | 128 gate rows]
 //   EPI_ADD        C += acc (+ bias)                               (accumulate into C)
+//   EPI_ROUTE      every 8-column group of a row goes to its own destination (a route
+//                  table of addresses), and the 128-column q/k heads additionally get the
+//                  per-head RMSNorm + rotate-half RoPE of the attention input
+//                  (softmax_attention/kernels.py:27-30) written to a second route. One
+//                  GEMM thus emits raw q/k/v/gates, normalised+rotated q/k, and places
+//                  each head where its consumer reads it: the attention's q/k buffers on
+//                  one GPU, or the Ulysses receive slabs (local or a peer's, through an
+//                  IPC mapping) under sequence parallelism.
 //
 // Every wait is bounded (common.cuh): a protocol failure records an error code, unwinds
 // the CTA, drains its own copies and MMAs and frees its TMEM instead of hanging the GPU.
@@ -37,8 +45,9 @@ constexpr int GM_STAGE_BYTES = GM_A_BYTES + GM_B_BYTES;
 constexpr int GM_THREADS = 192;
 constexpr int GM_GROUP_N = 16;  // n-blocks per raster band (weights of one band stay in L2)
 constexpr int GM_SMEM = GM_STAGES * GM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kMaxRoutePlanes = 8;
 
-enum EpiMode : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ADD = 3 };
+enum EpiMode : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ADD = 3, EPI_ROUTE = 4 };
 
 struct EpiParams {
   __nv_bfloat16* out;        // C / X / H
@@ -48,6 +57,17 @@ struct EpiParams {
   int64_t ldg;
   const int* gate_idx;       // EPI_RESIDUAL: per-row table index
   int* err;                  // device error word
+  // EPI_ROUTE
+  const long long* route;       // [planes][N/8] address of (row 0, column 8g), 0 = no store
+  int64_t route_ld[kMaxRoutePlanes];  // row stride (elements) of each plane's destinations
+  int planes;
+  int q0, q1, k0, k1;           // GEMM column ranges of the q heads and the k heads
+  const float* norm_q;          // [128] per-head RMSNorm weights
+  const float* norm_k;
+  float qk_eps;
+  const float* rope_cos;        // [M, ld_rope] fp32, rotate-half layout (cos[j] == cos[j+64])
+  const float* rope_sin;
+  int64_t ld_rope;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
@@ -61,6 +81,117 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   nb = n0 + (in_band - mb * gn);
 }
 
+// EPI_ROUTE helpers ------------------------------------------------------------------------
+__device__ __forceinline__ void route_store_chunk(const long long* route, int64_t ld, int col,
+                                                  int ngroups, int64_t row,
+                                                  const uint32_t* packed) {
+  // Up to 32 columns starting at `col` (a multiple of 8): 16-byte groups, each to its route.
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (g >= ngroups) break;
+    const long long dst = __ldg(route + (col >> 3) + g);
+    if (dst)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + row * ld) =
+          make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+  }
+}
+
+__device__ __forceinline__ void epilogue_route(const EpiParams& p, uint32_t lane_base, int row,
+                                               bool row_ok, int n0, int N) {
+#pragma unroll 1
+  for (int h2 = 0; h2 < GM_BN; h2 += 128) {
+    const int hc = n0 + h2;
+    if (hc >= N) break;
+    const bool isq = hc >= p.q0 && hc < p.q1;
+    const bool isk = hc >= p.k0 && hc < p.k1;
+    if (isq || isk) {
+      // One q/k head per thread-row: raw values rounded to bf16 (the projection's output
+      // dtype), RMS over the head, then rotate-half RoPE on the normalised values.
+      uint32_t hv[64];
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(lane_base + h2 + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float a0 = __uint_as_float(v[j]), a1 = __uint_as_float(v[j + 1]);
+          if (p.bias) {
+            a0 += __ldg(p.bias + hc + c + j);
+            a1 += __ldg(p.bias + hc + c + j + 1);
+          }
+          const uint32_t pk = pack_bf16(a0, a1);
+          hv[(c + j) >> 1] = pk;
+          const float r0 = bf16_lo(pk), r1 = bf16_hi(pk);
+          ss = fmaf(r0, r0, fmaf(r1, r1, ss));
+        }
+        if (row_ok) route_store_chunk(p.route, p.route_ld[0], hc + c, 4, row, hv + (c >> 1));
+      }
+      if (!row_ok) continue;
+      const float rstd = rsqrtf(ss * (1.f / 128.f) + p.qk_eps);
+      const float* w = isq ? p.norm_q : p.norm_k;
+      const float4* cr = reinterpret_cast<const float4*>(p.rope_cos + (int64_t)row * p.ld_rope);
+      const float4* sr = reinterpret_cast<const float4*>(p.rope_sin + (int64_t)row * p.ld_rope);
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 c4 = __ldg(cr + ((c + j) >> 2));
+          const float4 s4 = __ldg(sr + ((c + j) >> 2));
+          const float cs[4] = {c4.x, c4.y, c4.z, c4.w};
+          const float sn[4] = {s4.x, s4.y, s4.z, s4.w};
+          float o1[4], o2[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i1 = c + j + e, i2 = i1 + 64;
+            const uint32_t u1 = hv[i1 >> 1], u2 = hv[i2 >> 1];
+            const float x1 = ((i1 & 1) ? bf16_hi(u1) : bf16_lo(u1)) * rstd * __ldg(w + i1);
+            const float x2 = ((i2 & 1) ? bf16_hi(u2) : bf16_lo(u2)) * rstd * __ldg(w + i2);
+            // cos/sin repeat with period 64 in the rotate-half layout
+            o1[e] = x1 * cs[e] - x2 * sn[e];
+            o2[e] = x2 * cs[e] + x1 * sn[e];
+          }
+          lo[j >> 1] = pack_bf16(o1[0], o1[1]);
+          lo[(j >> 1) + 1] = pack_bf16(o1[2], o1[3]);
+          hi[j >> 1] = pack_bf16(o2[0], o2[1]);
+          hi[(j >> 1) + 1] = pack_bf16(o2[2], o2[3]);
+        }
+        const long long* proc = p.route + (N >> 3);  // plane 1: processed q/k
+        route_store_chunk(proc, p.route_ld[1], hc + c, 4, row, lo);
+        route_store_chunk(proc, p.route_ld[1], hc + c + 64, 4, row, hi);
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(lane_base + h2 + c, v);
+        tmem_wait_ld();
+        const int col0 = hc + c;
+        if (!row_ok || col0 >= N) continue;
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float a0 = __uint_as_float(v[j]), a1 = __uint_as_float(v[j + 1]);
+          if (p.bias && col0 + j < N) {
+            a0 += __ldg(p.bias + col0 + j);
+            a1 += __ldg(p.bias + col0 + j + 1);
+          }
+          packed[j >> 1] = pack_bf16(a0, a1);
+        }
+        // N is a multiple of 8, so a partial chunk ends on a whole 8-column group. Every
+        // plane with an address receives a copy (e.g. a field replicated to all ranks).
+        const int ngroups = min(4, (N - col0) >> 3);
+#pragma unroll 1
+        for (int pl = 0; pl < p.planes; ++pl)
+          route_store_chunk(p.route + (int64_t)pl * (N >> 3), p.route_ld[pl], col0, ngroups,
+                            row, packed);
+      }
+    }
+  }
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& p, uint32_t tacc, int quarter,
                                               int m0, int n0, int M, int N) {
@@ -68,6 +199,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, uint32_t tacc,
   const int row = m0 + quarter * 32 + lane;
   const uint32_t lane_base = tacc + ((uint32_t)(quarter * 32) << 16);
   const bool row_ok = row < M;
+  if constexpr (EPI == EPI_ROUTE) {
+    epilogue_route(p, lane_base, row, row_ok, n0, N);
+    return;
+  }
   if constexpr (EPI == EPI_SWIGLU) {
     // columns [0,128) value, [128,256) gate -> 128 outputs at n0/2.
     const int out_c0 = n0 >> 1;
@@ -356,6 +491,30 @@ static void launch_gemm(const GemmArgs& a, EpiParams p, cudaStream_t stream) {
   const int tiles = ((a.M + GM_BM - 1) / GM_BM) * ((a.N + GM_BN - 1) / GM_BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
   gemm_bf16_kernel<EPI><<<grid, GM_THREADS, GM_SMEM, stream>>>(ta, tb, p, a.M, a.N, a.K);
+}
+
+void launch_gemm_bf16_routed(const GemmArgs& a, const GemmRoute& r, const float* bias, int* err,
+                             cudaStream_t stream) {
+  if (a.M == 0 || a.N == 0) return;
+  EpiParams p{};
+  p.bias = bias;
+  p.err = err;
+  if (r.planes < 1 || r.planes > kMaxRoutePlanes)
+    throw std::runtime_error("routed GEMM: 1..8 route planes");
+  p.route = r.route;
+  p.planes = r.planes;
+  for (int i = 0; i < r.planes; ++i) p.route_ld[i] = r.route_ld[i];
+  p.q0 = r.q0;
+  p.q1 = r.q1;
+  p.k0 = r.k0;
+  p.k1 = r.k1;
+  p.norm_q = r.norm_q;
+  p.norm_k = r.norm_k;
+  p.qk_eps = r.qk_eps;
+  p.rope_cos = r.rope_cos;
+  p.rope_sin = r.rope_sin;
+  p.ld_rope = r.ld_rope;
+  launch_gemm<EPI_ROUTE>(a, p, stream);
 }
 
 void launch_gemm_bf16(const GemmArgs& a, int mode, void* out, int64_t ldo, const float* bias,

@@ -18,6 +18,25 @@ void launch_gemm_bf16(const GemmArgs& a, int mode, void* out, int64_t ldo, const
                       const void* gate, int64_t ldg, const int* gate_idx, int* err,
                       cudaStream_t stream);
 
+// Routed epilogue (see gemm.cu, EPI_ROUTE). `route` holds `planes` tables of N/8 addresses;
+// every column group is stored to each plane that has an address for it, except the
+// 128-wide q/k heads in [q0,q1) and [k0,k1): raw values to plane 0, normalised + rotated
+// values to plane 1.
+struct GemmRoute {
+  const long long* route;
+  int64_t route_ld[8];
+  int planes;
+  int q0, q1, k0, k1;
+  const float* norm_q;
+  const float* norm_k;
+  float qk_eps;
+  const float* rope_cos;
+  const float* rope_sin;
+  int64_t ld_rope;
+};
+void launch_gemm_bf16_routed(const GemmArgs& a, const GemmRoute& r, const float* bias, int* err,
+                             cudaStream_t stream);
+
 void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps, const void* table,
                           int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
                           int64_t ldo, int T, int D, cudaStream_t stream);

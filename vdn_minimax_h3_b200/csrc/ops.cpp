@@ -94,6 +94,57 @@ void gemm_bf16_swiglu(torch::Tensor A, torch::Tensor B, torch::Tensor H,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void gemm_bf16_routed(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> bias,
+                      torch::Tensor route, std::vector<int64_t> route_ld, int64_t q0, int64_t q1,
+                      int64_t k0, int64_t k1, c10::optional<torch::Tensor> norm_q,
+                      c10::optional<torch::Tensor> norm_k, double qk_eps,
+                      c10::optional<torch::Tensor> cosv, c10::optional<torch::Tensor> sinv,
+                      torch::Tensor err) {
+  GemmArgs a = gemm_args(A, B);
+  TORCH_CHECK(a.N % 8 == 0, "routed GEMM needs N % 8 == 0");
+  TORCH_CHECK(route.is_cuda() && route.scalar_type() == at::kLong && route.is_contiguous() &&
+                  route.dim() == 2 && route.size(1) == a.N / 8,
+              "route must be a contiguous int64 CUDA tensor [planes, N/8]");
+  const int planes = (int)route.size(0);
+  TORCH_CHECK(planes >= 1 && planes <= 8 && (int)route_ld.size() == planes,
+              "1..8 route planes, one row stride each");
+  GemmRoute r{};
+  r.route = reinterpret_cast<const long long*>(route.data_ptr<int64_t>());
+  r.planes = planes;
+  for (int i = 0; i < planes; ++i) {
+    TORCH_CHECK(route_ld[i] % 8 == 0, "route row strides must be multiples of 8 elements");
+    r.route_ld[i] = route_ld[i];
+  }
+  r.q0 = (int)q0;
+  r.q1 = (int)q1;
+  r.k0 = (int)k0;
+  r.k1 = (int)k1;
+  if (q1 > q0 || k1 > k0) {
+    TORCH_CHECK(planes >= 2, "q/k processing needs plane 1 for the processed heads");
+    TORCH_CHECK(q0 % 128 == 0 && q1 % 128 == 0 && k0 % 128 == 0 && k1 % 128 == 0 &&
+                    q1 <= a.N && k1 <= a.N,
+                "q/k column ranges must lie on 128-column head boundaries");
+    TORCH_CHECK(norm_q && norm_k && cosv && sinv, "q/k processing needs norms and rope tables");
+    for (const auto* t : {&*cosv, &*sinv}) {
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->dim() == 2 &&
+                      t->size(0) >= a.M && t->size(1) == 128 && t->stride(1) == 1 &&
+                      t->stride(0) % 4 == 0 &&
+                      reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+                  "rope tables must be fp32 [M, 128] with 16-byte aligned rows");
+    }
+    TORCH_CHECK(cosv->stride(0) == sinv->stride(0), "rope tables must share a row stride");
+    r.norm_q = opt_f32(norm_q, 128, "norm_q");
+    r.norm_k = opt_f32(norm_k, 128, "norm_k");
+    r.qk_eps = (float)qk_eps;
+    r.rope_cos = cosv->data_ptr<float>();
+    r.rope_sin = sinv->data_ptr<float>();
+    r.ld_rope = cosv->stride(0);
+  }
+  c10::cuda::CUDAGuard g(A.device());
+  launch_gemm_bf16_routed(a, r, opt_f32(bias, a.N, "bias"), err_ptr(err),
+                          at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 void adaln_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, torch::Tensor table,
                    int64_t shift_col, int64_t scale_col, torch::Tensor idx, torch::Tensor out) {
@@ -340,6 +391,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "bf16 tcgen05 GEMM with gated-residual epilogue: X += gate[idx] * (A @ B^T + bias)");
   m.def("gemm_bf16_swiglu", &vdn::gemm_bf16_swiglu,
         "bf16 tcgen05 GEMM with SwiGLU epilogue over interleaved value|gate weight tiles");
+  m.def("gemm_bf16_routed", &vdn::gemm_bf16_routed,
+        "bf16 tcgen05 GEMM whose epilogue scatters 8-column groups through a route table and "
+        "applies QK RMSNorm + RoPE to the q/k heads");
   m.def("adaln_rmsnorm", &vdn::adaln_rmsnorm, "RMSNorm * w * (1 + scale[idx]) + shift[idx]");
   m.def("frame_sums", &vdn::frame_sums, "per-frame fp32 column sums of video rows");
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");

@@ -4,8 +4,9 @@ Per block (T packed rows, D = 5376, inner = 56 x 128):
 
     n1   = adaln_rmsnorm(x)                          norm.cu (+ per-frame sums of n1)
     qkvg = n1 @ [Wq; Wk; Wv; Wsgate; Wbeta; Wgdown]^T  gemm.cu, ONE GEMM for the three
-                                                     projections and the three gate inputs
-    q, k = qk_prep(qkvg)                             norm.cu (QK RMSNorm + 3D RoPE)
+                                                     projections and the three gate inputs;
+    q, k = qk_prep(qkvg)                             its routed epilogue also writes the
+                                                     QK-RMSNorm + 3D-RoPE'd q and k
     cat[:, :inner] = window_attention(q, k, v) * sigmoid(sgate)   attention.cu
     cat[video, inner:] = linear branch readout       linear_branch.cu chain
     x   += gate_msa[idx] * (cat @ [Wo | Wo_lin]^T + bo)  gemm.cu, K-concatenated O-proj and
@@ -142,6 +143,7 @@ class InferenceEngine:
         self.plan = None
         self.dense_plan = None
         self._buffers = {}
+        self._routes = {}
         self._cat_dirty = False
         self.timer = SectionTimer(False)
 
@@ -199,18 +201,24 @@ class InferenceEngine:
             norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1)
             frame_sums = norm_ops.frame_sums(n1, Fr, S, 0, vs) if linear_on else None
         qkvg = self._buf("qkvg", (T, pb.w_qkvg.shape[0]), x.dtype, dev)
-        with sec("gemm_qkv"):
-            gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
         c = pb.cols
-        q_raw = qkvg[:, c["q"][0]:c["q"][1]]
-        k_raw = qkvg[:, c["k"][0]:c["k"][1]]
-        v = qkvg[:, c["v"][0]:c["v"][1]]
         cos, sin = rope
         q = self._buf("q", (T, inner), x.dtype, dev)
         k = self._buf("k", (T, inner), x.dtype, dev)
-        with sec("qk_prep"):
-            norm_ops.qk_prep(q_raw, H, pb.norm_q, pb.qk_eps, cos, sin, out=q)
-            norm_ops.qk_prep(k_raw, H, pb.norm_k, pb.qk_eps, cos, sin, out=k)
+        if fused_qk_ok(pb, cos):
+            route = self._qkv_route(pb, qkvg, q, k)
+            with sec("gemm_qkv"):
+                gemm.linear_routed(n1, pb.w_qkvg, pb.b_qkvg, route, c["q"], c["k"], pb.norm_q,
+                                   pb.norm_k, pb.qk_eps, cos, sin)
+        else:
+            with sec("gemm_qkv"):
+                gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
+            with sec("qk_prep"):
+                norm_ops.qk_prep(qkvg[:, c["q"][0]:c["q"][1]], H, pb.norm_q, pb.qk_eps, cos, sin,
+                                 out=q)
+                norm_ops.qk_prep(qkvg[:, c["k"][0]:c["k"][1]], H, pb.norm_k, pb.qk_eps, cos, sin,
+                                 out=k)
+        v = qkvg[:, c["v"][0]:c["v"][1]]
         kcat = pb.w_o.shape[1]
         cat = self._buf("cat", (T, kcat), x.dtype, dev, zero=True)
         sgate = qkvg[:, c["sgate"][0]:c["sgate"][1]] if pb.has_sgate else None
@@ -237,6 +245,20 @@ class InferenceEngine:
         with sec("gemm_ff_down"):
             gemm.linear_gated_residual(h, pb.w_down, pb.b_down, x, table[:, 5 * D:6 * D], adaln_idx)
         return x
+
+    def _qkv_route(self, pb, qkvg, q, k):
+        """Raw projection -> qkvg (all columns); normalised + rotated q/k -> q, k."""
+        key = (qkvg.data_ptr(), tuple(qkvg.shape), q.data_ptr(), k.data_ptr(),
+               tuple(sorted(pb.cols.items())))
+        route = self._routes.get(key)
+        if route is None:
+            c = pb.cols
+            route = gemm.ColumnRoute(qkvg.shape[1], planes=2)
+            route.place(0, qkvg, plane=0)
+            route.place(c["q"][0], q, plane=1)
+            route.place(c["k"][0], k, plane=1)
+            self._routes[key] = route
+        return route
 
     def _linear_branch(self, pb, attn, layout, n1, qkvg, frame_sums, out):
         """The linear branch over the video rows, all heads; readout into `out` (video rows;
@@ -271,6 +293,14 @@ class InferenceEngine:
         return m.head(x.unsqueeze(0), temb, timestep_indices, video_indices, audio_indices)
 
     __call__ = forward
+
+
+def fused_qk_ok(pb, cos):
+    """The QKV GEMM's routed epilogue handles 128-wide heads with full-width rotate-half
+    RoPE on 128-column boundaries of the packed projection."""
+    c = pb.cols
+    return (cos.is_cuda and pb.head_dim == 128 and cos.shape[-1] == 128
+            and cos.dtype == torch.float32 and c["q"][0] % 128 == 0 and c["k"][0] % 128 == 0)
 
 
 def linear_branch_core(pb, attn, layout, bounds, q_raw, k_raw, v_raw, beta_logits, ghid,

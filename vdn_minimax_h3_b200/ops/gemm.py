@@ -80,3 +80,103 @@ def linear_swiglu(x, weight_interleaved, bias_interleaved=None, tile=256):
     ext().gemm_bf16_swiglu(x, weight_interleaved, out, _bias32(bias_interleaved),
                            error_word(x.device))
     return out
+
+
+class ColumnRoute:
+    """Where each 8-column group of a routed GEMM's output goes.
+
+    The route has `planes` destination tables. `place(col, view, plane)` sends output
+    columns [col, col + view.shape[1]) of every row r to view[r]; a column group placed in
+    several planes is stored to each (a field replicated to several ranks). For the q/k
+    head columns of `linear_routed`, plane 0 receives the raw projection and plane 1 the
+    per-head RMSNorm + RoPE'd values. Views may live anywhere the GPU can store to: a local
+    buffer, a slab of a Ulysses exchange buffer, or a peer GPU's buffer mapped into this
+    process. The views of one plane share a row stride. Columns never placed are computed
+    and dropped."""
+
+    MAX_PLANES = 8
+
+    def __init__(self, n_cols, planes=2):
+        if n_cols % 8:
+            raise ValueError("routed GEMM output width must be a multiple of 8")
+        if not 1 <= planes <= self.MAX_PLANES:
+            raise ValueError(f"1..{self.MAX_PLANES} planes")
+        self.n_cols = n_cols
+        self.entries = [[] for _ in range(planes)]
+        self._dev = None
+
+    @property
+    def raw(self):
+        return self.entries[0]
+
+    @property
+    def proc(self):
+        return self.entries[1] if len(self.entries) > 1 else []
+
+    def place(self, col, view, plane=0):
+        w = view.shape[1]
+        if col % 8 or w % 8 or col + w > self.n_cols:
+            raise ValueError(f"columns [{col}, {col + w}) are not whole 8-column groups of "
+                             f"[0, {self.n_cols})")
+        if view.dim() != 2 or view.stride(1) != 1:
+            raise ValueError("route destinations are 2-D views with contiguous rows")
+        if view.is_cuda and view.dtype != torch.bfloat16:
+            raise ValueError("CUDA route destinations are bf16")
+        self.entries[plane].append((col, view))
+        self._dev = None
+        return self
+
+    def tables(self, device):
+        """(route [planes, N/8] int64 addresses on `device`, [row stride per plane])."""
+        if self._dev is None:
+            rows, lds = [], []
+            for plane, entries in enumerate(self.entries):
+                t = [0] * (self.n_cols // 8)
+                ld = {v.stride(0) for _, v in entries}
+                if len(ld) > 1:
+                    raise ValueError(f"plane {plane} destinations need one row stride, "
+                                     f"got {sorted(ld)}")
+                for col, v in entries:
+                    if v.data_ptr() % 16 or (v.stride(0) * 2) % 16:
+                        raise ValueError("route destinations must be 16-byte aligned")
+                    for g in range(v.shape[1] // 8):
+                        t[col // 8 + g] = v.data_ptr() + 16 * g
+                rows.append(t)
+                lds.append(ld.pop() if ld else 8)
+            self._dev = (torch.tensor(rows, dtype=torch.int64, device=device), lds)
+        return self._dev
+
+    def emulate(self, y):
+        """CPU semantics of the raw stores: copy y's placed columns into every plane."""
+        for plane, entries in enumerate(self.entries):
+            for col, v in entries:
+                v.copy_(y[:, col:col + v.shape[1]])
+
+
+def linear_routed(x, weight, bias, route, q_cols=(0, 0), k_cols=(0, 0), norm_q=None,
+                  norm_k=None, qk_eps=1e-6, cos=None, sin=None):
+    """y = x @ weight.T + bias, scattered through `route` (ColumnRoute). Columns in
+    q_cols / k_cols are 128-wide heads: their raw values go to plane 0 and
+    rms_norm(head) * norm_{q,k} followed by rotate-half RoPE (cos/sin [M, 128]) to plane 1.
+    One GEMM replaces projection + QK-prep + the Ulysses pack."""
+    qk = q_cols[1] > q_cols[0] or k_cols[1] > k_cols[0]
+    in_qk = lambda c: q_cols[0] <= c < q_cols[1] or k_cols[0] <= c < k_cols[1]  # noqa: E731
+    if not x.is_cuda:
+        from vdn_minimax_h3_b200.ops.norm import qk_prep_reference
+        y = F.linear(x.float(), weight.float(), None if bias is None else bias.float())
+        y = y.to(x.dtype)
+        for plane, entries in enumerate(route.entries):
+            for col, v in entries:
+                if plane == 1 and in_qk(col):
+                    w = norm_q if q_cols[0] <= col < q_cols[1] else norm_k
+                    v.copy_(qk_prep_reference(y[:, col:col + v.shape[1]], v.shape[1] // 128, w,
+                                              qk_eps, cos, sin))
+                else:
+                    v.copy_(y[:, col:col + v.shape[1]])
+        return route
+    table, lds = route.tables(x.device)
+    f32 = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
+    ext().gemm_bf16_routed(x, weight, _bias32(bias), table, lds, q_cols[0], q_cols[1],
+                           k_cols[0], k_cols[1], f32(norm_q), f32(norm_k), float(qk_eps),
+                           cos if qk else None, sin if qk else None, error_word(x.device))
+    return route
