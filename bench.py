@@ -36,6 +36,9 @@ def parse(argv=None):
     p.add_argument("--fp8", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
+                   help="Ulysses exchange: symmetric-memory stores fused into the producing "
+                        "kernels (p2p) or NCCL all_to_all_single (nccl)")
     p.add_argument("--num-layers", type=int, default=None, help=argparse.SUPPRESS)
     return p.parse_args(argv)
 
@@ -145,7 +148,7 @@ def main(argv=None):
     if world > 1:
         from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
         runtime = init_ulysses()
-        transformer = UlyssesEngine(engine, runtime)
+        transformer = UlyssesEngine(engine, runtime, exchange=args.exchange)
 
     # ---- synthetic request: prompt embeddings + noise for a 14.4 s clip
     g = torch.Generator().manual_seed(args.seed + 100)
@@ -257,12 +260,14 @@ def main(argv=None):
                        "global_batch": 1, "seq_len": S, "num_frames": NUM_FRAMES,
                        "latent_frames": geo.num_latent_frames, "text_len": TEXT_LEN, "nfe": NFE,
                        "parallelism": "single-gpu" if world == 1 else f"ulysses{world}",
+                       "exchange": None if world == 1 else args.exchange,
                        "l2": "inputs larger than L2 (66 GB of weights stream per step)"},
             "clocks": clock_info, "gpu_launches": launches, "e2e": e2e,
             "build_s": round(build_s, 1),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        transformer.close()
         torch.distributed.destroy_process_group()
     return 0
 

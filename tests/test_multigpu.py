@@ -1,5 +1,7 @@
-"""Ulysses on 2 GPUs (NCCL): the sequence-parallel engine equals the single-GPU engine on a
-reduced geometry with head_dim 128 and the released transform. Skipped with < 2 GPUs."""
+"""Ulysses on 2 GPUs: the sequence-parallel engine (NCCL all-to-all, or the symmetric-memory
+exchange fused into the producing kernels) equals the single-GPU engine on a reduced geometry
+with head_dim 128 and the released transform; the symmetric heap moves bytes between ranks.
+Each rank is its own process on its own GPU. Skipped with < 2 GPUs."""
 import copy
 import os
 import socket
@@ -19,7 +21,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, exchange):
     import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -52,11 +54,15 @@ def _worker(rank, world, port, q):
         with torch.no_grad():
             single = InferenceEngine(copy.deepcopy(gm))
             ref_v, _ = single(**kwg, layout=layout)
-            sp = UlyssesEngine(InferenceEngine(gm), init_ulysses())
+            sp = UlyssesEngine(InferenceEngine(gm), init_ulysses(), exchange=exchange)
             out_v, _ = sp(**kwg, layout=layout)
+            out_v2, _ = sp(**kwg, layout=layout)
+            sp.close()
         torch.cuda.synchronize()
         check_device_error()
         err = ((out_v.float() - ref_v.float()).norm() / ref_v.float().norm()).item()
+        if not torch.equal(out_v, out_v2):
+            err = "second forward differs from the first"
         q.put((rank, err))
     except Exception as exc:  # noqa: BLE001
         q.put((rank, repr(exc)))
@@ -64,13 +70,68 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.timeout(300)
-def test_ulysses_two_gpus_match_single():
+def _heap_worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from vdn_minimax_h3_b200.parallel.symmetric import SymmetricHeap
+        heap = SymmetricHeap(1 << 20, device=dev, timeout_s=20.0)
+        buf = heap.alloc("x", (world, 1000), torch.float32)
+        for it in range(3):
+            for p in range(world):   # write my row into every rank's copy
+                heap.peer("x", p)[rank].fill_(100 * it + rank)
+            heap.barrier()
+            torch.cuda.synchronize()
+            want = torch.tensor([100 * it + r for r in range(world)], dtype=torch.float32, device=dev)
+            ok = torch.equal(buf[:, 0], want) and torch.equal(buf[:, -1], want)
+            heap.barrier()   # nobody overwrites before everyone has read
+            if not ok:
+                break
+        heap.check()
+        heap.close()
+        q.put((rank, ok))
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(target, world, *args):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=(r, world, port, q) + args) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=280)
+    return dict(q.get(timeout=10) for _ in range(world))
+
+
+TWO_GPUS = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                              reason="needs 2 GPUs")
+
+
+@TWO_GPUS
+@pytest.mark.timeout(300)
+def test_symmetric_heap_two_gpus():
+    res = _spawn(_heap_worker, 2)
+    assert all(v is True for v in res.values()), res
+
+
+@TWO_GPUS
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_ulysses_two_gpus_match_single(exchange):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

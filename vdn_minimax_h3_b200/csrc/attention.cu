@@ -58,6 +58,7 @@ struct AttnParams {
   int64_t ldg;
   __nv_bfloat16* out;        // [T, ldo], head h at column h*128
   int64_t ldo;
+  RowScatter scatter;        // optional: rows to their Ulysses owners
   float scale_log2;          // softmax scale * log2(e)
   int* err;
 };
@@ -482,7 +483,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i)
             o[i] = pack_bf16(__uint_as_float(u[2 * i]) * gscale, __uint_as_float(u[2 * i + 1]) * gscale);
-          uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t)row * p.ldo + head * AT_D + c);
+          uint4* dst = reinterpret_cast<uint4*>(p.scatter.row_ptr(p.out, p.ldo, row) + head * AT_D + c);
 #pragma unroll
           for (int q = 0; q < 4; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
         }
@@ -503,7 +504,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                              int64_t ldv, int T, int H, const int* tiles, int n_tiles,
                              const int* kv, const void* gate, int64_t ldg, void* out,
-                             int64_t ldo, float scale, int* err, cudaStream_t stream) {
+                             int64_t ldo, float scale, int* err, cudaStream_t stream,
+                             const RowScatter* scatter) {
   if (n_tiles == 0 || H == 0) return;
   static bool attr = false;
   if (!attr) {
@@ -527,6 +529,8 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
   p.ldg = ldg;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
+  p.scatter = RowScatter{};
+  if (scatter) p.scatter = *scatter;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
   const int items = n_tiles * H;

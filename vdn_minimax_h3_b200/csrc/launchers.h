@@ -4,7 +4,32 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cuda_bf16.h>
+
 namespace vdn {
+
+// Row-owner scatter of an epilogue's output rows. Under Ulysses the rows of the packed
+// sequence are owned in contiguous shards of `rows_per_rank`; an epilogue that produced row
+// g (g = row0 + local output row) stores it to base[g / rows_per_rank] at row
+// g % rows_per_rank: the owner's buffer, local or a peer's mapped into this process.
+// n == 0 disables the scatter (plain out + row * ldo).
+constexpr int kMaxScatterRanks = 8;
+struct RowScatter {
+  __nv_bfloat16* base[kMaxScatterRanks];  // bf16 pointers
+  int64_t row0;
+  int rows_per_rank;
+  int n;
+#ifdef __CUDACC__
+  __device__ __forceinline__ __nv_bfloat16* row_ptr(__nv_bfloat16* out, int64_t ldo,
+                                                    int64_t row) const {
+    if (n == 0) return out + row * ldo;
+    const int64_t g = row0 + row;
+    const int r = (int)(g / rows_per_rank);
+    return base[r] + (g - (int64_t)r * rows_per_rank) * ldo;
+  }
+#endif
+};
+
 
 struct GemmArgs {
   const void* A;   // [M, K] bf16, row stride lda (elements)
@@ -49,9 +74,19 @@ void launch_qk_prep(const void* src, int64_t lds, int T, int H, int d, const flo
 void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                              int64_t ldv, int T, int H, const int* tiles, int n_tiles,
                              const int* kv, const void* gate, int64_t ldg, void* out,
-                             int64_t ldo, float scale, int* err, cudaStream_t stream);
+                             int64_t ldo, float scale, int* err, cudaStream_t stream,
+                             const RowScatter* scatter = nullptr);
 
 void attention_set_poly_every(int n);
+
+// Symmetric memory (symmetric.cu): IPC-exported regions and the peer flag barrier.
+void* symm_malloc(size_t nbytes, void* handle_out);
+void* symm_open(const void* handle);
+void symm_close(void* peer_ptr);
+void symm_free(void* p);
+void launch_symm_barrier(unsigned long long* counter, unsigned long long* local_flags,
+                         unsigned long long* const* peer_flags, int rank, int P,
+                         long long timeout_ns, int* err, cudaStream_t stream);
 void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, int64_t ldo, int l2,
                         cudaStream_t stream);
 void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,
@@ -69,6 +104,7 @@ void launch_lb_gather(const float* prefix, const float* suffix, const int* idx, 
                       cudaStream_t stream);
 void launch_lb_readout(const void* q, int64_t ldq, const void* state, int F, int S, int H,
                        const float* w, const void* gate, int64_t ldg, int gate_logits, void* out,
-                       int64_t ldo, float eps, int* err, cudaStream_t stream);
+                       int64_t ldo, float eps, int* err, cudaStream_t stream,
+                       const RowScatter* scatter = nullptr);
 
 }  // namespace vdn

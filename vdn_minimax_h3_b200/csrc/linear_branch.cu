@@ -639,7 +639,8 @@ constexpr int RO_SMEM = 2 * RO_TILE + 1024 + 64;
 __global__ void __launch_bounds__(128) lb_readout_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmS, int S,
     int H, const float* __restrict__ w, const __nv_bfloat16* __restrict__ gate, int64_t ldg,
-    int gate_logits, __nv_bfloat16* __restrict__ out, int64_t ldo, float eps, int* err) {
+    int gate_logits, __nv_bfloat16* __restrict__ out, int64_t ldo, float eps, int* err,
+    const RowScatter scatter) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -708,7 +709,7 @@ __global__ void __launch_bounds__(128) lb_readout_kernel(
       const float rstd = rsqrtf(ss / 128.f + eps);
       const int64_t row = (int64_t)f * S + tok;
       const __nv_bfloat16* g = gate + row * ldg + h * 128;
-      __nv_bfloat16* o = out + row * ldo + h * 128;
+      __nv_bfloat16* o = scatter.row_ptr(out, ldo, row) + h * 128;
 #pragma unroll
       for (int c = 0; c < 128; c += 8) {
         const uint4 gv = *reinterpret_cast<const uint4*>(g + c);
@@ -739,7 +740,8 @@ __global__ void __launch_bounds__(128) lb_readout_kernel(
 
 void launch_lb_readout(const void* q, int64_t ldq, const void* state, int F, int S, int H,
                        const float* w, const void* gate, int64_t ldg, int gate_logits, void* out,
-                       int64_t ldo, float eps, int* err, cudaStream_t stream) {
+                       int64_t ldo, float eps, int* err, cudaStream_t stream,
+                       const RowScatter* scatter) {
   if (!F || !S || !H) return;
   static bool attr = false;
   if (!attr) {
@@ -753,7 +755,7 @@ void launch_lb_readout(const void* q, int64_t ldq, const void* state, int F, int
   const int tiles = F * H * ((S + 127) / 128);
   lb_readout_kernel<<<tiles, 128, RO_SMEM, stream>>>(
       tq, ts, S, H, w, reinterpret_cast<const __nv_bfloat16*>(gate), ldg, gate_logits,
-      reinterpret_cast<__nv_bfloat16*>(out), ldo, eps, err);
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, eps, err, scatter ? *scatter : RowScatter{});
 }
 
 }  // namespace vdn

@@ -214,15 +214,45 @@ void check_heads(const torch::Tensor& t, const char* name, int64_t T, int64_t H)
 }
 }  // namespace
 
+namespace {
+// Row-owner scatter from Python: one base address per owner rank (the owner's buffer at
+// row 0 and this producer's first column), the packed row of output row 0, the shard
+// height. An empty base list means no scatter.
+RowScatter make_scatter(const std::vector<int64_t>& base, int64_t row0, int64_t rows) {
+  RowScatter sc{};
+  TORCH_CHECK(base.size() <= (size_t)kMaxScatterRanks, "at most 8 scatter ranks");
+  sc.n = (int)base.size();
+  for (size_t i = 0; i < base.size(); ++i) {
+    TORCH_CHECK(base[i] % 16 == 0, "scatter destinations must be 16-byte aligned");
+    sc.base[i] = reinterpret_cast<__nv_bfloat16*>(base[i]);
+  }
+  sc.row0 = row0;
+  sc.rows_per_rank = (int)rows;
+  TORCH_CHECK(sc.n == 0 || rows > 0, "scatter needs a positive shard height");
+  return sc;
+}
+
+void check_out_or_scatter(const torch::Tensor& out, const RowScatter& sc, int64_t ld,
+                          int64_t rows, int64_t cols) {
+  check_2d_bf16(out, "out");
+  if (sc.n == 0) {
+    TORCH_CHECK(out.size(0) == rows && out.size(1) == cols, "out must be [", rows, ", ", cols, "]");
+  } else {
+    TORCH_CHECK(out.stride(0) == ld && ld % 8 == 0, "scatter row stride must match out's");
+  }
+}
+}  // namespace
+
 void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles,
                       torch::Tensor kv, c10::optional<torch::Tensor> gate, torch::Tensor out,
-                      double scale, torch::Tensor err) {
+                      double scale, torch::Tensor err, std::vector<int64_t> scatter_base,
+                      int64_t scatter_row0, int64_t scatter_rows) {
   const int64_t T = q.size(0), H = q.size(1);
   check_heads(q, "q", T, H);
   check_heads(k, "k", T, H);
   check_heads(v, "v", T, H);
-  check_2d_bf16(out, "out");
-  TORCH_CHECK(out.size(0) == T && out.size(1) == H * 128, "out must be [T, H*128]");
+  const RowScatter sc = make_scatter(scatter_base, scatter_row0, scatter_rows);
+  check_out_or_scatter(out, sc, out.stride(0), T, H * 128);
   TORCH_CHECK(tiles.is_cuda() && tiles.scalar_type() == at::kInt && tiles.is_contiguous() &&
                   tiles.dim() == 2 && tiles.size(1) == 4, "tiles must be int32 [n, 4]");
   TORCH_CHECK(kv.is_cuda() && kv.scalar_type() == at::kInt && kv.is_contiguous() &&
@@ -240,7 +270,7 @@ void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
   launch_window_attention(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(),
                           v.stride(0), (int)T, (int)H, tiles.data_ptr<int>(), (int)tiles.size(0),
                           kv.data_ptr<int>(), gp, ldg, out.data_ptr(), out.stride(0),
-                          (float)scale, err_ptr(err), at::cuda::getCurrentCUDAStream());
+                          (float)scale, err_ptr(err), at::cuda::getCurrentCUDAStream(), &sc);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -363,7 +393,8 @@ void lb_gather(torch::Tensor prefix, torch::Tensor suffix, torch::Tensor idx, to
 }
 
 void lb_readout(torch::Tensor q, torch::Tensor state, torch::Tensor w, torch::Tensor gate,
-                torch::Tensor out, double eps, bool gate_logits, torch::Tensor err) {
+                torch::Tensor out, double eps, bool gate_logits, torch::Tensor err,
+                std::vector<int64_t> scatter_base, int64_t scatter_row0, int64_t scatter_rows) {
   TORCH_CHECK(q.dim() == 4, "q must be [F, S, H, 128]");
   const int64_t F = q.size(0), S = q.size(1), H = q.size(2);
   TORCH_CHECK(q.stride(0) == S * q.stride(1), "q frames must be consecutive rows");
@@ -373,18 +404,76 @@ void lb_readout(torch::Tensor q, torch::Tensor state, torch::Tensor w, torch::Te
   check_f32(w, "norm weight", 128);
   TORCH_CHECK(gate.dim() == 3 && gate.size(0) == F * S && gate.size(1) == H, "gate [F*S, H, 128]");
   check_rows_heads(gate, "gate");
-  check_2d_bf16(out, "out");
-  TORCH_CHECK(out.size(0) == F * S && out.size(1) == H * 128, "out must be [F*S, H*128]");
+  const RowScatter sc = make_scatter(scatter_base, scatter_row0, scatter_rows);
+  check_out_or_scatter(out, sc, out.stride(0), F * S, H * 128);
   c10::cuda::CUDAGuard g(q.device());
   launch_lb_readout(q.data_ptr(), q.stride(1), state.data_ptr(), (int)F, (int)S, (int)H,
                     w.data_ptr<float>(), gate.data_ptr(), gate.stride(0), gate_logits,
-                    out.data_ptr(), out.stride(0), (float)eps, err_ptr(err), cur());
+                    out.data_ptr(), out.stride(0), (float)eps, err_ptr(err), cur(), &sc);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace vdn
+
+// ---------------------------------------------------------------- symmetric memory
+namespace vdn {
+
+py::tuple symm_alloc(int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  char handle[64];
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  void* p = symm_malloc((size_t)nbytes, handle);
+  return py::make_tuple((int64_t)reinterpret_cast<uintptr_t>(p), py::bytes(handle, 64));
+}
+
+int64_t symm_open_handle(py::bytes handle, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  std::string h = handle;
+  TORCH_CHECK(h.size() == 64, "IPC handle must be 64 bytes");
+  return (int64_t)reinterpret_cast<uintptr_t>(symm_open(h.data()));
+}
+
+void symm_close_handle(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  symm_close(reinterpret_cast<void*>(ptr));
+}
+
+void symm_free_ptr(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  symm_free(reinterpret_cast<void*>(ptr));
+}
+
+torch::Tensor bytes_at(int64_t ptr, int64_t nbytes, int64_t device) {
+  // A non-owning uint8 tensor over [ptr, ptr + nbytes) on `device` (local or peer memory
+  // mapped into this process). The region's owner controls its lifetime.
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {nbytes}, [](void*) {}, opts);
+}
+
+void symm_barrier(int64_t counter, int64_t local_flags, torch::Tensor peer_flags, int64_t rank,
+                  int64_t timeout_ns, torch::Tensor err) {
+  TORCH_CHECK(peer_flags.is_cuda() && peer_flags.scalar_type() == at::kLong &&
+                  peer_flags.is_contiguous(), "peer_flags must be int64 CUDA [P]");
+  const int P = (int)peer_flags.numel();
+  TORCH_CHECK(rank >= 0 && rank < P, "rank out of range");
+  c10::cuda::CUDAGuard g(peer_flags.device());
+  launch_symm_barrier(reinterpret_cast<unsigned long long*>(counter),
+                      reinterpret_cast<unsigned long long*>(local_flags),
+                      reinterpret_cast<unsigned long long* const*>(peer_flags.data_ptr<int64_t>()),
+                      (int)rank, P, (long long)timeout_ns, err_ptr(err),
+                      at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace vdn
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("symm_alloc", &vdn::symm_alloc, "cudaMalloc + IPC handle: (ptr, handle bytes)");
+  m.def("symm_open", &vdn::symm_open_handle, "map a peer's IPC handle: ptr");
+  m.def("symm_close", &vdn::symm_close_handle, "unmap a peer region");
+  m.def("symm_free", &vdn::symm_free_ptr, "free this rank's region");
+  m.def("bytes_at", &vdn::bytes_at, "non-owning uint8 tensor over device memory");
+  m.def("symm_barrier", &vdn::symm_barrier, "bounded all-ranks flag barrier over peer memory");
   m.doc() = "VDN-H3 sm_100a kernels";
   m.def("gemm_bf16", &vdn::gemm_bf16, "bf16 tcgen05 GEMM: out (+)= A @ B^T (+ bias)");
   m.def("gemm_bf16_residual", &vdn::gemm_bf16_residual,

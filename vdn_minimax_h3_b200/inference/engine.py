@@ -304,14 +304,16 @@ def fused_qk_ok(pb, cos):
 
 
 def linear_branch_core(pb, attn, layout, bounds, q_raw, k_raw, v_raw, beta_logits, ghid,
-                       frame_sums, heads, out, dtype):
+                       frame_sums, heads, out, dtype, scatter=None):
     """The forward-only linear branch for a head range over every video row.
 
     q_raw/k_raw/v_raw [T, n, d] and beta_logits [T, n] cover the packed sequence (rows of
     the whole sequence, this head range); ghid [T, rank] is the output gate's low-rank
     hidden; frame_sums [F, D] fp32 are the per-frame sums of the attention input over the
     whole clip. Writes the gated, normalised readout of the generated frames into
-    out[video rows] ([T, n*d] view); other rows are left untouched (zero)."""
+    out[video rows] ([T, n*d] view); other rows are left untouched (zero). With
+    scatter = (bases, _, rows_per_rank) the rows go to their Ulysses owners instead
+    (`out` then only gives the row stride)."""
     br = attn.linear_attention
     n, d = heads.stop - heads.start, pb.head_dim
     ch = slice(heads.start * d, heads.stop * d)
@@ -355,5 +357,9 @@ def linear_branch_core(pb, attn, layout, bounds, q_raw, k_raw, v_raw, beta_logit
     up_w = pb.gate_up_w[ch]
     up_b = None if pb.gate_up_b is None else pb.gate_up_b[ch]
     gate_logits = gemm.linear(ghid[r0:r1], up_w, up_b)
-    lb.readout(qf.view(nF, S, n, d), state, br.norm.weight, gate_logits.view(-1, n, d),
-               br.norm.eps, out=out[r0:r1], gate_logits=True)
+    if scatter is not None:
+        lb.readout(qf.view(nF, S, n, d), state, br.norm.weight, gate_logits.view(-1, n, d),
+                   br.norm.eps, out=out, gate_logits=True, scatter=(scatter[0], r0, scatter[2]))
+    else:
+        lb.readout(qf.view(nF, S, n, d), state, br.norm.weight, gate_logits.view(-1, n, d),
+                   br.norm.eps, out=out[r0:r1], gate_logits=True)

@@ -146,11 +146,20 @@ class ColumnRoute:
             self._dev = (torch.tensor(rows, dtype=torch.int64, device=device), lds)
         return self._dev
 
-    def emulate(self, y):
-        """CPU semantics of the raw stores: copy y's placed columns into every plane."""
+    def copy_from(self, y, processed=()):
+        """Host-side semantics of the routed stores: every placed view receives its columns
+        of y, except plane-1 views inside a `processed` range (col0, tensor), which receive
+        the tensor's columns. Used on CPU and for head widths the fused epilogue lacks."""
         for plane, entries in enumerate(self.entries):
             for col, v in entries:
-                v.copy_(y[:, col:col + v.shape[1]])
+                src = y
+                off = col
+                if plane == 1:
+                    for c0, t in processed:
+                        if c0 <= col < c0 + t.shape[1]:
+                            src, off = t, col - c0
+                            break
+                v.copy_(src[:, off:off + v.shape[1]])
 
 
 def linear_routed(x, weight, bias, route, q_cols=(0, 0), k_cols=(0, 0), norm_q=None,
@@ -160,19 +169,16 @@ def linear_routed(x, weight, bias, route, q_cols=(0, 0), k_cols=(0, 0), norm_q=N
     rms_norm(head) * norm_{q,k} followed by rotate-half RoPE (cos/sin [M, 128]) to plane 1.
     One GEMM replaces projection + QK-prep + the Ulysses pack."""
     qk = q_cols[1] > q_cols[0] or k_cols[1] > k_cols[0]
-    in_qk = lambda c: q_cols[0] <= c < q_cols[1] or k_cols[0] <= c < k_cols[1]  # noqa: E731
     if not x.is_cuda:
         from vdn_minimax_h3_b200.ops.norm import qk_prep_reference
         y = F.linear(x.float(), weight.float(), None if bias is None else bias.float())
         y = y.to(x.dtype)
-        for plane, entries in enumerate(route.entries):
-            for col, v in entries:
-                if plane == 1 and in_qk(col):
-                    w = norm_q if q_cols[0] <= col < q_cols[1] else norm_k
-                    v.copy_(qk_prep_reference(y[:, col:col + v.shape[1]], v.shape[1] // 128, w,
-                                              qk_eps, cos, sin))
-                else:
-                    v.copy_(y[:, col:col + v.shape[1]])
+        proc = []
+        for (lo, hi), w in ((q_cols, norm_q), (k_cols, norm_k)):
+            if hi > lo:
+                proc.append((lo, qk_prep_reference(y[:, lo:hi], (hi - lo) // w.numel(), w,
+                                                   qk_eps, cos, sin)))
+        route.copy_from(y, proc)
         return route
     table, lds = route.tables(x.device)
     f32 = lambda t: None if t is None else t.float().contiguous()  # noqa: E731

@@ -122,9 +122,13 @@ def readout_reference(q, state, norm_w, gate, eps, gate_logits=False):
     return (r.reshape(Fr * S, n, d) * gate.float()).reshape(Fr * S, n * d).to(q.dtype)
 
 
-def readout(q, state, norm_w, gate, eps, out=None, gate_logits=False):
+def readout(q, state, norm_w, gate, eps, out=None, gate_logits=False, scatter=None):
     """RMSNorm(q . state^T) * w * gate, token-major [F*S, n*d]. `out` may be a strided view
-    (the right half of the O-projection input). With gate_logits the gate is sigmoid(gate)."""
+    (the right half of the O-projection input). With gate_logits the gate is sigmoid(gate).
+    scatter = (bases, row0, rows_per_rank): rows go to their Ulysses owners (see
+    ops.attention.window_attention)."""
+    if scatter is not None and not _native(q):
+        raise ValueError("row-owner scatter needs the CUDA kernels")
     if not _native(q):
         r = readout_reference(q, state, norm_w, gate, eps, gate_logits)
         if out is not None:
@@ -134,8 +138,9 @@ def readout(q, state, norm_w, gate, eps, out=None, gate_logits=False):
     Fr, S, n, d = q.shape
     if out is None:
         out = torch.empty(Fr * S, n * d, dtype=q.dtype, device=q.device)
+    bases, row0, rows = scatter if scatter is not None else ([], 0, 0)
     ext().lb_readout(q, state.contiguous(), norm_w.float().contiguous(), gate, out, float(eps),
-                     bool(gate_logits), error_word(q.device))
+                     bool(gate_logits), error_word(q.device), list(bases), int(row0), int(rows))
     return out
 
 

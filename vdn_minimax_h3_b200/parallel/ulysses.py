@@ -11,15 +11,17 @@ collective inventory). Embedding, token refiner and the output head run replicat
 block residual is all-gathered once at the end.
 
 `exchange` selects the transport: "nccl" (torch.distributed all_to_all_single, the
-reference's own path) or "p2p" (this package's symmetric-memory peer kernels, see
-parallel/symmetric.py) once those are installed.
+reference's own path, fed by the routed QKV GEMM that packs the send buffer in its
+epilogue) or "p2p" (symmetric memory, parallel/symmetric.py: the producing kernels store
+straight into the peers' buffers and a device flag barrier orders each exchange).
 """
 import math
 
 import torch
 import torch.distributed as dist
 
-from vdn_minimax_h3_b200.inference.engine import InferenceEngine, linear_branch_core
+from vdn_minimax_h3_b200.inference.engine import (InferenceEngine, fused_qk_ok,
+                                                   linear_branch_core)
 from vdn_minimax_h3_b200.ops import attention as attn_ops
 from vdn_minimax_h3_b200.ops import gemm
 from vdn_minimax_h3_b200.ops import norm as norm_ops
@@ -90,14 +92,29 @@ def init_ulysses(profile=False):
 
 
 class UlyssesEngine:
-    """Sequence-parallel forward over an InferenceEngine's packed weights (one rank)."""
+    """Sequence-parallel forward over an InferenceEngine's packed weights (one rank).
+
+    Per block the QKV projection runs on this rank's rows through the routed GEMM, whose
+    epilogue writes every field straight into the seq->heads exchange layout [P, C, W]
+    (per destination rank p: q, k normalised + rotated, v, q_raw, k_raw for p's heads, then
+    the softmax-gate and beta logits of all heads and the output gate's low-rank hidden,
+    both replicated to every destination). With exchange="nccl" that is the local send
+    buffer of an all_to_all_single; with exchange="p2p" it is rank p's receive buffer in
+    symmetric memory, so the all-to-all happens inside the GEMM. Attention and the linear
+    readout then compute this rank's heads over the whole sequence; with "p2p" their
+    epilogues store each output row into its owner's O-projection input (row scatter),
+    otherwise a second all_to_all_single brings them back."""
 
     def __init__(self, engine: InferenceEngine, runtime: UlyssesRuntime, exchange="nccl"):
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange must be 'nccl' or 'p2p', got {exchange!r}")
         self.engine = engine
         self.model = engine.model
         self.rt = runtime
         self.exchange = exchange
         self._bufs = {}
+        self._routes = {}
+        self.heap = None
 
     def _buf(self, name, shape, dtype, device):
         b = self._bufs.get(name)
@@ -105,6 +122,69 @@ class UlyssesEngine:
             b = torch.empty(shape, dtype=dtype, device=device)
             self._bufs[name] = b
         return b
+
+    # -------------------------------------------------------------- exchange layout
+    def _fields(self, pb):
+        """Ordered (name, width) of one destination's slab row; every width a multiple of 8."""
+        c = pb.cols
+        Hp, d = self.rt.heads_per_rank, pb.head_dim
+        pad8 = lambda n: (n + 7) // 8 * 8  # noqa: E731
+        f = [("q", Hp * d), ("k", Hp * d), ("v", Hp * d), ("q_raw", Hp * d), ("k_raw", Hp * d)]
+        if pb.has_sgate:
+            f.append(("sgate", pad8(c["sgate"][1] - c["sgate"][0])))
+        if "beta" in c:
+            f.append(("beta", pad8(c["beta"][1] - c["beta"][0])))
+        if "ghid" in c:
+            f.append(("ghid", pad8(c["ghid"][1] - c["ghid"][0])))
+        offs, o = {}, 0
+        for name, w in f:
+            offs[name] = (o, w)
+            o += w
+        return offs, o
+
+    def _route(self, pb, slabs, offs):
+        """ColumnRoute of the QKV GEMM into per-destination slabs ([rows, W] views)."""
+        c = pb.cols
+        P = self.rt.world_size
+        Hp, d = self.rt.heads_per_rank, pb.head_dim
+        hw = Hp * d
+        route = gemm.ColumnRoute(pb.w_qkvg.shape[0], planes=max(2, P))
+        for p, slab in enumerate(slabs):
+            fv = lambda name: slab[:, offs[name][0]:offs[name][0] + offs[name][1]]  # noqa: E731
+            route.place(c["q"][0] + p * hw, fv("q_raw"), plane=0)
+            route.place(c["q"][0] + p * hw, fv("q"), plane=1)
+            route.place(c["k"][0] + p * hw, fv("k_raw"), plane=0)
+            route.place(c["k"][0] + p * hw, fv("k"), plane=1)
+            route.place(c["v"][0] + p * hw, fv("v"), plane=0)
+            for name in ("sgate", "beta", "ghid"):
+                if name in offs:
+                    lo, hi = c[name]
+                    width = (hi - lo + 7) // 8 * 8
+                    route.place(lo, slab[:, offs[name][0]:offs[name][0] + width], plane=p)
+        return route
+
+    def _ensure_heap(self, dev, C, W, kcat, dtype):
+        key = (C, W, kcat, dtype)
+        if self.heap is not None and self._heap_key == key:
+            return
+        if self.heap is not None:
+            self.heap.close()
+        from vdn_minimax_h3_b200.parallel.symmetric import SymmetricHeap
+        P = self.rt.world_size
+        specs = [((P, C, W), dtype), ((C, kcat), dtype)]
+        self.heap = SymmetricHeap(SymmetricHeap.required_bytes(specs), self.rt.group, dev)
+        self.heap.alloc("recv", (P, C, W), dtype)
+        self.heap.alloc("cat", (C, kcat), dtype)
+        self._heap_key = key
+        self._routes.clear()
+
+    def close(self):
+        if self.heap is not None:
+            self.heap.barrier()
+            torch.cuda.synchronize()
+            self.heap.check()
+            self.heap.close()
+            self.heap = None
 
     # ----------------------------------------------------------------------- block
     def block_forward(self, i, x, temb_act, adaln_idx, rope, layout):
@@ -120,7 +200,9 @@ class UlyssesEngine:
         D = x.shape[1]
         H, d = pb.heads, pb.head_dim
         Hp = rt.heads_per_rank
+        hw = Hp * d
         dev = x.device
+        p2p = self.exchange == "p2p"
         hybrid_on = pb.hybrid and not attn.teacher_mode and layout is not None
         plan = eng._plans(attn if hybrid_on else None, layout, T)
         linear_on = hybrid_on and attn.linear_attention_enabled and not eng.covered
@@ -134,70 +216,96 @@ class UlyssesEngine:
             fsum = norm_ops.frame_sums(n1, layout.num_frames, layout.tokens_per_frame, a0,
                                        layout.video_start)
             work = rt.all_reduce(fsum, async_op=True)
-        qkvg = self._buf("qkvg", (rows, pb.w_qkvg.shape[0]), x.dtype, dev)
-        with sec("gemm_qkv"):
-            gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
         c = pb.cols
         cos, sin = rope
-        # ---- seq -> heads: pack [P, C, W] (q, k, v, q_raw, k_raw, sgate, beta, ghid per rank)
-        rank_h = (c["ghid"][1] - c["ghid"][0]) if "ghid" in c else 0
-        pad8 = lambda n: (n + 7) // 8 * 8  # noqa: E731  (every field 16-byte aligned)
-        fields = [Hp * d] * 5 + [Hp if pb.has_sgate else 0, Hp if "beta" in c else 0, rank_h]
-        widths = [pad8(w) for w in fields]
-        W = sum(widths)
-        send = self._buf("send", (P, C, W), x.dtype, dev)
-        with sec("qk_prep+pack"):
-            q = self._buf("q", (rows, H * d), x.dtype, dev)
-            k = self._buf("k", (rows, H * d), x.dtype, dev)
-            norm_ops.qk_prep(qkvg[:, c["q"][0]:c["q"][1]], H, pb.norm_q, pb.qk_eps, cos, sin, out=q)
-            norm_ops.qk_prep(qkvg[:, c["k"][0]:c["k"][1]], H, pb.norm_k, pb.qk_eps, cos, sin, out=k)
-            sv = send[:, :rows]
-            hv = lambda t, w: t.view(rows, P, w).transpose(0, 1)  # noqa: E731
-            srcs = [q, k, qkvg[:, c["v"][0]:c["v"][1]], qkvg[:, c["q"][0]:c["q"][1]],
-                    qkvg[:, c["k"][0]:c["k"][1]]]
-            srcs.append(qkvg[:, c["sgate"][0]:c["sgate"][1]] if pb.has_sgate else None)
-            srcs.append(qkvg[:, c["beta"][0]:c["beta"][1]] if "beta" in c else None)
-            off = 0
-            for src, w, wp in zip(srcs, fields[:7], widths[:7]):
-                if src is not None and w:
-                    sv[:, :, off:off + w].copy_(hv(src, w))
-                off += wp
-            if rank_h:
-                sv[:, :, off:off + rank_h].copy_(
-                    qkvg[:, c["ghid"][0]:c["ghid"][1]].unsqueeze(0).expand(P, rows, rank_h))
-        recv = self._buf("recv", (P, C, W), x.dtype, dev)
+        offs, W = self._fields(pb)
+        kcat_max = 2 * H * d
+        # ---- seq -> heads, fused into the QKV GEMM epilogue
+        if p2p:
+            self._ensure_heap(dev, C, W, kcat_max, x.dtype)
+            recv = self.heap.local("recv")
+            key = ("p2p", tuple(sorted(c.items())), rows)
+            route = self._routes.get(key)
+            if route is None:
+                slabs = [self.heap.peer("recv", p)[r, :rows] for p in range(P)]
+                route = self._routes[key] = self._route(pb, slabs, offs)
+        else:
+            send = self._buf("send", (P, C, W), x.dtype, dev)
+            recv = self._buf("recv", (P, C, W), x.dtype, dev)
+            key = ("nccl", send.data_ptr(), tuple(sorted(c.items())), rows)
+            route = self._routes.get(key)
+            if route is None:
+                route = self._routes[key] = self._route(pb, [send[p, :rows] for p in range(P)], offs)
+        with sec("gemm_qkv"):
+            if x.is_cuda and not fused_qk_ok(pb, cos):
+                # heads other than 128 wide: projection, then QK-prep, then the placement
+                qkvg = self._buf("qkvg", (rows, pb.w_qkvg.shape[0]), x.dtype, dev)
+                gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
+                proc = []
+                for name, w in (("q", pb.norm_q), ("k", pb.norm_k)):
+                    lo, hi = c[name]
+                    proc.append((lo, norm_ops.qk_prep(qkvg[:, lo:hi], H, w, pb.qk_eps, cos, sin)))
+                route.copy_from(qkvg, proc)
+            else:
+                gemm.linear_routed(n1, pb.w_qkvg, pb.b_qkvg, route, c["q"], c["k"], pb.norm_q,
+                                   pb.norm_k, pb.qk_eps, cos, sin)
         with sec("a2a_dispatch"):
-            rt.all_to_all(recv.view(-1), send.view(-1))
+            if p2p:
+                self.heap.barrier()
+            else:
+                rt.all_to_all(recv.view(-1), send.view(-1))
         full = recv.view(P * C, W)[:T]
-        off = 0
-        views = []
-        for w, wp in zip(fields, widths):
-            views.append(full[:, off:off + w])
-            off += wp
-        q_h, k_h, v_h, qr_h, kr_h, sg_h, bt_h, gh_h = views
-        ret = self._buf("ret", (P * C, 2 * Hp * d), x.dtype, dev)
+        fv = lambda name, a=0, n=None: full[:, offs[name][0] + a:offs[name][0] + a + (  # noqa: E731
+            offs[name][1] if n is None else n)]
+        q_h, k_h, v_h = fv("q"), fv("k"), fv("v")
+        qr_h, kr_h = fv("q_raw"), fv("k_raw")
+        sg_h = fv("sgate", r * Hp, Hp) if pb.has_sgate else None
+        bt_h = fv("beta", r * Hp, Hp) if "beta" in offs else None
+        gh_h = fv("ghid", 0, c["ghid"][1] - c["ghid"][0]) if "ghid" in offs else None
+        if p2p:
+            cat_peers = [self.heap.peer("cat", p) for p in range(P)]
+            cat_local = self.heap.local("cat")
+            scat = lambda col, row0: ([t.data_ptr() + 2 * col for t in cat_peers], row0, C)  # noqa: E731
+            attn_out = cat_local[:, r * hw:(r + 1) * hw]
+            attn_scatter = scat(r * hw, 0)
+        else:
+            ret = self._buf("ret", (P * C, 2 * hw), x.dtype, dev)
+            attn_out = ret[:T, :hw]
+            attn_scatter = None
         with sec("attention"):
             attn_ops.window_attention(q_h.view(T, Hp, d), k_h.view(T, Hp, d), v_h.view(T, Hp, d),
-                                      plan, d ** -0.5, gate_logits=sg_h if pb.has_sgate else None,
-                                      out=ret[:T, :Hp * d])
+                                      plan, d ** -0.5, gate_logits=sg_h, out=attn_out,
+                                      scatter=attn_scatter)
         if pb.hybrid:
-            ret[:T, Hp * d:].zero_()
             if linear_on:
                 work.wait()
+                lin_out = cat_local[:, H * d + r * hw:H * d + (r + 1) * hw] if p2p else ret[:T, hw:]
+                if not p2p:
+                    lin_out.zero_()
                 with sec("linear_branch"):
                     linear_branch_core(pb, attn, layout, eng.bounds, qr_h.view(T, Hp, d),
                                        kr_h.view(T, Hp, d), v_h.view(T, Hp, d), bt_h, gh_h, fsum,
-                                       slice(r * Hp, (r + 1) * Hp), ret[:T, Hp * d:], x.dtype)
-        # ---- heads -> seq
-        back = self._buf("back", (P, C, 2 * Hp * d), x.dtype, dev)
-        with sec("a2a_return"):
-            rt.all_to_all(back.view(-1), ret.view(-1))
+                                       slice(r * Hp, (r + 1) * Hp), lin_out, x.dtype,
+                                       scatter=scat(H * d + r * hw, None) if p2p else None)
+            elif p2p:
+                cat_local[:rows, H * d:].zero_()
+            else:
+                ret[:T, hw:].zero_()
         kcat = pb.w_o.shape[1]
-        cat = self._buf("cat", (rows, kcat), x.dtype, dev)
-        with sec("unpack"):
-            nb = 2 if pb.hybrid else 1
-            src = back[:, :rows].unflatten(-1, (2, Hp, d))[:, :, :nb]
-            cat.view(rows, nb, P, Hp, d).copy_(src.permute(1, 2, 0, 3, 4))
+        # ---- heads -> seq
+        if p2p:
+            with sec("a2a_return"):
+                self.heap.barrier()
+            cat = cat_local[:rows, :kcat]
+        else:
+            back = self._buf("back", (P, C, 2 * hw), x.dtype, dev)
+            with sec("a2a_return"):
+                rt.all_to_all(back.view(-1), ret.view(-1))
+            cat = self._buf("cat", (rows, kcat), x.dtype, dev)
+            with sec("unpack"):
+                nb = 2 if pb.hybrid else 1
+                src = back[:, :rows].unflatten(-1, (2, Hp, d))[:, :, :nb]
+                cat.view(rows, nb, P, Hp, d).copy_(src.permute(1, 2, 0, 3, 4))
         with sec("gemm_o"):
             gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D], adaln_idx)
         n2 = n1
