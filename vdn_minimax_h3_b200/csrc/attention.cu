@@ -7,15 +7,16 @@
 // the [T, H, d] projections -- no gather, no mask tensor; only the ragged tail of a range
 // is masked.
 //
-// Roles (320 threads, one CTA per SM, persistent over head-major work items so the CTAs in
-// flight share one head's K/V in L2):
+// Roles (384 threads = 3 warpgroups, one CTA per SM, persistent over head-major work items
+// so the CTAs in flight share one head's K/V in L2):
 //   warp 0      TMA producers: lane 0 both Q tiles once per item and K blocks into a
 //               2-stage ring, lane 1 V blocks (single buffer, refilled while the softmax
 //               of the block runs).
 //   warp 1      MMA issuer (one thread): per block, S_t = Q_t K^T for both tiles into TMEM
 //               (kind::f16, M=128, N=128), then O_t += P_t V for the previous block (P from
 //               shared memory, V as an MN-major operand).
-//   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1 (thread = query row): S row
+//   warps 2-3   idle (they complete warpgroup 0, whose registers go to the softmax)
+//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1 (thread = query row): S row
 //               from TMEM, online softmax in the exp2 domain with a lazy rescale (O in TMEM
 //               is rescaled only when the running max grows by more than 2^8), P written as
 //               bf16 into the 128B-swizzled shared operand, epilogue O / l * sigmoid(gate).
@@ -33,6 +34,8 @@
 #include "launchers.h"
 #include "tma.cuh"
 
+#include <stdexcept>
+
 namespace vdn {
 
 constexpr int AT_BM = 128;                         // query rows per tile (2 tiles per item)
@@ -42,7 +45,12 @@ constexpr int AT_KSTAGES = 2;                      // K ring; V is single-buffer
 constexpr int AT_Q_BYTES = AT_BM * AT_D * 2;       // 32 KB per Q tile (2 atoms of 16 KB)
 constexpr int AT_KV_BYTES = AT_BN * AT_D * 2;      // 32 KB per K or V block (2 atoms of 16 KB)
 constexpr int AT_P_BYTES = AT_BM * AT_BN * 2;      // 32 KB per P tile (2 atom columns)
-constexpr int AT_THREADS = 320;
+constexpr int AT_THREADS = 384;
+// Register split after launch (384 threads x 168): warpgroup 0 (producer, MMA, two idle
+// warps) drops to 80, the two softmax warpgroups rise to 208: 128*80 + 256*208 <= 384*168.
+constexpr int AT_REGS_LOW = 80;
+constexpr int AT_REGS_HIGH = 208;
+static_assert(128 * AT_REGS_LOW + 256 * AT_REGS_HIGH <= AT_THREADS * 168, "register split");
 constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + 1) * AT_KV_BYTES + 2 * AT_P_BYTES + 1024 + 384;
 constexpr int AT_MAX_RANGES = 4;
 // One exponential in every 8 * POLY_EVERY runs on the FMA pipe (0: all on MUFU); the
@@ -181,6 +189,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // The register re-split sits inside each role's branch, so every role's code is
+  // dominated by exactly one limit.
+  if (warp < 4) {
+  setmaxnreg_dec<AT_REGS_LOW>();
   if (warp == 0) {
     // --------------------------------------------- TMA producers: lane 0 Q + K, lane 1 V
     if (lane == 0) {
@@ -356,9 +368,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       while (!mbar_try_wait(mma_done, 0) && clock64() - t0 < kWaitBudgetCycles) {
       }
     }
+  }
   } else {
     // ------------------------------------------------------- softmax + epilogue warps
-    const int qt = (warp - 2) >> 2;           // which query tile
+    setmaxnreg_inc<AT_REGS_HIGH>();
+    const int qt = (warp - 4) >> 2;           // which query tile
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;        // row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -513,6 +527,16 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
     cudaFuncSetAttribute(window_attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
     cudaFuncSetAttribute(window_attention_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
     cudaFuncSetAttribute(window_attention_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
+    // setmaxnreg.inc waits until the registers it asks for are free: refuse to launch if
+    // the compiled launch register count cannot fund the split.
+    for (auto fn : {window_attention_kernel<0>, window_attention_kernel<1>,
+                    window_attention_kernel<2>, window_attention_kernel<4>}) {
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess ||
+          fa.numRegs * AT_THREADS < 128 * AT_REGS_LOW + 256 * AT_REGS_HIGH)
+        throw std::runtime_error("window attention: launch registers cannot fund the "
+                                 "warpgroup register split");
+    }
     attr = true;
   }
   const uint64_t cols = (uint64_t)H * AT_D;

@@ -268,4 +268,15 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Warpgroup register re-split (all four warps of a warpgroup execute it together). The sum
+// over warpgroups must stay within the registers the block was launched with.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N));
+}
+
 }  // namespace vdn
