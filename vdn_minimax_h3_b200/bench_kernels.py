@@ -55,6 +55,33 @@ def bench_gemm():
     return rows
 
 
+def bench_norm():
+    """AdaLN-RMSNorm, frame sums and QK-prep on the full packed sequence (HBM-bound)."""
+    from vdn_minimax_h3_b200.ops import norm
+    from vdn_minimax_h3_b200.models.h3 import RotaryEmbedding3D
+    T, D, F, S = M_ROWS, 5376, 102, 1008
+    x = torch.randn(T, D, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(x)
+    w = torch.rand(D, device="cuda") + 0.5
+    table = torch.randn(6, 6 * D, device="cuda", dtype=torch.bfloat16) * 0.1
+    idx = torch.randint(0, 6, (T,), device="cuda", dtype=torch.int32)
+    rows = []
+    ms = timed(lambda: norm.adaln_rmsnorm(x, w, 1e-6, table, 0, D, idx, out=out))
+    rows.append(dict(case="adaln_rmsnorm", ms=ms, gbps=2 * x.numel() * 2 / ms / 1e6))
+    ms = timed(lambda: norm.frame_sums(x, F, S, 0, T - F * S))
+    rows.append(dict(case="frame_sums", ms=ms, gbps=F * S * D * 2 / ms / 1e6))
+    pos = torch.stack([torch.arange(T) // 1008, (torch.arange(T) // 42) % 24, torch.arange(T) % 42], 1)
+    cos, sin = RotaryEmbedding3D((32, 48, 48))(pos.cuda())
+    src = torch.randn(T, 7168, device="cuda", dtype=torch.bfloat16)
+    qo = torch.empty_like(src)
+    nw = torch.rand(128, device="cuda") + 0.5
+    ms = timed(lambda: norm.qk_prep(src, 56, nw, 1e-6, cos, sin, out=qo))
+    rows.append(dict(case="qk_prep", ms=ms, gbps=2 * src.numel() * 2 / ms / 1e6))
+    for r in rows:
+        print(json.dumps(r), flush=True)
+    return rows
+
+
 def profile_small():
     """Single launches on small inputs, for a one-pass-per-kernel profiler capture."""
     from vdn_minimax_h3_b200.models.delta_rule import VdnDelta
@@ -89,6 +116,7 @@ def main(argv=None):
     p.add_argument("--gemm", action="store_true")
     p.add_argument("--attention", action="store_true")
     p.add_argument("--linear", action="store_true")
+    p.add_argument("--norm", action="store_true")
     p.add_argument("--profile-small", action="store_true",
                    help="one launch each of window attention, SPD inverse and conv features on "
                         "small inputs (an ncu-sized driver)")
@@ -105,6 +133,8 @@ def main(argv=None):
     if a.linear:
         from vdn_minimax_h3_b200.ops.linear_branch import bench_linear
         bench_linear(timed)
+    if a.norm:
+        bench_norm()
     if a.profile_small:
         profile_small()
     if a.attention_small:

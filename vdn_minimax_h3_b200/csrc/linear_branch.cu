@@ -53,34 +53,72 @@ void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, in
 // --------------------------------------------------------------- separable short conv
 // Block = (grid row y, head h, chunk of LB_FC frames); warp w owns positions 4w..4w+3 of the
 // row, lane owns 4 channels, so a warp covers the head's 128 channels and the L2 norm is a
-// warp reduction. Per frame and tap row, one 8-position input window (8 loads) feeds all
-// 20 (position, tap) products of the row; the five latest spatial results per output sit
-// in a register ring for the temporal taps. Frames are chunked (2-frame halo each side).
+// warp reduction. The five input rows y-2..y+2 of a frame (all positions, the head's 128
+// channels) are staged in shared memory by cp.async, double-buffered across frames so the
+// next frame's rows are in flight while this frame's 25 spatial taps run; rows and
+// positions outside the grid stay zero (the convolution's zero padding). The five latest
+// spatial results per output sit in a register ring for the temporal taps. Frames are
+// chunked (2-frame halo each side).
 constexpr int LB_FC = 16;
 constexpr int LB_PPW = 4;                 // positions per warp
 constexpr int LB_MAXW = 48;               // widest supported grid row
+constexpr int LB_XPAD = LB_MAXW + 4;      // staged positions per row (2 halo each side)
+constexpr int LB_ROW_BYTES = LB_XPAD * 256;        // one staged row: 128 bf16 per position
+constexpr int LB_STAGE_BYTES = 5 * LB_ROW_BYTES;   // five input rows of one frame
+constexpr int LB_CONV_SMEM = 2 * LB_STAGE_BYTES;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
 __global__ void __launch_bounds__(384) lb_conv_kernel(
     const __nv_bfloat16* __restrict__ in, int64_t ldi, const float* __restrict__ wsp,
     const float* __restrict__ wtm, __nv_bfloat16* __restrict__ out, int64_t ldo, int F, int gh,
     int gw, int H, int l2) {
+  extern __shared__ __align__(16) uint8_t lb_smem[];
   __shared__ __align__(16) float s_wsp[25][128];
   __shared__ __align__(16) float s_wtm[5][128];
   const int y = blockIdx.x, h = blockIdx.y;
   const int f0 = blockIdx.z * LB_FC;
   const int S = gh * gw;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < 25 * 128; i += blockDim.x) {
+  const int nthr = blockDim.x;
+  for (int i = tid; i < 25 * 128; i += nthr) {
     const int tap = i / 128, c = i % 128;
     s_wsp[tap][c] = wsp[(int64_t)(h * 128 + c) * 25 + tap];
   }
-  for (int i = tid; i < 5 * 128; i += blockDim.x) {
+  for (int i = tid; i < 5 * 128; i += nthr) {
     const int tap = i / 128, c = i % 128;
     s_wtm[tap][c] = wtm[(int64_t)(h * 128 + c) * 5 + tap];
   }
+  // zero both stages once: the halo positions and the rows outside the grid are never written
+  for (int i = tid; i < LB_CONV_SMEM / 16; i += nthr)
+    reinterpret_cast<uint4*>(lb_smem)[i] = make_uint4(0, 0, 0, 0);
   __syncthreads();
+  const int f_end = min(F, f0 + LB_FC);
+  const int f_first = max(f0 - 2, 0), f_last = min(f_end + 2, F);  // frames with input
+  const int per_frame = 5 * gw * 16;                                 // 16-byte chunks
+  auto load_frame = [&](int f, int stage) {
+    uint8_t* base = lb_smem + stage * LB_STAGE_BYTES;
+    for (int idx = tid; idx < per_frame; idx += nthr) {
+      const int chunk = idx & 15;
+      const int pos = (idx >> 4) % gw;
+      const int i = (idx >> 4) / gw;
+      const int yy = y + i - 2;
+      if (yy < 0 || yy >= gh) continue;
+      const __nv_bfloat16* src =
+          in + ((int64_t)f * S + (int64_t)yy * gw + pos) * ldi + (int64_t)h * 128 + chunk * 8;
+      cp_async16(base + i * LB_ROW_BYTES + (pos + 2) * 256 + chunk * 16, src);
+    }
+  };
+  if (f_first < f_last) load_frame(f_first, f_first & 1);
+  cp_async_commit();
+
   const int x0 = warp * LB_PPW;
-  if (x0 >= gw) return;
+  const bool active = x0 < gw;
   const int c0 = lane * 4;
   const int64_t chan = (int64_t)h * 128 + c0;
   float ring[5][LB_PPW][4];
@@ -90,40 +128,39 @@ __global__ void __launch_bounds__(384) lb_conv_kernel(
     for (int q = 0; q < LB_PPW; ++q)
 #pragma unroll
       for (int b = 0; b < 4; ++b) ring[a][q][b] = 0.f;
-  const float4 t0 = *reinterpret_cast<const float4*>(&s_wtm[0][c0]);
-  const float4 t1 = *reinterpret_cast<const float4*>(&s_wtm[1][c0]);
-  const float4 t2 = *reinterpret_cast<const float4*>(&s_wtm[2][c0]);
-  const float4 t3 = *reinterpret_cast<const float4*>(&s_wtm[3][c0]);
-  const float4 t4 = *reinterpret_cast<const float4*>(&s_wtm[4][c0]);
-  const float tw[5][4] = {{t0.x, t0.y, t0.z, t0.w}, {t1.x, t1.y, t1.z, t1.w},
-                          {t2.x, t2.y, t2.z, t2.w}, {t3.x, t3.y, t3.z, t3.w},
-                          {t4.x, t4.y, t4.z, t4.w}};
-  const int f_end = min(F, f0 + LB_FC);
+  float tw[5][4];
+#pragma unroll
+  for (int dt = 0; dt < 5; ++dt) {
+    const float4 t = *reinterpret_cast<const float4*>(&s_wtm[dt][c0]);
+    tw[dt][0] = t.x;
+    tw[dt][1] = t.y;
+    tw[dt][2] = t.z;
+    tw[dt][3] = t.w;
+  }
   for (int f = f0 - 2; f < f_end + 2; ++f) {
+    const bool have = f >= f_first && f < f_last;
+    // prefetch the next frame into the other stage, then wait for this frame's rows
+    if (f + 1 >= f_first && f + 1 < f_last) load_frame(f + 1, (f + 1) & 1);
+    cp_async_commit();
+    cp_async_wait1();
+    __syncthreads();
     float sp[LB_PPW][4];
 #pragma unroll
     for (int q = 0; q < LB_PPW; ++q)
 #pragma unroll
       for (int b = 0; b < 4; ++b) sp[q][b] = 0.f;
-    if (f >= 0 && f < F) {
+    if (have && active) {
+      const uint8_t* base = lb_smem + (f & 1) * LB_STAGE_BYTES + c0 * 2;
 #pragma unroll
       for (int i = 0; i < 5; ++i) {
-        const int yy = y + i - 2;
-        if (yy < 0 || yy >= gh) continue;
-        const __nv_bfloat16* rowp = in + ((int64_t)f * S + (int64_t)yy * gw) * ldi + chan;
         float win[LB_PPW + 4][4];
 #pragma unroll
         for (int u = 0; u < LB_PPW + 4; ++u) {
-          const int xx = x0 + u - 2;
-          if (xx >= 0 && xx < gw) {
-            const uint2 v = *reinterpret_cast<const uint2*>(rowp + (int64_t)xx * ldi);
-            win[u][0] = bf16_lo(v.x);
-            win[u][1] = bf16_hi(v.x);
-            win[u][2] = bf16_lo(v.y);
-            win[u][3] = bf16_hi(v.y);
-          } else {
-            win[u][0] = win[u][1] = win[u][2] = win[u][3] = 0.f;
-          }
+          const uint2 v = *reinterpret_cast<const uint2*>(base + i * LB_ROW_BYTES + (x0 + u) * 256);
+          win[u][0] = bf16_lo(v.x);
+          win[u][1] = bf16_hi(v.x);
+          win[u][2] = bf16_lo(v.y);
+          win[u][3] = bf16_hi(v.y);
         }
 #pragma unroll
         for (int j = 0; j < 5; ++j) {
@@ -138,6 +175,7 @@ __global__ void __launch_bounds__(384) lb_conv_kernel(
         }
       }
     }
+    __syncthreads();  // this stage is refilled two frames from now
 #pragma unroll
     for (int q = 0; q < LB_PPW; ++q)
 #pragma unroll
@@ -149,7 +187,7 @@ __global__ void __launch_bounds__(384) lb_conv_kernel(
         ring[4][q][b] = sp[q][b];
       }
     const int fo = f - 2;
-    if (fo < f0) continue;
+    if (fo < f0 || !active) continue;
 #pragma unroll
     for (int q = 0; q < LB_PPW; ++q) {
       const int x = x0 + q;
@@ -178,9 +216,14 @@ void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* 
                     int64_t ldo, int F, int gh, int gw, int H, int l2, cudaStream_t stream) {
   if (!F || !gh || !gw) return;
   if (gw > LB_MAXW) throw std::runtime_error("short conv: grid width above 48 is not supported");
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(lb_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LB_CONV_SMEM);
+    attr = true;
+  }
   const int warps = (gw + LB_PPW - 1) / LB_PPW;
   dim3 grid(gh, H, (F + LB_FC - 1) / LB_FC);
-  lb_conv_kernel<<<grid, warps * 32, 0, stream>>>(
+  lb_conv_kernel<<<grid, warps * 32, LB_CONV_SMEM, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(in), ldi, wsp, wtm,
       reinterpret_cast<__nv_bfloat16*>(out), ldo, F, gh, gw, H, l2);
 }

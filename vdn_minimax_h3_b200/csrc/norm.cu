@@ -52,11 +52,16 @@ __global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
       const uint32_t* shu = reinterpret_cast<const uint32_t*>(&sh);
       const uint32_t* scu = reinterpret_cast<const uint32_t*>(&sc);
       uint32_t res[4];
+      float wv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+      if (w) {
+        const float4 wa = __ldg(reinterpret_cast<const float4*>(w + c * 8));
+        const float4 wb = __ldg(reinterpret_cast<const float4*>(w + c * 8 + 4));
+        wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
+        wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int col = c * 8 + 2 * j;
-        float w0 = w ? w[col] : 1.f, w1 = w ? w[col + 1] : 1.f;
-        float a = bf16_lo(u[j]) * rstd * w0, b = bf16_hi(u[j]) * rstd * w1;
+        float a = bf16_lo(u[j]) * rstd * wv[2 * j], b = bf16_hi(u[j]) * rstd * wv[2 * j + 1];
         a = a * (1.f + bf16_lo(scu[j])) + bf16_lo(shu[j]);
         b = b * (1.f + bf16_hi(scu[j])) + bf16_hi(shu[j]);
         res[j] = pack_bf16(a, b);

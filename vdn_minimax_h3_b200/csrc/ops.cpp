@@ -159,7 +159,9 @@ void adaln_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, 
   TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.is_contiguous() &&
                   idx.numel() >= T, "idx must be contiguous int32 [T]");
   c10::cuda::CUDAGuard g(x.device());
-  launch_adaln_rmsnorm(x.data_ptr(), x.stride(0), opt_f32(w, D, "w"), (float)eps, table.data_ptr(),
+  const float* wp = opt_f32(w, D, "w");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(wp) % 16 == 0, "norm weight must be 16-byte aligned");
+  launch_adaln_rmsnorm(x.data_ptr(), x.stride(0), wp, (float)eps, table.data_ptr(),
                        table.stride(0), (int)shift_col, (int)scale_col, idx.data_ptr<int>(),
                        out.data_ptr(), out.stride(0), T, D, at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
