@@ -279,4 +279,84 @@ __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N));
 }
 
+// ---------------------------------------------------------------- block-scaled fp8
+// Untiled bulk copy global -> shared (no multicast), completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// kind::mxf8f6f4 with per-32-element UE8M0 scale factors read from TMEM (scale_vec::1X).
+__device__ __forceinline__ void umma_mxf8_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t tsfa, uint32_t tsfb,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
+      : "memory");
+}
+
+// Shared -> TMEM copy of 32 rows x 128 bits, broadcast to the four lane quarters.
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// Shared-memory descriptor of an unswizzled K-major block of 16-byte rows (8-row core
+// matrices 128 B apart): the source of the scale-factor copies.
+__device__ __forceinline__ uint64_t umma_desc_interleave_rows16(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);
+  d |= (uint64_t)(128 >> 4) << 16;          // LBO (a single 16-byte column is read)
+  d |= (uint64_t)(128 >> 4) << 32;          // SBO: next 8-row core matrix
+  d |= (uint64_t)1 << 46;                   // descriptor version (sm100)
+  return d;                                 // layout type 0: no swizzle
+}
+
+// Instruction descriptor, kind::mxf8f6f4 block-scaled: E4M3 x E4M3, UE8M0 scales, both
+// K-major; `sf_id` selects the byte (32-element K block) within each scale-factor word.
+__host__ __device__ constexpr uint32_t umma_idesc_mxf8(int M, int N, int sf_id) {
+  return ((uint32_t)sf_id << 4)             // B scale-factor id
+         | (0u << 7) | (0u << 10)           // A, B: E4M3
+         | ((uint32_t)(N >> 3) << 17)       // N
+         | (1u << 23)                       // scale format: UE8M0
+         | ((uint32_t)(M >> 4) << 24)       // M
+         | ((uint32_t)sf_id << 29);         // A scale-factor id
+}
+
+// Power-of-two scale for a block with absolute maximum `amax`: the smallest e with
+// amax / 2^e <= 448 (the largest finite E4M3). Returns e in [-127, 127]; read from the
+// IEEE-754 fields of amax / 448 (ceil(log2 v) = exponent, +1 unless v is a power of 2).
+__device__ __forceinline__ int e8_exponent(float amax) {
+  const float v = amax * (1.0f / 448.0f);
+  const uint32_t b = __float_as_uint(v);
+  const int E = (int)((b >> 23) & 0xFF);
+  if (E == 0) return -127;                  // zero or subnormal: the smallest scale
+  int e = E - 127 + ((b & 0x7FFFFF) ? 1 : 0);
+  return e > 127 ? 127 : e;
+}
+__device__ __forceinline__ float exp2_int(int e) {   // 2^e for e in [-126, 127]
+  return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+// Two floats -> two E4M3 bytes (round to nearest even, saturating).
+__device__ __forceinline__ uint16_t pack_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Byte offset of the scale factor of (row r, 32-element K block kb) in the blocked layout
+// the MMA's scale-factor copies read: 128-row x 4-block atoms of 512 B, row-major over
+// (r / 128, kb / 4); inside an atom byte (r % 32) * 16 + (r % 128 / 32) * 4 + kb % 4.
+__host__ __device__ __forceinline__ int64_t sf_offset(int64_t r, int64_t kb, int64_t kb_total) {
+  return ((r >> 7) * (kb_total >> 2) + (kb >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 +
+         (kb & 3);
+}
+
 }  // namespace vdn

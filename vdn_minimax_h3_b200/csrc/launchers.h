@@ -62,6 +62,23 @@ struct GemmRoute {
 void launch_gemm_bf16_routed(const GemmArgs& a, const GemmRoute& r, const float* bias, int* err,
                              cudaStream_t stream);
 
+// Block-scaled fp8 GEMM (gemm_fp8.cu). A [M, K], B [N, K] E4M3 with row strides in bytes;
+// sfa / sfb the blocked UE8M0 scale factors (A per 128 rows, B per 256-row tile).
+struct GemmFp8Args {
+  const void* A;
+  const void* B;
+  int64_t lda, ldb;
+  const void* sfa;
+  const void* sfb;
+  int M, N, K;
+};
+// mode: 0 store bf16, 1 gated residual, 2 swiglu -> E4M3 + scale factors
+void launch_gemm_fp8(const GemmFp8Args& a, int mode, void* out, int64_t ldo, const float* bias,
+                     const void* gate, int64_t ldg, const int* gate_idx, void* q_out, int64_t ldq,
+                     void* q_sf, int* err, cudaStream_t stream);
+void launch_quant_rows(const void* x, int64_t ldx, int M, int K, void* q, int64_t ldq, void* sf,
+                       cudaStream_t stream);
+
 void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps, const void* table,
                           int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
                           int64_t ldo, int T, int D, cudaStream_t stream);

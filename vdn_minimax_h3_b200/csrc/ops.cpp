@@ -146,6 +146,90 @@ void gemm_bf16_routed(torch::Tensor A, torch::Tensor B, c10::optional<torch::Ten
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+namespace {
+void check_2d_bytes(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.element_size() == 1 && t.dim() == 2 && t.stride(1) == 1, name,
+              " must be a 2-D one-byte (E4M3) CUDA tensor with contiguous rows");
+  TORCH_CHECK(t.stride(0) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
+              " rows must be 16-byte aligned");
+}
+void check_sf(const torch::Tensor& t, int64_t nbytes, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.element_size() == 1 && t.is_contiguous() && t.numel() >= nbytes &&
+                  reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              name, " must be a contiguous 16-byte aligned byte tensor of >= ", nbytes, " bytes");
+}
+}  // namespace
+
+void gemm_fp8(torch::Tensor A, torch::Tensor B, torch::Tensor sfa, torch::Tensor sfb, int64_t mode,
+              c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> bias,
+              c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> gate_idx,
+              c10::optional<torch::Tensor> q_out, c10::optional<torch::Tensor> q_sf,
+              torch::Tensor err) {
+  check_2d_bytes(A, "A");
+  check_2d_bytes(B, "B");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K, "K mismatch");
+  TORCH_CHECK(K % 128 == 0 && N % 32 == 0, "fp8 GEMM needs K % 128 == 0 and N % 32 == 0");
+  check_sf(sfa, ((M + 127) / 128) * (K / 128) * 512, "sfa");
+  check_sf(sfb, ((N + 255) / 256) * (K / 128) * 1024, "sfb");
+  GemmFp8Args a{A.data_ptr(), B.data_ptr(), A.stride(0), B.stride(0), sfa.data_ptr(),
+                sfb.data_ptr(), (int)M, (int)N, (int)K};
+  void* op = nullptr;
+  int64_t ldo = 0;
+  const void* gp = nullptr;
+  int64_t ldg = 0;
+  const int* gi = nullptr;
+  void* qp = nullptr;
+  int64_t ldq = 0;
+  void* qs = nullptr;
+  if (mode == 0 || mode == 1) {
+    TORCH_CHECK(out.has_value(), "out required");
+    check_2d_bf16(*out, "out");
+    TORCH_CHECK(out->size(0) == M && out->size(1) == N, "out shape mismatch");
+    op = out->data_ptr();
+    ldo = out->stride(0);
+    if (mode == 1) {
+      TORCH_CHECK(gate && gate_idx, "residual epilogue needs gate and gate_idx");
+      check_2d_bf16(*gate, "gate");
+      TORCH_CHECK(gate->size(1) >= N, "gate table narrower than N");
+      TORCH_CHECK(gate_idx->is_cuda() && gate_idx->scalar_type() == at::kInt &&
+                      gate_idx->is_contiguous() && gate_idx->numel() >= M,
+                  "gate_idx must be contiguous int32 [M]");
+      gp = gate->data_ptr();
+      ldg = gate->stride(0);
+      gi = gate_idx->data_ptr<int>();
+    }
+  } else if (mode == 2) {
+    TORCH_CHECK(N % 256 == 0, "swiglu fp8 GEMM needs N % 256 == 0");
+    TORCH_CHECK(q_out && q_sf, "swiglu fp8 GEMM needs q_out and q_sf");
+    check_2d_bytes(*q_out, "q_out");
+    TORCH_CHECK(q_out->size(0) == M && q_out->size(1) == N / 2, "q_out shape mismatch");
+    check_sf(*q_sf, ((M + 127) / 128) * ((N / 2) / 128) * 512, "q_sf");
+    qp = q_out->data_ptr();
+    ldq = q_out->stride(0);
+    qs = q_sf->data_ptr();
+  } else {
+    TORCH_CHECK(false, "unknown fp8 GEMM mode ", mode);
+  }
+  c10::cuda::CUDAGuard g(A.device());
+  launch_gemm_fp8(a, (int)mode, op, ldo, opt_f32(bias, N, "bias"), gp, ldg, gi, qp, ldq, qs,
+                  err_ptr(err), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf) {
+  check_2d_bf16(x, "x");
+  check_2d_bytes(q, "q");
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(q.size(0) == M && q.size(1) == K, "q shape mismatch");
+  TORCH_CHECK(K % 256 == 0, "quantiser needs K % 256 == 0");
+  check_sf(sf, ((M + 127) / 128) * (K / 128) * 512, "sf");
+  c10::cuda::CUDAGuard g(x.device());
+  launch_quant_rows(x.data_ptr(), x.stride(0), (int)M, (int)K, q.data_ptr(), q.stride(0),
+                    sf.data_ptr(), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void adaln_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, torch::Tensor table,
                    int64_t shift_col, int64_t scale_col, torch::Tensor idx, torch::Tensor out) {
   check_2d_bf16(x, "x");
@@ -485,6 +569,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_routed", &vdn::gemm_bf16_routed,
         "bf16 tcgen05 GEMM whose epilogue scatters 8-column groups through a route table and "
         "applies QK RMSNorm + RoPE to the q/k heads");
+  m.def("gemm_fp8", &vdn::gemm_fp8,
+        "block-scaled E4M3 tcgen05 GEMM (UE8M0 scale factors in TMEM); epilogue modes 0 store, "
+        "1 gated residual, 2 swiglu -> E4M3 + scale factors");
+  m.def("quant_rows", &vdn::quant_rows, "bf16 rows -> E4M3 with one UE8M0 scale per 1x128 block");
   m.def("adaln_rmsnorm", &vdn::adaln_rmsnorm, "RMSNorm * w * (1 + scale[idx]) + shift[idx]");
   m.def("frame_sums", &vdn::frame_sums, "per-frame fp32 column sums of video rows");
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");
