@@ -73,3 +73,34 @@ def test_gemm_fp8_swiglu_quant():
     y = (fp8.dequantize(xq, xsf, 128) @ fw.dequantized().t()).view(M, 2 * I // 128, 2, 64)
     ref = (y[:, :, 0] * torch.nn.functional.silu(y[:, :, 1])).reshape(M, I)
     assert _rel(h, ref) < 0.05
+
+
+def test_engine_fp8_close_to_bf16():
+    """The fp8 engine (QKV, FF-up, FF-down on the block-scaled GEMM) stays close to the bf16
+    engine on a reduced hybrid geometry with 128-wide heads."""
+    import copy
+    from tests.test_model_cpu import _forward_inputs, tiny_model
+    from vdn_minimax_h3_b200.inference.engine import InferenceEngine
+    from vdn_minimax_h3_b200.inference.render import render_geometry
+    from vdn_minimax_h3_b200.models.factory import RELEASED_HYBRID
+    from vdn_minimax_h3_b200.models.h3 import H3Config
+    from vdn_minimax_h3_b200.models.hybrid_transform import set_layout
+    cfg = H3Config(hidden_size=512, num_layers=2, num_attention_heads=4, attention_head_dim=128,
+                   in_channels=8, text_dim=96, time_embed_dim=64, time_freq_dim=32,
+                   ff_inner_dim=1024, num_refiner_layers=1, rope_axes_dim=(32, 48, 48))
+    model = tiny_model(RELEASED_HYBRID, cfg)
+    geo = render_geometry(cfg, 5, latent_h=8, latent_w=12, audio=True, num_latent_frames=9)
+    geo.num_audio_latents = 6
+    kw, layout = _forward_inputs(cfg, geo, 24)
+    gm = model.to(device="cuda", dtype=torch.bfloat16)
+    gm.time_embedder.float()
+    for blk in gm.transformer_blocks:
+        blk.attn.linear_attention.alpha.float()
+    set_layout(gm, layout)
+    kwg = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in kw.items()}
+    with torch.no_grad():
+        ref_v, _ = InferenceEngine(copy.deepcopy(gm))(**kwg, layout=layout)
+        out_v, _ = InferenceEngine(gm, fp8=True)(**kwg, layout=layout)
+    torch.cuda.synchronize()
+    check_device_error()
+    assert _rel(out_v, ref_v) < 0.08

@@ -55,6 +55,50 @@ def bench_gemm():
     return rows
 
 
+def bench_gemm_fp8():
+    """Block-scaled fp8 GEMMs on the H3 shapes (and cuBLAS fp8 via torch._scaled_mm with
+    row/column scales as the library baseline)."""
+    from vdn_minimax_h3_b200.ops import fp8
+    from vdn_minimax_h3_b200.ops._ext import check_device_error
+    from vdn_minimax_h3_b200.ops.gemm import interleave_swiglu_rows
+    rows = []
+    for name, n, k in [("qkv", 21504, 5376), ("ff_up_swiglu", 28672, 5376), ("ff_down", 5376, 14336),
+                       ("o_proj", 5376, 14336)]:
+        m = M_ROWS
+        x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) / k ** 0.5
+        xq, xsf = fp8.quantize_act(x)
+        if name == "ff_up_swiglu":
+            fw = fp8.Fp8Weight(interleave_swiglu_rows(w, None, tile=128)[0])
+            hq = torch.empty(m, n // 2, dtype=torch.uint8, device="cuda")
+            hsf = torch.empty(fp8.sf_bytes(m, n // 2), dtype=torch.uint8, device="cuda")
+            ours = timed(lambda: fp8.linear_fp8_swiglu(xq, xsf, fw, hq, hsf))
+        else:
+            fw = fp8.Fp8Weight(w)
+            out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            ours = timed(lambda: fp8.linear_fp8(xq, xsf, fw, out))
+        check_device_error()
+        a8 = xq.view(torch.float8_e4m3fn)
+        b8 = fw.q.view(torch.float8_e4m3fn)
+        sa = torch.ones(m, 1, device="cuda")
+        sb = torch.ones(1, n, device="cuda")
+        try:
+            lib = timed(lambda: torch._scaled_mm(a8, b8.t(), scale_a=sa, scale_b=sb,
+                                                 out_dtype=torch.bfloat16))
+        except Exception as exc:  # noqa: BLE001
+            lib = float("nan")
+            print(json.dumps({"scaled_mm_error": repr(exc)[:200]}), flush=True)
+        quant = timed(lambda: fp8.quantize_act(x, xq, xsf))
+        flop = 2.0 * m * n * k
+        row = dict(case=name, M=m, N=n, K=k, ours_ms=ours, ours_tflops=flop / ours / 1e9,
+                   cublas_fp8_rowwise_ms=lib, cublas_tflops=flop / lib / 1e9, quant_act_ms=quant)
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+        del x, w, xq, xsf, fw
+        torch.cuda.empty_cache()
+    return rows
+
+
 def bench_norm():
     """AdaLN-RMSNorm, frame sums and QK-prep on the full packed sequence (HBM-bound)."""
     from vdn_minimax_h3_b200.ops import norm
@@ -117,6 +161,7 @@ def main(argv=None):
     p.add_argument("--attention", action="store_true")
     p.add_argument("--linear", action="store_true")
     p.add_argument("--norm", action="store_true")
+    p.add_argument("--gemm-fp8", action="store_true")
     p.add_argument("--profile-small", action="store_true",
                    help="one launch each of window attention, SPD inverse and conv features on "
                         "small inputs (an ncu-sized driver)")
@@ -135,6 +180,8 @@ def main(argv=None):
         bench_linear(timed)
     if a.norm:
         bench_norm()
+    if a.gemm_fp8:
+        bench_gemm_fp8()
     if a.profile_small:
         profile_small()
     if a.attention_small:

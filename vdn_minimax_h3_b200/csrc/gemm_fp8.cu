@@ -52,7 +52,7 @@ constexpr int F8_REGS_HIGH = 208;
 static_assert(F8_A_BYTES + F8_B_BYTES + F8_SFA_BYTES + F8_SFB_BYTES <= F8_STAGE_BYTES, "stage");
 static_assert(128 * F8_REGS_LOW + 256 * F8_REGS_HIGH <= F8_THREADS * 168, "register split");
 
-enum Fp8Epi : int { F8_STORE = 0, F8_RESIDUAL = 1, F8_SWIGLU_Q = 2 };
+enum Fp8Epi : int { F8_STORE = 0, F8_RESIDUAL = 1, F8_SWIGLU_Q = 2, F8_ROUTE = 3 };
 
 struct Fp8Params {
   const uint8_t* sfa;          // blocked scale factors of A
@@ -66,8 +66,101 @@ struct Fp8Params {
   uint8_t* q_out;              // SWIGLU_Q: E4M3 [M, N/2], row stride ldq
   int64_t ldq;
   uint8_t* q_sf;               // SWIGLU_Q: blocked scale factors of q_out
+  GemmRoute route;             // ROUTE: destinations and the q/k head processing
   int* err;
 };
+
+// ROUTE epilogue on one 128-column group held in registers: q/k heads get raw stores to
+// plane 0 and RMSNorm + rotate-half RoPE stores to plane 1; other columns are stored to
+// every plane with an address (the routed epilogue of gemm.cu, here after the accumulator
+// has been copied out of TMEM).
+__device__ __forceinline__ void f8_route_store(const GemmRoute& r, int plane, int N, int col,
+                                               int64_t row, const uint32_t* packed, int ngroups) {
+  const long long* tab = r.route + (int64_t)plane * (N >> 3);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (g >= ngroups) break;
+    const long long dst = __ldg(tab + (col >> 3) + g);
+    if (dst)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + row * r.route_ld[plane]) =
+          make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+  }
+}
+
+__device__ __forceinline__ void f8_route_epilogue(const Fp8Params& p, const uint32_t* v, int hc,
+                                                  int row, int N) {
+  const GemmRoute& r = p.route;
+  const bool isq = hc >= r.q0 && hc < r.q1;
+  const bool isk = hc >= r.k0 && hc < r.k1;
+  if (isq || isk) {
+    uint32_t hv[64];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 128; j += 2) {
+      float a0 = __uint_as_float(v[j]), a1 = __uint_as_float(v[j + 1]);
+      if (p.bias) {
+        a0 += __ldg(p.bias + hc + j);
+        a1 += __ldg(p.bias + hc + j + 1);
+      }
+      const uint32_t pk = pack_bf16(a0, a1);
+      hv[j >> 1] = pk;
+      const float r0 = bf16_lo(pk), r1 = bf16_hi(pk);
+      ss = fmaf(r0, r0, fmaf(r1, r1, ss));
+    }
+#pragma unroll
+    for (int c = 0; c < 128; c += 32) f8_route_store(r, 0, N, hc + c, row, hv + (c >> 1), 4);
+    const float rstd = rsqrtf(ss * (1.f / 128.f) + r.qk_eps);
+    const float* w = isq ? r.norm_q : r.norm_k;
+    const float4* cr = reinterpret_cast<const float4*>(r.rope_cos + (int64_t)row * r.ld_rope);
+    const float4* sr = reinterpret_cast<const float4*>(r.rope_sin + (int64_t)row * r.ld_rope);
+#pragma unroll
+    for (int c = 0; c < 64; c += 32) {
+      uint32_t lo[16], hi[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 c4 = __ldg(cr + ((c + j) >> 2));
+        const float4 s4 = __ldg(sr + ((c + j) >> 2));
+        const float cs[4] = {c4.x, c4.y, c4.z, c4.w};
+        const float sn[4] = {s4.x, s4.y, s4.z, s4.w};
+        float o1[4], o2[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i1 = c + j + e, i2 = i1 + 64;
+          const uint32_t u1 = hv[i1 >> 1], u2 = hv[i2 >> 1];
+          const float x1 = ((i1 & 1) ? bf16_hi(u1) : bf16_lo(u1)) * rstd * __ldg(w + i1);
+          const float x2 = ((i2 & 1) ? bf16_hi(u2) : bf16_lo(u2)) * rstd * __ldg(w + i2);
+          o1[e] = x1 * cs[e] - x2 * sn[e];
+          o2[e] = x2 * cs[e] + x1 * sn[e];
+        }
+        lo[j >> 1] = pack_bf16(o1[0], o1[1]);
+        lo[(j >> 1) + 1] = pack_bf16(o1[2], o1[3]);
+        hi[j >> 1] = pack_bf16(o2[0], o2[1]);
+        hi[(j >> 1) + 1] = pack_bf16(o2[2], o2[3]);
+      }
+      f8_route_store(r, 1, N, hc + c, row, lo, 4);
+      f8_route_store(r, 1, N, hc + c + 64, row, hi, 4);
+    }
+    return;
+  }
+#pragma unroll
+  for (int c = 0; c < 128; c += 32) {
+    const int col0 = hc + c;
+    if (col0 >= N) break;
+    uint32_t packed[16];
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      float a0 = __uint_as_float(v[c + j]), a1 = __uint_as_float(v[c + j + 1]);
+      if (p.bias) {
+        a0 += __ldg(p.bias + col0 + j);
+        a1 += __ldg(p.bias + col0 + j + 1);
+      }
+      packed[j >> 1] = pack_bf16(a0, a1);
+    }
+    const int ngroups = min(4, (N - col0) >> 3);
+#pragma unroll 1
+    for (int pl = 0; pl < r.planes; ++pl) f8_route_store(r, pl, N, col0, row, packed, ngroups);
+  }
+}
 
 __device__ __forceinline__ void f8_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
   constexpr int group = 16;  // n-blocks per raster band: one band's weights stay in L2
@@ -122,6 +215,10 @@ __device__ __forceinline__ void f8_epilogue(const Fp8Params& p, const uint32_t* 
     return;
   }
   if (!row_ok || col0 >= N) return;
+  if constexpr (EPI == F8_ROUTE) {
+    f8_route_epilogue(p, v, col0, row, N);
+    return;
+  }
 #pragma unroll
   for (int c = 0; c < 128; c += 32) {
     if (col0 + c >= N) break;
@@ -367,6 +464,20 @@ void launch_gemm_fp8(const GemmFp8Args& a, int mode, void* out, int64_t ldo, con
   }
 }
 
+void launch_gemm_fp8_routed(const GemmFp8Args& a, const GemmRoute& r, const float* bias, int* err,
+                            cudaStream_t stream) {
+  if (a.M == 0 || a.N == 0) return;
+  if (a.K % F8_BK) throw std::runtime_error("fp8 GEMM: K must be a multiple of 128");
+  if (r.planes < 1 || r.planes > 8) throw std::runtime_error("routed GEMM: 1..8 route planes");
+  Fp8Params p{};
+  p.sfa = reinterpret_cast<const uint8_t*>(a.sfa);
+  p.sfb = reinterpret_cast<const uint8_t*>(a.sfb);
+  p.bias = bias;
+  p.route = r;
+  p.err = err;
+  launch_fp8<F8_ROUTE>(a, p, stream);
+}
+
 // ------------------------------------------------------------------ activation quantiser
 // One warp per row; each half-warp owns a 1x128 block (16 lanes x 8 elements): block
 // amax by shuffles, one power-of-two scale, E4M3 bytes and the scale-factor word.
@@ -378,20 +489,26 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
   const int kb32_total = K / 32;
-  for (int c = lane; c < K / 8; c += 32) {   // K % 256 == 0: whole warps per iteration
-    const uint4 u = *reinterpret_cast<const uint4*>(x + (int64_t)row * ldx + c * 8);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&u);
-    float f[8];
+  const int nvec = K / 8;
+  for (int base = 0; base < nvec; base += 32) {   // K % 128 == 0: half-warps are whole blocks
+    const int c = base + lane;
+    const bool valid = c < nvec;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + (int64_t)row * ldx + c * 8);
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(&u);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      f[2 * j] = bf16_lo(w[j]);
-      f[2 * j + 1] = bf16_hi(w[j]);
+      for (int j = 0; j < 4; ++j) {
+        f[2 * j] = bf16_lo(w[j]);
+        f[2 * j + 1] = bf16_hi(w[j]);
+      }
     }
     float amax = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (!valid) continue;
     const int e = e8_exponent(amax);
     const float inv = exp2_int(-e < -126 ? -126 : (-e > 127 ? 127 : -e));
     uint32_t lo = (uint32_t)pack_e4m3x2(f[0] * inv, f[1] * inv) |
@@ -410,7 +527,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
 void launch_quant_rows(const void* x, int64_t ldx, int M, int K, void* q, int64_t ldq, void* sf,
                        cudaStream_t stream) {
   if (M == 0) return;
-  if (K % 256) throw std::runtime_error("fp8 quantiser: K must be a multiple of 256");
+  if (K % 128) throw std::runtime_error("fp8 quantiser: K must be a multiple of 128");
   quant_rows_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K, reinterpret_cast<uint8_t*>(q), ldq,
       reinterpret_cast<uint8_t*>(sf));

@@ -76,12 +76,16 @@ struct GemmFp8Args {
 void launch_gemm_fp8(const GemmFp8Args& a, int mode, void* out, int64_t ldo, const float* bias,
                      const void* gate, int64_t ldg, const int* gate_idx, void* q_out, int64_t ldq,
                      void* q_sf, int* err, cudaStream_t stream);
+void launch_gemm_fp8_routed(const GemmFp8Args& a, const GemmRoute& r, const float* bias, int* err,
+                            cudaStream_t stream);
 void launch_quant_rows(const void* x, int64_t ldx, int M, int K, void* q, int64_t ldq, void* sf,
                        cudaStream_t stream);
 
+// out (bf16) and/or q + qsf (E4M3 with one scale per 1x128 block; D % 256 == 0)
 void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps, const void* table,
                           int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
-                          int64_t ldo, int T, int D, cudaStream_t stream);
+                          int64_t ldo, int T, int D, cudaStream_t stream, void* q = nullptr,
+                          int64_t ldq = 0, void* qsf = nullptr);
 void launch_frame_sums(const void* x, int64_t ldx, int64_t row0, int64_t nrows, int64_t vs,
                        int F, int S, int D, float* out, cudaStream_t stream);
 void launch_qk_prep(const void* src, int64_t lds, int T, int H, int d, const float* w, float eps,

@@ -16,7 +16,8 @@ template <int VPL>
 __global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t ldx, const float* __restrict__ w, float eps,
     const __nv_bfloat16* __restrict__ table, int64_t ldt, int shift_col, int scale_col,
-    const int* __restrict__ idx, __nv_bfloat16* __restrict__ out, int64_t ldo, int T, int D) {
+    const int* __restrict__ idx, __nv_bfloat16* __restrict__ out, int64_t ldo, int T, int D,
+    uint8_t* __restrict__ q, int64_t ldq, uint8_t* __restrict__ qsf) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -66,14 +67,42 @@ __global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
         b = b * (1.f + bf16_hi(scu[j])) + bf16_hi(shu[j]);
         res[j] = pack_bf16(a, b);
       }
-      orow[c] = make_uint4(res[0], res[1], res[2], res[3]);
+      if (out) orow[c] = make_uint4(res[0], res[1], res[2], res[3]);
+      if (q) {
+        // E4M3 copy for an fp8 GEMM: a half-warp holds one 1x128 block (D % 256 == 0, so
+        // every lane of the warp is here); the bf16-rounded values are quantised
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          f[2 * j] = bf16_lo(res[j]);
+          f[2 * j + 1] = bf16_hi(res[j]);
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const int e = e8_exponent(amax);
+        const float inv = exp2_int(-e < -126 ? -126 : (-e > 127 ? 127 : -e));
+        const uint32_t lo = (uint32_t)pack_e4m3x2(f[0] * inv, f[1] * inv) |
+                            ((uint32_t)pack_e4m3x2(f[2] * inv, f[3] * inv) << 16);
+        const uint32_t hi = (uint32_t)pack_e4m3x2(f[4] * inv, f[5] * inv) |
+                            ((uint32_t)pack_e4m3x2(f[6] * inv, f[7] * inv) << 16);
+        *reinterpret_cast<uint2*>(q + (int64_t)row * ldq + c * 8) = make_uint2(lo, hi);
+        if ((lane & 15) == 0) {
+          const uint32_t bb = (uint32_t)(e + 127) & 0xFF;
+          *reinterpret_cast<uint32_t*>(qsf + sf_offset(row, (int64_t)(c / 16) * 4, D / 32)) =
+              bb | (bb << 8) | (bb << 16) | (bb << 24);
+        }
+      }
     }
   }
 }
 
 void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps, const void* table,
                           int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
-                          int64_t ldo, int T, int D, cudaStream_t stream) {
+                          int64_t ldo, int T, int D, cudaStream_t stream, void* q, int64_t ldq,
+                          void* qsf) {
   if (T == 0) return;
   const int nvec = D / 8;
   const int need = (nvec + 31) / 32;
@@ -83,7 +112,9 @@ void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps,
   auto ob = reinterpret_cast<__nv_bfloat16*>(out);
 #define VDN_ADALN(N)                                                                          \
   adaln_rmsnorm_kernel<N><<<grid, block, 0, stream>>>(xb, ldx, w, eps, tb, ldt, shift_col,    \
-                                                       scale_col, idx, ob, ldo, T, D)
+                                                       scale_col, idx, ob, ldo, T, D,           \
+                                                       reinterpret_cast<uint8_t*>(q), ldq,         \
+                                                       reinterpret_cast<uint8_t*>(qsf))
   if (need <= 1) VDN_ADALN(1);
   else if (need <= 2) VDN_ADALN(2);
   else if (need <= 4) VDN_ADALN(4);

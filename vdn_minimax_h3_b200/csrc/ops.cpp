@@ -34,6 +34,18 @@ int* err_ptr(const torch::Tensor& err) {
   return err.data_ptr<int>();
 }
 
+void check_2d_bytes(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.element_size() == 1 && t.dim() == 2 && t.stride(1) == 1, name,
+              " must be a 2-D one-byte (E4M3) CUDA tensor with contiguous rows");
+  TORCH_CHECK(t.stride(0) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
+              " rows must be 16-byte aligned");
+}
+void check_sf(const torch::Tensor& t, int64_t nbytes, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.element_size() == 1 && t.is_contiguous() && t.numel() >= nbytes &&
+                  reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              name, " must be a contiguous 16-byte aligned byte tensor of >= ", nbytes, " bytes");
+}
+
 GemmArgs gemm_args(const torch::Tensor& A, const torch::Tensor& B) {
   check_2d_bf16(A, "A");
   check_2d_bf16(B, "B");
@@ -94,16 +106,16 @@ void gemm_bf16_swiglu(torch::Tensor A, torch::Tensor B, torch::Tensor H,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void gemm_bf16_routed(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> bias,
-                      torch::Tensor route, std::vector<int64_t> route_ld, int64_t q0, int64_t q1,
-                      int64_t k0, int64_t k1, c10::optional<torch::Tensor> norm_q,
-                      c10::optional<torch::Tensor> norm_k, double qk_eps,
-                      c10::optional<torch::Tensor> cosv, c10::optional<torch::Tensor> sinv,
-                      torch::Tensor err) {
-  GemmArgs a = gemm_args(A, B);
-  TORCH_CHECK(a.N % 8 == 0, "routed GEMM needs N % 8 == 0");
+namespace {
+GemmRoute build_route(int64_t M, int64_t N, const torch::Tensor& route,
+                      const std::vector<int64_t>& route_ld, int64_t q0, int64_t q1, int64_t k0,
+                      int64_t k1, const c10::optional<torch::Tensor>& norm_q,
+                      const c10::optional<torch::Tensor>& norm_k, double qk_eps,
+                      const c10::optional<torch::Tensor>& cosv,
+                      const c10::optional<torch::Tensor>& sinv) {
+  TORCH_CHECK(N % 8 == 0, "routed GEMM needs N % 8 == 0");
   TORCH_CHECK(route.is_cuda() && route.scalar_type() == at::kLong && route.is_contiguous() &&
-                  route.dim() == 2 && route.size(1) == a.N / 8,
+                  route.dim() == 2 && route.size(1) == N / 8,
               "route must be a contiguous int64 CUDA tensor [planes, N/8]");
   const int planes = (int)route.size(0);
   TORCH_CHECK(planes >= 1 && planes <= 8 && (int)route_ld.size() == planes,
@@ -121,13 +133,13 @@ void gemm_bf16_routed(torch::Tensor A, torch::Tensor B, c10::optional<torch::Ten
   r.k1 = (int)k1;
   if (q1 > q0 || k1 > k0) {
     TORCH_CHECK(planes >= 2, "q/k processing needs plane 1 for the processed heads");
-    TORCH_CHECK(q0 % 128 == 0 && q1 % 128 == 0 && k0 % 128 == 0 && k1 % 128 == 0 &&
-                    q1 <= a.N && k1 <= a.N,
+    TORCH_CHECK(q0 % 128 == 0 && q1 % 128 == 0 && k0 % 128 == 0 && k1 % 128 == 0 && q1 <= N &&
+                    k1 <= N,
                 "q/k column ranges must lie on 128-column head boundaries");
     TORCH_CHECK(norm_q && norm_k && cosv && sinv, "q/k processing needs norms and rope tables");
     for (const auto* t : {&*cosv, &*sinv}) {
       TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->dim() == 2 &&
-                      t->size(0) >= a.M && t->size(1) == 128 && t->stride(1) == 1 &&
+                      t->size(0) >= M && t->size(1) == 128 && t->stride(1) == 1 &&
                       t->stride(0) % 4 == 0 &&
                       reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
                   "rope tables must be fp32 [M, 128] with 16-byte aligned rows");
@@ -140,25 +152,25 @@ void gemm_bf16_routed(torch::Tensor A, torch::Tensor B, c10::optional<torch::Ten
     r.rope_sin = sinv->data_ptr<float>();
     r.ld_rope = cosv->stride(0);
   }
+  return r;
+}
+}  // namespace
+
+void gemm_bf16_routed(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> bias,
+                      torch::Tensor route, std::vector<int64_t> route_ld, int64_t q0, int64_t q1,
+                      int64_t k0, int64_t k1, c10::optional<torch::Tensor> norm_q,
+                      c10::optional<torch::Tensor> norm_k, double qk_eps,
+                      c10::optional<torch::Tensor> cosv, c10::optional<torch::Tensor> sinv,
+                      torch::Tensor err) {
+  GemmArgs a = gemm_args(A, B);
+  GemmRoute r = build_route(a.M, a.N, route, route_ld, q0, q1, k0, k1, norm_q, norm_k, qk_eps,
+                            cosv, sinv);
   c10::cuda::CUDAGuard g(A.device());
   launch_gemm_bf16_routed(a, r, opt_f32(bias, a.N, "bias"), err_ptr(err),
                           at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-namespace {
-void check_2d_bytes(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.element_size() == 1 && t.dim() == 2 && t.stride(1) == 1, name,
-              " must be a 2-D one-byte (E4M3) CUDA tensor with contiguous rows");
-  TORCH_CHECK(t.stride(0) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
-              " rows must be 16-byte aligned");
-}
-void check_sf(const torch::Tensor& t, int64_t nbytes, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.element_size() == 1 && t.is_contiguous() && t.numel() >= nbytes &&
-                  reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
-              name, " must be a contiguous 16-byte aligned byte tensor of >= ", nbytes, " bytes");
-}
-}  // namespace
 
 void gemm_fp8(torch::Tensor A, torch::Tensor B, torch::Tensor sfa, torch::Tensor sfb, int64_t mode,
               c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> bias,
@@ -217,12 +229,35 @@ void gemm_fp8(torch::Tensor A, torch::Tensor B, torch::Tensor sfa, torch::Tensor
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void gemm_fp8_routed(torch::Tensor A, torch::Tensor B, torch::Tensor sfa, torch::Tensor sfb,
+                     c10::optional<torch::Tensor> bias, torch::Tensor route,
+                     std::vector<int64_t> route_ld, int64_t q0, int64_t q1, int64_t k0, int64_t k1,
+                     c10::optional<torch::Tensor> norm_q, c10::optional<torch::Tensor> norm_k,
+                     double qk_eps, c10::optional<torch::Tensor> cosv,
+                     c10::optional<torch::Tensor> sinv, torch::Tensor err) {
+  check_2d_bytes(A, "A");
+  check_2d_bytes(B, "B");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K, "K mismatch");
+  TORCH_CHECK(K % 128 == 0 && N % 32 == 0, "fp8 GEMM needs K % 128 == 0 and N % 32 == 0");
+  check_sf(sfa, ((M + 127) / 128) * (K / 128) * 512, "sfa");
+  check_sf(sfb, ((N + 255) / 256) * (K / 128) * 1024, "sfb");
+  GemmFp8Args a{A.data_ptr(), B.data_ptr(), A.stride(0), B.stride(0), sfa.data_ptr(),
+                sfb.data_ptr(), (int)M, (int)N, (int)K};
+  GemmRoute r = build_route(M, N, route, route_ld, q0, q1, k0, k1, norm_q, norm_k, qk_eps, cosv,
+                            sinv);
+  c10::cuda::CUDAGuard g(A.device());
+  launch_gemm_fp8_routed(a, r, opt_f32(bias, N, "bias"), err_ptr(err),
+                         at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf) {
   check_2d_bf16(x, "x");
   check_2d_bytes(q, "q");
   const int64_t M = x.size(0), K = x.size(1);
   TORCH_CHECK(q.size(0) == M && q.size(1) == K, "q shape mismatch");
-  TORCH_CHECK(K % 256 == 0, "quantiser needs K % 256 == 0");
+  TORCH_CHECK(K % 128 == 0, "quantiser needs K % 128 == 0");
   check_sf(sf, ((M + 127) / 128) * (K / 128) * 512, "sf");
   c10::cuda::CUDAGuard g(x.device());
   launch_quant_rows(x.data_ptr(), x.stride(0), (int)M, (int)K, q.data_ptr(), q.stride(0),
@@ -231,13 +266,25 @@ void quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf) {
 }
 
 void adaln_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, torch::Tensor table,
-                   int64_t shift_col, int64_t scale_col, torch::Tensor idx, torch::Tensor out) {
+                   int64_t shift_col, int64_t scale_col, torch::Tensor idx,
+                   c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> q,
+                   c10::optional<torch::Tensor> qsf) {
   check_2d_bf16(x, "x");
   check_2d_bf16(table, "table");
-  check_2d_bf16(out, "out");
   const int T = x.size(0), D = x.size(1);
   TORCH_CHECK(D % 8 == 0, "hidden size must be a multiple of 8");
-  TORCH_CHECK(out.size(0) == T && out.size(1) == D, "out shape mismatch");
+  TORCH_CHECK(out || q, "adaln_rmsnorm needs a bf16 and/or an E4M3 output");
+  if (out) {
+    check_2d_bf16(*out, "out");
+    TORCH_CHECK(out->size(0) == T && out->size(1) == D, "out shape mismatch");
+  }
+  if (q) {
+    TORCH_CHECK(D % 256 == 0, "the E4M3 output needs D % 256 == 0");
+    check_2d_bytes(*q, "q");
+    TORCH_CHECK(q->size(0) == T && q->size(1) == D, "q shape mismatch");
+    TORCH_CHECK(qsf.has_value(), "the E4M3 output needs its scale-factor buffer");
+    check_sf(*qsf, ((T + 127) / 128) * (D / 128) * 512, "qsf");
+  }
   TORCH_CHECK(shift_col % 8 == 0 && scale_col % 8 == 0, "table columns must be 8-aligned");
   TORCH_CHECK(shift_col + D <= table.size(1) && scale_col + D <= table.size(1), "table too narrow");
   TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.is_contiguous() &&
@@ -247,7 +294,9 @@ void adaln_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, 
   TORCH_CHECK(reinterpret_cast<uintptr_t>(wp) % 16 == 0, "norm weight must be 16-byte aligned");
   launch_adaln_rmsnorm(x.data_ptr(), x.stride(0), wp, (float)eps, table.data_ptr(),
                        table.stride(0), (int)shift_col, (int)scale_col, idx.data_ptr<int>(),
-                       out.data_ptr(), out.stride(0), T, D, at::cuda::getCurrentCUDAStream());
+                       out ? out->data_ptr() : nullptr, out ? out->stride(0) : 0, T, D,
+                       at::cuda::getCurrentCUDAStream(), q ? q->data_ptr() : nullptr,
+                       q ? q->stride(0) : 0, q ? qsf->data_ptr() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -572,6 +621,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8", &vdn::gemm_fp8,
         "block-scaled E4M3 tcgen05 GEMM (UE8M0 scale factors in TMEM); epilogue modes 0 store, "
         "1 gated residual, 2 swiglu -> E4M3 + scale factors");
+  m.def("gemm_fp8_routed", &vdn::gemm_fp8_routed,
+        "block-scaled E4M3 GEMM with the routed epilogue (column routes, QK-norm + RoPE)");
   m.def("quant_rows", &vdn::quant_rows, "bf16 rows -> E4M3 with one UE8M0 scale per 1x128 block");
   m.def("adaln_rmsnorm", &vdn::adaln_rmsnorm, "RMSNorm * w * (1 + scale[idx]) + shift[idx]");
   m.def("frame_sums", &vdn::frame_sums, "per-frame fp32 column sums of video rows");

@@ -44,11 +44,9 @@ def build_synthetic_model(cfg: H3Config = None, hybrid=RELEASED_HYBRID, device="
 
 
 def build_inference_engine(model, fp8=False):
-    engine = InferenceEngine(model)
-    if fp8:
-        from vdn_minimax_h3_b200.ops.fp8 import convert_engine_to_fp8
-        convert_engine_to_fp8(engine)
-    return engine
+    """The fused-kernel engine; fp8=True quantises the QKV / FF projections to block-scaled
+    E4M3 once here (the reference's assembly step 'fp8', assemble.py:101-180)."""
+    return InferenceEngine(model, fp8=fp8)
 
 
 def build_from_checkpoint(artifact, device="cuda", base_source=None, init="load"):

@@ -43,7 +43,7 @@ def _f32(t):
 class PackedBlock:
     """Concatenated / interleaved weights of one hybrid DiT block."""
 
-    def __init__(self, block, cfg):
+    def __init__(self, block, cfg, fp8=False):
         attn = block.attn
         hybrid = isinstance(attn, HybridAttention)
         orig = attn.orig if hybrid else attn
@@ -67,6 +67,7 @@ class PackedBlock:
             return (n + 7) // 8 * 8
         # every column group starts 16-byte aligned (a TMA / vector-load requirement)
         rows_pad = 3 * pad8(inner) + sum(pad8(w.shape[0]) for _, w, _ in extra)
+        rows_pad = (rows_pad + 31) // 32 * 32   # whole 32-column groups (fp8 GEMM tiles)
         W = torch.zeros(rows_pad, D, device=dev, dtype=dt)
         b = torch.zeros(rows_pad, device=dev, dtype=torch.float32)
         off = 0
@@ -106,6 +107,14 @@ class PackedBlock:
         ff = block.ff
         self.ff_act = ff.activation
         up = ff.net[0].proj
+        self.fp8 = fp8
+        if fp8:
+            from vdn_minimax_h3_b200.ops.fp8 import Fp8Weight
+            self.w8_qkvg = Fp8Weight(self.w_qkvg, self.b_qkvg)
+            if self.ff_act == "swiglu":
+                self.w8_up = Fp8Weight(*gemm.interleave_swiglu_rows(up.weight.data, up.bias,
+                                                                    tile=128))
+            self.w8_down = Fp8Weight(ff.net[2].weight.data, ff.net[2].bias)
         if self.ff_act == "swiglu":
             wi, bi = gemm.interleave_swiglu_rows(up.weight.data, up.bias)
             up.weight.data = wi   # NOTE: the module now holds the interleaved layout
@@ -130,13 +139,18 @@ class PackedBlock:
 class InferenceEngine:
     """Runs an H3Transformer (dense or hybrid) forward through the fused kernels."""
 
-    def __init__(self, model: H3Transformer):
+    def __init__(self, model: H3Transformer, fp8=False):
+        """fp8=True: the QKV, FF-up and FF-down projections run on the block-scaled fp8
+        GEMM (weights quantised once here, 128x128 blocks; activations quantised by the
+        kernels that produce them, 1x128 blocks), as the reference's Fp8Linear conversion
+        of the large Linears (src/models/ops/fp8_linear.py:286-323)."""
         self.model = model
         self.cfg = model.config
+        self.fp8 = fp8
         self.blocks = []
         with torch.no_grad():
             for block in model.transformer_blocks:
-                self.blocks.append(PackedBlock(block, self.cfg))
+                self.blocks.append(PackedBlock(block, self.cfg, fp8=fp8))
                 if block.ff.activation == "swiglu":
                     block.ff.net[0].interleaved = 256
         self._plan_key = None
@@ -197,15 +211,27 @@ class InferenceEngine:
         S = layout.tokens_per_frame if linear_on else 1
         vs = layout.video_start if linear_on else 0
         n1 = self._buf("normed", (T, D), x.dtype, dev)
+        f8 = pb.fp8 and x.is_cuda
+        if f8:
+            from vdn_minimax_h3_b200.ops import fp8 as fp8_ops
+            nq = self._buf("normed_q", (T, D), torch.uint8, dev)
+            nsf = self._buf("normed_sf", (fp8_ops.sf_bytes(T, D),), torch.uint8, dev)
         with sec("norm"):
-            norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1)
+            norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx,
+                                   out=n1 if (linear_on or not f8) else False,
+                                   fp8_out=(nq, nsf) if f8 else None)
             frame_sums = norm_ops.frame_sums(n1, Fr, S, 0, vs) if linear_on else None
         qkvg = self._buf("qkvg", (T, pb.w_qkvg.shape[0]), x.dtype, dev)
         c = pb.cols
         cos, sin = rope
         q = self._buf("q", (T, inner), x.dtype, dev)
         k = self._buf("k", (T, inner), x.dtype, dev)
-        if fused_qk_ok(pb, cos):
+        if f8 and fused_qk_ok(pb, cos):
+            route = self._qkv_route(pb, qkvg, q, k)
+            with sec("gemm_qkv"):
+                fp8_ops.linear_routed_fp8(nq, nsf, pb.w8_qkvg, route, c["q"], c["k"], pb.norm_q,
+                                          pb.norm_k, pb.qk_eps, cos, sin)
+        elif fused_qk_ok(pb, cos):
             route = self._qkv_route(pb, qkvg, q, k)
             with sec("gemm_qkv"):
                 gemm.linear_routed(n1, pb.w_qkvg, pb.b_qkvg, route, c["q"], c["k"], pb.norm_q,
@@ -235,6 +261,19 @@ class InferenceEngine:
         with sec("gemm_o"):
             gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D], adaln_idx)
         n2 = n1
+        if f8 and pb.ff_interleaved:
+            with sec("norm"):
+                norm_ops.adaln_rmsnorm(x, pb.norm2, pb.eps, table, 3 * D, 4 * D, adaln_idx,
+                                       out=False, fp8_out=(nq, nsf))
+            inter = pb.w8_up.shape[0] // 2
+            hq = self._buf("h_q", (T, inter), torch.uint8, dev)
+            hsf = self._buf("h_sf", (fp8_ops.sf_bytes(T, inter),), torch.uint8, dev)
+            with sec("gemm_ff_up"):
+                fp8_ops.linear_fp8_swiglu(nq, nsf, pb.w8_up, hq, hsf)
+            with sec("gemm_ff_down"):
+                fp8_ops.linear_fp8_gated_residual(hq, hsf, pb.w8_down, x, table[:, 5 * D:6 * D],
+                                                  adaln_idx)
+            return x
         with sec("norm"):
             norm_ops.adaln_rmsnorm(x, pb.norm2, pb.eps, table, 3 * D, 4 * D, adaln_idx, out=n2)
         with sec("gemm_ff_up"):

@@ -177,3 +177,28 @@ def linear_fp8_swiglu(xq, xsf, w: Fp8Weight, q_out=None, q_sf=None):
     ext().gemm_fp8(xq, w.q, xsf, w.sf, 2, None, w.bias, None, None, q_out, q_sf,
                    error_word(xq.device))
     return q_out, q_sf
+
+
+def linear_routed_fp8(xq, xsf, w: Fp8Weight, route, q_cols=(0, 0), k_cols=(0, 0), norm_q=None,
+                      norm_k=None, qk_eps=1e-6, cos=None, sin=None):
+    """The routed projection (ops.gemm.linear_routed) on the block-scaled fp8 GEMM."""
+    qk = q_cols[1] > q_cols[0] or k_cols[1] > k_cols[0]
+    if not xq.is_cuda:
+        from vdn_minimax_h3_b200.ops.norm import qk_prep_reference
+        y = _oracle(xq, xsf, w)
+        if w.bias is not None:
+            y = y + w.bias
+        y = y.to(torch.bfloat16)
+        proc = []
+        for (lo, hi), nw in ((q_cols, norm_q), (k_cols, norm_k)):
+            if hi > lo:
+                proc.append((lo, qk_prep_reference(y[:, lo:hi], (hi - lo) // nw.numel(), nw,
+                                                   qk_eps, cos, sin)))
+        route.copy_from(y, proc)
+        return route
+    table, lds = route.tables(xq.device)
+    f32 = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
+    ext().gemm_fp8_routed(xq, w.q, xsf, w.sf, w.bias, table, lds, q_cols[0], q_cols[1],
+                          k_cols[0], k_cols[1], f32(norm_q), f32(norm_k), float(qk_eps),
+                          cos if qk else None, sin if qk else None, error_word(xq.device))
+    return route

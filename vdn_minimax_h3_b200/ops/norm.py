@@ -20,8 +20,23 @@ def adaln_rmsnorm_reference(x, weight, eps, table, shift_col, scale_col, idx):
     return (n * (1.0 + scale) + shift).to(x.dtype)
 
 
-def adaln_rmsnorm(x, weight, eps, table, shift_col, scale_col, idx, out=None):
-    """out = RMSNorm(x) * w * (1 + table[idx, scale]) + table[idx, shift]; [T, D] bf16."""
+def adaln_rmsnorm(x, weight, eps, table, shift_col, scale_col, idx, out=None, fp8_out=None):
+    """out = RMSNorm(x) * w * (1 + table[idx, scale]) + table[idx, shift]; [T, D] bf16.
+
+    fp8_out = (q [T, D] uint8, sf) additionally (or, with out=False, only) writes the E4M3
+    copy with one power-of-two scale per 1x128 block (ops.fp8 layout) for an fp8 GEMM."""
+    if not x.is_cuda and fp8_out is not None:
+        from vdn_minimax_h3_b200.ops import fp8
+        y = adaln_rmsnorm_reference(x, weight, eps, table, shift_col, scale_col, idx)
+        q, sf = fp8.quantize_act(y.to(torch.bfloat16))
+        fp8_out[0].copy_(q)
+        fp8_out[1].copy_(sf)
+        if out is False:
+            return fp8_out
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
     if not x.is_cuda:
         y = adaln_rmsnorm_reference(x, weight, eps, table, shift_col, scale_col, idx)
         if out is not None:
@@ -31,8 +46,10 @@ def adaln_rmsnorm(x, weight, eps, table, shift_col, scale_col, idx, out=None):
     if out is None:
         out = torch.empty_like(x)
     w = None if weight is None else weight.float().contiguous()
-    ext().adaln_rmsnorm(x, w, float(eps), table, int(shift_col), int(scale_col), idx, out)
-    return out
+    q, sf = fp8_out if fp8_out is not None else (None, None)
+    ext().adaln_rmsnorm(x, w, float(eps), table, int(shift_col), int(scale_col), idx,
+                        None if out is False else out, q, sf)
+    return fp8_out if out is False else out
 
 
 def frame_sums(rows, num_frames, tokens_per_frame, row0=0, video_start=0):
