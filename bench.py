@@ -36,6 +36,8 @@ def parse(argv=None):
     p.add_argument("--fp8", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--tp", type=int, default=1,
+                   help="tensor-parallel degree (TP x Ulysses, producer/consumer-fused exchanges)")
     p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
                    help="Ulysses exchange: symmetric-memory stores fused into the producing "
                         "kernels (p2p) or NCCL all_to_all_single (nccl)")
@@ -145,7 +147,11 @@ def main(argv=None):
     model, build_s = build_synthetic_model(cfg, device=dev, seed=args.seed)
     engine = build_inference_engine(model, fp8=args.fp8)
     transformer = engine
-    if world > 1:
+    if world > 1 and args.tp > 1:
+        from vdn_minimax_h3_b200.parallel.hybrid import HybridEngine, HybridRuntime
+        runtime = HybridRuntime(args.tp)
+        transformer = HybridEngine(engine, runtime, fp8=args.fp8)
+    elif world > 1:
         from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
         runtime = init_ulysses()
         transformer = UlyssesEngine(engine, runtime, exchange=args.exchange)
@@ -259,7 +265,9 @@ def main(argv=None):
                                 "c1 window + vdn_solve linear branch, LoRA default+turbo merged)",
                        "global_batch": 1, "seq_len": S, "num_frames": NUM_FRAMES,
                        "latent_frames": geo.num_latent_frames, "text_len": TEXT_LEN, "nfe": NFE,
-                       "parallelism": "single-gpu" if world == 1 else f"ulysses{world}",
+                       "parallelism": ("single-gpu" if world == 1 else
+                                       f"tp{args.tp}xulysses{world // args.tp}" if args.tp > 1
+                                       else f"ulysses{world}"),
                        "exchange": None if world == 1 else args.exchange,
                        "l2": "inputs larger than L2 (66 GB of weights stream per step)"},
             "clocks": clock_info, "gpu_launches": launches, "e2e": e2e,

@@ -138,3 +138,63 @@ def test_ulysses_two_gpus_match_single(exchange):
         p.join(timeout=280)
     res = dict(q.get() for _ in range(2))
     assert all(isinstance(v, float) and v < 2e-2 for v in res.values()), res
+
+
+def _hybrid_worker(rank, world, port, q, tp, fp8):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from tests.test_model_cpu import _forward_inputs, tiny_model
+        from vdn_minimax_h3_b200.inference.engine import InferenceEngine
+        from vdn_minimax_h3_b200.inference.render import render_geometry
+        from vdn_minimax_h3_b200.models.factory import RELEASED_HYBRID
+        from vdn_minimax_h3_b200.models.h3 import H3Config
+        from vdn_minimax_h3_b200.models.hybrid_transform import set_layout
+        from vdn_minimax_h3_b200.ops._ext import check_device_error
+        from vdn_minimax_h3_b200.parallel.hybrid import HybridEngine, HybridRuntime
+        cfg = H3Config(hidden_size=512, num_layers=2, num_attention_heads=8, attention_head_dim=128,
+                       in_channels=8, text_dim=96, time_embed_dim=64, time_freq_dim=32,
+                       ff_inner_dim=1024, num_refiner_layers=1, rope_axes_dim=(32, 48, 48))
+        model = tiny_model(RELEASED_HYBRID, cfg)
+        geo = render_geometry(cfg, 5, latent_h=8, latent_w=12, audio=True, num_latent_frames=17)
+        geo.num_audio_latents = 6
+        kw, layout = _forward_inputs(cfg, geo, 24)
+        gm = model.to(device=dev, dtype=torch.bfloat16)
+        gm.time_embedder.float()
+        for blk in gm.transformer_blocks:
+            blk.attn.linear_attention.alpha.float()
+        set_layout(gm, layout)
+        kwg = {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in kw.items()}
+        with torch.no_grad():
+            single = InferenceEngine(copy.deepcopy(gm), fp8=fp8)
+            ref_v, _ = single(**kwg, layout=layout)
+            hp = HybridEngine(InferenceEngine(gm, fp8=fp8), HybridRuntime(tp), fp8=fp8)
+            out_v, _ = hp(**kwg, layout=layout)
+            out_v2, _ = hp(**kwg, layout=layout)
+            hp.close()
+        torch.cuda.synchronize()
+        check_device_error()
+        err = ((out_v.float() - ref_v.float()).norm() / ref_v.float().norm()).item()
+        if not torch.equal(out_v, out_v2):
+            err = "second forward differs from the first"
+        q.put((rank, err))
+    except Exception as exc:  # noqa: BLE001
+        import traceback
+        q.put((rank, repr(exc) + traceback.format_exc()[-1500:]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("world,tp,fp8", [(2, 2, False), (2, 2, True), (4, 2, True)])
+def test_tp_ulysses_match_single(world, tp, fp8):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _spawn(_hybrid_worker, world, tp, fp8)
+    tol = 4e-2 if fp8 else 2e-2
+    assert all(isinstance(v, float) and v < tol for v in res.values()), res

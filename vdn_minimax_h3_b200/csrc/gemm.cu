@@ -18,6 +18,8 @@
 //   EPI_SWIGLU     H = (acc_v + b_v) * silu(acc_g + b_g); the weight rows are interleaved
 //                  per 256-row tile as [128 value rows | 128 gate rows]
 //   EPI_ADD        C += acc (+ bias)                               (accumulate into C)
+//   EPI_STORE_F32  fp32 C without bias, each row stored to its owner's buffer (the
+//                  reduce-scatter of a row-parallel GEMM: partial sums cross NVLink once)
 //   EPI_ROUTE      every 8-column group of a row goes to its own destination (a route
 //                  table of addresses), and the 128-column q/k heads additionally get the
 //                  per-head RMSNorm + rotate-half RoPE of the attention input
@@ -47,7 +49,8 @@ constexpr int GM_GROUP_N = 16;  // n-blocks per raster band (weights of one band
 constexpr int GM_SMEM = GM_STAGES * GM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int kMaxRoutePlanes = 8;
 
-enum EpiMode : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ADD = 3, EPI_ROUTE = 4 };
+enum EpiMode : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ADD = 3, EPI_ROUTE = 4,
+                    EPI_STORE_F32 = 5 };
 
 struct EpiParams {
   __nv_bfloat16* out;        // C / X / H
@@ -57,6 +60,7 @@ struct EpiParams {
   int64_t ldg;
   const int* gate_idx;       // EPI_RESIDUAL: per-row table index
   int* err;                  // device error word
+  RowScatter scatter;           // EPI_STORE_F32: rows to their tensor-parallel owners
   // EPI_ROUTE
   const long long* route;       // [planes][N/8] address of (row 0, column 8g), 0 = no store
   int64_t route_ld[kMaxRoutePlanes];  // row stride (elements) of each plane's destinations
@@ -201,6 +205,33 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, uint32_t tacc,
   const bool row_ok = row < M;
   if constexpr (EPI == EPI_ROUTE) {
     epilogue_route(p, lane_base, row, row_ok, n0, N);
+    return;
+  }
+  if constexpr (EPI == EPI_STORE_F32) {
+    float* rowp = nullptr;
+    if (row_ok) {
+      if (p.scatter.n == 0) {
+        rowp = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
+      } else {
+        const int64_t g = p.scatter.row0 + row;
+        const int r = (int)(g / p.scatter.rows_per_rank);
+        rowp = reinterpret_cast<float*>(p.scatter.base[r]) +
+               (g - (int64_t)r * p.scatter.rows_per_rank) * p.ldo;
+      }
+    }
+#pragma unroll 1
+    for (int c = 0; c < GM_BN; c += 32) {
+      uint32_t v[32];
+      tmem_ld32(lane_base + c, v);
+      tmem_wait_ld();
+      const int col0 = n0 + c;
+      if (!row_ok || col0 >= N) continue;
+      float4* d = reinterpret_cast<float4*>(rowp + col0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        d[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                           __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+    }
     return;
   }
   if constexpr (EPI == EPI_SWIGLU) {
@@ -515,6 +546,17 @@ void launch_gemm_bf16_routed(const GemmArgs& a, const GemmRoute& r, const float*
   p.rope_sin = r.rope_sin;
   p.ld_rope = r.ld_rope;
   launch_gemm<EPI_ROUTE>(a, p, stream);
+}
+
+void launch_gemm_bf16_f32_scatter(const GemmArgs& a, void* out, int64_t ldo, const RowScatter& sc,
+                                  int* err, cudaStream_t stream) {
+  if (a.M == 0 || a.N == 0) return;
+  EpiParams p{};
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.scatter = sc;
+  p.err = err;
+  launch_gemm<EPI_STORE_F32>(a, p, stream);
 }
 
 void launch_gemm_bf16(const GemmArgs& a, int mode, void* out, int64_t ldo, const float* bias,

@@ -52,7 +52,7 @@ constexpr int F8_REGS_HIGH = 208;
 static_assert(F8_A_BYTES + F8_B_BYTES + F8_SFA_BYTES + F8_SFB_BYTES <= F8_STAGE_BYTES, "stage");
 static_assert(128 * F8_REGS_LOW + 256 * F8_REGS_HIGH <= F8_THREADS * 168, "register split");
 
-enum Fp8Epi : int { F8_STORE = 0, F8_RESIDUAL = 1, F8_SWIGLU_Q = 2, F8_ROUTE = 3 };
+enum Fp8Epi : int { F8_STORE = 0, F8_RESIDUAL = 1, F8_SWIGLU_Q = 2, F8_ROUTE = 3, F8_STORE_F32 = 4 };
 
 struct Fp8Params {
   const uint8_t* sfa;          // blocked scale factors of A
@@ -67,6 +67,7 @@ struct Fp8Params {
   int64_t ldq;
   uint8_t* q_sf;               // SWIGLU_Q: blocked scale factors of q_out
   GemmRoute route;             // ROUTE: destinations and the q/k head processing
+  RowScatter scatter;          // STORE_F32: rows to their tensor-parallel owners
   int* err;
 };
 
@@ -217,6 +218,26 @@ __device__ __forceinline__ void f8_epilogue(const Fp8Params& p, const uint32_t* 
   if (!row_ok || col0 >= N) return;
   if constexpr (EPI == F8_ROUTE) {
     f8_route_epilogue(p, v, col0, row, N);
+    return;
+  }
+  if constexpr (EPI == F8_STORE_F32) {
+    // fp32 partial sums, no bias: the reduce-scatter of a row-parallel GEMM
+    float* rowp;
+    if (p.scatter.n == 0) {
+      rowp = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
+    } else {
+      const int64_t g = p.scatter.row0 + row;
+      const int r = (int)(g / p.scatter.rows_per_rank);
+      rowp = reinterpret_cast<float*>(p.scatter.base[r]) +
+             (g - (int64_t)r * p.scatter.rows_per_rank) * p.ldo;
+    }
+#pragma unroll
+    for (int c = 0; c < 128; c += 4) {
+      if (col0 + c >= N) break;
+      *reinterpret_cast<float4*>(rowp + col0 + c) =
+          make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
+                      __uint_as_float(v[c + 3]));
+    }
     return;
   }
 #pragma unroll
@@ -462,6 +483,20 @@ void launch_gemm_fp8(const GemmFp8Args& a, int mode, void* out, int64_t ldo, con
     case F8_SWIGLU_Q: launch_fp8<F8_SWIGLU_Q>(a, p, stream); break;
     default: throw std::runtime_error("unknown fp8 GEMM epilogue mode");
   }
+}
+
+void launch_gemm_fp8_f32_scatter(const GemmFp8Args& a, void* out, int64_t ldo, const RowScatter& sc,
+                                 int* err, cudaStream_t stream) {
+  if (a.M == 0 || a.N == 0) return;
+  if (a.K % F8_BK) throw std::runtime_error("fp8 GEMM: K must be a multiple of 128");
+  Fp8Params p{};
+  p.sfa = reinterpret_cast<const uint8_t*>(a.sfa);
+  p.sfb = reinterpret_cast<const uint8_t*>(a.sfb);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.scatter = sc;
+  p.err = err;
+  launch_fp8<F8_STORE_F32>(a, p, stream);
 }
 
 void launch_gemm_fp8_routed(const GemmFp8Args& a, const GemmRoute& r, const float* bias, int* err,

@@ -78,9 +78,29 @@ void launch_gemm_fp8(const GemmFp8Args& a, int mode, void* out, int64_t ldo, con
                      void* q_sf, int* err, cudaStream_t stream);
 void launch_gemm_fp8_routed(const GemmFp8Args& a, const GemmRoute& r, const float* bias, int* err,
                             cudaStream_t stream);
+void launch_gemm_fp8_f32_scatter(const GemmFp8Args& a, void* out, int64_t ldo, const RowScatter& sc,
+                                 int* err, cudaStream_t stream);
+void launch_gemm_bf16_f32_scatter(const GemmArgs& a, void* out, int64_t ldo, const RowScatter& sc,
+                                  int* err, cudaStream_t stream);
+void launch_residual_combine(void* x, int64_t ldx, const float* a, const float* b, int64_t ldp,
+                             const float* bias, const void* gate, int64_t ldg, const int* idx,
+                             int R, int D, cudaStream_t stream);
 void launch_quant_rows(const void* x, int64_t ldx, int M, int K, void* q, int64_t ldq, void* sf,
                        cudaStream_t stream);
 
+// Destinations of the AdaLN norm: up to two copies (this GPU's buffer and a peer's, for a
+// tensor-parallel all-gather done by the producer) of the bf16 rows and/or their E4M3
+// quantisation; local row r lands at row row0 + r of each.
+struct NormDst {
+  __nv_bfloat16* out[2];
+  uint8_t* q[2];
+  uint8_t* qsf[2];
+  int64_t ldo, ldq, row0;
+};
+void launch_adaln_rmsnorm_dst(const void* x, int64_t ldx, const float* w, float eps,
+                              const void* table, int64_t ldt, int shift_col, int scale_col,
+                              const int* idx, const NormDst& dst, int T, int D,
+                              cudaStream_t stream);
 // out (bf16) and/or q + qsf (E4M3 with one scale per 1x128 block; D % 256 == 0)
 void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps, const void* table,
                           int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,

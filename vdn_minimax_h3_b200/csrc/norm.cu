@@ -16,8 +16,7 @@ template <int VPL>
 __global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t ldx, const float* __restrict__ w, float eps,
     const __nv_bfloat16* __restrict__ table, int64_t ldt, int shift_col, int scale_col,
-    const int* __restrict__ idx, __nv_bfloat16* __restrict__ out, int64_t ldo, int T, int D,
-    uint8_t* __restrict__ q, int64_t ldq, uint8_t* __restrict__ qsf) {
+    const int* __restrict__ idx, NormDst dst, int T, int D) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -42,7 +41,7 @@ __global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
   const float rstd = rsqrtf(ss / (float)D + eps);
   const int ti = idx[row];
   const __nv_bfloat16* trow = table + (int64_t)ti * ldt;
-  uint4* orow = reinterpret_cast<uint4*>(out + (int64_t)row * ldo);
+  const int64_t drow = dst.row0 + row;   // row in the destination buffers
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int c = lane + i * 32;
@@ -67,8 +66,12 @@ __global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
         b = b * (1.f + bf16_hi(scu[j])) + bf16_hi(shu[j]);
         res[j] = pack_bf16(a, b);
       }
-      if (out) orow[c] = make_uint4(res[0], res[1], res[2], res[3]);
-      if (q) {
+#pragma unroll
+      for (int d = 0; d < 2; ++d)
+        if (dst.out[d])
+          reinterpret_cast<uint4*>(dst.out[d] + drow * dst.ldo)[c] =
+              make_uint4(res[0], res[1], res[2], res[3]);
+      if (dst.q[0]) {
         // E4M3 copy for an fp8 GEMM: a half-warp holds one 1x128 block (D % 256 == 0, so
         // every lane of the warp is here); the bf16-rounded values are quantised
         float f[8];
@@ -88,11 +91,14 @@ __global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
                             ((uint32_t)pack_e4m3x2(f[2] * inv, f[3] * inv) << 16);
         const uint32_t hi = (uint32_t)pack_e4m3x2(f[4] * inv, f[5] * inv) |
                             ((uint32_t)pack_e4m3x2(f[6] * inv, f[7] * inv) << 16);
-        *reinterpret_cast<uint2*>(q + (int64_t)row * ldq + c * 8) = make_uint2(lo, hi);
-        if ((lane & 15) == 0) {
-          const uint32_t bb = (uint32_t)(e + 127) & 0xFF;
-          *reinterpret_cast<uint32_t*>(qsf + sf_offset(row, (int64_t)(c / 16) * 4, D / 32)) =
-              bb | (bb << 8) | (bb << 16) | (bb << 24);
+        const uint32_t bb = (uint32_t)(e + 127) & 0xFF;
+#pragma unroll
+        for (int d = 0; d < 2; ++d) {
+          if (!dst.q[d]) continue;
+          *reinterpret_cast<uint2*>(dst.q[d] + drow * dst.ldq + c * 8) = make_uint2(lo, hi);
+          if ((lane & 15) == 0)
+            *reinterpret_cast<uint32_t*>(dst.qsf[d] + sf_offset(drow, (int64_t)(c / 16) * 4, D / 32)) =
+                bb | (bb << 8) | (bb << 16) | (bb << 24);
         }
       }
     }
@@ -103,18 +109,28 @@ void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps,
                           int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
                           int64_t ldo, int T, int D, cudaStream_t stream, void* q, int64_t ldq,
                           void* qsf) {
+  NormDst dst{};
+  dst.out[0] = reinterpret_cast<__nv_bfloat16*>(out);
+  dst.ldo = ldo;
+  dst.q[0] = reinterpret_cast<uint8_t*>(q);
+  dst.qsf[0] = reinterpret_cast<uint8_t*>(qsf);
+  dst.ldq = ldq;
+  launch_adaln_rmsnorm_dst(x, ldx, w, eps, table, ldt, shift_col, scale_col, idx, dst, T, D, stream);
+}
+
+void launch_adaln_rmsnorm_dst(const void* x, int64_t ldx, const float* w, float eps,
+                              const void* table, int64_t ldt, int shift_col, int scale_col,
+                              const int* idx, const NormDst& dst, int T, int D,
+                              cudaStream_t stream) {
   if (T == 0) return;
   const int nvec = D / 8;
   const int need = (nvec + 31) / 32;
   dim3 grid((T + 7) / 8), block(256);
   auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
   auto tb = reinterpret_cast<const __nv_bfloat16*>(table);
-  auto ob = reinterpret_cast<__nv_bfloat16*>(out);
 #define VDN_ADALN(N)                                                                          \
   adaln_rmsnorm_kernel<N><<<grid, block, 0, stream>>>(xb, ldx, w, eps, tb, ldt, shift_col,    \
-                                                       scale_col, idx, ob, ldo, T, D,           \
-                                                       reinterpret_cast<uint8_t*>(q), ldq,         \
-                                                       reinterpret_cast<uint8_t*>(qsf))
+                                                       scale_col, idx, dst, T, D)
   if (need <= 1) VDN_ADALN(1);
   else if (need <= 2) VDN_ADALN(2);
   else if (need <= 4) VDN_ADALN(4);
@@ -226,6 +242,52 @@ void launch_qk_prep(const void* src, int64_t lds, int T, int H, int d, const flo
   qk_prep_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(src), lds, T, H, d, w, eps, cosv, sinv, rot,
       reinterpret_cast<__nv_bfloat16*>(out), ldo);
+}
+
+// Tensor-parallel residual: x += gate[idx[r]] * (a + b + bias), a and b the two ranks'
+// fp32 partial sums of a row-parallel GEMM for this rank's rows. One warp per row, 8
+// columns per lane per step.
+__global__ void __launch_bounds__(256) residual_combine_kernel(
+    __nv_bfloat16* __restrict__ x, int64_t ldx, const float* __restrict__ a,
+    const float* __restrict__ b, int64_t ldp, const float* __restrict__ bias,
+    const __nv_bfloat16* __restrict__ gate, int64_t ldg, const int* __restrict__ idx, int R,
+    int D) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= R) return;
+  const __nv_bfloat16* g = gate + (int64_t)idx[row] * ldg;
+  for (int c = lane * 8; c < D; c += 256) {
+    const float4 a0 = *reinterpret_cast<const float4*>(a + (int64_t)row * ldp + c);
+    const float4 a1 = *reinterpret_cast<const float4*>(a + (int64_t)row * ldp + c + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(b + (int64_t)row * ldp + c);
+    const float4 b1 = *reinterpret_cast<const float4*>(b + (int64_t)row * ldp + c + 4);
+    float y[8] = {a0.x + b0.x, a0.y + b0.y, a0.z + b0.z, a0.w + b0.w,
+                  a1.x + b1.x, a1.y + b1.y, a1.z + b1.z, a1.w + b1.w};
+    if (bias) {
+      const float4 c0 = *reinterpret_cast<const float4*>(bias + c);
+      const float4 c1 = *reinterpret_cast<const float4*>(bias + c + 4);
+      y[0] += c0.x; y[1] += c0.y; y[2] += c0.z; y[3] += c0.w;
+      y[4] += c1.x; y[5] += c1.y; y[6] += c1.z; y[7] += c1.w;
+    }
+    uint4 xv = *reinterpret_cast<const uint4*>(x + (int64_t)row * ldx + c);
+    const uint4 gv = *reinterpret_cast<const uint4*>(g + c);
+    uint32_t* xw = reinterpret_cast<uint32_t*>(&xv);
+    const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      xw[j] = pack_bf16(bf16_lo(xw[j]) + bf16_lo(gw[j]) * y[2 * j],
+                        bf16_hi(xw[j]) + bf16_hi(gw[j]) * y[2 * j + 1]);
+    *reinterpret_cast<uint4*>(x + (int64_t)row * ldx + c) = xv;
+  }
+}
+
+void launch_residual_combine(void* x, int64_t ldx, const float* a, const float* b, int64_t ldp,
+                             const float* bias, const void* gate, int64_t ldg, const int* idx,
+                             int R, int D, cudaStream_t stream) {
+  if (R == 0) return;
+  residual_combine_kernel<<<(R + 7) / 8, 256, 0, stream>>>(
+      reinterpret_cast<__nv_bfloat16*>(x), ldx, a, b, ldp, bias,
+      reinterpret_cast<const __nv_bfloat16*>(gate), ldg, idx, R, D);
 }
 
 }  // namespace vdn

@@ -300,6 +300,108 @@ void adaln_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void adaln_rmsnorm_dst(torch::Tensor x, c10::optional<torch::Tensor> w, double eps,
+                       torch::Tensor table, int64_t shift_col, int64_t scale_col, torch::Tensor idx,
+                       int64_t row0, std::vector<torch::Tensor> outs, std::vector<torch::Tensor> qs,
+                       std::vector<torch::Tensor> sfs) {
+  check_2d_bf16(x, "x");
+  check_2d_bf16(table, "table");
+  const int T = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % 256 == 0, "adaln_rmsnorm_dst needs D % 256 == 0");
+  TORCH_CHECK(outs.size() <= 2 && qs.size() <= 2 && qs.size() == sfs.size() &&
+                  (outs.size() + qs.size()) > 0,
+              "one or two bf16 and/or E4M3 destinations");
+  NormDst dst{};
+  dst.row0 = row0;
+  for (size_t i = 0; i < outs.size(); ++i) {
+    check_2d_bf16(outs[i], "out");
+    TORCH_CHECK(outs[i].size(1) == D && outs[i].size(0) >= row0 + T, "out too small");
+    TORCH_CHECK(i == 0 || outs[i].stride(0) == outs[0].stride(0), "outs share a row stride");
+    dst.out[i] = reinterpret_cast<__nv_bfloat16*>(outs[i].data_ptr());
+    dst.ldo = outs[i].stride(0);
+  }
+  for (size_t i = 0; i < qs.size(); ++i) {
+    check_2d_bytes(qs[i], "q");
+    TORCH_CHECK(qs[i].size(1) == D && qs[i].size(0) >= row0 + T, "q too small");
+    TORCH_CHECK(i == 0 || qs[i].stride(0) == qs[0].stride(0), "qs share a row stride");
+    check_sf(sfs[i], ((qs[i].size(0) + 127) / 128) * (D / 128) * 512, "sf");
+    dst.q[i] = reinterpret_cast<uint8_t*>(qs[i].data_ptr());
+    dst.qsf[i] = reinterpret_cast<uint8_t*>(sfs[i].data_ptr());
+    dst.ldq = qs[i].stride(0);
+  }
+  TORCH_CHECK(shift_col % 8 == 0 && scale_col % 8 == 0, "table columns must be 8-aligned");
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.is_contiguous() &&
+                  idx.numel() >= T, "idx must be contiguous int32 [T]");
+  c10::cuda::CUDAGuard g(x.device());
+  const float* wp = opt_f32(w, D, "w");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(wp) % 16 == 0, "norm weight must be 16-byte aligned");
+  launch_adaln_rmsnorm_dst(x.data_ptr(), x.stride(0), wp, (float)eps, table.data_ptr(),
+                           table.stride(0), (int)shift_col, (int)scale_col, idx.data_ptr<int>(),
+                           dst, T, D, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gemm_f32_scatter(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> sfa,
+                      c10::optional<torch::Tensor> sfb, torch::Tensor out,
+                      std::vector<int64_t> bases, int64_t row0, int64_t rows, torch::Tensor err) {
+  // fp32 partial products stored to their row owners (bf16 operands, or E4M3 with sfa/sfb)
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.dim() == 2 &&
+                  out.stride(1) == 1 && out.stride(0) % 4 == 0,
+              "out must be fp32 2-D with 16-byte aligned rows");
+  RowScatter sc{};
+  TORCH_CHECK(bases.size() <= (size_t)kMaxScatterRanks, "at most 8 owners");
+  sc.n = (int)bases.size();
+  for (size_t i = 0; i < bases.size(); ++i) {
+    TORCH_CHECK(bases[i] % 16 == 0, "scatter destinations must be 16-byte aligned");
+    sc.base[i] = reinterpret_cast<__nv_bfloat16*>(bases[i]);
+  }
+  sc.row0 = row0;
+  sc.rows_per_rank = (int)rows;
+  c10::cuda::CUDAGuard g(A.device());
+  if (sfa) {
+    check_2d_bytes(A, "A");
+    check_2d_bytes(B, "B");
+    const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+    TORCH_CHECK(K % 128 == 0 && N % 32 == 0 && B.size(1) == K, "fp8 shapes");
+    TORCH_CHECK(sc.n || (out.size(0) == M && out.size(1) == N), "out shape mismatch");
+    check_sf(*sfa, ((M + 127) / 128) * (K / 128) * 512, "sfa");
+    check_sf(*sfb, ((N + 255) / 256) * (K / 128) * 1024, "sfb");
+    GemmFp8Args a{A.data_ptr(), B.data_ptr(), A.stride(0), B.stride(0), sfa->data_ptr(),
+                  sfb->data_ptr(), (int)M, (int)N, (int)K};
+    launch_gemm_fp8_f32_scatter(a, out.data_ptr(), out.stride(0), sc, err_ptr(err),
+                                at::cuda::getCurrentCUDAStream());
+  } else {
+    GemmArgs a = gemm_args(A, B);
+    TORCH_CHECK(a.N % 32 == 0, "N % 32 == 0");
+    TORCH_CHECK(sc.n || (out.size(0) == a.M && out.size(1) == a.N), "out shape mismatch");
+    launch_gemm_bf16_f32_scatter(a, out.data_ptr(), out.stride(0), sc, err_ptr(err),
+                                 at::cuda::getCurrentCUDAStream());
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void residual_combine(torch::Tensor x, torch::Tensor a, torch::Tensor b,
+                      c10::optional<torch::Tensor> bias, torch::Tensor gate, torch::Tensor idx) {
+  check_2d_bf16(x, "x");
+  check_2d_bf16(gate, "gate");
+  const int R = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % 8 == 0, "D % 8 == 0");
+  for (const auto* t : {&a, &b}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->dim() == 2 &&
+                    t->size(0) >= R && t->size(1) == D && t->stride(1) == 1 &&
+                    t->stride(0) == a.stride(0) && t->stride(0) % 4 == 0,
+                "partials must be fp32 [>=R, D] with one 16-byte aligned row stride");
+  }
+  TORCH_CHECK(gate.size(1) >= D, "gate table narrower than D");
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.is_contiguous() &&
+                  idx.numel() >= R, "idx must be contiguous int32 [R]");
+  c10::cuda::CUDAGuard g(x.device());
+  launch_residual_combine(x.data_ptr(), x.stride(0), a.data_ptr<float>(), b.data_ptr<float>(),
+                          a.stride(0), opt_f32(bias, D, "bias"), gate.data_ptr(), gate.stride(0),
+                          idx.data_ptr<int>(), R, D, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void frame_sums(torch::Tensor x, int64_t row0, int64_t video_start, int64_t F, int64_t S,
                 torch::Tensor out) {
   check_2d_bf16(x, "x");
@@ -624,6 +726,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8_routed", &vdn::gemm_fp8_routed,
         "block-scaled E4M3 GEMM with the routed epilogue (column routes, QK-norm + RoPE)");
   m.def("quant_rows", &vdn::quant_rows, "bf16 rows -> E4M3 with one UE8M0 scale per 1x128 block");
+  m.def("adaln_rmsnorm_dst", &vdn::adaln_rmsnorm_dst,
+        "AdaLN-RMSNorm into up to two destinations (local + peer) at a row offset, bf16 and/or E4M3");
+  m.def("gemm_f32_scatter", &vdn::gemm_f32_scatter,
+        "GEMM whose fp32 partial rows go to their owners (row-parallel GEMM -> reduce-scatter)");
+  m.def("residual_combine", &vdn::residual_combine,
+        "x += gate[idx] * (partial_a + partial_b + bias)");
   m.def("adaln_rmsnorm", &vdn::adaln_rmsnorm, "RMSNorm * w * (1 + scale[idx]) + shift[idx]");
   m.def("frame_sums", &vdn::frame_sums, "per-frame fp32 column sums of video rows");
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");

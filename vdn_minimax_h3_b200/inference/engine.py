@@ -115,6 +115,7 @@ class PackedBlock:
                 self.w8_up = Fp8Weight(*gemm.interleave_swiglu_rows(up.weight.data, up.bias,
                                                                     tile=128))
             self.w8_down = Fp8Weight(ff.net[2].weight.data, ff.net[2].bias)
+            self.w8_o = Fp8Weight(Wo, orig.to_out[0].bias)
         if self.ff_act == "swiglu":
             wi, bi = gemm.interleave_swiglu_rows(up.weight.data, up.bias)
             up.weight.data = wi   # NOTE: the module now holds the interleaved layout
@@ -259,7 +260,15 @@ class InferenceEngine:
                 cat[:, inner:].zero_()
                 self._cat_dirty = False
         with sec("gemm_o"):
-            gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D], adaln_idx)
+            if f8:
+                cq = self._buf("cat_q", tuple(cat.shape), torch.uint8, dev)
+                csf = self._buf("cat_sf", (fp8_ops.sf_bytes(T, cat.shape[1]),), torch.uint8, dev)
+                fp8_ops.quantize_act(cat, cq, csf)
+                fp8_ops.linear_fp8_gated_residual(cq, csf, pb.w8_o, x, table[:, 2 * D:3 * D],
+                                                  adaln_idx)
+            else:
+                gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D],
+                                           adaln_idx)
         n2 = n1
         if f8 and pb.ff_interleaved:
             with sec("norm"):

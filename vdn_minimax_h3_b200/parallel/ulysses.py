@@ -209,8 +209,15 @@ class UlyssesEngine:
         with sec("adaln_table"):
             table = gemm.linear(temb_act, pb.adaln_w, pb.adaln_b).view(-1, 6 * D)
         n1 = self._buf("n1", (rows, D), x.dtype, dev)
+        f8 = pb.fp8 and x.is_cuda and fused_qk_ok(pb, rope[0])
+        if f8:
+            from vdn_minimax_h3_b200.ops import fp8 as fp8_ops
+            nq = self._buf("n_q", (rows, D), torch.uint8, dev)
+            nsf = self._buf("n_sf", (fp8_ops.sf_bytes(rows, D),), torch.uint8, dev)
         with sec("norm"):
-            norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx, out=n1)
+            norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx,
+                                   out=n1 if (linear_on or not f8) else False,
+                                   fp8_out=(nq, nsf) if f8 else None)
         work = None
         if linear_on:
             fsum = norm_ops.frame_sums(n1, layout.num_frames, layout.tokens_per_frame, a0,
@@ -237,7 +244,10 @@ class UlyssesEngine:
             if route is None:
                 route = self._routes[key] = self._route(pb, [send[p, :rows] for p in range(P)], offs)
         with sec("gemm_qkv"):
-            if x.is_cuda and not fused_qk_ok(pb, cos):
+            if f8:
+                fp8_ops.linear_routed_fp8(nq, nsf, pb.w8_qkvg, route, c["q"], c["k"], pb.norm_q,
+                                          pb.norm_k, pb.qk_eps, cos, sin)
+            elif x.is_cuda and not fused_qk_ok(pb, cos):
                 # heads other than 128 wide: projection, then QK-prep, then the placement
                 qkvg = self._buf("qkvg", (rows, pb.w_qkvg.shape[0]), x.dtype, dev)
                 gemm.linear(n1, pb.w_qkvg, pb.b_qkvg, out=qkvg)
@@ -307,8 +317,29 @@ class UlyssesEngine:
                 src = back[:, :rows].unflatten(-1, (2, Hp, d))[:, :, :nb]
                 cat.view(rows, nb, P, Hp, d).copy_(src.permute(1, 2, 0, 3, 4))
         with sec("gemm_o"):
-            gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D], adaln_idx)
+            if f8:
+                cq = self._buf("cat_q", tuple(cat.shape), torch.uint8, dev)
+                csf = self._buf("cat_sf", (fp8_ops.sf_bytes(rows, cat.shape[1]),), torch.uint8, dev)
+                fp8_ops.quantize_act(cat, cq, csf)
+                fp8_ops.linear_fp8_gated_residual(cq, csf, pb.w8_o, x, table[:, 2 * D:3 * D],
+                                                  adaln_idx)
+            else:
+                gemm.linear_gated_residual(cat, pb.w_o, pb.b_o, x, table[:, 2 * D:3 * D],
+                                           adaln_idx)
         n2 = n1
+        if f8 and pb.ff_interleaved:
+            with sec("norm"):
+                norm_ops.adaln_rmsnorm(x, pb.norm2, pb.eps, table, 3 * D, 4 * D, adaln_idx,
+                                       out=False, fp8_out=(nq, nsf))
+            inter = pb.w8_up.shape[0] // 2
+            hq = self._buf("h_q", (rows, inter), torch.uint8, dev)
+            hsf = self._buf("h_sf", (fp8_ops.sf_bytes(rows, inter),), torch.uint8, dev)
+            with sec("gemm_ff_up"):
+                fp8_ops.linear_fp8_swiglu(nq, nsf, pb.w8_up, hq, hsf)
+            with sec("gemm_ff_down"):
+                fp8_ops.linear_fp8_gated_residual(hq, hsf, pb.w8_down, x, table[:, 5 * D:6 * D],
+                                                  adaln_idx)
+            return x
         with sec("norm"):
             norm_ops.adaln_rmsnorm(x, pb.norm2, pb.eps, table, 3 * D, 4 * D, adaln_idx, out=n2)
         with sec("gemm_ff_up"):
