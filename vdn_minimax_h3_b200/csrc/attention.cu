@@ -10,22 +10,23 @@
 // Roles (384 threads = 3 warpgroups, one CTA per SM, persistent over head-major work items
 // so the CTAs in flight share one head's K/V in L2):
 //   warp 0      TMA producers: lane 0 both Q tiles once per item and K blocks into a
-//               2-stage ring, lane 1 V blocks (single buffer, refilled while the softmax
-//               of the block runs).
-//   warp 1      MMA issuer (one thread): per block, S_t = Q_t K^T for both tiles into TMEM
-//               (kind::f16, M=128, N=128), then O_t += P_t V for the previous block (P from
-//               shared memory, V as an MN-major operand).
+//               2-stage ring, lane 1 V blocks into a 2-stage ring.
+//   warp 1      MMA issuer (one thread): per block j and tile t, first O_t += P_t V for
+//               block j-1 with P read from TMEM (tcgen05.mma with the A operand in TMEM),
+//               then S_t = Q_t K_j^T (kind::f16, M=128, N=128) into the same TMEM columns;
+//               MMAs execute in issue order, so the S write follows the P read.
 //   warps 2-3   idle (they complete warpgroup 0, whose registers go to the softmax)
 //   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1 (thread = query row): S row
-//               from TMEM, online softmax in the exp2 domain with a lazy rescale (O in TMEM
-//               is rescaled only when the running max grows by more than 2^8), P written as
-//               bf16 into the 128B-swizzled shared operand, epilogue O / l * sigmoid(gate).
-//               While one tile's softmax runs, the tensor core works on the other tile.
-//               A fraction of the exponentials run as a cubic polynomial on the FMA pipe
-//               (2^x = 2^n * p(f), Cody-Waite split, p fitted for minimax relative error
-//               8.6e-5 on [0,1)) so the MUFU unit is not the bottleneck.
-// TMEM (512 columns): S[tile] at 128 * tile, O[tile] at 256 + 128 * tile. The softmax warps
-// copy S to registers first thing, so the next block's S MMA can start while they work.
+//               from TMEM into registers, online softmax in the exp2 domain with a lazy
+//               rescale (O in TMEM is rescaled only when the running max grows by more
+//               than 2^8), P written back as packed bf16 over S in TMEM, epilogue
+//               O / l * sigmoid(gate). While one tile's softmax runs, the tensor core works
+//               on the other tile. Keeping P out of shared memory leaves the shared-memory
+//               bandwidth to the Q, K and V operand reads. Optionally a fraction of the
+//               exponentials run as a cubic polynomial on the FMA pipe (2^x = 2^n * p(f),
+//               Cody-Waite split, p fitted for minimax relative error 8.6e-5 on [0,1)).
+// TMEM (512 columns): S[tile] (and P over its first 64 columns) at 128 * tile, O[tile] at
+// 256 + 128 * tile.
 //
 // Every wait is bounded; a protocol failure unwinds, drains and frees TMEM (common.cuh).
 // Reference parity: the window softmax of src/models/softmax_attention/ (decomposed.py's
@@ -41,7 +42,8 @@ namespace vdn {
 constexpr int AT_BM = 128;                         // query rows per tile (2 tiles per item)
 constexpr int AT_BN = 128;                         // keys per block
 constexpr int AT_D = 128;                          // head dim
-constexpr int AT_KSTAGES = 2;                      // K ring; V is single-buffered
+constexpr int AT_KSTAGES = 2;                      // K ring
+constexpr int AT_VSTAGES = 2;                      // V ring
 constexpr int AT_Q_BYTES = AT_BM * AT_D * 2;       // 32 KB per Q tile (2 atoms of 16 KB)
 constexpr int AT_KV_BYTES = AT_BN * AT_D * 2;      // 32 KB per K or V block (2 atoms of 16 KB)
 constexpr int AT_P_BYTES = AT_BM * AT_BN * 2;      // 32 KB per P tile (2 atom columns)
@@ -51,7 +53,7 @@ constexpr int AT_THREADS = 384;
 constexpr int AT_REGS_LOW = 80;
 constexpr int AT_REGS_HIGH = 208;
 static_assert(128 * AT_REGS_LOW + 256 * AT_REGS_HIGH <= AT_THREADS * 168, "register split");
-constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + 1) * AT_KV_BYTES + 2 * AT_P_BYTES + 1024 + 384;
+constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + AT_VSTAGES) * AT_KV_BYTES + 1024 + 384;
 constexpr int AT_MAX_RANGES = 4;
 // One exponential in every 8 * POLY_EVERY runs on the FMA pipe (0: all on MUFU); the
 // launcher picks the instance (attention_set_poly_every, default 0: measured fastest,
@@ -138,23 +140,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                   // [2 tiles][32 KB]
-  uint8_t* sK = sQ + 2 * AT_Q_BYTES;                    // [2 stages][32 KB]
-  uint8_t* sV = sK + AT_KSTAGES * AT_KV_BYTES;          // [32 KB]
-  uint8_t* sP = sV + AT_KV_BYTES;                       // [2 tiles][32 KB]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * AT_P_BYTES);
+  uint8_t* sK = sQ + 2 * AT_Q_BYTES;                    // [AT_KSTAGES][32 KB]
+  uint8_t* sV = sK + AT_KSTAGES * AT_KV_BYTES;          // [AT_VSTAGES][32 KB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + AT_VSTAGES * AT_KV_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;             // [2]
-  uint64_t* k_empty = bars + 4;            // [2]
-  uint64_t* v_full = bars + 6;
-  uint64_t* v_empty = bars + 7;
-  uint64_t* s_full = bars + 8;             // [tile]
-  uint64_t* s_empty = bars + 10;           // [tile]
-  uint64_t* p_full = bars + 12;            // [tile]
-  uint64_t* pv_done = bars + 14;           // [tile]
-  uint64_t* o_empty = bars + 16;           // [tile]
-  uint64_t* mma_done = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t* k_full = bars + 2;                   // [AT_KSTAGES]
+  uint64_t* k_empty = k_full + AT_KSTAGES;       // [AT_KSTAGES]
+  uint64_t* v_full = k_empty + AT_KSTAGES;       // [AT_VSTAGES]
+  uint64_t* v_empty = v_full + AT_VSTAGES;       // [AT_VSTAGES]
+  uint64_t* s_full = v_empty + AT_VSTAGES;       // [tile]
+  uint64_t* p_full = s_full + 2;                 // [tile]
+  uint64_t* pv_done = p_full + 2;                // [tile]
+  uint64_t* o_empty = pv_done + 2;               // [tile]
+  uint64_t* mma_done = o_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -167,11 +167,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
     }
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
+    for (int s = 0; s < AT_VSTAGES; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_empty[t], 128);
       mbar_init(&p_full[t], 128);
       mbar_init(&pv_done[t], 1);
       mbar_init(&o_empty[t], 128);
@@ -249,9 +250,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
     } else if (lane == 1) {
       tma_prefetch_desc(&tmV);
+      int stage = 0;
       uint32_t phase = 0;
-      int last = -1;
       bool ok = true;
+      int last_phase[AT_VSTAGES];
+      for (int i = 0; i < AT_VSTAGES; ++i) last_phase[i] = -1;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         int head, tile;
         item_coords(p, item, head, tile);
@@ -259,32 +262,42 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         for (; !w.done(); w.next()) {
-          if (!mbar_wait(v_empty, phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+          if (!mbar_wait(&v_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
-          last = (int)phase;
-          mbar_arrive_expect_tx(v_full, AT_KV_BYTES);
-          tma_load_2d(sV, &tmV, v_full, head * AT_D, w.start());
-          tma_load_2d(sV + AT_KV_BYTES / 2, &tmV, v_full, head * AT_D + 64, w.start());
-          phase ^= 1;
+          uint8_t* v = sV + stage * AT_KV_BYTES;
+          last_phase[stage] = (int)phase;
+          mbar_arrive_expect_tx(&v_full[stage], AT_KV_BYTES);
+          tma_load_2d(v, &tmV, &v_full[stage], head * AT_D, w.start());
+          tma_load_2d(v + AT_KV_BYTES / 2, &tmV, &v_full[stage], head * AT_D + 64, w.start());
+          if (++stage == AT_VSTAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
       }
-      if ((!ok || *abort_flag) && last >= 0) {
+      if (!ok || *abort_flag) {
         long long t0 = clock64();
-        while (!mbar_try_wait(v_full, (uint32_t)last) && clock64() - t0 < kWaitBudgetCycles) {
+        for (int i = 0; i < AT_VSTAGES; ++i) {
+          if (last_phase[i] < 0) continue;
+          while (!mbar_try_wait(&v_full[i], (uint32_t)last_phase[i]) && clock64() - t0 < kWaitBudgetCycles) {
+          }
         }
       }
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------------- MMA issuer
+    // Per block j and tile t, in this order: O_t += P_t(j-1) V(j-1) with P read from TMEM
+    // (where the softmax stored it over S_t), then S_t = Q_t K(j)^T. MMAs run in issue
+    // order, so the S_t write follows the P_t read.
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(AT_BM, AT_BN, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(AT_BM, AT_D, false, true);
-      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP), aV = smem_u32(sV);
-      int stage = 0;
-      uint32_t phase = 0, vphase = 0;
-      uint32_t g = 0;  // global block counter: S_t / P_t / PV_t phases are g & 1
+      const uint32_t aQ = smem_u32(sQ), aV0 = smem_u32(sV);
+      int kstage = 0, vstage = 0;
+      uint32_t kphase = 0, vphase = 0;
+      uint32_t g = 0;  // global block counter: S_t / P_t phases are g & 1
       int local = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++local) {
@@ -296,41 +309,34 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         int j = 0;
-        uint32_t g_prev = 0;
-        while (true) {
+        while (ok) {
           const bool have = !w.done();
+          if (!have && j == 0) {
+            // no K/V at all: release the epilogue (it writes zeros)
+            umma_commit(&pv_done[0]);
+            umma_commit(&pv_done[1]);
+            break;
+          }
+          uint32_t aK = 0, aV = 0;
           if (have) {
-            if (!mbar_wait(&k_full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+            if (!mbar_wait(&k_full[kstage], kphase, abort_flag, p.err, kErrTimeoutMma)) {
               ok = false;
               break;
             }
-            const uint32_t aK = smem_u32(sK + stage * AT_KV_BYTES);
-            for (int qt = 0; qt < 2 && ok; ++qt) {
-              // S_t is free once the softmax warps copied the previous S_t to registers
-              if (!mbar_wait(&s_empty[qt], (g & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-#pragma unroll
-              for (int k = 0; k < AT_D / 16; ++k) {
-                const uint32_t off = (k >> 2) * (AT_Q_BYTES / 2) + (k & 3) * 32;
-                umma_f16_ss(tmem + qt * AT_BN, umma_desc_kmajor_sw128(aQ + qt * AT_Q_BYTES + off),
-                            umma_desc_kmajor_sw128(aK + off), idesc_s, k != 0);
-              }
-              umma_commit(&s_full[qt]);
-            }
-            if (!ok) break;
-            umma_commit(&k_empty[stage]);
+            aK = smem_u32(sK + kstage * AT_KV_BYTES);
           }
           if (j > 0) {
-            // O_t += P_t V for the previous block
-            if (!mbar_wait(v_full, vphase, abort_flag, p.err, kErrTimeoutMma)) {
+            if (!mbar_wait(&v_full[vstage], vphase, abort_flag, p.err, kErrTimeoutMma)) {
               ok = false;
               break;
             }
-            for (int qt = 0; qt < 2 && ok; ++qt) {
-              if (!mbar_wait(&p_full[qt], g_prev & 1, abort_flag, p.err, kErrTimeoutMma) ||
+            aV = aV0 + vstage * AT_KV_BYTES;
+          }
+          tc_fence_after();
+          for (int qt = 0; qt < 2 && ok; ++qt) {
+            const uint32_t tS = tmem + qt * AT_BN;
+            if (j > 0) {
+              if (!mbar_wait(&p_full[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutMma) ||
                   (j == 1 && local > 0 &&
                    !mbar_wait(&o_empty[qt], (local - 1) & 1, abort_flag, p.err, kErrTimeoutMma))) {
                 ok = false;
@@ -338,24 +344,38 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
               }
               tc_fence_after();
 #pragma unroll
-              for (int k = 0; k < AT_BN / 16; ++k) {
-                const uint32_t offP = (k >> 2) * (AT_P_BYTES / 2) + (k & 3) * 32;
-                umma_f16_ss(tmem + 256 + qt * 128, umma_desc_kmajor_sw128(aP + qt * AT_P_BYTES + offP),
+              for (int k = 0; k < AT_BN / 16; ++k)
+                umma_f16_ts(tmem + 256 + qt * 128, tS + k * 8,
                             umma_desc_mnmajor_sw128(aV + k * 2048, AT_KV_BYTES / 2), idesc_o,
                             (j > 1 || k > 0) ? 1u : 0u);
-              }
-              umma_commit(&pv_done[qt]);
+              if (!have) umma_commit(&pv_done[qt]);
             }
-            if (!ok) break;
-            umma_commit(v_empty);
-            vphase ^= 1;
+            if (have) {
+#pragma unroll
+              for (int k = 0; k < AT_D / 16; ++k) {
+                const uint32_t off = (k >> 2) * (AT_Q_BYTES / 2) + (k & 3) * 32;
+                umma_f16_ss(tS, umma_desc_kmajor_sw128(aQ + qt * AT_Q_BYTES + off),
+                            umma_desc_kmajor_sw128(aK + off), idesc_s, k != 0);
+              }
+              umma_commit(&s_full[qt]);
+            }
+          }
+          if (!ok) break;
+          if (have) {
+            umma_commit(&k_empty[kstage]);
+            if (++kstage == AT_KSTAGES) {
+              kstage = 0;
+              kphase ^= 1;
+            }
+          }
+          if (j > 0) {
+            umma_commit(&v_empty[vstage]);
+            if (++vstage == AT_VSTAGES) {
+              vstage = 0;
+              vphase ^= 1;
+            }
           }
           if (!have) break;
-          g_prev = g;
-          if (++stage == AT_KSTAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
           ++g;
           ++j;
           w.next();
@@ -378,7 +398,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + qt * AT_BN;
     const uint32_t tO = tmem + lane_off + 256 + qt * 128;
-    uint8_t* prow = sP + qt * AT_P_BYTES + r * 128;
     uint32_t g = 0;
     int local = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++local) {
@@ -405,8 +424,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(u[i]);
         }
         tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&s_empty[qt]);
         // row max on the raw scores (8 independent chains); only a ragged block is masked
         const int valid = w.valid();
         if (valid < AT_BN) {
@@ -431,61 +448,51 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           m_ref = m_new;
           l *= factor;
         }
-        // p = 2^(s * scale_log2 - m) into packed bf16 registers (the exps overlap the
-        // previous block's P.V on the tensor core)
+        // S_t was issued after the previous block's P.V, so that P.V is complete: O may be
+        // rescaled before this block's P is published.
+        if (j > 0 && warp_need) {
+#pragma unroll 1
+          for (int c = 0; c < AT_D; c += 32) {
+            uint32_t u[32];
+            tmem_ld32(tO + c, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
+            tmem_st32(tO + c, u);
+          }
+        }
+        // p = 2^(s * scale_log2 - m), packed bf16 pairs written over S_t in TMEM
         const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
         float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[AT_BN / 2];
 #pragma unroll
-        for (int c = 0; c < AT_BN; c += 8) {
-          float e[8];
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pk[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float x = fmaf(s[c + i], p.scale_log2, neg_m);
-            e[i] = (AT_POLY_EVERY > 0 && i == 7 && ((c / 8) % AT_POLY_EVERY) == 0) ? ex2_poly(x) : ex2(x);
-            sums[i] += e[i];
+          for (int c = 0; c < 64; c += 8) {
+            float e[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float x = fmaf(s[h * 64 + c + i], p.scale_log2, neg_m);
+              e[i] = (AT_POLY_EVERY > 0 && i == 7 && ((c / 8) % AT_POLY_EVERY) == 0) ? ex2_poly(x) : ex2(x);
+              sums[i] += e[i];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pk[c / 2 + i] = pack_bf16(e[2 * i], e[2 * i + 1]);
           }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) pk[c / 2 + i] = pack_bf16(e[2 * i], e[2 * i + 1]);
+          tmem_st32(tS + h * 32, pk);
         }
         l += ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
-        // P.V of the previous block must finish before O or the P buffer is touched.
-        if (j > 0) {
-          if (!mbar_wait(&pv_done[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          if (warp_need) {
-#pragma unroll 1
-            for (int c = 0; c < AT_D; c += 32) {
-              uint32_t u[32];
-              tmem_ld32(tO + c, u);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
-              tmem_st32(tO + c, u);
-            }
-            tmem_wait_st();
-          }
-        }
-#pragma unroll
-        for (int c8 = 0; c8 < AT_BN / 8; ++c8) {
-          const int atom = c8 >> 3, jj = c8 & 7;
-          *reinterpret_cast<uint4*>(prow + atom * (AT_P_BYTES / 2) + ((jj ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
-        }
-        fence_proxy_async_smem();
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[qt]);
       }
       if (!ok) break;
-      // Epilogue: wait for the last P.V, O / l * gate -> bf16.
-      if (!mbar_wait(&pv_done[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
+      // Epilogue: wait for the item's last P.V, O / l * gate -> bf16.
+      if (!mbar_wait(&pv_done[qt], local & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
       tc_fence_after();
       const int row = t[0] + qt * AT_BM + r;
       const bool row_ok = row < t[1];
-      float gscale = 1.f / l;
+      float gscale = j > 0 ? 1.f / l : 0.f;   // an item without K/V writes zeros
       if (p.gate && row_ok) gscale *= sigmoidf_(__bfloat162float(p.gate[(int64_t)row * p.ldg + head]));
 #pragma unroll 1
       for (int c = 0; c < AT_D; c += 32) {
