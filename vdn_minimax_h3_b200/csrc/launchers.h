@@ -131,7 +131,8 @@ void launch_symm_barrier(unsigned long long* counter, unsigned long long* local_
 void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, int64_t ldo, int l2,
                         cudaStream_t stream);
 void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,
-                    int64_t ldo, int F, int gh, int gw, int H, int l2, cudaStream_t stream);
+                    int64_t ldo, int F, int gh, int gw, int H, int l2, int* err,
+                    cudaStream_t stream);
 void launch_lb_frame_stats(const void* k, int64_t ldk, const void* v, int64_t ldv, int F, int S,
                            int H, const float* beta, float* A, float* B, int* err,
                            cudaStream_t stream);

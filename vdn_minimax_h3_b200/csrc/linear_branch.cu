@@ -54,31 +54,29 @@ void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, in
 // Block = (grid row y, head h, chunk of LB_FC frames); warp w owns positions 4w..4w+3 of the
 // row, lane owns 4 channels, so a warp covers the head's 128 channels and the L2 norm is a
 // warp reduction. The five input rows y-2..y+2 of a frame (all positions, the head's 128
-// channels) are staged in shared memory by cp.async, double-buffered across frames so the
-// next frame's rows are in flight while this frame's 25 spatial taps run; rows and
-// positions outside the grid stay zero (the convolution's zero padding). The five latest
-// spatial results per output sit in a register ring for the temporal taps. Frames are
-// chunked (2-frame halo each side).
+// channels) are staged in shared memory by TMA (one box per row, issued by one thread) in
+// a LB_STAGES-deep ring of frames, so later frames are in flight while this frame's 25
+// spatial taps run; rows and positions outside the grid stay zero (the convolution's zero
+// padding). The five latest spatial results per output sit in a register ring for the
+// temporal taps. Frames are chunked (2-frame halo each side).
 constexpr int LB_FC = 16;
 constexpr int LB_PPW = 4;                 // positions per warp
 constexpr int LB_MAXW = 48;               // widest supported grid row
 constexpr int LB_XPAD = LB_MAXW + 4;      // staged positions per row (2 halo each side)
 constexpr int LB_ROW_BYTES = LB_XPAD * 256;        // one staged row: 128 bf16 per position
 constexpr int LB_STAGE_BYTES = 5 * LB_ROW_BYTES;   // five input rows of one frame
-constexpr int LB_CONV_SMEM = 2 * LB_STAGE_BYTES;
-
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem_dst)),
-               "l"(gmem_src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+constexpr int LB_STAGES = 3;
+constexpr int LB_CONV_SMEM = LB_STAGES * LB_STAGE_BYTES + 1024 /*align*/ + 64 /*barriers*/;
 
 __global__ void __launch_bounds__(384) lb_conv_kernel(
-    const __nv_bfloat16* __restrict__ in, int64_t ldi, const float* __restrict__ wsp,
+    const __grid_constant__ CUtensorMap tmIn, const float* __restrict__ wsp,
     const float* __restrict__ wtm, __nv_bfloat16* __restrict__ out, int64_t ldo, int F, int gh,
-    int gw, int H, int l2) {
-  extern __shared__ __align__(16) uint8_t lb_smem[];
+    int gw, int H, int l2, int* err) {
+  extern __shared__ uint8_t lb_smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(lb_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + LB_STAGES * LB_STAGE_BYTES);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + LB_STAGES);
   __shared__ __align__(16) float s_wsp[25][128];
   __shared__ __align__(16) float s_wtm[5][128];
   const int y = blockIdx.x, h = blockIdx.y;
@@ -94,28 +92,36 @@ __global__ void __launch_bounds__(384) lb_conv_kernel(
     const int tap = i / 128, c = i % 128;
     s_wtm[tap][c] = wtm[(int64_t)(h * 128 + c) * 5 + tap];
   }
-  // zero both stages once: the halo positions and the rows outside the grid are never written
-  for (int i = tid; i < LB_CONV_SMEM / 16; i += nthr)
-    reinterpret_cast<uint4*>(lb_smem)[i] = make_uint4(0, 0, 0, 0);
+  // zero the ring once: halo positions and rows outside the grid are never written
+  for (int i = tid; i < LB_STAGES * LB_STAGE_BYTES / 16; i += nthr)
+    reinterpret_cast<uint4*>(stages)[i] = make_uint4(0, 0, 0, 0);
+  if (tid == 0) {
+    for (int s = 0; s < LB_STAGES; ++s) mbar_init(&full[s], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  fence_proxy_async_smem();   // the zeros are visible to the TMA writes that follow
   __syncthreads();
   const int f_end = min(F, f0 + LB_FC);
   const int f_first = max(f0 - 2, 0), f_last = min(f_end + 2, F);  // frames with input
-  const int per_frame = 5 * gw * 16;                                 // 16-byte chunks
-  auto load_frame = [&](int f, int stage) {
-    uint8_t* base = lb_smem + stage * LB_STAGE_BYTES;
-    for (int idx = tid; idx < per_frame; idx += nthr) {
-      const int chunk = idx & 15;
-      const int pos = (idx >> 4) % gw;
-      const int i = (idx >> 4) / gw;
+  const int n_in = f_last - f_first;
+  int rows_valid = 0;
+  for (int i = 0; i < 5; ++i) rows_valid += (y + i - 2 >= 0 && y + i - 2 < gh) ? 1 : 0;
+  auto issue = [&](int ii) {   // input frame f_first + ii into stage ii % LB_STAGES
+    const int st = ii % LB_STAGES;
+    const int f = f_first + ii;
+    uint8_t* base = stages + st * LB_STAGE_BYTES;
+    mbar_arrive_expect_tx(&full[st], (uint32_t)(rows_valid * gw * 256));
+    for (int i = 0; i < 5; ++i) {
       const int yy = y + i - 2;
       if (yy < 0 || yy >= gh) continue;
-      const __nv_bfloat16* src =
-          in + ((int64_t)f * S + (int64_t)yy * gw + pos) * ldi + (int64_t)h * 128 + chunk * 8;
-      cp_async16(base + i * LB_ROW_BYTES + (pos + 2) * 256 + chunk * 16, src);
+      tma_load_2d(base + i * LB_ROW_BYTES + 2 * 256, &tmIn, &full[st], h * 128, f * S + yy * gw);
     }
   };
-  if (f_first < f_last) load_frame(f_first, f_first & 1);
-  cp_async_commit();
+  if (tid == 0) {
+    tma_prefetch_desc(&tmIn);
+    for (int ii = 0; ii < min(LB_STAGES, n_in); ++ii) issue(ii);
+  }
 
   const int x0 = warp * LB_PPW;
   const bool active = x0 < gw;
@@ -137,20 +143,20 @@ __global__ void __launch_bounds__(384) lb_conv_kernel(
     tw[dt][2] = t.z;
     tw[dt][3] = t.w;
   }
+  int issued = min(LB_STAGES, n_in);
   for (int f = f0 - 2; f < f_end + 2; ++f) {
     const bool have = f >= f_first && f < f_last;
-    // prefetch the next frame into the other stage, then wait for this frame's rows
-    if (f + 1 >= f_first && f + 1 < f_last) load_frame(f + 1, (f + 1) & 1);
-    cp_async_commit();
-    cp_async_wait1();
-    __syncthreads();
+    const int ii = f - f_first;
+    bool ok = true;
+    if (have) ok = mbar_wait(&full[ii % LB_STAGES], (uint32_t)((ii / LB_STAGES) & 1), abort_flag, err,
+                             kErrTimeoutProducer);
     float sp[LB_PPW][4];
 #pragma unroll
     for (int q = 0; q < LB_PPW; ++q)
 #pragma unroll
       for (int b = 0; b < 4; ++b) sp[q][b] = 0.f;
-    if (have && active) {
-      const uint8_t* base = lb_smem + (f & 1) * LB_STAGE_BYTES + c0 * 2;
+    if (have && ok && active) {
+      const uint8_t* base = stages + (ii % LB_STAGES) * LB_STAGE_BYTES + c0 * 2;
 #pragma unroll
       for (int i = 0; i < 5; ++i) {
         float win[LB_PPW + 4][4];
@@ -175,7 +181,9 @@ __global__ void __launch_bounds__(384) lb_conv_kernel(
         }
       }
     }
-    __syncthreads();  // this stage is refilled two frames from now
+    // every thread is done with this stage (and agrees on aborting) before it is refilled
+    if (__syncthreads_or(!ok)) break;
+    if (tid == 0 && have && issued < n_in && ii + LB_STAGES == issued) issue(issued++);
 #pragma unroll
     for (int q = 0; q < LB_PPW; ++q)
 #pragma unroll
@@ -210,10 +218,20 @@ __global__ void __launch_bounds__(384) lb_conv_kernel(
             make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
     }
   }
+  // an aborted block waits (bounded) for its own copies in flight before exiting
+  if (tid == 0 && *abort_flag) {
+    const long long t0 = clock64();
+    for (int ii = max(0, issued - LB_STAGES); ii < issued; ++ii) {
+      while (!mbar_try_wait(&full[ii % LB_STAGES], (uint32_t)((ii / LB_STAGES) & 1)) &&
+             clock64() - t0 < kWaitBudgetCycles) {
+      }
+    }
+  }
 }
 
 void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,
-                    int64_t ldo, int F, int gh, int gw, int H, int l2, cudaStream_t stream) {
+                    int64_t ldo, int F, int gh, int gw, int H, int l2, int* err,
+                    cudaStream_t stream) {
   if (!F || !gh || !gw) return;
   if (gw > LB_MAXW) throw std::runtime_error("short conv: grid width above 48 is not supported");
   static bool attr = false;
@@ -221,11 +239,13 @@ void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* 
     cudaFuncSetAttribute(lb_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LB_CONV_SMEM);
     attr = true;
   }
+  // rows = packed tokens of the F frames, one 128-channel head per box column
+  CUtensorMap tm = make_tmap_2d(in, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * 128,
+                                (uint64_t)F * gh * gw, ldi * 2, 128, gw, CU_TENSOR_MAP_SWIZZLE_NONE);
   const int warps = (gw + LB_PPW - 1) / LB_PPW;
   dim3 grid(gh, H, (F + LB_FC - 1) / LB_FC);
   lb_conv_kernel<<<grid, warps * 32, LB_CONV_SMEM, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(in), ldi, wsp, wtm,
-      reinterpret_cast<__nv_bfloat16*>(out), ldo, F, gh, gw, H, l2);
+      tm, wsp, wtm, reinterpret_cast<__nv_bfloat16*>(out), ldo, F, gh, gw, H, l2, err);
 }
 
 // ------------------------------------------------------------------ frame statistics

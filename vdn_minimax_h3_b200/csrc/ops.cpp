@@ -539,7 +539,7 @@ void lb_activate(torch::Tensor in, torch::Tensor out, bool l2) {
 }
 
 void lb_conv_features(torch::Tensor in, torch::Tensor wsp, torch::Tensor wtm, torch::Tensor out,
-                      int64_t F, int64_t gh, int64_t gw, bool l2) {
+                      int64_t F, int64_t gh, int64_t gw, bool l2, torch::Tensor err) {
   check_rows_heads(in, "in");
   check_rows_heads(out, "out");
   const int64_t H = in.size(1);
@@ -548,7 +548,8 @@ void lb_conv_features(torch::Tensor in, torch::Tensor wsp, torch::Tensor wtm, to
   check_f32(wtm, "w_temporal", H * 128 * 5);
   c10::cuda::CUDAGuard g(in.device());
   launch_lb_conv(in.data_ptr(), in.stride(0), wsp.data_ptr<float>(), wtm.data_ptr<float>(),
-                 out.data_ptr(), out.stride(0), (int)F, (int)gh, (int)gw, (int)H, l2, cur());
+                 out.data_ptr(), out.stride(0), (int)F, (int)gh, (int)gw, (int)H, l2,
+                 err_ptr(err), cur());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -38,7 +38,7 @@ def conv_features(tokens, w_sp, w_tm, num_frames, frame_size, l2norm):
     out = torch.empty(tokens.shape, dtype=tokens.dtype, device=tokens.device)
     ext().lb_conv_features(tokens, w_sp.float().reshape(-1).contiguous(),
                            w_tm.float().reshape(-1).contiguous(), out, num_frames, gh, gw,
-                           bool(l2norm))
+                           bool(l2norm), error_word(tokens.device))
     return out
 
 
