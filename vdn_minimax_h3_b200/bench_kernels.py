@@ -162,6 +162,8 @@ def main(argv=None):
     p.add_argument("--linear", action="store_true")
     p.add_argument("--norm", action="store_true")
     p.add_argument("--gemm-fp8", action="store_true")
+    p.add_argument("--attention-trace", action="store_true",
+                   help="clock64 phase durations of CTA 0's attention pipeline")
     p.add_argument("--profile-small", action="store_true",
                    help="one launch each of window attention, SPD inverse and conv features on "
                         "small inputs (an ncu-sized driver)")
@@ -182,6 +184,9 @@ def main(argv=None):
         bench_norm()
     if a.gemm_fp8:
         bench_gemm_fp8()
+    if a.attention_trace:
+        from vdn_minimax_h3_b200.ops.attention import trace_attention
+        trace_attention()
     if a.profile_small:
         profile_small()
     if a.attention_small:

@@ -69,6 +69,7 @@ struct AttnParams {
   __nv_bfloat16* out;        // [T, ldo], head h at column h*128
   int64_t ldo;
   RowScatter scatter;        // optional: rows to their Ulysses owners
+  long long* trace;          // optional: clock64 stamps of CTA 0's pipeline events
   float scale_log2;          // softmax scale * log2(e)
   int* err;
 };
@@ -125,6 +126,18 @@ struct KvWalk {
     skip_empty();
   }
 };
+
+// Pipeline tracing (diagnostics, off unless p.trace is set): CTA 0 records clock64 at
+// events of its first AT_TRACE_BLOCKS blocks, slot = (event * 2 + tile) * AT_TRACE_BLOCKS + block.
+constexpr int AT_TRACE_BLOCKS = 64;
+enum AtTraceEvent : int {
+  TR_S_WAIT = 0, TR_S_READY, TR_LD_DONE, TR_MAX_DONE, TR_EXP_DONE, TR_P_ARRIVE,
+  TR_MMA_P_WAIT, TR_MMA_P_READY, TR_MMA_ISSUED, TR_EVENTS
+};
+__device__ __forceinline__ void at_trace(const AttnParams& p, int ev, int tile, uint32_t blk) {
+  if (p.trace && blockIdx.x == 0 && blk < (uint32_t)AT_TRACE_BLOCKS)
+    p.trace[(ev * 2 + tile) * AT_TRACE_BLOCKS + blk] = clock64();
+}
 
 __device__ __forceinline__ void item_coords(const AttnParams& p, int item, int& head, int& tile) {
   head = item / p.n_tiles;
@@ -336,6 +349,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           for (int qt = 0; qt < 2 && ok; ++qt) {
             const uint32_t tS = tmem + qt * AT_BN;
             if (j > 0) {
+              at_trace(p, TR_MMA_P_WAIT, qt, g - 1);
               if (!mbar_wait(&p_full[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutMma) ||
                   (j == 1 && local > 0 &&
                    !mbar_wait(&o_empty[qt], (local - 1) & 1, abort_flag, p.err, kErrTimeoutMma))) {
@@ -343,6 +357,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 break;
               }
               tc_fence_after();
+              at_trace(p, TR_MMA_P_READY, qt, g - 1);
 #pragma unroll
               for (int k = 0; k < AT_BN / 16; ++k)
                 umma_f16_ts(tmem + 256 + qt * 128, tS + k * 8,
@@ -358,6 +373,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                             umma_desc_kmajor_sw128(aK + off), idesc_s, k != 0);
               }
               umma_commit(&s_full[qt]);
+              at_trace(p, TR_MMA_ISSUED, qt, g);
             }
           }
           if (!ok) break;
@@ -409,12 +425,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       float m_ref = -INFINITY, l = 0.f;
       int j = 0;
       bool ok = true;
+      const bool tr = (r == 0);
       for (; !w.done(); w.next(), ++j, ++g) {
+        if (tr) at_trace(p, TR_S_WAIT, qt, g);
         if (!mbar_wait(&s_full[qt], g & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        if (tr) at_trace(p, TR_S_READY, qt, g);
         float s[AT_BN];
 #pragma unroll
         for (int c = 0; c < AT_BN; c += 32) {
@@ -424,6 +443,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(u[i]);
         }
         tmem_wait_ld();
+        if (tr) at_trace(p, TR_LD_DONE, qt, g);
         // row max on the raw scores (8 independent chains); only a ragged block is masked
         const int valid = w.valid();
         if (valid < AT_BN) {
@@ -442,6 +462,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         const float m_new = fmaxf(m_ref, mx);
         const bool need = m_new > m_ref + 8.0f;
         const bool warp_need = __any_sync(0xffffffffu, need);
+        if (tr) at_trace(p, TR_MAX_DONE, qt, g);
         float factor = 1.f;
         if (need) {
           factor = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - m_new);
@@ -482,9 +503,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           tmem_st32(tS + h * 32, pk);
         }
         l += ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
+        if (tr) at_trace(p, TR_EXP_DONE, qt, g);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[qt]);
+        if (tr) at_trace(p, TR_P_ARRIVE, qt, g);
       }
       if (!ok) break;
       // Epilogue: wait for the item's last P.V, O / l * gate -> bf16.
@@ -526,7 +549,7 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              int64_t ldv, int T, int H, const int* tiles, int n_tiles,
                              const int* kv, const void* gate, int64_t ldg, void* out,
                              int64_t ldo, float scale, int* err, cudaStream_t stream,
-                             const RowScatter* scatter) {
+                             const RowScatter* scatter, long long* trace) {
   if (n_tiles == 0 || H == 0) return;
   static bool attr = false;
   if (!attr) {
@@ -562,6 +585,7 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
   p.ldo = ldo;
   p.scatter = RowScatter{};
   if (scatter) p.scatter = *scatter;
+  p.trace = trace;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
   const int items = n_tiles * H;

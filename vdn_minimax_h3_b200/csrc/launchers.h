@@ -116,7 +116,7 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              int64_t ldv, int T, int H, const int* tiles, int n_tiles,
                              const int* kv, const void* gate, int64_t ldg, void* out,
                              int64_t ldo, float scale, int* err, cudaStream_t stream,
-                             const RowScatter* scatter = nullptr);
+                             const RowScatter* scatter = nullptr, long long* trace = nullptr);
 
 void attention_set_poly_every(int n);
 

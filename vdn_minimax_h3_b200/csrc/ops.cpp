@@ -483,13 +483,18 @@ void check_out_or_scatter(const torch::Tensor& out, const RowScatter& sc, int64_
 void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles,
                       torch::Tensor kv, c10::optional<torch::Tensor> gate, torch::Tensor out,
                       double scale, torch::Tensor err, std::vector<int64_t> scatter_base,
-                      int64_t scatter_row0, int64_t scatter_rows) {
+                      int64_t scatter_row0, int64_t scatter_rows,
+                      c10::optional<torch::Tensor> trace) {
   const int64_t T = q.size(0), H = q.size(1);
   check_heads(q, "q", T, H);
   check_heads(k, "k", T, H);
   check_heads(v, "v", T, H);
   const RowScatter sc = make_scatter(scatter_base, scatter_row0, scatter_rows);
   check_out_or_scatter(out, sc, out.stride(0), T, H * 128);
+  if (trace)
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous() &&
+                    trace->numel() >= 18 * 64,
+                "trace must be a contiguous int64 CUDA tensor of >= 1152 entries");
   TORCH_CHECK(tiles.is_cuda() && tiles.scalar_type() == at::kInt && tiles.is_contiguous() &&
                   tiles.dim() == 2 && tiles.size(1) == 4, "tiles must be int32 [n, 4]");
   TORCH_CHECK(kv.is_cuda() && kv.scalar_type() == at::kInt && kv.is_contiguous() &&
@@ -507,7 +512,8 @@ void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
   launch_window_attention(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(),
                           v.stride(0), (int)T, (int)H, tiles.data_ptr<int>(), (int)tiles.size(0),
                           kv.data_ptr<int>(), gp, ldg, out.data_ptr(), out.stride(0),
-                          (float)scale, err_ptr(err), at::cuda::getCurrentCUDAStream(), &sc);
+                          (float)scale, err_ptr(err), at::cuda::getCurrentCUDAStream(), &sc,
+                          trace ? reinterpret_cast<long long*>(trace->data_ptr<int64_t>()) : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -31,7 +31,7 @@ def window_attention_reference(q, k, v, plan, scale, gate_logits=None):
     return out.reshape(T, H * d).to(q.dtype)
 
 
-def window_attention(q, k, v, plan, scale, gate_logits=None, out=None, scatter=None):
+def window_attention(q, k, v, plan, scale, gate_logits=None, out=None, scatter=None, trace=None):
     """q, k, v: [T, H, d] views (row stride allowed, d contiguous). out: [T, H*d] view.
 
     scatter = (bases, row0, rows_per_rank) sends output row t to its Ulysses owner
@@ -50,7 +50,7 @@ def window_attention(q, k, v, plan, scale, gate_logits=None, out=None, scatter=N
         out = torch.empty(T, H * d, dtype=q.dtype, device=q.device)
     bases, row0, rows = scatter if scatter is not None else ([], 0, 0)
     ext().window_attention(q, k, v, plan.tiles, plan.kv, gate_logits, out, float(scale),
-                           error_word(q.device), list(bases), int(row0), int(rows))
+                           error_word(q.device), list(bases), int(row0), int(rows), trace)
     return out
 
 
@@ -73,3 +73,40 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
         print(json.dumps(dict(case="window_attention_c1_both", T=T, heads=H, poly_every=pe, ms=ms,
                               tflops=fl / ms / 1e9)), flush=True)
     ext().attention_set_poly_every(0)
+
+
+TRACE_EVENTS = ("s_wait", "s_ready", "ld_done", "max_done", "exp_done", "p_arrive",
+                "mma_p_wait", "mma_p_ready", "mma_issued")
+
+
+def trace_attention(frames=102, heads=56, blocks=(8, 60)):  # pragma: no cover - GPU tool
+    """Per-phase clock cycles of CTA 0's softmax / MMA pipeline (kernel timestamps)."""
+    import json
+    from vdn_minimax_h3_b200.models.layout import SequenceLayout
+    from vdn_minimax_h3_b200.models.window import AttentionPlan, window_bounds
+    S = 1008
+    lay = SequenceLayout(seq_len=1950 + frames * S, video_start=1950, num_frames=frames,
+                         tokens_per_frame=S, frame_height=24, frame_width=42, text_start=0,
+                         text_len=800)
+    plan = AttentionPlan(lay, window_bounds(frames, 1, 5), "both", device="cuda")
+    q = torch.randn(lay.seq_len, heads, 128, device="cuda", dtype=torch.bfloat16)
+    tr = torch.zeros(18 * 64, dtype=torch.int64, device="cuda")
+    window_attention(q, q, q, plan, 128 ** -0.5)
+    window_attention(q, q, q, plan, 128 ** -0.5, trace=tr)
+    torch.cuda.synchronize()
+    t = tr.view(9, 2, 64).cpu().double()
+    a, b = blocks
+    ev = {n: t[i] for i, n in enumerate(TRACE_EVENTS)}
+    out = {}
+    for tile in (0, 1):
+        d = lambda x, y: float((ev[y][tile, a:b] - ev[x][tile, a:b]).mean())  # noqa: E731
+        out[f"tile{tile}"] = {
+            "wait_S": d("s_wait", "s_ready"), "tmem_load": d("s_ready", "ld_done"),
+            "row_max": d("ld_done", "max_done"), "exp_pack_store": d("max_done", "exp_done"),
+            "wait_st_arrive": d("exp_done", "p_arrive"),
+            "mma_wait_P": d("mma_p_wait", "mma_p_ready"),
+            "P_arrive_to_next_S": float((ev["s_ready"][tile, a + 1:b + 1] - ev["p_arrive"][tile, a:b]).mean()),
+            "block_period": float((ev["s_ready"][tile, a + 1:b + 1] - ev["s_ready"][tile, a:b]).mean()),
+        }
+    print(json.dumps({"attention_trace_cycles": out}), flush=True)
+    return out
