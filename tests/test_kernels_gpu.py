@@ -98,3 +98,26 @@ def test_window_attention_dense_gated_strided():
     ref = attn_ops.window_attention_reference(q.cpu(), k.cpu(), v.cpu(), plan, 0.1, gate.cpu())
     assert _rel(out_full[:, :H * 128].cpu(), ref) < 2e-2
     assert out_full[:, H * 128:].abs().max().item() == 0
+
+
+@pytest.mark.parametrize("poly", [1, 2, 3])
+def test_window_attention_poly_exp(poly):
+    """The kernel instances that evaluate part of the exponentials as the FMA-pipe polynomial
+    match the oracle like the all-MUFU instance."""
+    from vdn_minimax_h3_b200.ops._ext import ext
+    torch.manual_seed(2)
+    lay = _layout(40, 30, 12, 100)
+    bounds = window_bounds(12, 1, 2)
+    plan = AttentionPlan(lay, bounds, "both", device="cuda")
+    T = lay.seq_len
+    q = torch.randn(T, 2, 128, device="cuda", dtype=torch.bfloat16) * 2
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    ext().attention_set_poly_every(poly)
+    try:
+        out = attn_ops.window_attention(q, k, v, plan, 128 ** -0.5)
+        check_device_error()
+    finally:
+        ext().attention_set_poly_every(0)
+    ref = window_softmax_reference(q.float().cpu(), k.float().cpu(), v.float().cpu(), lay, bounds,
+                                   128 ** -0.5, "both").reshape(T, 2 * 128)
+    assert _rel(out.cpu(), ref) < 2e-2

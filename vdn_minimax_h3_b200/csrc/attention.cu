@@ -55,9 +55,8 @@ constexpr int AT_REGS_HIGH = 208;
 static_assert(128 * AT_REGS_LOW + 256 * AT_REGS_HIGH <= AT_THREADS * 168, "register split");
 constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + AT_VSTAGES) * AT_KV_BYTES + 1024 + 384;
 constexpr int AT_MAX_RANGES = 4;
-// One exponential in every 8 * POLY_EVERY runs on the FMA pipe (0: all on MUFU); the
-// launcher picks the instance (attention_set_poly_every, default 0: measured fastest,
-// the kernel is issue-bound rather than MUFU-bound).
+// AT_POLY_EVERY of every 8 exponentials run as a polynomial on the FMA pipe (0: all on
+// MUFU); the launcher picks the instance (attention_set_poly_every).
 static int g_poly_every = 0;
 
 struct AttnParams {
@@ -80,14 +79,26 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe: x = n + f, n = floor(x), 2^f by a cubic fitted for minimax relative
-// error (8.6e-5 on [0,1)), 2^n by adding n to the exponent field. Valid for x >= -126.
+// 2^x on the FMA / integer pipes only (no conversion instructions, which share the MUFU
+// pipe): n = round(x) by adding and subtracting 1.5 * 2^23, f = x - n in [-0.5, 0.5],
+// 2^f by a cubic fitted here for minimax relative error (8.4e-5 on [-0.5, 0.5], Lawson's
+// iteratively reweighted least squares), 2^n by adding n to the exponent field read from
+// the rounding sum's bits. Valid for x >= -125.
 __device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.f);
-  const float n = floorf(x);
+  x = fmaxf(x, -125.f);
+  const float j = x + 12582912.0f;
+  const float n = j - 12582912.0f;
   const float f = x - n;
-  const float p = fmaf(fmaf(fmaf(0.07706641f, f, 0.2276457f), f, 0.69511664f), f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
+  const float p = fmaf(fmaf(fmaf(0.0552129932f, f, 0.2427141405f), f, 0.6932621603f), f,
+                       0.9999195980f);
+  const int ni = __float_as_int(j) - 0x4B400000;
+  return __int_as_float(__float_as_int(p) + (ni << 23));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // Iterates the 128-key blocks of a segment's K/V ranges (at most four). The ranges are
@@ -454,9 +465,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) mxv[i] = s[i];
 #pragma unroll
-        for (int c = 8; c < AT_BN; c += 8)
+        for (int c = 8; c < AT_BN; c += 16)
 #pragma unroll
-          for (int i = 0; i < 8; ++i) mxv[i] = fmaxf(mxv[i], s[c + i]);
+          for (int i = 0; i < 8; ++i) mxv[i] = fmax3(mxv[i], s[c + i], s[c + 8 + i]);
         const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
                                fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * p.scale_log2;
         const float m_new = fmaxf(m_ref, mx);
@@ -494,7 +505,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               const float x = fmaf(s[h * 64 + c + i], p.scale_log2, neg_m);
-              e[i] = (AT_POLY_EVERY > 0 && i == 7 && ((c / 8) % AT_POLY_EVERY) == 0) ? ex2_poly(x) : ex2(x);
+              e[i] = (i >= 8 - AT_POLY_EVERY) ? ex2_poly(x) : ex2(x);
               sums[i] += e[i];
             }
 #pragma unroll
@@ -556,11 +567,11 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
     cudaFuncSetAttribute(window_attention_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
     cudaFuncSetAttribute(window_attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
     cudaFuncSetAttribute(window_attention_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
-    cudaFuncSetAttribute(window_attention_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
+    cudaFuncSetAttribute(window_attention_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
     // setmaxnreg.inc waits until the registers it asks for are free: refuse to launch if
     // the compiled launch register count cannot fund the split.
     for (auto fn : {window_attention_kernel<0>, window_attention_kernel<1>,
-                    window_attention_kernel<2>, window_attention_kernel<4>}) {
+                    window_attention_kernel<2>, window_attention_kernel<3>}) {
       cudaFuncAttributes fa;
       if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess ||
           fa.numRegs * AT_THREADS < 128 * AT_REGS_LOW + 256 * AT_REGS_HIGH)
@@ -593,8 +604,8 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
   switch (g_poly_every) {
     case 0: window_attention_kernel<0><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
     case 1: window_attention_kernel<1><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
-    case 4: window_attention_kernel<4><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
-    default: window_attention_kernel<2><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
+    case 2: window_attention_kernel<2><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
+    default: window_attention_kernel<3><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
   }
 }
 

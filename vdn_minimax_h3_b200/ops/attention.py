@@ -67,7 +67,7 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
     q = torch.randn(T, H, d, device="cuda", dtype=torch.bfloat16)
     k, v = torch.randn_like(q), torch.randn_like(q)
     fl = plan.flops(H, d)
-    for pe in (0, 1, 2, 4):
+    for pe in (0, 1, 2, 3):
         ext().attention_set_poly_every(pe)
         ms = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
         print(json.dumps(dict(case="window_attention_c1_both", T=T, heads=H, poly_every=pe, ms=ms,
