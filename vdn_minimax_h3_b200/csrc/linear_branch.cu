@@ -443,7 +443,9 @@ void launch_lb_frame_stats(const void* k, int64_t ldk, const void* v, int64_t ld
 // Gauss-Jordan inversion with the matrix held in registers: thread (ti, tj) of 16 x 16 owns
 // the 8 x 8 block rows 8ti.., cols 8tj..; step k broadcasts only pivot column k and pivot
 // row k through shared memory. SPD (I + aA): no row exchanges needed.
-constexpr int SPD_SMEM = (128 * 129 + 2 * 128) * 4;
+constexpr int SPD_LD = 132;                       // padded row stride (16-byte aligned rows)
+constexpr int SPD_BK = 32;                        // B columns staged per chunk
+constexpr int SPD_SMEM = (128 * SPD_LD + SPD_BK * SPD_LD + 2 * 128) * 4;
 
 __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
     const float* __restrict__ A, const float* __restrict__ B, const float* __restrict__ alpha,
@@ -451,7 +453,8 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
   extern __shared__ float sm[];
   float* colk = sm;            // [128]
   float* rowk = sm + 128;      // [128]
-  float* Ms = sm + 256;        // [128][129] final inverse, for the injection product
+  float* Ms = sm + 256;        // [128][SPD_LD] final inverse, for the injection product
+  float* Bt = Ms + 128 * SPD_LD;  // [SPD_BK][SPD_LD] a chunk of B^T (k-major)
   const int64_t mat = blockIdx.x;
   const float* a = A + mat * 16384;
   const int tid = threadIdx.x, ti = tid >> 4, tj = tid & 15;
@@ -491,7 +494,7 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
     }
     __syncthreads();
     const float piv = colk[k];
-    const float inv_p = 1.f / piv;
+    const float inv_p = __frcp_rn(piv);
     float cr[8], rr[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -513,7 +516,7 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) Ms[(ti * 8 + i) * 129 + tj * 8 + j] = m[i][j];
+    for (int j = 0; j < 8; ++j) Ms[(ti * 8 + i) * SPD_LD + tj * 8 + j] = m[i][j];
   __syncthreads();
   const float* al = alpha + mat * 128;
   float* tr = trans + mat * 16384;
@@ -523,7 +526,7 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int c = tj * 8 + j;
-      m[i][j] = 0.5f * (Ms[r * 129 + c] + Ms[c * 129 + r]);
+      m[i][j] = 0.5f * (Ms[r * SPD_LD + c] + Ms[c * SPD_LD + r]);
     }
   }
   __syncthreads();
@@ -532,29 +535,40 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
     const int r = ti * 8 + i;
     const float ar = al[r];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) Ms[r * 129 + tj * 8 + j] = m[i][j];
+    for (int j = 0; j < 8; ++j) Ms[r * SPD_LD + tj * 8 + j] = m[i][j];
     float4* dst = reinterpret_cast<float4*>(tr + r * 128 + tj * 8);
     dst[0] = make_float4(ar * m[i][0], ar * m[i][1], ar * m[i][2], ar * m[i][3]);
     dst[1] = make_float4(ar * m[i][4], ar * m[i][5], ar * m[i][6], ar * m[i][7]);
   }
   __syncthreads();
-  // injection = (b_scale * B) @ inv
+  // injection = (b_scale * B) @ inv, B staged k-major through shared memory in chunks so
+  // the inner loop is four 16-byte shared loads per 64 FMAs
   const float* bm = B + mat * 16384;
   float* out = inj + mat * 16384;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) m[i][j] = 0.f;
-  for (int kk = 0; kk < 128; ++kk) {
-    float bi[8], mj[8];
+  for (int k0 = 0; k0 < 128; k0 += SPD_BK) {
+    __syncthreads();   // the previous chunk is consumed
+    for (int e = tid; e < 128 * SPD_BK; e += 256) {
+      const int row = e / SPD_BK, kk = e % SPD_BK;
+      Bt[kk * SPD_LD + row] = bm[row * 128 + k0 + kk];
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = 0; kk < SPD_BK; ++kk) {
+      const float4 b0 = *reinterpret_cast<const float4*>(Bt + kk * SPD_LD + ti * 8);
+      const float4 b1 = *reinterpret_cast<const float4*>(Bt + kk * SPD_LD + ti * 8 + 4);
+      const float4 m0 = *reinterpret_cast<const float4*>(Ms + (k0 + kk) * SPD_LD + tj * 8);
+      const float4 m1 = *reinterpret_cast<const float4*>(Ms + (k0 + kk) * SPD_LD + tj * 8 + 4);
+      const float bi[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const float mj[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) bi[i] = bm[(ti * 8 + i) * 128 + kk];
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) mj[j] = Ms[kk * 129 + tj * 8 + j];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) m[i][j] += bi[i] * mj[j];
+        for (int j = 0; j < 8; ++j) m[i][j] = fmaf(bi[i], mj[j], m[i][j]);
+    }
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
