@@ -1,9 +1,15 @@
 """Headline benchmark: VDN-H3 T2VA denoising of a 14.4 s clip (345 frames, 768x1344,
-102 latent frames, 104,766 packed rows), 8 NFE, bf16, random-init weights of the full
+102 latent frames, 104,766 packed rows), 8 NFE, random-init weights of the full
 architecture, synthetic latents and prompt embeddings.
 
-    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
-    torchrun --nproc-per-node N ... bench.py --gpus N ...   (Ulysses sequence parallel)
+Default: the block-scaled fp8 configuration (E4M3 projections with 1x128 activation /
+128x128 weight scales; attention and the linear branch in bf16), tensor parallel 2 x
+Ulysses N/2 on N >= 2 GPUs -- the precision of the published headline numbers (MXFP8) and
+the hybrid layout of the fp8 configuration. `--bf16` runs every GEMM in bf16 with plain
+Ulysses over N GPUs.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--bf16]
+    torchrun --nproc-per-node N ... bench.py --gpus N ...
 
 One "step" is one NFE (one transformer forward + the scheduler's Euler step) of the
 8-step schedule; W untimed steps, then exactly K steps timed with CUDA events between a
@@ -33,11 +39,15 @@ def parse(argv=None):
     p.add_argument("--steps", type=int, default=8)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--fp8", action="store_true")
+    p.add_argument("--fp8", action="store_true", default=True,
+                   help="block-scaled fp8 projections (default)")
+    p.add_argument("--bf16", dest="fp8", action="store_false",
+                   help="bf16 projections, Ulysses over all GPUs")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--tp", type=int, default=1,
-                   help="tensor-parallel degree (TP x Ulysses, producer/consumer-fused exchanges)")
+    p.add_argument("--tp", type=int, default=None,
+                   help="tensor-parallel degree (TP x Ulysses); default 2 with fp8 on an even "
+                        "number of GPUs, else 1")
     p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
                    help="Ulysses exchange: symmetric-memory stores fused into the producing "
                         "kernels (p2p) or NCCL all_to_all_single (nccl)")
@@ -122,6 +132,8 @@ def main(argv=None):
         return reference_arm(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.tp is None:
+        args.tp = 2 if (args.fp8 and world >= 2 and world % 2 == 0) else 1
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
@@ -258,7 +270,8 @@ def main(argv=None):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
             "higher_is_better": False, "scaling": "strong",
             "vs_baseline": round(value / base, 3) if base else None,
-            "dtype": "fp8" if args.fp8 else "bf16",
+            "dtype": ("fp8 (E4M3 block-scaled projections: 1x128 activation / 128x128 weight "
+                      "scales; bf16 attention, linear branch, norms)") if args.fp8 else "bf16",
             "data": "synthetic (random-normal latents and prompt embeddings; random-init weights)",
             "config": {"model": f"VDN-H3 (MiniMax-H3 geometry, {cfg.num_layers} blocks, hidden "
                                 f"{cfg.hidden_size}, {cfg.num_attention_heads}x{cfg.attention_head_dim} heads, "
@@ -268,8 +281,10 @@ def main(argv=None):
                        "parallelism": ("single-gpu" if world == 1 else
                                        f"tp{args.tp}xulysses{world // args.tp}" if args.tp > 1
                                        else f"ulysses{world}"),
-                       "exchange": None if world == 1 else args.exchange,
-                       "l2": "inputs larger than L2 (66 GB of weights stream per step)"},
+                       "exchange": None if world == 1 else ("p2p" if args.tp > 1 else args.exchange),
+                       "baseline_config": ("block-scaled fp8, TP=2 x Ulysses (BASELINE config 3)"
+                                           if args.fp8 else "bf16 Ulysses (BASELINE config 2)"),
+                       "l2": "inputs larger than L2 (the weights, 33-66 GB, stream every step)"},
             "clocks": clock_info, "gpu_launches": launches, "e2e": e2e,
             "build_s": round(build_s, 1),
         }

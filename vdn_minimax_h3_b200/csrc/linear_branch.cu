@@ -459,15 +459,30 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
   const float* a = A + mat * 16384;
   const int tid = threadIdx.x, ti = tid >> 4, tj = tid & 15;
   float m[8][8];
+  // M = I + a_scale * (A + A^T) / 2: A staged through shared memory (coalesced 16-byte
+  // global loads), the transposed block read back with 16-byte shared loads
+  for (int e = tid * 4; e < 16384; e += 256 * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(a + e);
+    *reinterpret_cast<float4*>(Ms + (e >> 7) * SPD_LD + (e & 127)) = v;
+  }
+  __syncthreads();
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int r = ti * 8 + i;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = tj * 8 + j;
-      m[i][j] = a_scale * 0.5f * (a[r * 128 + c] + a[c * 128 + r]) + (r == c ? 1.f : 0.f);
-    }
+    const float4 v0 = *reinterpret_cast<const float4*>(Ms + (ti * 8 + i) * SPD_LD + tj * 8);
+    const float4 v1 = *reinterpret_cast<const float4*>(Ms + (ti * 8 + i) * SPD_LD + tj * 8 + 4);
+    m[i][0] = v0.x; m[i][1] = v0.y; m[i][2] = v0.z; m[i][3] = v0.w;
+    m[i][4] = v1.x; m[i][5] = v1.y; m[i][6] = v1.z; m[i][7] = v1.w;
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 t0 = *reinterpret_cast<const float4*>(Ms + (tj * 8 + j) * SPD_LD + ti * 8);
+    const float4 t1 = *reinterpret_cast<const float4*>(Ms + (tj * 8 + j) * SPD_LD + ti * 8 + 4);
+    const float tv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m[i][j] = a_scale * 0.5f * (m[i][j] + tv[i]) + ((ti * 8 + i) == (tj * 8 + j) ? 1.f : 0.f);
+  }
+  __syncthreads();
   // Step k of Gauss-Jordan as ONE uniform rank-1 update: with c the pivot column, r the
   // pivot row and p = M[k][k], set c'_k = p - 1 and r'_k = p + 1; then
   // M -= c' r'^T / p gives the eliminated entries, the scaled pivot row r/p, the column
@@ -495,17 +510,18 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
     __syncthreads();
     const float piv = colk[k];
     const float inv_p = __frcp_rn(piv);
+    // the pivot column and row through 16-byte loads (bank-conflict-free)
+    const float4 c0 = *reinterpret_cast<const float4*>(colk + ti * 8);
+    const float4 c1 = *reinterpret_cast<const float4*>(colk + ti * 8 + 4);
+    const float4 r0 = *reinterpret_cast<const float4*>(rowk + tj * 8);
+    const float4 r1 = *reinterpret_cast<const float4*>(rowk + tj * 8 + 4);
+    const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
     float cr[8], rr[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float v = colk[ti * 8 + i];
-      cr[i] = (ti * 8 + i == k) ? piv - 1.f : v;
-    }
+    for (int i = 0; i < 8; ++i) cr[i] = (ti * 8 + i == k) ? piv - 1.f : cv[i];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float v = rowk[tj * 8 + j];
-      rr[j] = ((tj * 8 + j == k) ? piv + 1.f : v) * inv_p;
-    }
+    for (int j = 0; j < 8; ++j) rr[j] = ((tj * 8 + j == k) ? piv + 1.f : rv[j]) * inv_p;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -521,13 +537,12 @@ __global__ void __launch_bounds__(256) lb_spd_factor_kernel(
   const float* al = alpha + mat * 128;
   float* tr = trans + mat * 16384;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = ti * 8 + i;
+  for (int j = 0; j < 8; ++j) {   // row tj*8+j of M holds column tj*8+j of M^T
+    const float4 t0 = *reinterpret_cast<const float4*>(Ms + (tj * 8 + j) * SPD_LD + ti * 8);
+    const float4 t1 = *reinterpret_cast<const float4*>(Ms + (tj * 8 + j) * SPD_LD + ti * 8 + 4);
+    const float tv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = tj * 8 + j;
-      m[i][j] = 0.5f * (Ms[r * SPD_LD + c] + Ms[c * SPD_LD + r]);
-    }
+    for (int i = 0; i < 8; ++i) m[i][j] = 0.5f * (m[i][j] + tv[i]);
   }
   __syncthreads();
 #pragma unroll
