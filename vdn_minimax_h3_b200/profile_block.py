@@ -21,6 +21,7 @@ def main(argv=None):
     p.add_argument("--num-layers", type=int, default=50)
     p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p")
     p.add_argument("--fp8", action="store_true")
+    p.add_argument("--tp", type=int, default=1)
     a = p.parse_args(argv)
     import bench  # noqa: F401  (same synthetic request as the headline bench)
     from vdn_minimax_h3_b200.inference.assemble import build_inference_engine, build_synthetic_model
@@ -39,7 +40,12 @@ def main(argv=None):
     model, _ = build_synthetic_model(cfg, device=dev)
     engine = build_inference_engine(model, fp8=a.fp8)
     transformer, timer = engine, engine.timer
-    if world > 1:
+    if world > 1 and a.tp > 1:
+        from vdn_minimax_h3_b200.parallel.hybrid import HybridEngine, HybridRuntime
+        rt = HybridRuntime(a.tp)
+        transformer = HybridEngine(engine, rt, fp8=a.fp8)
+        timer = rt.timer
+    elif world > 1:
         from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
         rt = init_ulysses()
         transformer = UlyssesEngine(engine, rt, exchange=a.exchange)
@@ -52,7 +58,7 @@ def main(argv=None):
     rep = timer.report()
     per_nfe = {k: round(v / a.nfe, 2) for k, v in rep.items()}
     line = {"ms_per_nfe_by_section": per_nfe, "total_ms_per_nfe": round(sum(per_nfe.values()), 1),
-            "num_layers": a.num_layers, "world": world, "fp8": a.fp8}
+            "num_layers": a.num_layers, "world": world, "fp8": a.fp8, "tp": a.tp}
     if world > 1:
         import torch.distributed as dist
         lines = [None] * world
