@@ -18,7 +18,7 @@
 //   EPI_SWIGLU     H = (acc_v + b_v) * silu(acc_g + b_g); the weight rows are interleaved
 //                  per 256-row tile as [128 value rows | 128 gate rows]
 //   EPI_ADD        C += acc (+ bias)                               (accumulate into C)
-//   EPI_STORE_F32  fp32 C without bias, each row stored to its owner's buffer (the
+//   EPI_STORE_F32  C without bias as bf16, each row stored to its owner's buffer (the
 //                  reduce-scatter of a row-parallel GEMM: partial sums cross NVLink once)
 //   EPI_ROUTE      every 8-column group of a row goes to its own destination (a route
 //                  table of addresses), and the 128-column q/k heads additionally get the
@@ -46,7 +46,8 @@ constexpr int GM_B_BYTES = GM_BN * GM_BK * 2;  // 32 KB
 constexpr int GM_STAGE_BYTES = GM_A_BYTES + GM_B_BYTES;
 constexpr int GM_THREADS = 192;
 constexpr int GM_GROUP_N = 16;  // n-blocks per raster band (weights of one band stay in L2)
-constexpr int GM_SMEM = GM_STAGES * GM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int GM_ROUTE_STAGE = 4 * 32 * 5 * 16;  // epilogue warps' route staging (10 KB)
+constexpr int GM_SMEM = GM_STAGES * GM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + GM_ROUTE_STAGE;
 constexpr int kMaxRoutePlanes = 8;
 
 enum EpiMode : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ADD = 3, EPI_ROUTE = 4,
@@ -86,22 +87,38 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 }
 
 // EPI_ROUTE helpers ------------------------------------------------------------------------
+// Warp-cooperative store of one 32-column chunk of 32 rows (lane = row, 16 packed bf16
+// pairs per lane) through the route: the chunk is transposed through a 2.5 KB shared
+// staging area so that each store instruction writes 8 rows x 64 contiguous bytes instead
+// of 32 rows x 16 bytes -- the destinations are often a peer GPU's memory, where small
+// scattered writes waste NVLink bandwidth. Every lane of the warp must call it.
+constexpr int kRouteStageWords = 32 * 5;   // uint4 per warp: 32 rows x (4 + 1 pad)
+
 __device__ __forceinline__ void route_store_chunk(const long long* route, int64_t ld, int col,
-                                                  int ngroups, int64_t row,
-                                                  const uint32_t* packed) {
-  // Up to 32 columns starting at `col` (a multiple of 8): 16-byte groups, each to its route.
+                                                  int ngroups, int row_base, int M,
+                                                  uint4* stage, const uint32_t* packed) {
+  const int lane = lane_id();
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    if (g >= ngroups) break;
-    const long long dst = __ldg(route + (col >> 3) + g);
-    if (dst)
-      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + row * ld) =
-          make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+  for (int g = 0; g < 4; ++g)
+    stage[lane * 5 + g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int step = 0; step < 4; ++step) {
+    const int r = step * 8 + (lane >> 2), g = lane & 3;
+    const int row = row_base + r;
+    if (g < ngroups && row < M) {
+      const long long dst = __ldg(route + (col >> 3) + g);
+      if (dst)
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + (int64_t)row * ld) =
+            stage[r * 5 + g];
+    }
   }
+  __syncwarp();
 }
 
 __device__ __forceinline__ void epilogue_route(const EpiParams& p, uint32_t lane_base, int row,
-                                               bool row_ok, int n0, int N) {
+                                               bool row_ok, int n0, int N, int M, uint4* stage) {
+  const int row_base = row - lane_id();
 #pragma unroll 1
   for (int h2 = 0; h2 < GM_BN; h2 += 128) {
     const int hc = n0 + h2;
@@ -130,13 +147,15 @@ __device__ __forceinline__ void epilogue_route(const EpiParams& p, uint32_t lane
           const float r0 = bf16_lo(pk), r1 = bf16_hi(pk);
           ss = fmaf(r0, r0, fmaf(r1, r1, ss));
         }
-        if (row_ok) route_store_chunk(p.route, p.route_ld[0], hc + c, 4, row, hv + (c >> 1));
+        route_store_chunk(p.route, p.route_ld[0], hc + c, 4, row_base, M, stage, hv + (c >> 1));
       }
-      if (!row_ok) continue;
       const float rstd = rsqrtf(ss * (1.f / 128.f) + p.qk_eps);
       const float* w = isq ? p.norm_q : p.norm_k;
-      const float4* cr = reinterpret_cast<const float4*>(p.rope_cos + (int64_t)row * p.ld_rope);
-      const float4* sr = reinterpret_cast<const float4*>(p.rope_sin + (int64_t)row * p.ld_rope);
+      // rows past M have no rope table row: they compute on row 0 and are not stored
+      const int64_t rrow = row_ok ? row : 0;
+      const float4* cr = reinterpret_cast<const float4*>(p.rope_cos + rrow * p.ld_rope);
+      const float4* sr = reinterpret_cast<const float4*>(p.rope_sin + rrow * p.ld_rope);
+      const long long* proc = p.route + (N >> 3);  // plane 1: processed q/k
 #pragma unroll
       for (int c = 0; c < 64; c += 32) {
         uint32_t lo[16], hi[16];
@@ -162,9 +181,8 @@ __device__ __forceinline__ void epilogue_route(const EpiParams& p, uint32_t lane
           hi[j >> 1] = pack_bf16(o2[0], o2[1]);
           hi[(j >> 1) + 1] = pack_bf16(o2[2], o2[3]);
         }
-        const long long* proc = p.route + (N >> 3);  // plane 1: processed q/k
-        route_store_chunk(proc, p.route_ld[1], hc + c, 4, row, lo);
-        route_store_chunk(proc, p.route_ld[1], hc + c + 64, 4, row, hi);
+        route_store_chunk(proc, p.route_ld[1], hc + c, 4, row_base, M, stage, lo);
+        route_store_chunk(proc, p.route_ld[1], hc + c + 64, 4, row_base, M, stage, hi);
       }
     } else {
 #pragma unroll 1
@@ -173,7 +191,7 @@ __device__ __forceinline__ void epilogue_route(const EpiParams& p, uint32_t lane
         tmem_ld32(lane_base + h2 + c, v);
         tmem_wait_ld();
         const int col0 = hc + c;
-        if (!row_ok || col0 >= N) continue;
+        if (col0 >= N) continue;   // warp-uniform
         uint32_t packed[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
@@ -190,7 +208,7 @@ __device__ __forceinline__ void epilogue_route(const EpiParams& p, uint32_t lane
 #pragma unroll 1
         for (int pl = 0; pl < p.planes; ++pl)
           route_store_chunk(p.route + (int64_t)pl * (N >> 3), p.route_ld[pl], col0, ngroups,
-                            row, packed);
+                            row_base, M, stage, packed);
       }
     }
   }
@@ -198,27 +216,19 @@ __device__ __forceinline__ void epilogue_route(const EpiParams& p, uint32_t lane
 
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& p, uint32_t tacc, int quarter,
-                                              int m0, int n0, int M, int N) {
+                                              int m0, int n0, int M, int N, uint4* stage) {
   const int lane = lane_id();
   const int row = m0 + quarter * 32 + lane;
   const uint32_t lane_base = tacc + ((uint32_t)(quarter * 32) << 16);
   const bool row_ok = row < M;
   if constexpr (EPI == EPI_ROUTE) {
-    epilogue_route(p, lane_base, row, row_ok, n0, N);
+    epilogue_route(p, lane_base, row, row_ok, n0, N, M, stage);
     return;
   }
   if constexpr (EPI == EPI_STORE_F32) {
-    float* rowp = nullptr;
-    if (row_ok) {
-      if (p.scatter.n == 0) {
-        rowp = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
-      } else {
-        const int64_t g = p.scatter.row0 + row;
-        const int r = (int)(g / p.scatter.rows_per_rank);
-        rowp = reinterpret_cast<float*>(p.scatter.base[r]) +
-               (g - (int64_t)r * p.scatter.rows_per_rank) * p.ldo;
-      }
-    }
+    // bf16 partial products without bias, each row to its owner's buffer
+    __nv_bfloat16* rowp = nullptr;
+    if (row_ok) rowp = p.scatter.n == 0 ? p.out + (int64_t)row * p.ldo : p.scatter.row_ptr(p.out, p.ldo, row);
 #pragma unroll 1
     for (int c = 0; c < GM_BN; c += 32) {
       uint32_t v[32];
@@ -226,11 +236,13 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, uint32_t tacc,
       tmem_wait_ld();
       const int col0 = n0 + c;
       if (!row_ok || col0 >= N) continue;
-      float4* d = reinterpret_cast<float4*>(rowp + col0);
+      uint32_t packed[16];
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        d[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                           __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+      for (int j = 0; j < 16; ++j) packed[j] = pack_bf16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+      uint4* d = reinterpret_cast<uint4*>(rowp + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        d[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
     }
     return;
   }
@@ -369,6 +381,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint4* route_stage = reinterpret_cast<uint4*>(smem + GM_STAGES * GM_STAGE_BYTES + 256);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -492,7 +505,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       const uint32_t use = (uint32_t)(local >> 1);
       if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-      epilogue_tile<EPI>(p, tmem_base + buf * GM_BN, quarter, mb * GM_BM, nb * GM_BN, M, N);
+      epilogue_tile<EPI>(p, tmem_base + buf * GM_BN, quarter, mb * GM_BM, nb * GM_BN, M, N,
+                         route_stage + quarter * kRouteStageWords);
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
     }

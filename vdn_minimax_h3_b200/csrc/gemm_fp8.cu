@@ -44,11 +44,12 @@ constexpr int F8_SFA_BYTES = 512;                // 128 rows x 4 K-blocks
 constexpr int F8_SFB_BYTES = 1024;               // 256 rows x 4 K-blocks
 constexpr int F8_STAGE_BYTES = 51200;            // A | B | SFA | SFB, padded to 1 KB
 constexpr int F8_THREADS = 384;
-constexpr int F8_SMEM = F8_STAGES * F8_STAGE_BYTES + 1024 /*align*/ + 2048 /*bars, amax*/;
+constexpr int F8_ROUTE_STAGE = 8 * 32 * 5 * 16;   // epilogue warps' route staging (20 KB)
+constexpr int F8_SMEM = F8_STAGES * F8_STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers*/ + F8_ROUTE_STAGE;
 constexpr int F8_SF_COL = 256;                   // TMEM column of the first scale factors
 constexpr int F8_SF_STAGE_COLS = 16;             // SFA 4 columns, SFB 8
 constexpr int F8_REGS_LOW = 72;
-constexpr int F8_REGS_HIGH = 208;
+constexpr int F8_REGS_HIGH = 216;
 static_assert(F8_A_BYTES + F8_B_BYTES + F8_SFA_BYTES + F8_SFB_BYTES <= F8_STAGE_BYTES, "stage");
 static_assert(128 * F8_REGS_LOW + 256 * F8_REGS_HIGH <= F8_THREADS * 168, "register split");
 
@@ -75,21 +76,38 @@ struct Fp8Params {
 // plane 0 and RMSNorm + rotate-half RoPE stores to plane 1; other columns are stored to
 // every plane with an address (the routed epilogue of gemm.cu, here after the accumulator
 // has been copied out of TMEM).
+// Warp-cooperative store of one 32-column chunk of 32 rows through the route, transposed
+// through shared memory so each store instruction writes 8 rows x 64 contiguous bytes (the
+// destinations are often a peer GPU's memory). Every lane of the warp must call it.
+constexpr int kF8StageWords = 32 * 5;
+
 __device__ __forceinline__ void f8_route_store(const GemmRoute& r, int plane, int N, int col,
-                                               int64_t row, const uint32_t* packed, int ngroups) {
+                                               int row_base, int M, uint4* stage,
+                                               const uint32_t* packed, int ngroups) {
   const long long* tab = r.route + (int64_t)plane * (N >> 3);
+  const int lane = lane_id();
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    if (g >= ngroups) break;
-    const long long dst = __ldg(tab + (col >> 3) + g);
-    if (dst)
-      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + row * r.route_ld[plane]) =
-          make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+  for (int g = 0; g < 4; ++g)
+    stage[lane * 5 + g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int step = 0; step < 4; ++step) {
+    const int rr = step * 8 + (lane >> 2), g = lane & 3;
+    const int row = row_base + rr;
+    if (g < ngroups && row < M) {
+      const long long dst = __ldg(tab + (col >> 3) + g);
+      if (dst)
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + (int64_t)row * r.route_ld[plane]) =
+            stage[rr * 5 + g];
+    }
   }
+  __syncwarp();
 }
 
 __device__ __forceinline__ void f8_route_epilogue(const Fp8Params& p, const uint32_t* v, int hc,
-                                                  int row, int N) {
+                                                  int row, int N, int M, uint4* stage) {
+  const int row_base = row - lane_id();
+  const bool row_ok = row < M;
   const GemmRoute& r = p.route;
   const bool isq = hc >= r.q0 && hc < r.q1;
   const bool isk = hc >= r.k0 && hc < r.k1;
@@ -109,11 +127,14 @@ __device__ __forceinline__ void f8_route_epilogue(const Fp8Params& p, const uint
       ss = fmaf(r0, r0, fmaf(r1, r1, ss));
     }
 #pragma unroll
-    for (int c = 0; c < 128; c += 32) f8_route_store(r, 0, N, hc + c, row, hv + (c >> 1), 4);
+    for (int c = 0; c < 128; c += 32)
+      f8_route_store(r, 0, N, hc + c, row_base, M, stage, hv + (c >> 1), 4);
     const float rstd = rsqrtf(ss * (1.f / 128.f) + r.qk_eps);
     const float* w = isq ? r.norm_q : r.norm_k;
-    const float4* cr = reinterpret_cast<const float4*>(r.rope_cos + (int64_t)row * r.ld_rope);
-    const float4* sr = reinterpret_cast<const float4*>(r.rope_sin + (int64_t)row * r.ld_rope);
+    // rows past M have no rope table row: they compute on row 0 and are not stored
+    const int64_t rrow = row_ok ? row : 0;
+    const float4* cr = reinterpret_cast<const float4*>(r.rope_cos + rrow * r.ld_rope);
+    const float4* sr = reinterpret_cast<const float4*>(r.rope_sin + rrow * r.ld_rope);
 #pragma unroll
     for (int c = 0; c < 64; c += 32) {
       uint32_t lo[16], hi[16];
@@ -138,8 +159,8 @@ __device__ __forceinline__ void f8_route_epilogue(const Fp8Params& p, const uint
         hi[j >> 1] = pack_bf16(o2[0], o2[1]);
         hi[(j >> 1) + 1] = pack_bf16(o2[2], o2[3]);
       }
-      f8_route_store(r, 1, N, hc + c, row, lo, 4);
-      f8_route_store(r, 1, N, hc + c + 64, row, hi, 4);
+      f8_route_store(r, 1, N, hc + c, row_base, M, stage, lo, 4);
+      f8_route_store(r, 1, N, hc + c + 64, row_base, M, stage, hi, 4);
     }
     return;
   }
@@ -159,7 +180,8 @@ __device__ __forceinline__ void f8_route_epilogue(const Fp8Params& p, const uint
     }
     const int ngroups = min(4, (N - col0) >> 3);
 #pragma unroll 1
-    for (int pl = 0; pl < r.planes; ++pl) f8_route_store(r, pl, N, col0, row, packed, ngroups);
+    for (int pl = 0; pl < r.planes; ++pl)
+      f8_route_store(r, pl, N, col0, row_base, M, stage, packed, ngroups);
   }
 }
 
@@ -176,8 +198,12 @@ __device__ __forceinline__ void f8_tile_coords(int tile, int num_m, int num_n, i
 
 template <int EPI>
 __device__ __forceinline__ void f8_epilogue(const Fp8Params& p, const uint32_t* v, int ew, int row,
-                                            bool row_ok, int nb, int M, int N) {
+                                            bool row_ok, int nb, int M, int N, uint4* stage) {
   const int col0 = nb * F8_BN + ew * 128;
+  if constexpr (EPI == F8_ROUTE) {
+    if (col0 < N) f8_route_epilogue(p, v, col0, row, N, M, stage);   // col0: warp-uniform
+    return;
+  }
   if constexpr (EPI == F8_SWIGLU_Q) {
     // this warpgroup's 128 columns: [64 value | 64 gate] -> 64 outputs, one scale per 1x64
     // block (two 32-element scale-factor bytes, written as one 16-bit half of the word)
@@ -216,27 +242,18 @@ __device__ __forceinline__ void f8_epilogue(const Fp8Params& p, const uint32_t* 
     return;
   }
   if (!row_ok || col0 >= N) return;
-  if constexpr (EPI == F8_ROUTE) {
-    f8_route_epilogue(p, v, col0, row, N);
-    return;
-  }
   if constexpr (EPI == F8_STORE_F32) {
-    // fp32 partial sums, no bias: the reduce-scatter of a row-parallel GEMM
-    float* rowp;
-    if (p.scatter.n == 0) {
-      rowp = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
-    } else {
-      const int64_t g = p.scatter.row0 + row;
-      const int r = (int)(g / p.scatter.rows_per_rank);
-      rowp = reinterpret_cast<float*>(p.scatter.base[r]) +
-             (g - (int64_t)r * p.scatter.rows_per_rank) * p.ldo;
-    }
+    // bf16 partial products, no bias: the reduce-scatter of a row-parallel GEMM
+    __nv_bfloat16* rowp = p.scatter.n == 0 ? p.out + (int64_t)row * p.ldo
+                                           : p.scatter.row_ptr(p.out, p.ldo, row);
 #pragma unroll
-    for (int c = 0; c < 128; c += 4) {
+    for (int c = 0; c < 128; c += 8) {
       if (col0 + c >= N) break;
-      *reinterpret_cast<float4*>(rowp + col0 + c) =
-          make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
-                      __uint_as_float(v[c + 3]));
+      *reinterpret_cast<uint4*>(rowp + col0 + c) =
+          make_uint4(pack_bf16(__uint_as_float(v[c]), __uint_as_float(v[c + 1])),
+                     pack_bf16(__uint_as_float(v[c + 2]), __uint_as_float(v[c + 3])),
+                     pack_bf16(__uint_as_float(v[c + 4]), __uint_as_float(v[c + 5])),
+                     pack_bf16(__uint_as_float(v[c + 6]), __uint_as_float(v[c + 7])));
     }
     return;
   }
@@ -290,6 +307,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
   uint64_t* mma_done = tempty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint4* route_stage = reinterpret_cast<uint4*>(smem + F8_STAGES * F8_STAGE_BYTES + 2048);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -429,7 +447,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       tc_fence_before();
       mbar_arrive(tempty);   // the accumulator is free for the next tile's MMAs
       const int row = mb * F8_BM + r_in_tile;
-      f8_epilogue<EPI>(p, v, ew, row, row < M, nb, M, N);
+      f8_epilogue<EPI>(p, v, ew, row, row < M, nb, M, N, route_stage + (warp - 4) * kF8StageWords);
     }
   }
 

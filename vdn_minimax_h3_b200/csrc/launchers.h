@@ -82,7 +82,7 @@ void launch_gemm_fp8_f32_scatter(const GemmFp8Args& a, void* out, int64_t ldo, c
                                  int* err, cudaStream_t stream);
 void launch_gemm_bf16_f32_scatter(const GemmArgs& a, void* out, int64_t ldo, const RowScatter& sc,
                                   int* err, cudaStream_t stream);
-void launch_residual_combine(void* x, int64_t ldx, const float* a, const float* b, int64_t ldp,
+void launch_residual_combine(void* x, int64_t ldx, const void* a, const void* b, int64_t ldp,
                              const float* bias, const void* gate, int64_t ldg, const int* idx,
                              int R, int D, cudaStream_t stream);
 void launch_quant_rows(const void* x, int64_t ldx, int M, int K, void* q, int64_t ldq, void* sf,

@@ -245,11 +245,11 @@ void launch_qk_prep(const void* src, int64_t lds, int T, int H, int d, const flo
 }
 
 // Tensor-parallel residual: x += gate[idx[r]] * (a + b + bias), a and b the two ranks'
-// fp32 partial sums of a row-parallel GEMM for this rank's rows. One warp per row, 8
-// columns per lane per step.
+// bf16 partial sums of a row-parallel GEMM for this rank's rows (added in fp32). One warp
+// per row, 8 columns per lane per step.
 __global__ void __launch_bounds__(256) residual_combine_kernel(
-    __nv_bfloat16* __restrict__ x, int64_t ldx, const float* __restrict__ a,
-    const float* __restrict__ b, int64_t ldp, const float* __restrict__ bias,
+    __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ a,
+    const __nv_bfloat16* __restrict__ b, int64_t ldp, const float* __restrict__ bias,
     const __nv_bfloat16* __restrict__ gate, int64_t ldg, const int* __restrict__ idx, int R,
     int D) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -257,12 +257,16 @@ __global__ void __launch_bounds__(256) residual_combine_kernel(
   if (row >= R) return;
   const __nv_bfloat16* g = gate + (int64_t)idx[row] * ldg;
   for (int c = lane * 8; c < D; c += 256) {
-    const float4 a0 = *reinterpret_cast<const float4*>(a + (int64_t)row * ldp + c);
-    const float4 a1 = *reinterpret_cast<const float4*>(a + (int64_t)row * ldp + c + 4);
-    const float4 b0 = *reinterpret_cast<const float4*>(b + (int64_t)row * ldp + c);
-    const float4 b1 = *reinterpret_cast<const float4*>(b + (int64_t)row * ldp + c + 4);
-    float y[8] = {a0.x + b0.x, a0.y + b0.y, a0.z + b0.z, a0.w + b0.w,
-                  a1.x + b1.x, a1.y + b1.y, a1.z + b1.z, a1.w + b1.w};
+    const uint4 av = *reinterpret_cast<const uint4*>(a + (int64_t)row * ldp + c);
+    const uint4 bv = *reinterpret_cast<const uint4*>(b + (int64_t)row * ldp + c);
+    const uint32_t* aw = reinterpret_cast<const uint32_t*>(&av);
+    const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      y[2 * j] = bf16_lo(aw[j]) + bf16_lo(bw[j]);
+      y[2 * j + 1] = bf16_hi(aw[j]) + bf16_hi(bw[j]);
+    }
     if (bias) {
       const float4 c0 = *reinterpret_cast<const float4*>(bias + c);
       const float4 c1 = *reinterpret_cast<const float4*>(bias + c + 4);
@@ -281,12 +285,13 @@ __global__ void __launch_bounds__(256) residual_combine_kernel(
   }
 }
 
-void launch_residual_combine(void* x, int64_t ldx, const float* a, const float* b, int64_t ldp,
+void launch_residual_combine(void* x, int64_t ldx, const void* a, const void* b, int64_t ldp,
                              const float* bias, const void* gate, int64_t ldg, const int* idx,
                              int R, int D, cudaStream_t stream) {
   if (R == 0) return;
   residual_combine_kernel<<<(R + 7) / 8, 256, 0, stream>>>(
-      reinterpret_cast<__nv_bfloat16*>(x), ldx, a, b, ldp, bias,
+      reinterpret_cast<__nv_bfloat16*>(x), ldx, reinterpret_cast<const __nv_bfloat16*>(a),
+      reinterpret_cast<const __nv_bfloat16*>(b), ldp, bias,
       reinterpret_cast<const __nv_bfloat16*>(gate), ldg, idx, R, D);
 }
 

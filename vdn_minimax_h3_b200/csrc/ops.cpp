@@ -344,10 +344,10 @@ void adaln_rmsnorm_dst(torch::Tensor x, c10::optional<torch::Tensor> w, double e
 void gemm_f32_scatter(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> sfa,
                       c10::optional<torch::Tensor> sfb, torch::Tensor out,
                       std::vector<int64_t> bases, int64_t row0, int64_t rows, torch::Tensor err) {
-  // fp32 partial products stored to their row owners (bf16 operands, or E4M3 with sfa/sfb)
-  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.dim() == 2 &&
-                  out.stride(1) == 1 && out.stride(0) % 4 == 0,
-              "out must be fp32 2-D with 16-byte aligned rows");
+  // bf16 partial products stored to their row owners (bf16 operands, or E4M3 with sfa/sfb)
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 &&
+                  out.stride(1) == 1 && out.stride(0) % 8 == 0,
+              "out must be bf16 2-D with 16-byte aligned rows");
   RowScatter sc{};
   TORCH_CHECK(bases.size() <= (size_t)kMaxScatterRanks, "at most 8 owners");
   sc.n = (int)bases.size();
@@ -387,16 +387,16 @@ void residual_combine(torch::Tensor x, torch::Tensor a, torch::Tensor b,
   const int R = x.size(0), D = x.size(1);
   TORCH_CHECK(D % 8 == 0, "D % 8 == 0");
   for (const auto* t : {&a, &b}) {
-    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->dim() == 2 &&
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 &&
                     t->size(0) >= R && t->size(1) == D && t->stride(1) == 1 &&
-                    t->stride(0) == a.stride(0) && t->stride(0) % 4 == 0,
-                "partials must be fp32 [>=R, D] with one 16-byte aligned row stride");
+                    t->stride(0) == a.stride(0) && t->stride(0) % 8 == 0,
+                "partials must be bf16 [>=R, D] with one 16-byte aligned row stride");
   }
   TORCH_CHECK(gate.size(1) >= D, "gate table narrower than D");
   TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.is_contiguous() &&
                   idx.numel() >= R, "idx must be contiguous int32 [R]");
   c10::cuda::CUDAGuard g(x.device());
-  launch_residual_combine(x.data_ptr(), x.stride(0), a.data_ptr<float>(), b.data_ptr<float>(),
+  launch_residual_combine(x.data_ptr(), x.stride(0), a.data_ptr(), b.data_ptr(),
                           a.stride(0), opt_f32(bias, D, "bias"), gate.data_ptr(), gate.stride(0),
                           idx.data_ptr<int>(), R, D, at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -736,7 +736,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adaln_rmsnorm_dst", &vdn::adaln_rmsnorm_dst,
         "AdaLN-RMSNorm into up to two destinations (local + peer) at a row offset, bf16 and/or E4M3");
   m.def("gemm_f32_scatter", &vdn::gemm_f32_scatter,
-        "GEMM whose fp32 partial rows go to their owners (row-parallel GEMM -> reduce-scatter)");
+        "GEMM whose bf16 partial rows go to their owners (row-parallel GEMM -> reduce-scatter)");
   m.def("residual_combine", &vdn::residual_combine,
         "x += gate[idx] * (partial_a + partial_b + bias)");
   m.def("adaln_rmsnorm", &vdn::adaln_rmsnorm, "RMSNorm * w * (1 + scale[idx]) + shift[idx]");

@@ -14,9 +14,10 @@ Per block, every exchange is a store issued by the kernel that produces the data
              its Ulysses destination's receive slab (peer memory).
   attention  + linear branch over all rows for H/world heads; epilogues store each output
              row into its row owner's O-projection input (row scatter).
-  O-proj     row-parallel (this TP rank's heads along K); the epilogue stores fp32 partial
+  O-proj     row-parallel (this TP rank's heads along K); the epilogue stores bf16 partial
              rows into the owning TP rank's partial buffer: the reduce-scatter is done by
-             the GEMM. A combine kernel adds both partials, bias and the gated residual.
+             the GEMM. A combine kernel adds both (bf16) partials, bias and the gated
+             residual in fp32.
   FF         the same pattern: norm all-gather -> column-parallel SwiGLU (E4M3 out) ->
              row-parallel down projection with the partial-sum scatter -> combine.
 Device flag barriers (parallel/symmetric.py) order each exchange inside the TP pair or the
@@ -188,12 +189,12 @@ class HybridEngine:
         C, CS = rt.C, rt.CS
         from vdn_minimax_h3_b200.ops.fp8 import sf_bytes
         tp_specs = [((CS, D), dtype), ((CS, D), torch.uint8), ((sf_bytes(CS, D),), torch.uint8),
-                    ((rt.tp, C, D), torch.float32)]
+                    ((rt.tp, C, D), dtype)]
         self.tp_heap = SymmetricHeap(SymmetricHeap.required_bytes(tp_specs), rt.tp_group, dev)
         self.tp_heap.alloc("a", (CS, D), dtype)
         self.tp_heap.alloc("aq", (CS, D), torch.uint8)
         self.tp_heap.alloc("asf", (sf_bytes(CS, D),), torch.uint8)
-        self.tp_heap.alloc("part", (rt.tp, C, D), torch.float32)
+        self.tp_heap.alloc("part", (rt.tp, C, D), dtype)
         sp_specs = [((rt.sp, CS, W), dtype), ((CS, kcat), dtype)]
         self.sp_heap = SymmetricHeap(SymmetricHeap.required_bytes(sp_specs), rt.sp_group, dev)
         self.sp_heap.alloc("recv", (rt.sp, CS, W), dtype)
