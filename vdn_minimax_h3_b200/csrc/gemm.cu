@@ -226,23 +226,34 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, uint32_t tacc,
     return;
   }
   if constexpr (EPI == EPI_STORE_F32) {
-    // bf16 partial products without bias, each row to its owner's buffer
-    __nv_bfloat16* rowp = nullptr;
-    if (row_ok) rowp = p.scatter.n == 0 ? p.out + (int64_t)row * p.ldo : p.scatter.row_ptr(p.out, p.ldo, row);
+    // bf16 partial products without bias, each row to its owner's buffer, staged so each
+    // store writes 8 rows x 64 contiguous bytes
+    const int row_base = m0 + quarter * 32;
 #pragma unroll 1
     for (int c = 0; c < GM_BN; c += 32) {
       uint32_t v[32];
       tmem_ld32(lane_base + c, v);
       tmem_wait_ld();
       const int col0 = n0 + c;
-      if (!row_ok || col0 >= N) continue;
+      if (col0 >= N) continue;   // warp-uniform
       uint32_t packed[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) packed[j] = pack_bf16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-      uint4* d = reinterpret_cast<uint4*>(rowp + col0);
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        d[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      for (int g = 0; g < 4; ++g)
+        stage[lane * 5 + g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+      __syncwarp();
+#pragma unroll
+      for (int step = 0; step < 4; ++step) {
+        const int rr = step * 8 + (lane >> 2), g = lane & 3;
+        const int srow = row_base + rr;
+        if (srow < M) {
+          __nv_bfloat16* d = (p.scatter.n == 0 ? p.out + (int64_t)srow * p.ldo
+                                               : p.scatter.row_ptr(p.out, p.ldo, srow)) + col0 + 8 * g;
+          *reinterpret_cast<uint4*>(d) = stage[rr * 5 + g];
+        }
+      }
+      __syncwarp();
     }
     return;
   }

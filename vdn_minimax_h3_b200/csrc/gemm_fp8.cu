@@ -204,6 +204,36 @@ __device__ __forceinline__ void f8_epilogue(const Fp8Params& p, const uint32_t* 
     if (col0 < N) f8_route_epilogue(p, v, col0, row, N, M, stage);   // col0: warp-uniform
     return;
   }
+  if constexpr (EPI == F8_STORE_F32) {
+    // bf16 partial products, no bias, each row to its owner (the reduce-scatter of a
+    // row-parallel GEMM), staged so each store writes 8 rows x 64 contiguous bytes
+    const int lane = lane_id();
+    const int row_base = row - lane;
+#pragma unroll
+    for (int c = 0; c < 128; c += 32) {
+      if (col0 + c >= N) break;   // warp-uniform
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        packed[j] = pack_bf16(__uint_as_float(v[c + 2 * j]), __uint_as_float(v[c + 2 * j + 1]));
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        stage[lane * 5 + g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+      __syncwarp();
+#pragma unroll
+      for (int step = 0; step < 4; ++step) {
+        const int rr = step * 8 + (lane >> 2), g = lane & 3;
+        const int srow = row_base + rr;
+        if (srow < M) {
+          __nv_bfloat16* d = (p.scatter.n == 0 ? p.out + (int64_t)srow * p.ldo
+                                               : p.scatter.row_ptr(p.out, p.ldo, srow)) + col0 + c + 8 * g;
+          *reinterpret_cast<uint4*>(d) = stage[rr * 5 + g];
+        }
+      }
+      __syncwarp();
+    }
+    return;
+  }
   if constexpr (EPI == F8_SWIGLU_Q) {
     // this warpgroup's 128 columns: [64 value | 64 gate] -> 64 outputs, one scale per 1x64
     // block (two 32-element scale-factor bytes, written as one 16-bit half of the word)
@@ -242,21 +272,6 @@ __device__ __forceinline__ void f8_epilogue(const Fp8Params& p, const uint32_t* 
     return;
   }
   if (!row_ok || col0 >= N) return;
-  if constexpr (EPI == F8_STORE_F32) {
-    // bf16 partial products, no bias: the reduce-scatter of a row-parallel GEMM
-    __nv_bfloat16* rowp = p.scatter.n == 0 ? p.out + (int64_t)row * p.ldo
-                                           : p.scatter.row_ptr(p.out, p.ldo, row);
-#pragma unroll
-    for (int c = 0; c < 128; c += 8) {
-      if (col0 + c >= N) break;
-      *reinterpret_cast<uint4*>(rowp + col0 + c) =
-          make_uint4(pack_bf16(__uint_as_float(v[c]), __uint_as_float(v[c + 1])),
-                     pack_bf16(__uint_as_float(v[c + 2]), __uint_as_float(v[c + 3])),
-                     pack_bf16(__uint_as_float(v[c + 4]), __uint_as_float(v[c + 5])),
-                     pack_bf16(__uint_as_float(v[c + 6]), __uint_as_float(v[c + 7])));
-    }
-    return;
-  }
 #pragma unroll
   for (int c = 0; c < 128; c += 32) {
     if (col0 + c >= N) break;
