@@ -51,6 +51,9 @@ def parse(argv=None):
     p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
                    help="Ulysses exchange: symmetric-memory stores fused into the producing "
                         "kernels (p2p) or NCCL all_to_all_single (nccl)")
+    p.add_argument("--softmax-ranks", type=int, default=0,
+                   help="branch-parallel Ulysses: this many ranks run the window softmax, the "
+                        "rest the linear branch (0 = every rank runs both for its heads)")
     p.add_argument("--num-layers", type=int, default=None, help=argparse.SUPPRESS)
     return p.parse_args(argv)
 
@@ -133,7 +136,10 @@ def main(argv=None):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.tp is None:
-        args.tp = 2 if (args.fp8 and world >= 2 and world % 2 == 0) else 1
+        args.tp = 2 if (args.fp8 and world >= 2 and world % 2 == 0
+                        and not args.softmax_ranks) else 1
+    if args.softmax_ranks and args.tp > 1:
+        raise SystemExit("--softmax-ranks is a Ulysses-only layout; use --tp 1")
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
@@ -165,7 +171,7 @@ def main(argv=None):
         transformer = HybridEngine(engine, runtime, fp8=args.fp8)
     elif world > 1:
         from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
-        runtime = init_ulysses()
+        runtime = init_ulysses(softmax_ranks=args.softmax_ranks)
         transformer = UlyssesEngine(engine, runtime, exchange=args.exchange)
 
     # ---- synthetic request: prompt embeddings + noise for a 14.4 s clip
@@ -280,7 +286,10 @@ def main(argv=None):
                        "latent_frames": geo.num_latent_frames, "text_len": TEXT_LEN, "nfe": NFE,
                        "parallelism": ("single-gpu" if world == 1 else
                                        f"tp{args.tp}xulysses{world // args.tp}" if args.tp > 1
-                                       else f"ulysses{world}"),
+                                       else f"ulysses{world}" + (
+                                           f" (branch parallel {args.softmax_ranks} softmax + "
+                                           f"{world - args.softmax_ranks} linear ranks)"
+                                           if args.softmax_ranks else "")),
                        "exchange": None if world == 1 else ("p2p" if args.tp > 1 else args.exchange),
                        "baseline_config": ("block-scaled fp8, TP=2 x Ulysses (BASELINE config 3)"
                                            if args.fp8 else "bf16 Ulysses (BASELINE config 2)"),

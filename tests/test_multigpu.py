@@ -21,7 +21,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q, exchange):
+def _worker(rank, world, port, q, exchange, softmax_ranks=0):
     import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -54,7 +54,8 @@ def _worker(rank, world, port, q, exchange):
         with torch.no_grad():
             single = InferenceEngine(copy.deepcopy(gm))
             ref_v, _ = single(**kwg, layout=layout)
-            sp = UlyssesEngine(InferenceEngine(gm), init_ulysses(), exchange=exchange)
+            sp = UlyssesEngine(InferenceEngine(gm), init_ulysses(softmax_ranks=softmax_ranks),
+                               exchange=exchange)
             out_v, _ = sp(**kwg, layout=layout)
             out_v2, _ = sp(**kwg, layout=layout)
             sp.close()
@@ -124,19 +125,15 @@ def test_symmetric_heap_two_gpus():
     assert all(v is True for v in res.values()), res
 
 
-@TWO_GPUS
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
-def test_ulysses_two_gpus_match_single(exchange):
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, exchange)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=280)
-    res = dict(q.get() for _ in range(2))
+@pytest.mark.parametrize("world,exchange,softmax_ranks", [
+    (2, "nccl", 0), (2, "p2p", 0), (2, "nccl", 1), (2, "p2p", 1), (4, "p2p", 3), (4, "nccl", 1)])
+def test_ulysses_match_single(world, exchange, softmax_ranks):
+    """Plain Ulysses (softmax_ranks 0) and branch parallel: with 4 heads on 4 GPUs,
+    3 softmax ranks hold 2 + 1 + 1 heads and 1 linear rank all 4 (uneven splits)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _spawn(_worker, world, exchange, softmax_ranks)
     assert all(isinstance(v, float) and v < 2e-2 for v in res.values()), res
 
 

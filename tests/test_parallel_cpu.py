@@ -29,7 +29,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, softmax_ranks=0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -50,7 +50,7 @@ def _worker(rank, world, port, q):
         set_layout(model, layout)
         with torch.no_grad():
             ref_v, ref_a = InferenceEngine(copy.deepcopy(model))(**kw, layout=layout)
-            eng = UlyssesEngine(InferenceEngine(model), init_ulysses())
+            eng = UlyssesEngine(InferenceEngine(model), init_ulysses(softmax_ranks=softmax_ranks))
             out_v, out_a = eng(**kw, layout=layout)
         err = max(((out_v - ref_v).norm() / ref_v.norm()).item(),
                   ((out_a - ref_a).norm() / ref_a.norm()).item())
@@ -60,12 +60,16 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.timeout(300)
-def test_ulysses_matches_single_process():
-    world = 2
+@pytest.mark.parametrize("world,softmax_ranks", [(2, 0), (2, 1), (3, 1), (3, 2)])
+def test_ulysses_matches_single_process(world, softmax_ranks):
+    """softmax_ranks = 0 is plain Ulysses; otherwise branch parallel, with uneven head
+    splits at world 3 (1 softmax rank with 2 heads + 2 linear ranks with 1 head each, and
+    2 + 1)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, softmax_ranks))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -28,10 +28,18 @@ def main(argv=None):
     torch.cuda.set_device(device)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     from vdn_minimax_h3_b200.inference.infer import assemble, render
-    from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
     model, engine = assemble(cfg, device)
-    runtime = init_ulysses(profile=cfg.parallel.profile)
-    sp = UlyssesEngine(engine, runtime, exchange=cfg.parallel.exchange)
+    par = cfg.parallel
+    if par.tensor_parallel > 1:
+        if par.softmax_ranks:
+            raise ValueError("parallel.softmax_ranks (branch parallel) needs tensor_parallel = 1")
+        from vdn_minimax_h3_b200.parallel.hybrid import HybridEngine, HybridRuntime
+        runtime = HybridRuntime(par.tensor_parallel, profile=par.profile)
+        sp = HybridEngine(engine, runtime, fp8=cfg.precision.fp8.enabled)
+    else:
+        from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
+        runtime = init_ulysses(profile=par.profile, softmax_ranks=par.softmax_ranks)
+        sp = UlyssesEngine(engine, runtime, exchange=par.exchange)
     runtime.barrier()
     t_setup = time.perf_counter() - t_start
     lat, aud, steps, denoise = render(cfg, model, engine, device, runtime=runtime, transformer=sp)
@@ -50,6 +58,7 @@ def main(argv=None):
               f"{float(d.item()):.2f}s ({cfg.render.num_steps} NFE), decode+encode {t_decode:.1f}s, "
               f"E2E {time.perf_counter() - t_start:.1f}s" + (f", sections {prof}" if prof else ""),
               flush=True)
+    sp.close()   # symmetric-memory heaps are released on every rank before NCCL goes away
     dist.destroy_process_group()
     return 0
 

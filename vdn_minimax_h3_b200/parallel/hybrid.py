@@ -59,6 +59,9 @@ class HybridRuntime:
         self.timer = SectionTimer(profile)
         self.seq_len = None
 
+    def barrier(self):
+        dist.barrier()
+
     def configure(self, T, heads):
         if heads % self.world:
             raise ValueError(f"{heads} heads are not divisible by {self.world} ranks")

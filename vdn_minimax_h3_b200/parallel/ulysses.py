@@ -51,26 +51,69 @@ def balanced_splits(total, parts):
 
 
 class UlyssesRuntime:
-    """Rank layout of one sequence-parallel group."""
+    """Rank layout of one sequence-parallel group.
 
-    def __init__(self, group=None, profile=False):
+    With `softmax_ranks` = s > 0 the group is branch parallel (the reference's
+    `enable_branch_parallel`, src/inference/utils/ulysses_runtime.py:202-240): ranks
+    0..s-1 run the window softmax for contiguous, balanced head ranges and ranks s..P-1
+    run the linear branch for theirs, so the two branches' kernels run concurrently on
+    disjoint GPUs; every rank still owns a row shard of the residual."""
+
+    def __init__(self, group=None, profile=False, softmax_ranks=0):
         self.group = group
         self.world_size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.timer = SectionTimer(profile)
         self.seq_len = None
+        self.softmax_ranks = 0
+        if softmax_ranks:
+            self.enable_branch_parallel(softmax_ranks)
+
+    @property
+    def branch_parallel(self):
+        return self.softmax_ranks > 0
+
+    def enable_branch_parallel(self, softmax_ranks):
+        if not 0 < softmax_ranks < self.world_size:
+            raise ValueError(f"softmax_ranks must lie in [1, {self.world_size - 1}], "
+                             f"got {softmax_ranks}")
+        if self.seq_len is not None:
+            raise RuntimeError("enable branch parallelism before the first forward")
+        self.softmax_ranks = softmax_ranks
 
     def configure(self, seq_len, num_heads):
-        if num_heads % self.world_size:
+        if not self.branch_parallel and num_heads % self.world_size:
             raise ValueError(f"{num_heads} heads are not divisible by {self.world_size} ranks")
         if self.seq_len == seq_len:
             return
+        if seq_len < self.world_size:
+            raise ValueError(f"Ulysses needs at least one row per rank; T={seq_len}, "
+                             f"P={self.world_size}")
         self.seq_len = seq_len
+        self.num_heads = num_heads
         self.splits = sequence_splits(seq_len, self.world_size)
         self.rows = math.ceil(seq_len / self.world_size)          # padded shard height
         self.local_start = sum(self.splits[:self.rank])
         self.local_end = self.local_start + self.splits[self.rank]
-        self.heads_per_rank = num_heads // self.world_size
+        if self.branch_parallel:
+            self.softmax_head_splits = balanced_splits(num_heads, self.softmax_ranks)
+            self.linear_head_splits = balanced_splits(num_heads,
+                                                      self.world_size - self.softmax_ranks)
+        self.branch_kind, self.head_lo, self.head_hi = self.branch_of(self.rank)
+        self.heads_per_rank = self.head_hi - self.head_lo
+
+    def branch_of(self, p):
+        """(kind, first head, end head) of rank p; kind is "both" under plain Ulysses,
+        "softmax" or "linear" under branch parallelism."""
+        if not self.branch_parallel:
+            hp = self.num_heads // self.world_size
+            return "both", p * hp, (p + 1) * hp
+        if p < self.softmax_ranks:
+            splits, i, kind = self.softmax_head_splits, p, "softmax"
+        else:
+            splits, i, kind = self.linear_head_splits, p - self.softmax_ranks, "linear"
+        lo = sum(splits[:i])
+        return kind, lo, lo + splits[i]
 
     def barrier(self):
         dist.barrier(group=self.group)
@@ -85,10 +128,10 @@ class UlyssesRuntime:
         dist.all_gather_into_tensor(out, local, group=self.group)
 
 
-def init_ulysses(profile=False):
+def init_ulysses(profile=False, softmax_ranks=0):
     if not dist.is_initialized():
         raise RuntimeError("init_process_group(nccl) before init_ulysses()")
-    return UlyssesRuntime(profile=profile)
+    return UlyssesRuntime(profile=profile, softmax_ranks=softmax_ranks)
 
 
 class UlyssesEngine:
@@ -124,43 +167,69 @@ class UlyssesEngine:
         return b
 
     # -------------------------------------------------------------- exchange layout
-    def _fields(self, pb):
-        """Ordered (name, width) of one destination's slab row; every width a multiple of 8."""
+    def _fields(self, pb, p):
+        """Ordered {name: (offset, width)} of destination rank p's slab row; every width a
+        multiple of 8. A rank running both branches receives q, k (normalised + rotated),
+        v, q_raw, k_raw for its heads and the softmax-gate, beta and gate-hidden fields of
+        all heads; under branch parallelism a softmax rank receives only q, k, v and the
+        softmax gate, a linear rank only q_raw, k_raw, v, beta and the gate hidden."""
         c = pb.cols
-        Hp, d = self.rt.heads_per_rank, pb.head_dim
+        kind, lo, hi = self.rt.branch_of(p)
+        hw = (hi - lo) * pb.head_dim
         pad8 = lambda n: (n + 7) // 8 * 8  # noqa: E731
-        f = [("q", Hp * d), ("k", Hp * d), ("v", Hp * d), ("q_raw", Hp * d), ("k_raw", Hp * d)]
-        if pb.has_sgate:
+        f = []
+        if kind != "linear":
+            f += [("q", hw), ("k", hw)]
+        f.append(("v", hw))
+        if kind != "softmax":
+            f += [("q_raw", hw), ("k_raw", hw)]
+        if pb.has_sgate and kind != "linear":
             f.append(("sgate", pad8(c["sgate"][1] - c["sgate"][0])))
-        if "beta" in c:
-            f.append(("beta", pad8(c["beta"][1] - c["beta"][0])))
-        if "ghid" in c:
-            f.append(("ghid", pad8(c["ghid"][1] - c["ghid"][0])))
+        for name in ("beta", "ghid"):
+            if name in c and kind != "softmax":
+                f.append((name, pad8(c[name][1] - c[name][0])))
         offs, o = {}, 0
         for name, w in f:
             offs[name] = (o, w)
             o += w
         return offs, o
 
-    def _route(self, pb, slabs, offs):
-        """ColumnRoute of the QKV GEMM into per-destination slabs ([rows, W] views)."""
+    def _layouts(self, pb):
+        """Per destination rank slab layouts and the common slab width (their maximum)."""
+        lay = [self._fields(pb, p) for p in range(self.rt.world_size)]
+        return [o for o, _ in lay], max(w for _, w in lay)
+
+    def _route(self, pb, slabs, layouts):
+        """ColumnRoute of the QKV GEMM into per-destination slabs ([rows, W] views).
+
+        q/k head columns: plane 0 takes the raw projection (to the rank running that
+        head's linear branch), plane 1 the normalised + rotated values (to the rank running
+        its softmax). v goes to both owners (planes 0 and 1 when they differ); the
+        softmax-gate / beta / gate-hidden fields are replicated, one plane per receiver."""
         c = pb.cols
+        d = pb.head_dim
         P = self.rt.world_size
-        Hp, d = self.rt.heads_per_rank, pb.head_dim
-        hw = Hp * d
         route = gemm.ColumnRoute(pb.w_qkvg.shape[0], planes=max(2, P))
+        nxt = {}
         for p, slab in enumerate(slabs):
+            offs = layouts[p]
+            kind, lo, hi = self.rt.branch_of(p)
             fv = lambda name: slab[:, offs[name][0]:offs[name][0] + offs[name][1]]  # noqa: E731
-            route.place(c["q"][0] + p * hw, fv("q_raw"), plane=0)
-            route.place(c["q"][0] + p * hw, fv("q"), plane=1)
-            route.place(c["k"][0] + p * hw, fv("k_raw"), plane=0)
-            route.place(c["k"][0] + p * hw, fv("k"), plane=1)
-            route.place(c["v"][0] + p * hw, fv("v"), plane=0)
+            q0, k0, v0 = c["q"][0] + lo * d, c["k"][0] + lo * d, c["v"][0] + lo * d
+            if kind != "softmax":
+                route.place(q0, fv("q_raw"), plane=0)
+                route.place(k0, fv("k_raw"), plane=0)
+            if kind != "linear":
+                route.place(q0, fv("q"), plane=1)
+                route.place(k0, fv("k"), plane=1)
+            route.place(v0, fv("v"), plane=1 if kind == "linear" else 0)
             for name in ("sgate", "beta", "ghid"):
                 if name in offs:
-                    lo, hi = c[name]
-                    width = (hi - lo + 7) // 8 * 8
-                    route.place(lo, slab[:, offs[name][0]:offs[name][0] + width], plane=p)
+                    lo_c, hi_c = c[name]
+                    width = (hi_c - lo_c + 7) // 8 * 8
+                    plane = nxt.get(name, 0)
+                    nxt[name] = plane + 1
+                    route.place(lo_c, slab[:, offs[name][0]:offs[name][0] + width], plane=plane)
         return route
 
     def _ensure_heap(self, dev, C, W, kcat, dtype):
@@ -225,7 +294,10 @@ class UlyssesEngine:
             work = rt.all_reduce(fsum, async_op=True)
         c = pb.cols
         cos, sin = rope
-        offs, W = self._fields(pb)
+        layouts, W = self._layouts(pb)
+        offs = layouts[r]
+        kind, h0, h1 = rt.branch_of(r)
+        run_softmax, run_linear = kind != "linear", kind != "softmax"
         kcat_max = 2 * H * d
         # ---- seq -> heads, fused into the QKV GEMM epilogue
         if p2p:
@@ -235,14 +307,15 @@ class UlyssesEngine:
             route = self._routes.get(key)
             if route is None:
                 slabs = [self.heap.peer("recv", p)[r, :rows] for p in range(P)]
-                route = self._routes[key] = self._route(pb, slabs, offs)
+                route = self._routes[key] = self._route(pb, slabs, layouts)
         else:
             send = self._buf("send", (P, C, W), x.dtype, dev)
             recv = self._buf("recv", (P, C, W), x.dtype, dev)
             key = ("nccl", send.data_ptr(), tuple(sorted(c.items())), rows)
             route = self._routes.get(key)
             if route is None:
-                route = self._routes[key] = self._route(pb, [send[p, :rows] for p in range(P)], offs)
+                route = self._routes[key] = self._route(pb, [send[p, :rows] for p in range(P)],
+                                                        layouts)
         with sec("gemm_qkv"):
             if f8:
                 fp8_ops.linear_routed_fp8(nq, nsf, pb.w8_qkvg, route, c["q"], c["k"], pb.norm_q,
@@ -267,40 +340,44 @@ class UlyssesEngine:
         full = recv.view(P * C, W)[:T]
         fv = lambda name, a=0, n=None: full[:, offs[name][0] + a:offs[name][0] + a + (  # noqa: E731
             offs[name][1] if n is None else n)]
-        q_h, k_h, v_h = fv("q"), fv("k"), fv("v")
-        qr_h, kr_h = fv("q_raw"), fv("k_raw")
-        sg_h = fv("sgate", r * Hp, Hp) if pb.has_sgate else None
-        bt_h = fv("beta", r * Hp, Hp) if "beta" in offs else None
-        gh_h = fv("ghid", 0, c["ghid"][1] - c["ghid"][0]) if "ghid" in offs else None
+        v_h = fv("v")
+        # this rank's heads [h0, h1): attention output at cat column h0*d, linear at H*d + h0*d
         if p2p:
             cat_peers = [self.heap.peer("cat", p) for p in range(P)]
             cat_local = self.heap.local("cat")
             scat = lambda col, row0: ([t.data_ptr() + 2 * col for t in cat_peers], row0, C)  # noqa: E731
-            attn_out = cat_local[:, r * hw:(r + 1) * hw]
-            attn_scatter = scat(r * hw, 0)
+            attn_out = cat_local[:, h0 * d:h1 * d]
+            lin_out = cat_local[:, H * d + h0 * d:H * d + h1 * d]
         else:
-            ret = self._buf("ret", (P * C, 2 * hw), x.dtype, dev)
+            ret_w = 2 * hw if kind == "both" else max(
+                (rt.branch_of(p)[2] - rt.branch_of(p)[1]) * d for p in range(P))
+            ret = self._buf("ret", (P * C, ret_w), x.dtype, dev)
             attn_out = ret[:T, :hw]
-            attn_scatter = None
-        with sec("attention"):
-            attn_ops.window_attention(q_h.view(T, Hp, d), k_h.view(T, Hp, d), v_h.view(T, Hp, d),
-                                      plan, d ** -0.5, gate_logits=sg_h, out=attn_out,
-                                      scatter=attn_scatter)
-        if pb.hybrid:
+            lin_out = ret[:T, hw:2 * hw] if kind == "both" else ret[:T, :hw]
+        if run_softmax:
+            with sec("attention"):
+                attn_ops.window_attention(
+                    fv("q").view(T, Hp, d), fv("k").view(T, Hp, d), v_h.view(T, Hp, d), plan,
+                    d ** -0.5, gate_logits=fv("sgate", h0, Hp) if pb.has_sgate else None,
+                    out=attn_out, scatter=scat(h0 * d, 0) if p2p else None)
+        if linear_on:
+            work.wait()
+        if pb.hybrid and run_linear:
             if linear_on:
-                work.wait()
-                lin_out = cat_local[:, H * d + r * hw:H * d + (r + 1) * hw] if p2p else ret[:T, hw:]
                 if not p2p:
                     lin_out.zero_()
                 with sec("linear_branch"):
-                    linear_branch_core(pb, attn, layout, eng.bounds, qr_h.view(T, Hp, d),
-                                       kr_h.view(T, Hp, d), v_h.view(T, Hp, d), bt_h, gh_h, fsum,
-                                       slice(r * Hp, (r + 1) * Hp), lin_out, x.dtype,
-                                       scatter=scat(H * d + r * hw, None) if p2p else None)
-            elif p2p:
-                cat_local[:rows, H * d:].zero_()
-            else:
-                ret[:T, hw:].zero_()
+                    linear_branch_core(
+                        pb, attn, layout, eng.bounds, fv("q_raw").view(T, Hp, d),
+                        fv("k_raw").view(T, Hp, d), v_h.view(T, Hp, d),
+                        fv("beta", h0, Hp) if "beta" in offs else None,
+                        fv("ghid", 0, c["ghid"][1] - c["ghid"][0]) if "ghid" in offs else None,
+                        fsum, slice(h0, h1), lin_out, x.dtype,
+                        scatter=scat(H * d + h0 * d, None) if p2p else None)
+            elif not p2p:
+                lin_out.zero_()
+        if pb.hybrid and not linear_on and p2p:
+            cat_local[:rows, H * d:].zero_()   # own rows; no rank stores linear outputs
         kcat = pb.w_o.shape[1]
         # ---- heads -> seq
         if p2p:
@@ -308,14 +385,22 @@ class UlyssesEngine:
                 self.heap.barrier()
             cat = cat_local[:rows, :kcat]
         else:
-            back = self._buf("back", (P, C, 2 * hw), x.dtype, dev)
+            back = self._buf("back", (P, C, ret.shape[1]), x.dtype, dev)
             with sec("a2a_return"):
                 rt.all_to_all(back.view(-1), ret.view(-1))
             cat = self._buf("cat", (rows, kcat), x.dtype, dev)
             with sec("unpack"):
-                nb = 2 if pb.hybrid else 1
-                src = back[:, :rows].unflatten(-1, (2, Hp, d))[:, :, :nb]
-                cat.view(rows, nb, P, Hp, d).copy_(src.permute(1, 2, 0, 3, 4))
+                if kind == "both":
+                    nb = 2 if pb.hybrid else 1
+                    src = back[:, :rows].unflatten(-1, (2, Hp, d))[:, :, :nb]
+                    cat.view(rows, nb, P, Hp, d).copy_(src.permute(1, 2, 0, 3, 4))
+                else:
+                    for p in range(P):
+                        kp, lo, hi = rt.branch_of(p)
+                        if kp == "linear" and not pb.hybrid:
+                            continue
+                        col = lo * d if kp == "softmax" else H * d + lo * d
+                        cat[:, col:col + (hi - lo) * d].copy_(back[p, :rows, :(hi - lo) * d])
         with sec("gemm_o"):
             if f8:
                 cq = self._buf("cat_q", tuple(cat.shape), torch.uint8, dev)

@@ -22,6 +22,7 @@ def main(argv=None):
     p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p")
     p.add_argument("--fp8", action="store_true")
     p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--softmax-ranks", type=int, default=0)
     a = p.parse_args(argv)
     import bench  # noqa: F401  (same synthetic request as the headline bench)
     from vdn_minimax_h3_b200.inference.assemble import build_inference_engine, build_synthetic_model
@@ -47,7 +48,7 @@ def main(argv=None):
         timer = rt.timer
     elif world > 1:
         from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
-        rt = init_ulysses()
+        rt = init_ulysses(softmax_ranks=a.softmax_ranks)
         transformer = UlyssesEngine(engine, rt, exchange=a.exchange)
         timer = rt.timer
     emb = torch.randn(800, cfg.text_dim, device=dev, dtype=torch.bfloat16)
