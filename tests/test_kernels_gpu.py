@@ -100,10 +100,13 @@ def test_window_attention_dense_gated_strided():
     assert out_full[:, H * 128:].abs().max().item() == 0
 
 
-@pytest.mark.parametrize("poly", [1, 2, 3])
-def test_window_attention_poly_exp(poly):
-    """The kernel instances that evaluate part of the exponentials as the FMA-pipe polynomial
-    match the oracle like the all-MUFU instance."""
+@pytest.mark.parametrize("variant,growing", [(1, False), (2, False), (3, False), (4, False),
+                                             (4, True), (5, True), (6, False)])
+def test_window_attention_variants(variant, growing):
+    """Every kernel variant (polynomial share of the exponentials, speculative running max)
+    matches the oracle like the default instance. `growing` scales the keys up along the
+    sequence so later blocks raise the running max by more than 2^8 and the speculative
+    variants take their redo path."""
     from vdn_minimax_h3_b200.ops._ext import ext
     torch.manual_seed(2)
     lay = _layout(40, 30, 12, 100)
@@ -112,12 +115,16 @@ def test_window_attention_poly_exp(poly):
     T = lay.seq_len
     q = torch.randn(T, 2, 128, device="cuda", dtype=torch.bfloat16) * 2
     k, v = torch.randn_like(q), torch.randn_like(q)
-    ext().attention_set_poly_every(poly)
+    if growing:
+        ramp = torch.linspace(0.5, 6.0, T, device="cuda").view(T, 1, 1)
+        k = (k.float() * ramp).to(torch.bfloat16)
+    prev = ext().attention_variant()
+    ext().attention_set_variant(variant)
     try:
         out = attn_ops.window_attention(q, k, v, plan, 128 ** -0.5)
         check_device_error()
     finally:
-        ext().attention_set_poly_every(0)
+        ext().attention_set_variant(prev)
     ref = window_softmax_reference(q.float().cpu(), k.float().cpu(), v.float().cpu(), lay, bounds,
                                    128 ** -0.5, "both").reshape(T, 2 * 128)
     assert _rel(out.cpu(), ref) < 2e-2

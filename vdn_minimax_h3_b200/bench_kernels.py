@@ -186,7 +186,8 @@ def main(argv=None):
         bench_gemm_fp8()
     if a.attention_trace:
         from vdn_minimax_h3_b200.ops.attention import trace_attention
-        trace_attention()
+        trace_attention(variant=0)
+        trace_attention(variant=4)
     if a.profile_small:
         profile_small()
     if a.attention_small:

@@ -55,9 +55,13 @@ constexpr int AT_REGS_HIGH = 208;
 static_assert(128 * AT_REGS_LOW + 256 * AT_REGS_HIGH <= AT_THREADS * 168, "register split");
 constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + AT_VSTAGES) * AT_KV_BYTES + 1024 + 384;
 constexpr int AT_MAX_RANGES = 4;
-// AT_POLY_EVERY of every 8 exponentials run as a polynomial on the FMA pipe (0: all on
-// MUFU); the launcher picks the instance (attention_set_poly_every).
-static int g_poly_every = 0;
+// Kernel variants (attention_set_variant): bits 0-1 = how many of every 8 exponentials run
+// as a polynomial on the FMA pipe (0: all on MUFU); bit 2 = speculative running max (the
+// exponentials of block j use the running max of blocks < j and the block's own max is
+// taken in the same pass; only when it exceeds the running max by more than 2^8 is the
+// block redone against the new max).
+constexpr int AT_VARIANTS = 8;
+static int g_variant = 0;
 
 struct AttnParams {
   const int* tiles;          // [n_items_per_head, 4] (q0, q_end, segment, kv_len), q_end-q0 <= 256
@@ -155,7 +159,7 @@ __device__ __forceinline__ void item_coords(const AttnParams& p, int item, int& 
   tile = item - head * p.n_tiles;
 }
 
-template <int AT_POLY_EVERY>
+template <int AT_VARIANT>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                             const __grid_constant__ CUtensorMap tmK,
@@ -455,34 +459,40 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         tmem_wait_ld();
         if (tr) at_trace(p, TR_LD_DONE, qt, g);
-        // row max on the raw scores (8 independent chains); only a ragged block is masked
+        constexpr int AT_POLY_EVERY = AT_VARIANT & 3;
+        constexpr bool AT_SPEC = (AT_VARIANT & 4) != 0;
+        // only a ragged block is masked
         const int valid = w.valid();
         if (valid < AT_BN) {
 #pragma unroll
           for (int c = 0; c < AT_BN; ++c) s[c] = c < valid ? s[c] : -INFINITY;
         }
-        float mxv[8];
+        float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // p = 2^(s * scale_log2 - m), packed bf16 pairs written over S_t in TMEM
+        auto exp_pass = [&](float neg_m, float* mxv) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mxv[i] = s[i];
+          for (int i = 0; i < 8; ++i) sums[i] = 0.f;
 #pragma unroll
-        for (int c = 8; c < AT_BN; c += 16)
+          for (int h = 0; h < 2; ++h) {
+            uint32_t pk[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) mxv[i] = fmax3(mxv[i], s[c + i], s[c + 8 + i]);
-        const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
-                               fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * p.scale_log2;
-        const float m_new = fmaxf(m_ref, mx);
-        const bool need = m_new > m_ref + 8.0f;
-        const bool warp_need = __any_sync(0xffffffffu, need);
-        if (tr) at_trace(p, TR_MAX_DONE, qt, g);
-        float factor = 1.f;
-        if (need) {
-          factor = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - m_new);
-          m_ref = m_new;
-          l *= factor;
-        }
-        // S_t was issued after the previous block's P.V, so that P.V is complete: O may be
-        // rescaled before this block's P is published.
-        if (j > 0 && warp_need) {
+            for (int c = 0; c < 64; c += 8) {
+              float e[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float x = fmaf(s[h * 64 + c + i], p.scale_log2, neg_m);
+                if (mxv) mxv[i] = fmaxf(mxv[i], x);
+                e[i] = (i >= 8 - AT_POLY_EVERY) ? ex2_poly(x) : ex2(x);
+                sums[i] += e[i];
+              }
+#pragma unroll
+              for (int i = 0; i < 4; ++i) pk[c / 2 + i] = pack_bf16(e[2 * i], e[2 * i + 1]);
+            }
+            tmem_st32(tS + h * 32, pk);
+          }
+        };
+        // O rescale (warp-collective TMEM round trip; rows that keep their max use 1)
+        auto rescale_o = [&](float factor) {
 #pragma unroll 1
           for (int c = 0; c < AT_D; c += 32) {
             uint32_t u[32];
@@ -492,26 +502,57 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
             tmem_st32(tO + c, u);
           }
-        }
-        // p = 2^(s * scale_log2 - m), packed bf16 pairs written over S_t in TMEM
-        const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
-        float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        };
+        const bool spec = AT_SPEC && __all_sync(0xffffffffu, m_ref != -INFINITY);
+        if (spec) {
+          // exponentials against the running max; the block max (relative to it) comes
+          // out of the same pass. P <= 2^8 unless the max grew by more than that.
+          float mxv[8];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int c = 0; c < 64; c += 8) {
-            float e[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float x = fmaf(s[h * 64 + c + i], p.scale_log2, neg_m);
-              e[i] = (i >= 8 - AT_POLY_EVERY) ? ex2_poly(x) : ex2(x);
-              sums[i] += e[i];
+          for (int i = 0; i < 8; ++i) mxv[i] = -INFINITY;
+          if (tr) at_trace(p, TR_MAX_DONE, qt, g);
+          exp_pass(-m_ref, mxv);
+          const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
+                                 fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7])));
+          const bool need = mx > 8.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            // rare: redo the block against the new max (S_t was issued after the previous
+            // block's P.V, so O is complete and may be rescaled here)
+            float factor = 1.f;
+            if (need) {
+              factor = ex2(-mx);
+              m_ref += mx;
+              l *= factor;
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) pk[c / 2 + i] = pack_bf16(e[2 * i], e[2 * i + 1]);
+            tmem_wait_st();
+            if (j > 0) rescale_o(factor);
+            exp_pass(-m_ref, nullptr);
           }
-          tmem_st32(tS + h * 32, pk);
+        } else {
+          // row max on the raw scores (8 independent chains)
+          float mxv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mxv[i] = s[i];
+#pragma unroll
+          for (int c = 8; c < AT_BN; c += 16)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mxv[i] = fmax3(mxv[i], s[c + i], s[c + 8 + i]);
+          const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
+                                 fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * p.scale_log2;
+          const float m_new = fmaxf(m_ref, mx);
+          const bool need = m_new > m_ref + 8.0f;
+          const bool warp_need = __any_sync(0xffffffffu, need);
+          if (tr) at_trace(p, TR_MAX_DONE, qt, g);
+          float factor = 1.f;
+          if (need) {
+            factor = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - m_new);
+            m_ref = m_new;
+            l *= factor;
+          }
+          // S_t was issued after the previous block's P.V, so that P.V is complete: O may
+          // be rescaled before this block's P is published.
+          if (j > 0 && warp_need) rescale_o(factor);
+          exp_pass((m_ref == -INFINITY) ? 0.f : -m_ref, nullptr);
         }
         l += ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
         if (tr) at_trace(p, TR_EXP_DONE, qt, g);
@@ -563,15 +604,15 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              const RowScatter* scatter, long long* trace) {
   if (n_tiles == 0 || H == 0) return;
   static bool attr = false;
+  static void (*const kernels[AT_VARIANTS])(CUtensorMap, CUtensorMap, CUtensorMap, AttnParams) = {
+      window_attention_kernel<0>, window_attention_kernel<1>, window_attention_kernel<2>,
+      window_attention_kernel<3>, window_attention_kernel<4>, window_attention_kernel<5>,
+      window_attention_kernel<6>, window_attention_kernel<7>};
   if (!attr) {
-    cudaFuncSetAttribute(window_attention_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
-    cudaFuncSetAttribute(window_attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
-    cudaFuncSetAttribute(window_attention_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
-    cudaFuncSetAttribute(window_attention_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
     // setmaxnreg.inc waits until the registers it asks for are free: refuse to launch if
     // the compiled launch register count cannot fund the split.
-    for (auto fn : {window_attention_kernel<0>, window_attention_kernel<1>,
-                    window_attention_kernel<2>, window_attention_kernel<3>}) {
+    for (auto fn : kernels) {
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
       cudaFuncAttributes fa;
       if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess ||
           fa.numRegs * AT_THREADS < 128 * AT_REGS_LOW + 256 * AT_REGS_HIGH)
@@ -601,14 +642,13 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
   p.err = err;
   const int items = n_tiles * H;
   const int grid = items < num_sms() ? items : num_sms();
-  switch (g_poly_every) {
-    case 0: window_attention_kernel<0><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
-    case 1: window_attention_kernel<1><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
-    case 2: window_attention_kernel<2><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
-    default: window_attention_kernel<3><<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p); break;
-  }
+  kernels[g_variant]<<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p);
 }
 
-void attention_set_poly_every(int n) { g_poly_every = n; }
+void attention_set_variant(int v) {
+  if (v < 0 || v >= AT_VARIANTS) throw std::runtime_error("window attention: variant 0..7");
+  g_variant = v;
+}
+int attention_variant() { return g_variant; }
 
 }  // namespace vdn

@@ -118,7 +118,8 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              int64_t ldo, float scale, int* err, cudaStream_t stream,
                              const RowScatter* scatter = nullptr, long long* trace = nullptr);
 
-void attention_set_poly_every(int n);
+void attention_set_variant(int v);
+int attention_variant();
 
 // Symmetric memory (symmetric.cu): IPC-exported regions and the peer flag barrier.
 void* symm_malloc(size_t nbytes, void* handle_out);

@@ -744,8 +744,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");
   m.def("window_attention", &vdn::window_attention,
         "tcgen05 window softmax attention over an AttentionPlan (gated epilogue)");
-  m.def("attention_set_poly_every", &vdn::attention_set_poly_every,
-        "one exp in every 8*n on the FMA pipe (0, 1, 2, 4)");
+  m.def("attention_set_variant", &vdn::attention_set_variant,
+        "window attention kernel variant: bits 0-1 = polynomial exps per 8, bit 2 = "
+        "speculative running max");
+  m.def("attention_variant", &vdn::attention_variant, "current window attention variant");
   m.def("lb_activate", &vdn::lb_activate, "SiLU [+ L2] over 128-wide heads");
   m.def("lb_conv_features", &vdn::lb_conv_features, "separable 5x5x5 depthwise conv + SiLU [+ L2]");
   m.def("lb_frame_stats", &vdn::lb_frame_stats, "tcgen05 per-frame delta-rule statistics A, B");

@@ -67,20 +67,22 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
     q = torch.randn(T, H, d, device="cuda", dtype=torch.bfloat16)
     k, v = torch.randn_like(q), torch.randn_like(q)
     fl = plan.flops(H, d)
-    for pe in (0, 1, 2, 3):
-        ext().attention_set_poly_every(pe)
+    prev = ext().attention_variant()
+    for var in (0, 4, 5, 1):
+        ext().attention_set_variant(var)
         ms = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
-        print(json.dumps(dict(case="window_attention_c1_both", T=T, heads=H, poly_every=pe, ms=ms,
+        print(json.dumps(dict(case="window_attention_c1_both", T=T, heads=H, variant=var, ms=ms,
                               tflops=fl / ms / 1e9)), flush=True)
-    ext().attention_set_poly_every(0)
+    ext().attention_set_variant(prev)
 
 
 TRACE_EVENTS = ("s_wait", "s_ready", "ld_done", "max_done", "exp_done", "p_arrive",
                 "mma_p_wait", "mma_p_ready", "mma_issued")
 
 
-def trace_attention(frames=102, heads=56, blocks=(8, 60)):  # pragma: no cover - GPU tool
-    """Per-phase clock cycles of CTA 0's softmax / MMA pipeline (kernel timestamps)."""
+def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # pragma: no cover
+    """Per-phase clock cycles of CTA 0's softmax / MMA pipeline (kernel timestamps) for one
+    kernel variant (default: the current one). GPU tool."""
     import json
     from vdn_minimax_h3_b200.models.layout import SequenceLayout
     from vdn_minimax_h3_b200.models.window import AttentionPlan, window_bounds
@@ -90,10 +92,17 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60)):  # pragma: no cover -
                          text_len=800)
     plan = AttentionPlan(lay, window_bounds(frames, 1, 5), "both", device="cuda")
     q = torch.randn(lay.seq_len, heads, 128, device="cuda", dtype=torch.bfloat16)
+    k, v = torch.randn_like(q), torch.randn_like(q)
     tr = torch.zeros(18 * 64, dtype=torch.int64, device="cuda")
-    window_attention(q, q, q, plan, 128 ** -0.5)
-    window_attention(q, q, q, plan, 128 ** -0.5, trace=tr)
-    torch.cuda.synchronize()
+    prev = ext().attention_variant()
+    if variant is not None:
+        ext().attention_set_variant(variant)
+    try:
+        window_attention(q, k, v, plan, 128 ** -0.5)
+        window_attention(q, k, v, plan, 128 ** -0.5, trace=tr)
+        torch.cuda.synchronize()
+    finally:
+        ext().attention_set_variant(prev)
     t = tr.view(9, 2, 64).cpu().double()
     a, b = blocks
     ev = {n: t[i] for i, n in enumerate(TRACE_EVENTS)}
@@ -108,5 +117,13 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60)):  # pragma: no cover -
             "P_arrive_to_next_S": float((ev["s_ready"][tile, a + 1:b + 1] - ev["p_arrive"][tile, a:b]).mean()),
             "block_period": float((ev["s_ready"][tile, a + 1:b + 1] - ev["s_ready"][tile, a:b]).mean()),
         }
+    # timeline of a few blocks relative to tile 0's first S-ready: shows whether the two
+    # tiles' softmax phases alternate or overlap
+    t0 = ev["s_ready"][0, a]
+    line = {}
+    for n in ("s_ready", "max_done", "exp_done", "p_arrive", "mma_p_ready", "mma_issued"):
+        line[n] = [[int(ev[n][tile, i] - t0) for i in range(a, a + 6)] for tile in (0, 1)]
+    out["timeline"] = line
+    out["variant"] = ext().attention_variant() if variant is None else variant
     print(json.dumps({"attention_trace_cycles": out}), flush=True)
     return out
