@@ -38,14 +38,17 @@ def load_prompt(prompt_file, device):
 
 
 def save_prompt(path, prompt, prompt_embeds, text_token_tags=None, keyframe_anchors=(),
-                condition_latents=()):
+                condition_latents=(), **extra):
+    """Atomic write (.tmp then rename). `extra` carries the keyframe encoder's
+    keyframe_files / height / width / reference_size fields."""
     if text_token_tags is None:
         text_token_tags = torch.ones(prompt_embeds.shape[0], dtype=torch.long)
     payload = {"prompt": prompt, "prompt_embeds": prompt_embeds.to(torch.bfloat16).cpu(),
-               "text_token_tags": text_token_tags.cpu()}
+               "text_token_tags": torch.as_tensor(text_token_tags, dtype=torch.long).cpu()}
     if keyframe_anchors:
         payload["keyframe_anchors"] = list(keyframe_anchors)
         payload["condition_latents"] = [c.float().cpu() for c in condition_latents]
+    payload.update(extra)
     tmp = path + ".tmp"
     os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
     torch.save(payload, tmp)
