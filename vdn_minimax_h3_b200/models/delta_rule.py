@@ -59,5 +59,5 @@ class VdnScaledDelta(VdnDelta):
         self.b_scale = self.a_scale ** 0.5
 
 
+# keys are the checkpoint enum checkpoints.key_mapping.DELTA_RULE_VALUES
 DELTA_BACKENDS = {"sana_scaled": SanaDelta, "vdn_solve": VdnDelta, "vdn_scaled": VdnScaledDelta}
-DELTA_RULE_VALUES = tuple(DELTA_BACKENDS)
