@@ -30,13 +30,15 @@ def test_activate(l2):
     assert _rel(out, activate_ref(x.float().cpu(), l2)) < 1e-2
 
 
-@pytest.mark.parametrize("F,gh,gw,H,l2", [(7, 5, 6, 2, True), (18, 4, 3, 1, False)])
-def test_conv_features(F, gh, gw, H, l2):
+@pytest.mark.parametrize("two_pass", [True, False])
+@pytest.mark.parametrize("F,gh,gw,H,l2", [(7, 5, 6, 2, True), (18, 4, 3, 1, False),
+                                          (9, 24, 42, 9, True)])
+def test_conv_features(F, gh, gw, H, l2, two_pass):
     torch.manual_seed(0)
     x = torch.randn(F * gh * gw, H, 128, device="cuda", dtype=torch.bfloat16)
     w_sp = torch.randn(H * 128, 5, 5, device="cuda") / 5
     w_tm = torch.randn(H * 128, 5, device="cuda") / 2
-    out = lb.conv_features(x, w_sp, w_tm, F, (gh, gw), l2)
+    out = lb.conv_features(x, w_sp, w_tm, F, (gh, gw), l2, two_pass=two_pass)
     check_device_error()
     ref = conv_features_reference(x.float().cpu(), w_sp.cpu(), w_tm.cpu(), F, (gh, gw), l2)
     assert _rel(out, ref) < 1e-2

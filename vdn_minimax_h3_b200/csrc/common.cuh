@@ -266,6 +266,25 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 }
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// Packed fp32 pairs (one 64-bit register pair) for fma.rn.f32x2: one instruction performs
+// two independent fp32 FMAs.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  return (unsigned long long)__float_as_uint(lo) | ((unsigned long long)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+  lo = __uint_as_float((uint32_t)v);
+  hi = __uint_as_float((uint32_t)(v >> 32));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// bf16x2 (low half = first element) -> packed fp32 pair; exact (bf16 is the top half of fp32)
+__device__ __forceinline__ unsigned long long f2_from_bf16x2(uint32_t v) {
+  return f2_pack(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
 __device__ __forceinline__ float siluf_(float x) { return x / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -134,6 +134,11 @@ void launch_lb_activate(const void* in, int64_t ldi, int N, int H, void* out, in
 void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* out,
                     int64_t ldo, int F, int gh, int gw, int H, int l2, int* err,
                     cudaStream_t stream);
+// Two-pass form: spatial conv into `tmp` (bf16, [F*gh*gw, H*128] rows of stride ldt), then
+// temporal conv + SiLU [+ L2] into `out`.
+void launch_lb_conv2(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* tmp,
+                     int64_t ldt, void* out, int64_t ldo, int F, int gh, int gw, int H, int l2,
+                     int* err, cudaStream_t stream);
 void launch_lb_frame_stats(const void* k, int64_t ldk, const void* v, int64_t ldv, int F, int S,
                            int H, const float* beta, float* A, float* B, int* err,
                            cudaStream_t stream);

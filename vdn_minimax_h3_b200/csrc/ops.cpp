@@ -545,7 +545,8 @@ void lb_activate(torch::Tensor in, torch::Tensor out, bool l2) {
 }
 
 void lb_conv_features(torch::Tensor in, torch::Tensor wsp, torch::Tensor wtm, torch::Tensor out,
-                      int64_t F, int64_t gh, int64_t gw, bool l2, torch::Tensor err) {
+                      int64_t F, int64_t gh, int64_t gw, bool l2, torch::Tensor err,
+                      c10::optional<torch::Tensor> tmp) {
   check_rows_heads(in, "in");
   check_rows_heads(out, "out");
   const int64_t H = in.size(1);
@@ -553,9 +554,18 @@ void lb_conv_features(torch::Tensor in, torch::Tensor wsp, torch::Tensor wtm, to
   check_f32(wsp, "w_spatial", H * 128 * 25);
   check_f32(wtm, "w_temporal", H * 128 * 5);
   c10::cuda::CUDAGuard g(in.device());
-  launch_lb_conv(in.data_ptr(), in.stride(0), wsp.data_ptr<float>(), wtm.data_ptr<float>(),
-                 out.data_ptr(), out.stride(0), (int)F, (int)gh, (int)gw, (int)H, l2,
-                 err_ptr(err), cur());
+  if (tmp) {
+    // two passes through a bf16 intermediate of the output's shape
+    check_rows_heads(*tmp, "tmp");
+    TORCH_CHECK(tmp->size(0) == in.size(0) && tmp->size(1) == H, "tmp must match in");
+    launch_lb_conv2(in.data_ptr(), in.stride(0), wsp.data_ptr<float>(), wtm.data_ptr<float>(),
+                    tmp->data_ptr(), tmp->stride(0), out.data_ptr(), out.stride(0), (int)F,
+                    (int)gh, (int)gw, (int)H, l2, err_ptr(err), cur());
+  } else {
+    launch_lb_conv(in.data_ptr(), in.stride(0), wsp.data_ptr<float>(), wtm.data_ptr<float>(),
+                   out.data_ptr(), out.stride(0), (int)F, (int)gh, (int)gw, (int)H, l2,
+                   err_ptr(err), cur());
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -749,7 +759,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "speculative running max");
   m.def("attention_variant", &vdn::attention_variant, "current window attention variant");
   m.def("lb_activate", &vdn::lb_activate, "SiLU [+ L2] over 128-wide heads");
-  m.def("lb_conv_features", &vdn::lb_conv_features, "separable 5x5x5 depthwise conv + SiLU [+ L2]");
+  m.def("lb_conv_features", &vdn::lb_conv_features, "separable 5x5x5 depthwise conv + SiLU [+ L2]",
+        py::arg("in"), py::arg("wsp"), py::arg("wtm"), py::arg("out"), py::arg("F"), py::arg("gh"),
+        py::arg("gw"), py::arg("l2"), py::arg("err"), py::arg("tmp") = py::none());
   m.def("lb_frame_stats", &vdn::lb_frame_stats, "tcgen05 per-frame delta-rule statistics A, B");
   m.def("lb_spd_factor", &vdn::lb_spd_factor, "batched (I + aA)^-1, transition and injection");
   m.def("lb_scan", &vdn::lb_scan, "bidirectional serial state recurrences");

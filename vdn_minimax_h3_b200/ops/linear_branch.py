@@ -30,15 +30,23 @@ def activate(tokens, l2norm):
     return out
 
 
-def conv_features(tokens, w_sp, w_tm, num_frames, frame_size, l2norm):
-    """5x5 depthwise spatial conv, 5-tap temporal conv, SiLU [, L2] in one pass."""
+# The short conv runs as two kernels (5x5 spatial into a bf16 intermediate, then 5-tap
+# temporal + SiLU [+ L2]) unless this is False (one fused kernel, slower).
+CONV_TWO_PASS = True
+
+
+def conv_features(tokens, w_sp, w_tm, num_frames, frame_size, l2norm, two_pass=None):
+    """5x5 depthwise spatial conv, 5-tap temporal conv, SiLU [, L2]."""
     if not _native(tokens):
         return conv_features_reference(tokens, w_sp, w_tm, num_frames, frame_size, l2norm)
     gh, gw = frame_size
     out = torch.empty(tokens.shape, dtype=tokens.dtype, device=tokens.device)
+    tmp = None
+    if CONV_TWO_PASS if two_pass is None else two_pass:
+        tmp = torch.empty(tokens.shape, dtype=tokens.dtype, device=tokens.device)
     ext().lb_conv_features(tokens, w_sp.float().reshape(-1).contiguous(),
                            w_tm.float().reshape(-1).contiguous(), out, num_frames, gh, gw,
-                           bool(l2norm), error_word(tokens.device))
+                           bool(l2norm), error_word(tokens.device), tmp)
     return out
 
 
@@ -175,6 +183,8 @@ def bench_linear(timed, frames=100):  # pragma: no cover - GPU tool
     res = {}
     res["activate_q"] = timed(lambda: activate(q_raw, True))
     res["conv_features_k"] = timed(lambda: conv_features(k_raw, w_sp, w_tm, Fr, (gh, gw), True))
+    res["conv_features_k_fused"] = timed(
+        lambda: conv_features(k_raw, w_sp, w_tm, Fr, (gh, gw), True, two_pass=False))
     kf = conv_features(k_raw, w_sp, w_tm, Fr, (gh, gw), True)
     vf = conv_features(k_raw, w_sp, w_tm, Fr, (gh, gw), False)
     beta = torch.rand(Fr, S, n, device=dev)
