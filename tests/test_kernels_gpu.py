@@ -100,11 +100,11 @@ def test_window_attention_dense_gated_strided():
     assert out_full[:, H * 128:].abs().max().item() == 0
 
 
-@pytest.mark.parametrize("variant,growing", [(1, False), (2, False), (3, False), (4, False),
-                                             (4, True), (5, True), (6, False)])
+@pytest.mark.parametrize("variant,growing", [(1, False), (2, False), (2, True), (3, True),
+                                             (4, False), (5, False), (6, True), (7, False)])
 def test_window_attention_variants(variant, growing):
-    """Every kernel variant (polynomial share of the exponentials, speculative running max)
-    matches the oracle like the default instance. `growing` scales the keys up along the
+    """Every kernel variant (polynomial share of the exponentials, speculative running max,
+    truncated P pack) matches the oracle like the default instance. `growing` scales the keys up along the
     sequence so later blocks raise the running max by more than 2^8 and the speculative
     variants take their redo path."""
     from vdn_minimax_h3_b200.ops._ext import ext

@@ -147,9 +147,11 @@ def profile_small():
     A = A @ A.transpose(-1, -2)
     lb.factor_apply(VdnDelta(S), torch.rand(256, 128, device="cuda"), A.view(16, 16, 128, 128),
                     torch.randn(16, 16, 128, 128, device="cuda"))
-    x = torch.randn(8 * S, H, 128, device="cuda", dtype=torch.bfloat16)
-    lb.conv_features(x, torch.randn(H * 128, 5, 5, device="cuda"), torch.randn(H * 128, 5, device="cuda"),
-                     8, (24, 42), True)
+    # short conv at full head count over 20 frames (289 MB in, above L2): about one wave
+    Hc = 56
+    x = torch.randn(Fr * S, Hc, 128, device="cuda", dtype=torch.bfloat16)
+    lb.conv_features(x, torch.randn(Hc * 128, 5, 5, device="cuda"),
+                     torch.randn(Hc * 128, 5, device="cuda"), Fr, (24, 42), True)
     torch.cuda.synchronize()
     check_device_error()
     print("profile-small ok", flush=True)
@@ -187,7 +189,6 @@ def main(argv=None):
     if a.attention_trace:
         from vdn_minimax_h3_b200.ops.attention import trace_attention
         trace_attention(variant=0)
-        trace_attention(variant=4)
     if a.profile_small:
         profile_small()
     if a.attention_small:

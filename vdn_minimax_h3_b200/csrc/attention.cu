@@ -9,13 +9,14 @@
 //
 // Roles (384 threads = 3 warpgroups, one CTA per SM, persistent over head-major work items
 // so the CTAs in flight share one head's K/V in L2):
-//   warp 0      TMA producers: lane 0 both Q tiles once per item and K blocks into a
-//               2-stage ring, lane 1 V blocks into a 2-stage ring.
+//   warp 0      TMA producer: both Q tiles once per item and K blocks into a 3-stage ring
+//   warp 2      TMA producer: V blocks into a 2-stage ring (a warp of its own: two
+//               producers in one warp serialise their barrier waits)
 //   warp 1      MMA issuer (one thread): per block j and tile t, first O_t += P_t V for
 //               block j-1 with P read from TMEM (tcgen05.mma with the A operand in TMEM),
 //               then S_t = Q_t K_j^T (kind::f16, M=128, N=128) into the same TMEM columns;
 //               MMAs execute in issue order, so the S write follows the P read.
-//   warps 2-3   idle (they complete warpgroup 0, whose registers go to the softmax)
+//   warp 3      idle (completes warpgroup 0, whose registers go to the softmax)
 //   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1 (thread = query row): S row
 //               from TMEM into registers, online softmax in the exp2 domain with a lazy
 //               rescale (O in TMEM is rescaled only when the running max grows by more
@@ -42,7 +43,7 @@ namespace vdn {
 constexpr int AT_BM = 128;                         // query rows per tile (2 tiles per item)
 constexpr int AT_BN = 128;                         // keys per block
 constexpr int AT_D = 128;                          // head dim
-constexpr int AT_KSTAGES = 2;                      // K ring
+constexpr int AT_KSTAGES = 3;                      // K ring
 constexpr int AT_VSTAGES = 2;                      // V ring
 constexpr int AT_Q_BYTES = AT_BM * AT_D * 2;       // 32 KB per Q tile (2 atoms of 16 KB)
 constexpr int AT_KV_BYTES = AT_BN * AT_D * 2;      // 32 KB per K or V block (2 atoms of 16 KB)
@@ -55,11 +56,13 @@ constexpr int AT_REGS_HIGH = 208;
 static_assert(128 * AT_REGS_LOW + 256 * AT_REGS_HIGH <= AT_THREADS * 168, "register split");
 constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + AT_VSTAGES) * AT_KV_BYTES + 1024 + 384;
 constexpr int AT_MAX_RANGES = 4;
-// Kernel variants (attention_set_variant): bits 0-1 = how many of every 8 exponentials run
-// as a polynomial on the FMA pipe (0: all on MUFU); bit 2 = speculative running max (the
-// exponentials of block j use the running max of blocks < j and the block's own max is
-// taken in the same pass; only when it exceeds the running max by more than 2^8 is the
-// block redone against the new max).
+// Kernel variants (attention_set_variant): bit 0 = one of every 8 exponentials runs as a
+// polynomial on the FMA pipe; bit 1 = speculative running max (the exponentials of block j
+// use the running max of blocks < j and the block's own max is taken in the same pass;
+// only when it exceeds the running max by more than 2^8 is the block redone against the
+// new max); bit 2 = truncated P pack: the bf16 P pairs are assembled with a byte permute
+// (round toward zero) instead of the float->bf16x2 conversion, which issues on the same
+// pipe as the exponentials.
 constexpr int AT_VARIANTS = 8;
 static int g_variant = 0;
 
@@ -147,11 +150,26 @@ struct KvWalk {
 constexpr int AT_TRACE_BLOCKS = 64;
 enum AtTraceEvent : int {
   TR_S_WAIT = 0, TR_S_READY, TR_LD_DONE, TR_MAX_DONE, TR_EXP_DONE, TR_P_ARRIVE,
-  TR_MMA_P_WAIT, TR_MMA_P_READY, TR_MMA_ISSUED, TR_EVENTS
+  TR_MMA_P_WAIT, TR_MMA_P_READY, TR_MMA_ISSUED, TR_MMA_LOOP_TOP, TR_MMA_V_READY, TR_EVENTS
 };
 __device__ __forceinline__ void at_trace(const AttnParams& p, int ev, int tile, uint32_t blk) {
   if (p.trace && blockIdx.x == 0 && blk < (uint32_t)AT_TRACE_BLOCKS)
     p.trace[(ev * 2 + tile) * AT_TRACE_BLOCKS + blk] = clock64();
+}
+
+template <bool SLEEP>
+__device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                        int* err, int code) {
+  return SLEEP ? mbar_wait_sleep(bar, parity, abort, err, code)
+               : mbar_wait(bar, parity, abort, err, code);
+}
+
+// MMA-thread trace points cost the issuing thread time; they are compiled in only with
+// AT_TRACE_MMA defined (the softmax trace points stay).
+__device__ __forceinline__ void mma_trace(const AttnParams& p, int ev, int tile, uint32_t blk) {
+#ifdef AT_TRACE_MMA
+  at_trace(p, ev, tile, blk);
+#endif
 }
 
 __device__ __forceinline__ void item_coords(const AttnParams& p, int item, int& head, int& tile) {
@@ -187,17 +205,19 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
   const int warp = warp_id(), lane = lane_id();
   const int n_items = p.n_tiles * p.H;
+  constexpr bool AT_SLEEP = false;
+  constexpr int kIssuers = 1;
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    mbar_init(q_empty, kIssuers);
     for (int s = 0; s < AT_KSTAGES; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
+      mbar_init(&k_empty[s], kIssuers);
     }
     for (int s = 0; s < AT_VSTAGES; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+      mbar_init(&v_empty[s], kIssuers);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
@@ -205,7 +225,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&pv_done[t], 1);
       mbar_init(&o_empty[t], 128);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, kIssuers);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -223,7 +243,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   if (warp < 4) {
   setmaxnreg_dec<AT_REGS_LOW>();
   if (warp == 0) {
-    // --------------------------------------------- TMA producers: lane 0 Q + K, lane 1 V
+    // ------------------------------------------------------ TMA producer: Q + K
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -237,7 +257,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         int head, tile;
         item_coords(p, item, head, tile);
         const int* t = p.tiles + 4 * tile;
-        if (!mbar_wait(q_empty, (local & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+        if (!at_wait<AT_SLEEP>(q_empty, (local & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
           ok = false;
           break;
         }
@@ -252,7 +272,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         for (; !w.done(); w.next()) {
-          if (!mbar_wait(&k_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+          if (!at_wait<AT_SLEEP>(&k_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
@@ -276,7 +296,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           }
         }
       }
-    } else if (lane == 1) {
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------ TMA producer of V (its own warp, so
+    // its waits never serialise with the K producer's)
+    if (lane == 0) {
       tma_prefetch_desc(&tmV);
       int stage = 0;
       uint32_t phase = 0;
@@ -290,7 +314,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         for (; !w.done(); w.next()) {
-          if (!mbar_wait(&v_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+          if (!at_wait<AT_SLEEP>(&v_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
@@ -323,6 +347,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       constexpr uint32_t idesc_s = umma_idesc_bf16(AT_BM, AT_BN, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(AT_BM, AT_D, false, true);
       const uint32_t aQ = smem_u32(sQ), aV0 = smem_u32(sV);
+      const int qt0 = 0, qt1 = 2;
       int kstage = 0, vstage = 0;
       uint32_t kphase = 0, vphase = 0;
       uint32_t g = 0;  // global block counter: S_t / P_t phases are g & 1
@@ -332,47 +357,43 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         int head, tile;
         item_coords(p, item, head, tile);
         const int* t = p.tiles + 4 * tile;
-        if (!mbar_wait(q_full, local & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        if (!at_wait<AT_SLEEP>(q_full, local & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         int j = 0;
         while (ok) {
           const bool have = !w.done();
+          mma_trace(p, TR_MMA_LOOP_TOP, qt0, g);
           if (!have && j == 0) {
             // no K/V at all: release the epilogue (it writes zeros)
-            umma_commit(&pv_done[0]);
-            umma_commit(&pv_done[1]);
+            for (int qt = qt0; qt < qt1; ++qt) umma_commit(&pv_done[qt]);
             break;
           }
-          uint32_t aK = 0, aV = 0;
-          if (have) {
-            if (!mbar_wait(&k_full[kstage], kphase, abort_flag, p.err, kErrTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            aK = smem_u32(sK + kstage * AT_KV_BYTES);
-          }
-          if (j > 0) {
-            if (!mbar_wait(&v_full[vstage], vphase, abort_flag, p.err, kErrTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            aV = aV0 + vstage * AT_KV_BYTES;
-          }
-          tc_fence_after();
-          for (int qt = 0; qt < 2 && ok; ++qt) {
+          // waits are placed just before the operand they guard: P.V of tile 0 does not
+          // wait for this block's K, nor Q.K^T for the previous block's V
+          const uint32_t aK = smem_u32(sK + kstage * AT_KV_BYTES);
+          const uint32_t aV = aV0 + vstage * AT_KV_BYTES;
+          for (int qt = qt0; qt < qt1 && ok; ++qt) {
             const uint32_t tS = tmem + qt * AT_BN;
             if (j > 0) {
-              at_trace(p, TR_MMA_P_WAIT, qt, g - 1);
-              if (!mbar_wait(&p_full[qt], (g - 1) & 1, abort_flag, p.err, kErrTimeoutMma) ||
-                  (j == 1 && local > 0 &&
-                   !mbar_wait(&o_empty[qt], (local - 1) & 1, abort_flag, p.err, kErrTimeoutMma))) {
+              mma_trace(p, TR_MMA_P_WAIT, qt, g - 1);
+              if (qt == qt0) {
+                if (!at_wait<AT_SLEEP>(&v_full[vstage], vphase, abort_flag, p.err, kErrTimeoutMma)) {
+                  ok = false;
+                  break;
+                }
+                mma_trace(p, TR_MMA_V_READY, qt0, g);
+              }
+              if ((j == 1 && local > 0 &&
+                   !at_wait<AT_SLEEP>(&o_empty[qt], (local - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) ||
+                  !at_wait<AT_SLEEP>(&p_full[qt], (g - 1) & 1, abort_flag, p.err,
+                             kErrTimeoutMma)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              at_trace(p, TR_MMA_P_READY, qt, g - 1);
+              mma_trace(p, TR_MMA_P_READY, qt, g - 1);
 #pragma unroll
               for (int k = 0; k < AT_BN / 16; ++k)
                 umma_f16_ts(tmem + 256 + qt * 128, tS + k * 8,
@@ -381,6 +402,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
               if (!have) umma_commit(&pv_done[qt]);
             }
             if (have) {
+              if (qt == qt0) {
+                if (!at_wait<AT_SLEEP>(&k_full[kstage], kphase, abort_flag, p.err, kErrTimeoutMma)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+              }
 #pragma unroll
               for (int k = 0; k < AT_D / 16; ++k) {
                 const uint32_t off = (k >> 2) * (AT_Q_BYTES / 2) + (k & 3) * 32;
@@ -388,12 +416,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                             umma_desc_kmajor_sw128(aK + off), idesc_s, k != 0);
               }
               umma_commit(&s_full[qt]);
-              at_trace(p, TR_MMA_ISSUED, qt, g);
+              mma_trace(p, TR_MMA_ISSUED, qt, g);
             }
           }
           if (!ok) break;
           if (have) {
             umma_commit(&k_empty[kstage]);
+            mma_trace(p, TR_MMA_V_READY, 1, g);    // (tile slot 1: after the K release)
             if (++kstage == AT_KSTAGES) {
               kstage = 0;
               kphase ^= 1;
@@ -410,6 +439,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           ++g;
           ++j;
           w.next();
+          mma_trace(p, TR_MMA_LOOP_TOP, 1, g - 1);  // (tile slot 1: block bookkeeping done)
         }
         if (!ok) break;
         umma_commit(q_empty);
@@ -443,7 +473,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       const bool tr = (r == 0);
       for (; !w.done(); w.next(), ++j, ++g) {
         if (tr) at_trace(p, TR_S_WAIT, qt, g);
-        if (!mbar_wait(&s_full[qt], g & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+        if (!at_wait<AT_SLEEP>(&s_full[qt], g & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
           ok = false;
           break;
         }
@@ -459,8 +489,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         tmem_wait_ld();
         if (tr) at_trace(p, TR_LD_DONE, qt, g);
-        constexpr int AT_POLY_EVERY = AT_VARIANT & 3;
-        constexpr bool AT_SPEC = (AT_VARIANT & 4) != 0;
+        constexpr int AT_POLY_EVERY = AT_VARIANT & 1;
+        constexpr bool AT_SPEC = (AT_VARIANT & 2) != 0;
+        constexpr bool AT_TRUNC = (AT_VARIANT & 4) != 0;
         // only a ragged block is masked
         const int valid = w.valid();
         if (valid < AT_BN) {
@@ -483,10 +514,16 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 const float x = fmaf(s[h * 64 + c + i], p.scale_log2, neg_m);
                 if (mxv) mxv[i] = fmaxf(mxv[i], x);
                 e[i] = (i >= 8 - AT_POLY_EVERY) ? ex2_poly(x) : ex2(x);
+                // truncated pack: P is the top half of each fp32 (round toward zero) and the
+                // row sum adds exactly those values, so O / l stays a softmax of the scores
+                if (AT_TRUNC) e[i] = __uint_as_float(__float_as_uint(e[i]) & 0xffff0000u);
                 sums[i] += e[i];
               }
 #pragma unroll
-              for (int i = 0; i < 4; ++i) pk[c / 2 + i] = pack_bf16(e[2 * i], e[2 * i + 1]);
+              for (int i = 0; i < 4; ++i)
+                pk[c / 2 + i] = AT_TRUNC ? __byte_perm(__float_as_uint(e[2 * i]),
+                                                       __float_as_uint(e[2 * i + 1]), 0x7632)
+                                         : pack_bf16(e[2 * i], e[2 * i + 1]);
             }
             tmem_st32(tS + h * 32, pk);
           }
@@ -563,7 +600,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
       if (!ok) break;
       // Epilogue: wait for the item's last P.V, O / l * gate -> bf16.
-      if (!mbar_wait(&pv_done[qt], local & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
+      if (!at_wait<AT_SLEEP>(&pv_done[qt], local & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
       tc_fence_after();
       const int row = t[0] + qt * AT_BM + r;
       const bool row_ok = row < t[1];
@@ -604,7 +641,8 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              const RowScatter* scatter, long long* trace) {
   if (n_tiles == 0 || H == 0) return;
   static bool attr = false;
-  static void (*const kernels[AT_VARIANTS])(CUtensorMap, CUtensorMap, CUtensorMap, AttnParams) = {
+  using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, AttnParams);
+  static const KernelFn kernels[AT_VARIANTS] = {
       window_attention_kernel<0>, window_attention_kernel<1>, window_attention_kernel<2>,
       window_attention_kernel<3>, window_attention_kernel<4>, window_attention_kernel<5>,
       window_attention_kernel<6>, window_attention_kernel<7>};

@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+          if (!mbar_wait_sleep(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
@@ -473,14 +473,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t use = (uint32_t)(local >> 1);
-        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
+        if (!mbar_wait_sleep(&tempty[buf], (use & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t tacc = tmem_base + buf * GM_BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+          if (!mbar_wait_sleep(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       tile_coords(tile, num_m, num_n, mb, nb);
       const int buf = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
-      if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      if (!mbar_wait_sleep(&tfull[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       epilogue_tile<EPI>(p, tmem_base + buf * GM_BN, quarter, mb * GM_BM, nb * GM_BN, M, N,
                          route_stage + quarter * kRouteStageWords);

@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
         int mb, nb;
         f8_tile_coords(tile, num_m, num_n, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+          if (!mbar_wait_sleep(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
@@ -402,13 +402,13 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       bool ok = true;
       int local = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-        if (!mbar_wait(tempty, (local & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
+        if (!mbar_wait_sleep(tempty, (local & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+          if (!mbar_wait_sleep(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       int mb, nb;
       f8_tile_coords(tile, num_m, num_n, mb, nb);
-      if (!mbar_wait(tfull, local & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      if (!mbar_wait_sleep(tfull, local & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       uint32_t v[128];
 #pragma unroll

@@ -135,7 +135,7 @@ void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* 
                     int64_t ldo, int F, int gh, int gw, int H, int l2, int* err,
                     cudaStream_t stream);
 // Two-pass form: spatial conv into `tmp` (bf16, [F*gh*gw, H*128] rows of stride ldt), then
-// temporal conv + SiLU [+ L2] into `out`.
+// temporal conv + SiLU [+ L2] into `out`. Here `wsp` is TAP-major, [25, H*128].
 void launch_lb_conv2(const void* in, int64_t ldi, const float* wsp, const float* wtm, void* tmp,
                      int64_t ldt, void* out, int64_t ldo, int F, int gh, int gw, int H, int l2,
                      int* err, cudaStream_t stream);

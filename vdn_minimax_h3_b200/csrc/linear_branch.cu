@@ -251,41 +251,38 @@ void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* 
 // ------------------------------------------------- separable short conv, two passes
 // Pass 1 (lb_spatial_kernel): the 5x5 depthwise spatial conv, bf16 result (the reference's
 // spatial conv also hands a bf16 tensor to its temporal conv). Block = (chunk of SP_FC
-// frames, head h); warp w owns positions 4w..4w+3 of a grid row, lane 4 channels. The
-// block walks its frames' grid rows in order; every input row is brought into shared
-// memory once by TMA (one box of gw positions x 128 channels) into an 8-slot row ring
-// with 3 rows of prefetch, and output row y reads rows y-2..y+2 from the ring. The FMAs
-// run on packed channel pairs (fma.rn.f32x2). ~110 KB of shared memory and <= 93
-// registers give two blocks (22 warps) per SM.
+// frames, head h, channel half); warp w owns positions 4w..4w+3 of a grid row, lane 2
+// channels, whose 25 taps stay in registers as packed fp32 pairs (fma.rn.f32x2). The block
+// walks its frames' grid rows in order; every input row (gw positions x 64 channels) is
+// brought into shared memory once by TMA into an 8-slot row ring with 3 rows of prefetch,
+// and output row y reads rows y-2..y+2 (one 128-byte wavefront per position). ~50 KB of
+// shared memory and <= 93 registers give two to three blocks per SM.
 // Pass 2 (lb_temporal_kernel): 5-tap temporal conv + SiLU [+ L2 over the head's 128
 // channels]; one warp per (position, head) streams the frames with a register ring, so
 // every intermediate element is read once.
 constexpr int SP_SLOTS = 8;
 constexpr int SP_AHEAD = 3;               // rows of prefetch beyond the five in use
 constexpr int SP_FC = 4;                  // frames per block
-constexpr int SP_W_BYTES = 25 * 128 * 4;
-constexpr int SP_SMEM = SP_SLOTS * LB_ROW_BYTES + SP_W_BYTES + 1024 /*align*/ + 128 /*barriers*/;
+constexpr int SP_CH = 64;                 // channels per block (half a head)
+constexpr int SP_ROW_BYTES = LB_XPAD * SP_CH * 2;
+constexpr int SP_SMEM = SP_SLOTS * SP_ROW_BYTES + 1024 /*align*/ + 128 /*barriers*/;
 
 __global__ void __launch_bounds__(LB_MAXW / LB_PPW * 32, 2) lb_spatial_kernel(
-    const __grid_constant__ CUtensorMap tmIn, const float* __restrict__ wsp,
+    const __grid_constant__ CUtensorMap tmIn, const float* __restrict__ wsp, int C,
     __nv_bfloat16* __restrict__ tmp, int64_t ldt, int F, int gh, int gw, int* err) {
   extern __shared__ uint8_t lb_smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(lb_smem_raw) + 1023) & ~uintptr_t(1023));
-  float* s_w = reinterpret_cast<float*>(ring + SP_SLOTS * LB_ROW_BYTES);   // [25][128]
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + SP_SLOTS * LB_ROW_BYTES + SP_W_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + SP_SLOTS * SP_ROW_BYTES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + SP_SLOTS);
-  const int h = blockIdx.y;
+  const int h = blockIdx.y, half = blockIdx.z;
+  const int col0 = h * 128 + half * SP_CH;           // first channel of this block
   const int f0 = blockIdx.x * SP_FC, f1 = min(F, f0 + SP_FC);
   const int S = gh * gw;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nthr = blockDim.x;
-  for (int i = tid; i < 25 * 128; i += nthr) {
-    const int tap = i >> 7, c = i & 127;
-    s_w[i] = wsp[(int64_t)(h * 128 + c) * 25 + tap];
-  }
   // halo positions (2 each side) are never written by TMA: zero the ring once
-  for (int i = tid; i < SP_SLOTS * LB_ROW_BYTES / 16; i += nthr)
+  for (int i = tid; i < SP_SLOTS * SP_ROW_BYTES / 16; i += nthr)
     reinterpret_cast<uint4*>(ring)[i] = make_uint4(0, 0, 0, 0);
   if (tid == 0) {
     for (int i = 0; i < SP_SLOTS; ++i) mbar_init(&full[i], 1);
@@ -301,8 +298,8 @@ __global__ void __launch_bounds__(LB_MAXW / LB_PPW * 32, 2) lb_spatial_kernel(
     for (; issued < limit; ++issued) {
       const int slot = issued % SP_SLOTS;
       const int f = f0 + issued / gh, y = issued % gh;
-      mbar_arrive_expect_tx(&full[slot], (uint32_t)(gw * 256));
-      tma_load_2d(ring + slot * LB_ROW_BYTES + 2 * 256, &tmIn, &full[slot], h * 128,
+      mbar_arrive_expect_tx(&full[slot], (uint32_t)(gw * SP_CH * 2));
+      tma_load_2d(ring + slot * SP_ROW_BYTES + 2 * SP_CH * 2, &tmIn, &full[slot], col0,
                   f * S + y * gw);
     }
   };
@@ -310,9 +307,15 @@ __global__ void __launch_bounds__(LB_MAXW / LB_PPW * 32, 2) lb_spatial_kernel(
     tma_prefetch_desc(&tmIn);
     issue_upto(3 + SP_AHEAD);
   }
+  // this lane's two channels: 25 taps as packed pairs, one 8-byte load each from the
+  // tap-major weights [25, C]
+  const int c = 2 * lane;
+  unsigned long long wt[25];
+#pragma unroll
+  for (int t = 0; t < 25; ++t)
+    wt[t] = __ldg(reinterpret_cast<const unsigned long long*>(wsp + (int64_t)t * C + col0 + c));
   const int x0 = warp * LB_PPW;
   const bool active = x0 < gw;
-  const int c0 = lane * 4;
   int waited = 0;
   bool ok = true;
   for (int o = 0; o < n_loads; ++o) {
@@ -326,41 +329,30 @@ __global__ void __launch_bounds__(LB_MAXW / LB_PPW * 32, 2) lb_spatial_kernel(
       ok = mbar_wait(&full[waited % SP_SLOTS], (uint32_t)((waited / SP_SLOTS) & 1), abort_flag, err,
                      kErrTimeoutProducer);
     if (ok && active) {
-      unsigned long long acc[LB_PPW][2];
+      unsigned long long acc[LB_PPW];
 #pragma unroll
-      for (int q = 0; q < LB_PPW; ++q) acc[q][0] = acc[q][1] = 0ull;
+      for (int q = 0; q < LB_PPW; ++q) acc[q] = 0ull;
 #pragma unroll
       for (int i = 0; i < 5; ++i) {
         const int yy = y + i - 2;
         if (yy < 0 || yy >= gh) continue;   // block-uniform: the zero padding rows
-        const uint8_t* rowp = ring + ((base + yy) % SP_SLOTS) * LB_ROW_BYTES + c0 * 2;
-        unsigned long long win[LB_PPW + 4][2];
+        const uint8_t* rowp = ring + ((base + yy) % SP_SLOTS) * SP_ROW_BYTES + c * 2;
+        unsigned long long win[LB_PPW + 4];
 #pragma unroll
-        for (int u = 0; u < LB_PPW + 4; ++u) {
-          const uint2 v = *reinterpret_cast<const uint2*>(rowp + (x0 + u) * 256);
-          win[u][0] = f2_from_bf16x2(v.x);
-          win[u][1] = f2_from_bf16x2(v.y);
-        }
+        for (int u = 0; u < LB_PPW + 4; ++u)
+          win[u] = f2_from_bf16x2(*reinterpret_cast<const uint32_t*>(rowp + (x0 + u) * SP_CH * 2));
 #pragma unroll
-        for (int j = 0; j < 5; ++j) {
-          const float4 w = *reinterpret_cast<const float4*>(s_w + (i * 5 + j) * 128 + c0);
-          const unsigned long long w01 = f2_pack(w.x, w.y), w23 = f2_pack(w.z, w.w);
+        for (int j = 0; j < 5; ++j)
 #pragma unroll
-          for (int q = 0; q < LB_PPW; ++q) {
-            acc[q][0] = f2_fma(w01, win[q + j][0], acc[q][0]);
-            acc[q][1] = f2_fma(w23, win[q + j][1], acc[q][1]);
-          }
-        }
+          for (int q = 0; q < LB_PPW; ++q) acc[q] = f2_fma(wt[i * 5 + j], win[q + j], acc[q]);
       }
       const int64_t row0 = (int64_t)(f0 + fr) * S + (int64_t)y * gw;
 #pragma unroll
       for (int q = 0; q < LB_PPW; ++q) {
         if (x0 + q >= gw) break;
-        float a0, a1, a2, a3;
-        f2_unpack(acc[q][0], a0, a1);
-        f2_unpack(acc[q][1], a2, a3);
-        *reinterpret_cast<uint2*>(tmp + (row0 + x0 + q) * ldt + h * 128 + c0) =
-            make_uint2(pack_bf16(a0, a1), pack_bf16(a2, a3));
+        float a0, a1;
+        f2_unpack(acc[q], a0, a1);
+        *reinterpret_cast<uint32_t*>(tmp + (row0 + x0 + q) * ldt + col0 + c) = pack_bf16(a0, a1);
       }
     }
     if (__syncthreads_or(!ok)) break;
@@ -377,7 +369,10 @@ __global__ void __launch_bounds__(LB_MAXW / LB_PPW * 32, 2) lb_spatial_kernel(
 }
 
 constexpr int TC_WARPS = 8;
-__global__ void __launch_bounds__(TC_WARPS * 32) lb_temporal_kernel(
+// SiLU with the approximate divide (bf16 output)
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+__global__ void __launch_bounds__(TC_WARPS * 32, 4) lb_temporal_kernel(
     const __nv_bfloat16* __restrict__ tmp, int64_t ldt, const float* __restrict__ wtm,
     __nv_bfloat16* __restrict__ out, int64_t ldo, int F, int S, int H, int l2) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -390,58 +385,52 @@ __global__ void __launch_bounds__(TC_WARPS * 32) lb_temporal_kernel(
 #pragma unroll
     for (int dt = 0; dt < 5; ++dt) tw[dt][c] = __ldg(wtm + (chan + c) * 5 + dt);
   const __nv_bfloat16* src = tmp + (int64_t)pos * ldt + chan;
-  const int64_t fstride = (int64_t)S * ldt;
-  float ring[5][4];
+  __nv_bfloat16* dst = out + (int64_t)pos * ldo + chan;
+  const int64_t fs_in = (int64_t)S * ldt, fs_out = (int64_t)S * ldo;
+  // ring slot of frame f is f % 5: with the loop unrolled by 5 every slot index is a
+  // constant, so the ring never moves
+  uint2 ring[5];
+  ring[3] = ring[4] = make_uint2(0, 0);                     // frames -2, -1
+  auto load = [&](int f) {
+    return f < F ? __ldg(reinterpret_cast<const uint2*>(src + f * fs_in)) : make_uint2(0, 0);
+  };
+  ring[0] = load(0);
+  ring[1] = load(1);
+  ring[2] = load(2);
+  for (int f0 = 0; f0 < F; f0 += 5) {
+    // frames f0+3 .. f0+7 into slots 3, 4, 0, 1, 2 as they free up
+    uint2 nxt[5];
 #pragma unroll
-  for (int a = 0; a < 5; ++a)
+    for (int k = 0; k < 5; ++k) nxt[k] = load(f0 + 3 + k);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) ring[a][c] = 0.f;
-  constexpr int U = 4;   // frames per step; the next step's loads are in flight meanwhile
-  uint2 nxt[U];
+    for (int k = 0; k < 5; ++k) {
+      const int fo = f0 + k;                  // output frame: inputs fo-2 .. fo+2
+      if (fo >= F) break;
+      // slot of frame fo+2 is (k+2) % 5; it holds frame fo+2 once the previous step stored
+      if (k >= 1) ring[(k + 2) % 5] = nxt[k - 1];
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int k = 0; k < U; ++k)
-    nxt[k] = k < F ? __ldg(reinterpret_cast<const uint2*>(src + k * fstride)) : make_uint2(0, 0);
-  for (int f = 0; f < F + 2; f += U) {
-    uint2 cur[U];
-#pragma unroll
-    for (int k = 0; k < U; ++k) {
-      cur[k] = nxt[k];
-      const int fn = f + U + k;
-      nxt[k] = fn < F ? __ldg(reinterpret_cast<const uint2*>(src + fn * fstride)) : make_uint2(0, 0);
-    }
-#pragma unroll
-    for (int k = 0; k < U; ++k) {
-      const int fk = f + k;   // newest frame in the ring; output frame fk - 2
-      if (fk >= F + 2) break;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        ring[0][c] = ring[1][c];
-        ring[1][c] = ring[2][c];
-        ring[2][c] = ring[3][c];
-        ring[3][c] = ring[4][c];
+      for (int dt = 0; dt < 5; ++dt) {
+        const uint2 v = ring[(k + dt + 3) % 5];    // frame fo + dt - 2
+        o[0] = fmaf(tw[dt][0], bf16_lo(v.x), o[0]);
+        o[1] = fmaf(tw[dt][1], bf16_hi(v.x), o[1]);
+        o[2] = fmaf(tw[dt][2], bf16_lo(v.y), o[2]);
+        o[3] = fmaf(tw[dt][3], bf16_hi(v.y), o[3]);
       }
-      ring[4][0] = bf16_lo(cur[k].x);
-      ring[4][1] = bf16_hi(cur[k].x);
-      ring[4][2] = bf16_lo(cur[k].y);
-      ring[4][3] = bf16_hi(cur[k].y);
-      if (fk < 2) continue;
-      float o[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float t = 0.f;
-#pragma unroll
-        for (int dt = 0; dt < 5; ++dt) t = fmaf(tw[dt][c], ring[dt][c], t);
-        o[c] = siluf_(t);
-      }
+      for (int c = 0; c < 4; ++c) o[c] = silu_fast(o[c]);
       if (l2) {
+        // x / max(||x||, 1e-6) == x * rsqrt(max(||x||^2, 1e-12))
         const float ss = warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
-        const float inv = 1.f / fmaxf(sqrtf(ss), 1e-6f);
+        const float inv = rsqrtf(fmaxf(ss, 1e-12f));
 #pragma unroll
         for (int c = 0; c < 4; ++c) o[c] *= inv;
       }
-      *reinterpret_cast<uint2*>(out + ((int64_t)(fk - 2) * S + pos) * ldo + chan) =
+      *reinterpret_cast<uint2*>(dst + fo * fs_out) =
           make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
     }
+    // frame f0+7 (slot (f0+7) % 5 == 2) is needed by the next group's first output
+    ring[2] = nxt[4];
   }
 }
 
@@ -453,13 +442,16 @@ void launch_lb_conv2(const void* in, int64_t ldi, const float* wsp, const float*
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(lb_spatial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SP_SMEM);
+    // two blocks per SM need the largest shared-memory carveout
+    cudaFuncSetAttribute(lb_spatial_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
     attr = true;
   }
   CUtensorMap tm = make_tmap_2d(in, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * 128,
-                                (uint64_t)F * gh * gw, ldi * 2, 128, gw, CU_TENSOR_MAP_SWIZZLE_NONE);
+                                (uint64_t)F * gh * gw, ldi * 2, SP_CH, gw, CU_TENSOR_MAP_SWIZZLE_NONE);
   const int warps = (gw + LB_PPW - 1) / LB_PPW;
-  lb_spatial_kernel<<<dim3((F + SP_FC - 1) / SP_FC, H), warps * 32, SP_SMEM, stream>>>(
-      tm, wsp, reinterpret_cast<__nv_bfloat16*>(tmp), ldt, F, gh, gw, err);
+  lb_spatial_kernel<<<dim3((F + SP_FC - 1) / SP_FC, H, 128 / SP_CH), warps * 32, SP_SMEM, stream>>>(
+      tm, wsp, H * 128, reinterpret_cast<__nv_bfloat16*>(tmp), ldt, F, gh, gw, err);
   lb_temporal_kernel<<<dim3(gh * gw, (H + TC_WARPS - 1) / TC_WARPS), TC_WARPS * 32, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(tmp), ldt, wtm, reinterpret_cast<__nv_bfloat16*>(out),
       ldo, F, gh * gw, H, l2);

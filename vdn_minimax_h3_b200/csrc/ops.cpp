@@ -493,7 +493,7 @@ void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
   check_out_or_scatter(out, sc, out.stride(0), T, H * 128);
   if (trace)
     TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous() &&
-                    trace->numel() >= 18 * 64,
+                    trace->numel() >= 22 * 64,
                 "trace must be a contiguous int64 CUDA tensor of >= 1152 entries");
   TORCH_CHECK(tiles.is_cuda() && tiles.scalar_type() == at::kInt && tiles.is_contiguous() &&
                   tiles.dim() == 2 && tiles.size(1) == 4, "tiles must be int32 [n, 4]");
@@ -759,7 +759,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "speculative running max");
   m.def("attention_variant", &vdn::attention_variant, "current window attention variant");
   m.def("lb_activate", &vdn::lb_activate, "SiLU [+ L2] over 128-wide heads");
-  m.def("lb_conv_features", &vdn::lb_conv_features, "separable 5x5x5 depthwise conv + SiLU [+ L2]",
+  m.def("lb_conv_features", &vdn::lb_conv_features, "separable 5x5x5 depthwise conv + SiLU [+ L2]; "
+        "w_spatial is [C, 25] for the fused kernel, [25, C] (tap-major) when tmp is given",
         py::arg("in"), py::arg("wsp"), py::arg("wtm"), py::arg("out"), py::arg("F"), py::arg("gh"),
         py::arg("gw"), py::arg("l2"), py::arg("err"), py::arg("tmp") = py::none());
   m.def("lb_frame_stats", &vdn::lb_frame_stats, "tcgen05 per-frame delta-rule statistics A, B");

@@ -68,7 +68,7 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
     k, v = torch.randn_like(q), torch.randn_like(q)
     fl = plan.flops(H, d)
     prev = ext().attention_variant()
-    for var in (0, 4, 5, 1):
+    for var in (0, 2, 4):
         ext().attention_set_variant(var)
         ms = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
         print(json.dumps(dict(case="window_attention_c1_both", T=T, heads=H, variant=var, ms=ms,
@@ -77,7 +77,7 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
 
 
 TRACE_EVENTS = ("s_wait", "s_ready", "ld_done", "max_done", "exp_done", "p_arrive",
-                "mma_p_wait", "mma_p_ready", "mma_issued")
+                "mma_p_wait", "mma_p_ready", "mma_issued", "mma_loop_top", "mma_v_ready")
 
 
 def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # pragma: no cover
@@ -93,7 +93,7 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
     plan = AttentionPlan(lay, window_bounds(frames, 1, 5), "both", device="cuda")
     q = torch.randn(lay.seq_len, heads, 128, device="cuda", dtype=torch.bfloat16)
     k, v = torch.randn_like(q), torch.randn_like(q)
-    tr = torch.zeros(18 * 64, dtype=torch.int64, device="cuda")
+    tr = torch.zeros(22 * 64, dtype=torch.int64, device="cuda")
     prev = ext().attention_variant()
     if variant is not None:
         ext().attention_set_variant(variant)
@@ -103,7 +103,7 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
         torch.cuda.synchronize()
     finally:
         ext().attention_set_variant(prev)
-    t = tr.view(9, 2, 64).cpu().double()
+    t = tr.view(11, 2, 64).cpu().double()
     a, b = blocks
     ev = {n: t[i] for i, n in enumerate(TRACE_EVENTS)}
     out = {}
@@ -121,7 +121,8 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
     # tiles' softmax phases alternate or overlap
     t0 = ev["s_ready"][0, a]
     line = {}
-    for n in ("s_ready", "max_done", "exp_done", "p_arrive", "mma_p_ready", "mma_issued"):
+    for n in ("s_ready", "max_done", "exp_done", "p_arrive", "mma_loop_top", "mma_p_wait",
+              "mma_v_ready", "mma_p_ready", "mma_issued"):
         line[n] = [[int(ev[n][tile, i] - t0) for i in range(a, a + 6)] for tile in (0, 1)]
     out["timeline"] = line
     out["variant"] = ext().attention_variant() if variant is None else variant

@@ -42,9 +42,11 @@ def conv_features(tokens, w_sp, w_tm, num_frames, frame_size, l2norm, two_pass=N
     gh, gw = frame_size
     out = torch.empty(tokens.shape, dtype=tokens.dtype, device=tokens.device)
     tmp = None
+    w_spatial = w_sp.float().reshape(-1, 25)
     if CONV_TWO_PASS if two_pass is None else two_pass:
         tmp = torch.empty(tokens.shape, dtype=tokens.dtype, device=tokens.device)
-    ext().lb_conv_features(tokens, w_sp.float().reshape(-1).contiguous(),
+        w_spatial = w_spatial.t()           # the two-pass kernel reads taps [25, C]
+    ext().lb_conv_features(tokens, w_spatial.contiguous().reshape(-1),
                            w_tm.float().reshape(-1).contiguous(), out, num_frames, gh, gw,
                            bool(l2norm), error_word(tokens.device), tmp)
     return out
