@@ -205,8 +205,14 @@ class Qwen3VLConditioner:
 
 
 def make_conditioner(model_root=None, device="cuda:0", seed=0):
-    """The Qwen3-VL conditioner when a snapshot is given, else the stand-in."""
-    return Qwen3VLConditioner(model_root, device) if model_root else StandInConditioner(seed=seed)
+    """The Qwen3-VL conditioner when a snapshot is given ("hub": the MiniMax-H3 snapshot,
+    fetched on first use), else the stand-in."""
+    if not model_root:
+        return StandInConditioner(seed=seed)
+    from vdn_minimax_h3_b200.paths import resolve_repo_path, upstream_snapshot
+    root = upstream_snapshot("processor", "text_encoder") if model_root == "hub" else \
+        resolve_repo_path(model_root)
+    return Qwen3VLConditioner(root, device)
 
 
 def build_presentation(cond, prompt, images=()):

@@ -88,7 +88,8 @@ def build_model(spec: Union[ModelSpec, Dict[str, Any]], device="cpu", base_sourc
     if init == "random":
         random_init_(model, seed=seed)
     elif init == "load":
-        load_base_weights(model, base_source or base.source, base.subfolder)
+        from vdn_minimax_h3_b200.paths import resolve_weights
+        load_base_weights(model, resolve_weights(base_source or base.source), base.subfolder)
     else:
         raise ValueError(f"init must be 'load' or 'random', got {init!r}")
     verify_base_config(model, base)
