@@ -162,6 +162,8 @@ def main(argv=None):
     p.add_argument("--gemm", action="store_true")
     p.add_argument("--attention", action="store_true")
     p.add_argument("--linear", action="store_true")
+    p.add_argument("--linear-heads", type=int, nargs="*", default=[56],
+                   help="head counts for --linear (7 = one rank's share at 8-way Ulysses)")
     p.add_argument("--norm", action="store_true")
     p.add_argument("--gemm-fp8", action="store_true")
     p.add_argument("--attention-trace", action="store_true",
@@ -181,7 +183,8 @@ def main(argv=None):
         bench_attention(timed)
     if a.linear:
         from vdn_minimax_h3_b200.ops.linear_branch import bench_linear
-        bench_linear(timed)
+        for h in a.linear_heads:
+            bench_linear(timed, heads=h)
     if a.norm:
         bench_norm()
     if a.gemm_fp8:

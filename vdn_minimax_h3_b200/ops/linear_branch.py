@@ -169,13 +169,13 @@ def text_state(branch, text_raw, text_beta):
     return branch.TEXT_STATE_SCALE * inj[0]
 
 
-def bench_linear(timed, frames=100):  # pragma: no cover - GPU tool
+def bench_linear(timed, frames=100, heads=56):  # pragma: no cover - GPU tool
     """Each linear-branch stage at the full geometry: 100 inner frames x 1008 tokens x 56
-    heads (anchors both)."""
+    heads (anchors both); `heads` < 56 is one rank's share under sequence parallelism."""
     import json
     from vdn_minimax_h3_b200.models.delta_rule import VdnDelta
     from vdn_minimax_h3_b200.models.window import window_bounds
-    Fr, S, n, d, gh, gw = frames, 1008, 56, 128, 24, 42
+    Fr, S, n, d, gh, gw = frames, 1008, heads, 128, 24, 42
     dev = "cuda"
     raw = torch.randn(Fr * S, 3 * n * d + 8, device=dev, dtype=torch.bfloat16)
     q_raw = raw[:, :n * d].view(-1, n, d)
@@ -207,4 +207,5 @@ def bench_linear(timed, frames=100):  # pragma: no cover - GPU tool
     out = torch.empty(Fr * S, n * d, device=dev, dtype=torch.bfloat16)
     res["readout"] = timed(lambda: readout(qf.view(Fr, S, n, d), state, w, gate, 1e-6, out=out,
                                            gate_logits=True))
-    print(json.dumps({"linear_branch_ms": {k: round(v, 3) for k, v in res.items()}}), flush=True)
+    print(json.dumps({"heads": n, "linear_branch_ms": {k: round(v, 3) for k, v in res.items()}}),
+          flush=True)
