@@ -77,15 +77,23 @@ def test_spd_factor(rule):
     assert _rel(inj, inj_r) < 1e-4
 
 
+@pytest.mark.parametrize("cluster", [0, 1, 2, 4, 8, -2])
 @pytest.mark.parametrize("with_start", [False, True])
-def test_scan(with_start):
+def test_scan(with_start, cluster):
+    """The single-CTA scan and the cluster-split scan (state columns over 2/4/8 CTAs
+    exchanged through distributed shared memory) match the fp64 recurrence."""
+    from vdn_minimax_h3_b200.ops._ext import ext
     torch.manual_seed(0)
     F, H = 9, 3
     trans = torch.randn(F, H, 128, 128) * 0.08
     inj = torch.randn(F, H, 128, 128)
     start = torch.randn(H, 128, 128) if with_start else None
-    p, s = lb.run_scans(trans.cuda(), inj.cuda(), None if start is None else start.cuda())
-    check_device_error()
+    ext().lb_scan_set_cluster(cluster)
+    try:
+        p, s = lb.run_scans(trans.cuda(), inj.cuda(), None if start is None else start.cuda())
+        check_device_error()
+    finally:
+        ext().lb_scan_set_cluster(0)
     pr, sr = scan_ref.run_scans(trans.double(), inj.double(), None if start is None else start.double())
     assert _rel(p, pr) < 1e-4
     assert _rel(s, sr) < 1e-4

@@ -879,13 +879,160 @@ __global__ void __launch_bounds__(256) lb_scan_kernel(const float* __restrict__ 
   }
 }
 
+// Row-split scan for few heads (one rank's share under sequence parallelism). Each row of
+// the state evolves on its own, S_new[r, :] = S[r, :] T + inj[r, :], so the 128 rows of a
+// (head, direction) recurrence are split over RS independent CTAs (no communication): a
+// CTA keeps its 128/RS state rows in shared memory and streams the full transition of
+// each frame through a 2-slot ring filled by one bulk copy per frame (the copy of frame
+// t+1 lands while frame t computes; the RS CTAs of a head read the same T from L2). The
+// serial step count stays F; the work per step and CTA drops by RS.
+template <int RS, int NSLOT>
+__global__ void __launch_bounds__(256, NSLOT == 1 ? 2 : 1) lb_scan_rows_kernel(
+    const float* __restrict__ trans, const float* __restrict__ inj,
+    const float* __restrict__ start, int F, int H, float* __restrict__ prefix,
+    float* __restrict__ suffix, int* err) {
+  constexpr int NR = 128 / RS;            // state rows of this CTA
+  constexpr int RT = NR * 128 / 256 / 4;  // rows per thread (4 columns per thread)
+  constexpr int CG = 32;                  // column groups of 4
+  static_assert(RT >= 1 && CG * (NR / RT) == 256, "thread tiling");
+  extern __shared__ __align__(16) float smf[];
+  float* Tb = smf;                              // [NSLOT][128][128] transition ring
+  float* St = smf + NSLOT * 16384;              // [NR][SC_PITCH] state rows
+  uint64_t* full = reinterpret_cast<uint64_t*>(St + NR * SC_PITCH);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2);
+  const int h = blockIdx.x / RS, part = blockIdx.x % RS, dir = blockIdx.y;
+  const int row0 = part * NR;
+  const int tid = threadIdx.x;
+  const int tj = tid % CG, ti = tid / CG;       // column group, row group
+  const int c = tj * 4;
+  for (int i = tid; i < NR * 128; i += 256) {
+    const int r = i >> 7, cc = i & 127;
+    St[r * SC_PITCH + cc] = start ? start[(int64_t)h * 16384 + (row0 + r) * 128 + cc] : 0.f;
+  }
+  if (tid == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  float* bank = dir == 0 ? prefix : suffix;
+  auto base_of = [&](int step) {
+    const int f = dir == 0 ? step : F - 1 - step;
+    return ((int64_t)f * H + h) * 16384;
+  };
+  int issued = 0, done = 0;               // copies issued / consumed (thread 0's view)
+  auto issue = [&](int step) {            // thread 0: T of frame `step` into slot step % NSLOT
+    ++issued;
+    uint64_t* bar = &full[step % NSLOT];
+    mbar_arrive_expect_tx(bar, 16384 * 4);
+    bulk_load(Tb + (step % NSLOT) * 16384, trans + base_of(step), 16384 * 4, bar);
+  };
+  if (tid == 0) {
+    for (int q = 0; q < NSLOT && q < F; ++q) issue(q);
+  }
+  float4 inx[RT];
+#pragma unroll
+  for (int i = 0; i < RT; ++i)
+    inx[i] = __ldg(reinterpret_cast<const float4*>(inj + base_of(0) + (row0 + ti * RT + i) * 128 + c));
+  bool ok = true;
+  for (int step = 0; step < F; ++step) {
+    ok = mbar_wait(&full[step % NSLOT], (uint32_t)((step / NSLOT) & 1), abort_flag, err,
+                   kErrTimeoutProducer);
+    if (__syncthreads_or(!ok)) break;
+    done = step + 1;
+    float4 acc[RT];
+#pragma unroll
+    for (int i = 0; i < RT; ++i) acc[i] = inx[i];
+    if (step + 1 < F) {
+#pragma unroll
+      for (int i = 0; i < RT; ++i)
+        inx[i] = __ldg(reinterpret_cast<const float4*>(inj + base_of(step + 1) +
+                                                      (row0 + ti * RT + i) * 128 + c));
+    }
+    const float* T = Tb + (step % NSLOT) * 16384;
+#pragma unroll 4
+    for (int k = 0; k < 128; ++k) {
+      const float4 m = *reinterpret_cast<const float4*>(&T[k * 128 + c]);
+#pragma unroll
+      for (int i = 0; i < RT; ++i) {
+        const float si = St[(ti * RT + i) * SC_PITCH + k];
+        acc[i].x = fmaf(si, m.x, acc[i].x);
+        acc[i].y = fmaf(si, m.y, acc[i].y);
+        acc[i].z = fmaf(si, m.z, acc[i].z);
+        acc[i].w = fmaf(si, m.w, acc[i].w);
+      }
+    }
+    __syncthreads();     // every thread has read the state and this step's slot
+    if (tid == 0 && step + NSLOT < F) issue(step + NSLOT);
+    float* ob = bank + base_of(step);
+#pragma unroll
+    for (int i = 0; i < RT; ++i) {
+      const int r = ti * RT + i;
+      *reinterpret_cast<float4*>(&St[r * SC_PITCH + c]) = acc[i];
+      *reinterpret_cast<float4*>(ob + (row0 + r) * 128 + c) = acc[i];
+    }
+  }
+  // an aborted block waits (bounded) for its own copies in flight before exiting
+  if (tid == 0 && *abort_flag) {
+    const long long t0 = clock64();
+    for (int q = done; q < issued; ++q)
+      while (!mbar_try_wait(&full[q % NSLOT], (uint32_t)((q / NSLOT) & 1)) &&
+             clock64() - t0 < kWaitBudgetCycles) {
+      }
+  }
+}
+
+template <int RS, int NSLOT>
+static void launch_scan_rows(const float* trans, const float* inj, const float* start, int F,
+                             int H, float* prefix, float* suffix, int* err, cudaStream_t stream) {
+  constexpr int smem = (NSLOT * 16384 + (128 / RS) * SC_PITCH) * 4 + 64;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(lb_scan_rows_kernel<RS, NSLOT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         smem);
+    cudaFuncSetAttribute(lb_scan_rows_kernel<RS, NSLOT>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    attr = true;
+  }
+  lb_scan_rows_kernel<RS, NSLOT><<<dim3(H * RS, 2), 256, smem, stream>>>(trans, inj, start, F, H,
+                                                                          prefix, suffix, err);
+}
+
+// Row split for the scan: the largest of 1, 2, 4, 8 that keeps all 2*H*RS CTAs resident
+// (one per SM) on the device.
+static int scan_cluster_size(int H) {
+  const int sms = num_sms();
+  int cs = 1;
+  while (cs < 8 && 2 * H * cs * 2 <= sms) cs *= 2;
+  return cs;
+}
+
+static int g_scan_cluster = 0;   // 0: automatic; else forced: 1 (one CTA per recurrence),
+                                 // 2, 4, 8 (row parts, two slots), -2 (two parts, one slot)
+void lb_scan_set_cluster(int cs) { g_scan_cluster = cs; }
+
 void launch_lb_scan(const float* trans, const float* inj, const float* start, int F, int H,
-                    float* prefix, float* suffix, cudaStream_t stream) {
+                    float* prefix, float* suffix, int* err, cudaStream_t stream) {
   if (!F || !H) return;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(lb_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM);
     attr = true;
+  }
+  // many heads: two half-row CTAs per recurrence at two CTAs per SM (one transition slot);
+  // few heads: 2, 4 or 8 row parts per recurrence, one CTA per SM, two transition slots
+  const int cs = g_scan_cluster ? g_scan_cluster : scan_cluster_size(H);
+  if (cs == -2 || (cs == 1 && !g_scan_cluster && 2 * H * 2 <= 2 * num_sms())) {
+    launch_scan_rows<2, 1>(trans, inj, start, F, H, prefix, suffix, err, stream);
+    return;
+  }
+  switch (cs) {
+    case 2: launch_scan_rows<2, 2>(trans, inj, start, F, H, prefix, suffix, err, stream); return;
+    case 4: launch_scan_rows<4, 2>(trans, inj, start, F, H, prefix, suffix, err, stream); return;
+    case 8: launch_scan_rows<8, 2>(trans, inj, start, F, H, prefix, suffix, err, stream); return;
+    default: break;
   }
   lb_scan_kernel<<<dim3(H, 2), 256, SC_SMEM, stream>>>(trans, inj, start, F, H, prefix, suffix);
 }

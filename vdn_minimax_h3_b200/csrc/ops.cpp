@@ -619,7 +619,7 @@ void lb_scan(torch::Tensor trans, torch::Tensor inj, c10::optional<torch::Tensor
   }
   c10::cuda::CUDAGuard g(trans.device());
   launch_lb_scan(trans.data_ptr<float>(), inj.data_ptr<float>(), sp, (int)F, (int)H,
-                 prefix.data_ptr<float>(), suffix.data_ptr<float>(), cur());
+                 prefix.data_ptr<float>(), suffix.data_ptr<float>(), err_ptr(err), cur());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -766,6 +766,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lb_frame_stats", &vdn::lb_frame_stats, "tcgen05 per-frame delta-rule statistics A, B");
   m.def("lb_spd_factor", &vdn::lb_spd_factor, "batched (I + aA)^-1, transition and injection");
   m.def("lb_scan", &vdn::lb_scan, "bidirectional serial state recurrences");
+  m.def("lb_scan_set_cluster", &vdn::lb_scan_set_cluster,
+        "scan cluster size: 0 = by head count, else 1, 2, 4 or 8");
   m.def("lb_gather", &vdn::lb_gather, "window-complement state gather with alpha bridge");
   m.def("lb_readout", &vdn::lb_readout, "tcgen05 readout q.S^T + RMSNorm * w * gate");
 }

@@ -90,13 +90,28 @@ def run_scans(trans, inj, text_state=None):
     return prefix, suffix
 
 
+_GATHER_IDX = {}
+
+
+def _gather_index_tables(bounds, num_frames, device):
+    """The window-complement index tables of a layout, built once per (bounds, F, device):
+    building them from Python lists is a pageable host-to-device copy, which would make
+    the host wait for the stream on every layer."""
+    key = (tuple(tuple(b) for b in bounds), num_frames, str(device))
+    hit = _GATHER_IDX.get(key)
+    if hit is None:
+        idx = scan_ref.gather_indices(bounds, num_frames, device)
+        table = torch.stack([idx["before_idx"], idx["after_idx"], idx["has_before"].long(),
+                             idx["has_after"].long()], dim=1).to(torch.int32).contiguous()
+        hit = _GATHER_IDX[key] = (idx, table)
+    return hit
+
+
 def gather_tables(alpha, bounds, bridge):
     """Per-frame gather indices [F, 4] (before, after, has_before, has_after) and the bridge
     factors prod(alpha) over the skipped frames, [F, H, d] each (fp32, from log-prefix sums)."""
     F_ = alpha.shape[0]
-    idx = scan_ref.gather_indices(bounds, F_, alpha.device)
-    table = torch.stack([idx["before_idx"], idx["after_idx"], idx["has_before"].long(),
-                         idx["has_after"].long()], dim=1).to(torch.int32).contiguous()
+    idx, table = _gather_index_tables(bounds, F_, alpha.device)
     if bridge == "alpha":
         log_a = torch.log(alpha.float().clamp_min(1e-12))
         pre = torch.cat([torch.zeros_like(log_a[:1]), log_a.cumsum(0)])
