@@ -137,6 +137,12 @@ def profile_small():
     xa = torch.randn(16384, 5376, device="cuda", dtype=torch.bfloat16)
     wa = torch.randn(5376, 5376, device="cuda", dtype=torch.bfloat16) / 70
     gemm.linear(xa, wa)
+    from vdn_minimax_h3_b200.ops import fp8
+    w8 = fp8.Fp8Weight(torch.randn(21504, 5376, device="cuda", dtype=torch.bfloat16) / 70)
+    xq = torch.empty(16384, 5376, device="cuda", dtype=torch.uint8)
+    xsf = torch.empty(fp8.sf_bytes(16384, 5376), device="cuda", dtype=torch.uint8)
+    fp8.quantize_act(xa, xq, xsf)
+    fp8.linear_fp8(xq, xsf, w8, torch.empty(16384, 21504, device="cuda", dtype=torch.bfloat16))
     Fr, S, H = 20, 1008, 8
     lay = SequenceLayout(seq_len=1950 + Fr * S, video_start=1950, num_frames=Fr, tokens_per_frame=S,
                          frame_height=24, frame_width=42, text_start=0, text_len=800)
