@@ -172,6 +172,8 @@ def main(argv=None):
                    help="head counts for --linear (7 = one rank's share at 8-way Ulysses)")
     p.add_argument("--norm", action="store_true")
     p.add_argument("--gemm-fp8", action="store_true")
+    p.add_argument("--gemm-fp8-trace", action="store_true",
+                   help="fp8 GEMM wait-cycle counters (QKV shape)")
     p.add_argument("--attention-trace", action="store_true",
                    help="clock64 phase durations of CTA 0's attention pipeline")
     p.add_argument("--profile-small", action="store_true",
@@ -195,6 +197,9 @@ def main(argv=None):
         bench_norm()
     if a.gemm_fp8:
         bench_gemm_fp8()
+    if a.gemm_fp8_trace:
+        from vdn_minimax_h3_b200.ops.fp8 import trace_gemm_fp8
+        trace_gemm_fp8()
     if a.attention_trace:
         from vdn_minimax_h3_b200.ops.attention import trace_attention
         trace_attention(variant=0)

@@ -70,7 +70,14 @@ struct Fp8Params {
   GemmRoute route;             // ROUTE: destinations and the q/k head processing
   RowScatter scatter;          // STORE_F32: rows to their tensor-parallel owners
   int* err;
+  long long* trace;            // optional: per-CTA cycle counts of the producer / MMA waits
 };
+
+// Diagnostics (off unless set): per CTA [0] MMA-thread cycles, [1] of them waiting for
+// staged operands, [2] waiting for the accumulator, [3] producer cycles waiting for a free
+// stage, [4] tiles.
+static long long* g_fp8_trace = nullptr;
+void gemm_fp8_set_trace(long long* t) { g_fp8_trace = t; }
 
 // ROUTE epilogue on one 128-column group held in registers: q/k heads get raw stores to
 // plane 0 and RMSNorm + rotate-half RoPE stores to plane 1; other columns are stored to
@@ -361,14 +368,17 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       uint32_t issued_mask = 0, issued_par = 0;
+      long long t_empty = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
         f8_tile_coords(tile, num_m, num_n, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
+          const long long tw = p.trace ? clock64() : 0;
           if (!mbar_wait_sleep(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
+          if (p.trace) t_empty += clock64() - tw;
           uint8_t* sA = smem + stage * F8_STAGE_BYTES;
           uint8_t* sB = sA + F8_A_BYTES;
           uint8_t* sSFA = sB + F8_B_BYTES;
@@ -386,6 +396,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
           }
         }
       }
+      if (p.trace) p.trace[blockIdx.x * 8 + 3] = t_empty;
       if (!ok) {
         for (int s = 0; s < F8_STAGES; ++s) {
           if (!(issued_mask >> s & 1)) continue;
@@ -401,17 +412,23 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
+      const long long t_start = p.trace ? clock64() : 0;
+      long long t_full = 0, t_acc = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const long long ta = p.trace ? clock64() : 0;
         if (!mbar_wait_sleep(tempty, (local & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) {
           ok = false;
           break;
         }
+        if (p.trace) t_acc += clock64() - ta;
         tc_fence_after();
         for (int kb = 0; kb < num_kb; ++kb) {
+          const long long tf = p.trace ? clock64() : 0;
           if (!mbar_wait_sleep(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
+          if (p.trace) t_full += clock64() - tf;
           tc_fence_after();
           const uint32_t aA = smem_u32(smem + stage * F8_STAGE_BYTES);
           const uint32_t aB = aA + F8_A_BYTES;
@@ -435,6 +452,12 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
           }
         }
         if (ok) umma_commit(tfull);
+      }
+      if (p.trace) {
+        p.trace[blockIdx.x * 8 + 0] = clock64() - t_start;
+        p.trace[blockIdx.x * 8 + 1] = t_full;
+        p.trace[blockIdx.x * 8 + 2] = t_acc;
+        p.trace[blockIdx.x * 8 + 4] = local;
       }
       umma_commit(mma_done);
       long long t0 = clock64();
@@ -476,6 +499,7 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
 
 template <int EPI>
 static void launch_fp8(const GemmFp8Args& a, Fp8Params p, cudaStream_t stream) {
+  p.trace = g_fp8_trace;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(gemm_fp8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, F8_SMEM);

@@ -76,6 +76,7 @@ struct GemmFp8Args {
 void launch_gemm_fp8(const GemmFp8Args& a, int mode, void* out, int64_t ldo, const float* bias,
                      const void* gate, int64_t ldg, const int* gate_idx, void* q_out, int64_t ldq,
                      void* q_sf, int* err, cudaStream_t stream);
+void gemm_fp8_set_trace(long long* t);   // diagnostics: per-CTA wait cycles (or null)
 void launch_gemm_fp8_routed(const GemmFp8Args& a, const GemmRoute& r, const float* bias, int* err,
                             cudaStream_t stream);
 void launch_gemm_fp8_f32_scatter(const GemmFp8Args& a, void* out, int64_t ldo, const RowScatter& sc,

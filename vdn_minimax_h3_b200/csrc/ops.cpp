@@ -758,6 +758,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "window attention kernel variant: bits 0-1 = polynomial exps per 8, bit 2 = "
         "speculative running max");
   m.def("attention_variant", &vdn::attention_variant, "current window attention variant");
+  m.def("gemm_fp8_set_trace", [](c10::optional<torch::Tensor> t) {
+    vdn::gemm_fp8_set_trace(t ? reinterpret_cast<long long*>(t->data_ptr()) : nullptr);
+  }, "fp8 GEMM diagnostics: int64 [148 * 8] per-CTA wait cycles, or None");
   m.def("lb_activate", &vdn::lb_activate, "SiLU [+ L2] over 128-wide heads");
   m.def("lb_conv_features", &vdn::lb_conv_features, "separable 5x5x5 depthwise conv + SiLU [+ L2]; "
         "w_spatial is [C, 25] for the fused kernel, [25, C] (tap-major) when tmp is given",

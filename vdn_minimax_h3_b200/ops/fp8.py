@@ -202,3 +202,30 @@ def linear_routed_fp8(xq, xsf, w: Fp8Weight, route, q_cols=(0, 0), k_cols=(0, 0)
                           k_cols[0], k_cols[1], f32(norm_q), f32(norm_k), float(qk_eps),
                           cos if qk else None, sin if qk else None, error_word(xq.device))
     return route
+
+
+def trace_gemm_fp8(M=104766, N=21504, K=5376):  # pragma: no cover - GPU tool
+    """Where the fp8 GEMM's MMA thread spends its cycles (per-CTA counters, averaged):
+    waiting for staged operands, waiting for the accumulator to be drained, and the
+    producer waiting for a free stage."""
+    import json
+    w8 = Fp8Weight(torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / 70)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    xq, xsf = quantize_act(x)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    linear_fp8(xq, xsf, w8, out)
+    tr = torch.zeros(4096, dtype=torch.int64, device="cuda")
+    ext().gemm_fp8_set_trace(tr)
+    try:
+        linear_fp8(xq, xsf, w8, out)
+        torch.cuda.synchronize()
+    finally:
+        ext().gemm_fp8_set_trace(None)
+    t = tr.view(-1, 8)[:torch.cuda.get_device_properties(0).multi_processor_count].double()
+    tot = t[:, 0].mean().item()
+    res = {"mma_thread_cycles": tot, "wait_operands_frac": t[:, 1].mean().item() / tot,
+           "wait_accumulator_frac": t[:, 2].mean().item() / tot,
+           "producer_wait_stage_frac": t[:, 3].mean().item() / tot,
+           "tiles_per_cta": t[:, 4].mean().item()}
+    print(json.dumps({"gemm_fp8_trace": res}), flush=True)
+    return res
