@@ -149,27 +149,11 @@ struct KvWalk {
 // events of its first AT_TRACE_BLOCKS blocks, slot = (event * 2 + tile) * AT_TRACE_BLOCKS + block.
 constexpr int AT_TRACE_BLOCKS = 64;
 enum AtTraceEvent : int {
-  TR_S_WAIT = 0, TR_S_READY, TR_LD_DONE, TR_MAX_DONE, TR_EXP_DONE, TR_P_ARRIVE,
-  TR_MMA_P_WAIT, TR_MMA_P_READY, TR_MMA_ISSUED, TR_MMA_LOOP_TOP, TR_MMA_V_READY, TR_EVENTS
+  TR_S_WAIT = 0, TR_S_READY, TR_LD_DONE, TR_MAX_DONE, TR_EXP_DONE, TR_P_ARRIVE, TR_EVENTS
 };
 __device__ __forceinline__ void at_trace(const AttnParams& p, int ev, int tile, uint32_t blk) {
   if (p.trace && blockIdx.x == 0 && blk < (uint32_t)AT_TRACE_BLOCKS)
     p.trace[(ev * 2 + tile) * AT_TRACE_BLOCKS + blk] = clock64();
-}
-
-template <bool SLEEP>
-__device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                        int* err, int code) {
-  return SLEEP ? mbar_wait_sleep(bar, parity, abort, err, code)
-               : mbar_wait(bar, parity, abort, err, code);
-}
-
-// MMA-thread trace points cost the issuing thread time; they are compiled in only with
-// AT_TRACE_MMA defined (the softmax trace points stay).
-__device__ __forceinline__ void mma_trace(const AttnParams& p, int ev, int tile, uint32_t blk) {
-#ifdef AT_TRACE_MMA
-  at_trace(p, ev, tile, blk);
-#endif
 }
 
 __device__ __forceinline__ void item_coords(const AttnParams& p, int item, int& head, int& tile) {
@@ -205,7 +189,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
   const int warp = warp_id(), lane = lane_id();
   const int n_items = p.n_tiles * p.H;
-  constexpr bool AT_SLEEP = false;
   constexpr int kIssuers = 1;
 
   if (warp == 0 && lane == 0) {
@@ -257,7 +240,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         int head, tile;
         item_coords(p, item, head, tile);
         const int* t = p.tiles + 4 * tile;
-        if (!at_wait<AT_SLEEP>(q_empty, (local & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+        if (!mbar_wait(q_empty, (local & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
           ok = false;
           break;
         }
@@ -272,7 +255,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         for (; !w.done(); w.next()) {
-          if (!at_wait<AT_SLEEP>(&k_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+          if (!mbar_wait(&k_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
@@ -314,7 +297,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         KvWalk w;
         w.init(p.kv + 8 * t[2]);
         for (; !w.done(); w.next()) {
-          if (!at_wait<AT_SLEEP>(&v_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
+          if (!mbar_wait(&v_empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
@@ -342,12 +325,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     // -------------------------------------------------------------------- MMA issuer
     // Per block j and tile t, in this order: O_t += P_t(j-1) V(j-1) with P read from TMEM
     // (where the softmax stored it over S_t), then S_t = Q_t K(j)^T. MMAs run in issue
-    // order, so the S_t write follows the P_t read.
+    // order, so the S_t write follows the P_t read. The tcgen05 issue queue is about one
+    // MMA deep, so this thread's instruction count sits on the tensor pipe's critical path:
+    // the loop keeps only a block count (no range walk) and builds each operand descriptor
+    // once, advancing only its start-address field (addr >> 4 in the low 14 bits; shared
+    // memory is < 256 KB, so the add never carries out of the field).
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(AT_BM, AT_BN, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(AT_BM, AT_D, false, true);
-      const uint32_t aQ = smem_u32(sQ), aV0 = smem_u32(sV);
-      const int qt0 = 0, qt1 = 2;
+      const uint32_t dq_lo0 = (uint32_t)umma_desc_kmajor_sw128(smem_u32(sQ));
+      const uint32_t dq_hi = (uint32_t)(umma_desc_kmajor_sw128(smem_u32(sQ)) >> 32);
+      const uint32_t dk_lo0 = (uint32_t)umma_desc_kmajor_sw128(smem_u32(sK));
+      const uint32_t dv_lo0 = (uint32_t)umma_desc_mnmajor_sw128(smem_u32(sV), AT_KV_BYTES / 2);
+      const uint32_t dv_hi = (uint32_t)(umma_desc_mnmajor_sw128(smem_u32(sV), AT_KV_BYTES / 2) >> 32);
+      auto desc = [](uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; };
       int kstage = 0, vstage = 0;
       uint32_t kphase = 0, vphase = 0;
       uint32_t g = 0;  // global block counter: S_t / P_t phases are g & 1
@@ -357,72 +348,71 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         int head, tile;
         item_coords(p, item, head, tile);
         const int* t = p.tiles + 4 * tile;
-        if (!at_wait<AT_SLEEP>(q_full, local & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        // blocks of this item: 128-key blocks over its (at most four) K/V ranges
+        const int* kv = p.kv + 8 * t[2];
+        int nblk = 0;
+#pragma unroll
+        for (int rg = 0; rg < AT_MAX_RANGES; ++rg) {
+          const int len = kv[2 * rg + 1] - kv[2 * rg];
+          nblk += len > 0 ? (len + AT_BN - 1) / AT_BN : 0;
+        }
+        if (!mbar_wait(q_full, local & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
-        KvWalk w;
-        w.init(p.kv + 8 * t[2]);
-        int j = 0;
-        while (ok) {
-          const bool have = !w.done();
-          mma_trace(p, TR_MMA_LOOP_TOP, qt0, g);
-          if (!have && j == 0) {
-            // no K/V at all: release the epilogue (it writes zeros)
-            for (int qt = qt0; qt < qt1; ++qt) umma_commit(&pv_done[qt]);
-            break;
-          }
-          // waits are placed just before the operand they guard: P.V of tile 0 does not
-          // wait for this block's K, nor Q.K^T for the previous block's V
-          const uint32_t aK = smem_u32(sK + kstage * AT_KV_BYTES);
-          const uint32_t aV = aV0 + vstage * AT_KV_BYTES;
-          for (int qt = qt0; qt < qt1 && ok; ++qt) {
+        if (nblk == 0) {
+          // no K/V at all: release the epilogue (it writes zeros)
+          umma_commit(&pv_done[0]);
+          umma_commit(&pv_done[1]);
+          umma_commit(q_empty);
+          continue;
+        }
+        for (int j = 0; j <= nblk && ok; ++j) {
+          const bool have = j < nblk;
+          const uint32_t dk_lo = dk_lo0 + (uint32_t)(kstage * (AT_KV_BYTES >> 4));
+          const uint32_t dv_lo = dv_lo0 + (uint32_t)(vstage * (AT_KV_BYTES >> 4));
+#pragma unroll
+          for (int qt = 0; qt < 2; ++qt) {
             const uint32_t tS = tmem + qt * AT_BN;
             if (j > 0) {
-              mma_trace(p, TR_MMA_P_WAIT, qt, g - 1);
-              if (qt == qt0) {
-                if (!at_wait<AT_SLEEP>(&v_full[vstage], vphase, abort_flag, p.err, kErrTimeoutMma)) {
-                  ok = false;
-                  break;
-                }
-                mma_trace(p, TR_MMA_V_READY, qt0, g);
-              }
-              if ((j == 1 && local > 0 &&
-                   !at_wait<AT_SLEEP>(&o_empty[qt], (local - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) ||
-                  !at_wait<AT_SLEEP>(&p_full[qt], (g - 1) & 1, abort_flag, p.err,
-                             kErrTimeoutMma)) {
+              if ((qt == 0 && !mbar_wait(&v_full[vstage], vphase, abort_flag, p.err,
+                                                 kErrTimeoutMma)) ||
+                  (j == 1 && local > 0 &&
+                   !mbar_wait(&o_empty[qt], (local - 1) & 1, abort_flag, p.err,
+                                      kErrTimeoutMma)) ||
+                  !mbar_wait(&p_full[qt], (g - 1) & 1, abort_flag, p.err,
+                                     kErrTimeoutMma)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              mma_trace(p, TR_MMA_P_READY, qt, g - 1);
 #pragma unroll
               for (int k = 0; k < AT_BN / 16; ++k)
                 umma_f16_ts(tmem + 256 + qt * 128, tS + k * 8,
-                            umma_desc_mnmajor_sw128(aV + k * 2048, AT_KV_BYTES / 2), idesc_o,
+                            desc(dv_lo + (uint32_t)((k * 2048) >> 4), dv_hi), idesc_o,
                             (j > 1 || k > 0) ? 1u : 0u);
               if (!have) umma_commit(&pv_done[qt]);
             }
             if (have) {
-              if (qt == qt0) {
-                if (!at_wait<AT_SLEEP>(&k_full[kstage], kphase, abort_flag, p.err, kErrTimeoutMma)) {
+              if (qt == 0) {
+                if (!mbar_wait(&k_full[kstage], kphase, abort_flag, p.err,
+                                       kErrTimeoutMma)) {
                   ok = false;
                   break;
                 }
                 tc_fence_after();
               }
+              const uint32_t dq_lo = dq_lo0 + (uint32_t)(qt * (AT_Q_BYTES >> 4));
 #pragma unroll
               for (int k = 0; k < AT_D / 16; ++k) {
-                const uint32_t off = (k >> 2) * (AT_Q_BYTES / 2) + (k & 3) * 32;
-                umma_f16_ss(tS, umma_desc_kmajor_sw128(aQ + qt * AT_Q_BYTES + off),
-                            umma_desc_kmajor_sw128(aK + off), idesc_s, k != 0);
+                const uint32_t off = (uint32_t)(((k >> 2) * (AT_Q_BYTES / 2) + (k & 3) * 32) >> 4);
+                umma_f16_ss(tS, desc(dq_lo + off, dq_hi), desc(dk_lo + off, dq_hi), idesc_s,
+                            k != 0);
               }
               umma_commit(&s_full[qt]);
-              mma_trace(p, TR_MMA_ISSUED, qt, g);
             }
           }
           if (!ok) break;
           if (have) {
             umma_commit(&k_empty[kstage]);
-            mma_trace(p, TR_MMA_V_READY, 1, g);    // (tile slot 1: after the K release)
             if (++kstage == AT_KSTAGES) {
               kstage = 0;
               kphase ^= 1;
@@ -435,11 +425,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
               vphase ^= 1;
             }
           }
-          if (!have) break;
-          ++g;
-          ++j;
-          w.next();
-          mma_trace(p, TR_MMA_LOOP_TOP, 1, g - 1);  // (tile slot 1: block bookkeeping done)
+          if (have) ++g;
         }
         if (!ok) break;
         umma_commit(q_empty);
@@ -473,7 +459,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       const bool tr = (r == 0);
       for (; !w.done(); w.next(), ++j, ++g) {
         if (tr) at_trace(p, TR_S_WAIT, qt, g);
-        if (!at_wait<AT_SLEEP>(&s_full[qt], g & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+        if (!mbar_wait(&s_full[qt], g & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
           ok = false;
           break;
         }
@@ -600,7 +586,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
       if (!ok) break;
       // Epilogue: wait for the item's last P.V, O / l * gate -> bf16.
-      if (!at_wait<AT_SLEEP>(&pv_done[qt], local & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
+      if (!mbar_wait(&pv_done[qt], local & 1, abort_flag, p.err, kErrTimeoutSoftmax)) break;
       tc_fence_after();
       const int row = t[0] + qt * AT_BM + r;
       const bool row_ok = row < t[1];

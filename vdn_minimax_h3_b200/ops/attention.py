@@ -76,8 +76,7 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
     ext().attention_set_variant(prev)
 
 
-TRACE_EVENTS = ("s_wait", "s_ready", "ld_done", "max_done", "exp_done", "p_arrive",
-                "mma_p_wait", "mma_p_ready", "mma_issued", "mma_loop_top", "mma_v_ready")
+TRACE_EVENTS = ("s_wait", "s_ready", "ld_done", "max_done", "exp_done", "p_arrive")
 
 
 def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # pragma: no cover
@@ -93,7 +92,7 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
     plan = AttentionPlan(lay, window_bounds(frames, 1, 5), "both", device="cuda")
     q = torch.randn(lay.seq_len, heads, 128, device="cuda", dtype=torch.bfloat16)
     k, v = torch.randn_like(q), torch.randn_like(q)
-    tr = torch.zeros(22 * 64, dtype=torch.int64, device="cuda")
+    tr = torch.zeros(12 * 64, dtype=torch.int64, device="cuda")
     prev = ext().attention_variant()
     if variant is not None:
         ext().attention_set_variant(variant)
@@ -103,7 +102,7 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
         torch.cuda.synchronize()
     finally:
         ext().attention_set_variant(prev)
-    t = tr.view(11, 2, 64).cpu().double()
+    t = tr.view(6, 2, 64).cpu().double()
     a, b = blocks
     ev = {n: t[i] for i, n in enumerate(TRACE_EVENTS)}
     out = {}
@@ -113,7 +112,6 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
             "wait_S": d("s_wait", "s_ready"), "tmem_load": d("s_ready", "ld_done"),
             "row_max": d("ld_done", "max_done"), "exp_pack_store": d("max_done", "exp_done"),
             "wait_st_arrive": d("exp_done", "p_arrive"),
-            "mma_wait_P": d("mma_p_wait", "mma_p_ready"),
             "P_arrive_to_next_S": float((ev["s_ready"][tile, a + 1:b + 1] - ev["p_arrive"][tile, a:b]).mean()),
             "block_period": float((ev["s_ready"][tile, a + 1:b + 1] - ev["s_ready"][tile, a:b]).mean()),
         }
@@ -121,8 +119,7 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
     # tiles' softmax phases alternate or overlap
     t0 = ev["s_ready"][0, a]
     line = {}
-    for n in ("s_ready", "max_done", "exp_done", "p_arrive", "mma_loop_top", "mma_p_wait",
-              "mma_v_ready", "mma_p_ready", "mma_issued"):
+    for n in ("s_ready", "max_done", "exp_done", "p_arrive"):
         line[n] = [[int(ev[n][tile, i] - t0) for i in range(a, a + 6)] for tile in (0, 1)]
     out["timeline"] = line
     out["variant"] = ext().attention_variant() if variant is None else variant
