@@ -1,0 +1,164 @@
+"""Training throughput: Stage B (LoRA `default` + linear branch against the dense teacher).
+
+    python bench_train.py [--steps K --warmup W]                                  # 1 GPU
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench_train.py --gpus N --steps K --warmup W            # N GPUs, FSDP2
+
+One step on every rank = one synthetic clip (per-GPU batch 1) of the BASELINE training
+shape: 81 latent frames at the inference spatial latent size (48 x 84 -> 24 x 42 tokens per
+frame), the matching audio latents and an 800 x 5120 prompt; the full VDN-H3 geometry with
+random weights (backbone frozen; trainable: the hybrid branch and a rank-64 LoRA on the DiT
+and refiner attention); FSDP2 with per-block activation checkpointing; the dense teacher
+forward (no grad), the student forward + backward, gradient clipping and the AdamW step are
+all inside the timed region. Timing: W untimed steps, then K steps between a barrier +
+device synchronisation, CUDA events, max over ranks. Rank 0 prints one JSON line whose
+`value` is the whole job's samples per second. `--tiny` swaps in a two-block model for CPU
+tests (its numbers mean nothing).
+
+Reference parity: the Stage B loop of src/training/train_stage_b.py:175-450 (here through
+vdn_minimax_h3_b200.training: the same batch packing, teacher velocity, student forward,
+loss and optimizer groups as `training.trainers.run_stage_b`).
+"""
+import argparse
+import datetime
+import json
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+LORA_TARGETS = ["attn.orig.to_q", "attn.orig.to_k", "attn.orig.to_v", "attn.orig.to_out.0",
+                "token_refiner.refiner_blocks.*.attn.to_q", "token_refiner.refiner_blocks.*.attn.to_k",
+                "token_refiner.refiner_blocks.*.attn.to_v",
+                "token_refiner.refiner_blocks.*.attn.to_out.0"]
+
+
+def parse(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--warmup", type=int, default=1)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--latent-frames", type=int, default=81)
+    p.add_argument("--lora-rank", type=int, default=64)
+    p.add_argument("--tiny", action="store_true", help="two-block model (CPU tests only)")
+    return p.parse_args(argv)
+
+
+def main(argv=None):
+    args = parse(argv)
+    from vdn_minimax_h3_b200.models.factory import RELEASED_HYBRID, TINY_HYBRID, build_model, make_spec
+    from vdn_minimax_h3_b200.models.h3 import h3_full_config, h3_tiny_config
+    from vdn_minimax_h3_b200.models.hybrid_transform import set_layout
+    from vdn_minimax_h3_b200.models.lora import inject_lora
+    from vdn_minimax_h3_b200.training import fsdp_stage as fs
+    from vdn_minimax_h3_b200.training.batch import pack_noisy_batch
+    from vdn_minimax_h3_b200.training.dataset import SyntheticLatentDataset
+    from vdn_minimax_h3_b200.utils.activation_checkpointing import enable_block_checkpointing
+
+    cuda = torch.cuda.is_available()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local) if cuda else torch.device("cpu")
+    if cuda:
+        torch.cuda.set_device(device)
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
+        dist.init_process_group("nccl" if cuda else "gloo", timeout=datetime.timedelta(seconds=900),
+                                **({"device_id": device} if cuda else {}))
+    world, rank = dist.get_world_size(), dist.get_rank()
+    torch.manual_seed(args.seed)
+
+    cfg = h3_tiny_config() if args.tiny else h3_full_config()
+    hybrid = TINY_HYBRID if args.tiny else RELEASED_HYBRID
+    t0 = time.perf_counter()
+    spec = make_spec(cfg, hybrid, dtype="float32" if args.tiny else "bfloat16")
+    model = build_model(spec, device="cpu" if args.tiny else device, init="random", seed=args.seed)
+    inject_lora(model, "default", args.lora_rank, args.lora_rank, LORA_TARGETS)
+    select = fs.trainable_select(include_lora=True)
+    for n, p in model.named_parameters():
+        p.requires_grad_(select(n, p))
+    model.to(device)
+    if world > 1:
+        fs.shard_model(model, device, None, activation_checkpointing=True)
+    else:
+        enable_block_checkpointing(model, split=True)
+    groups = fs.build_param_groups(model, 1e-4, big_scale=0.4, small_scale=2.0, lora_scale=1.0)
+    optimizer = torch.optim.AdamW(groups, lr=1e-4, weight_decay=0.0)
+    trainable = [p for p in model.parameters() if p.requires_grad]
+    gens = fs.make_generators(args.seed, rank, device)
+    if args.tiny:
+        shape, n_audio, text_len, text_dim = (cfg.in_channels, 3, 16, 16), 4, 8, cfg.text_dim
+    else:
+        shape = (cfg.in_channels, args.latent_frames, 48, 84)
+        n_audio = max(8, args.latent_frames * 455 // 102)
+        text_len, text_dim = 800, cfg.text_dim
+    data = SyntheticLatentDataset(args.warmup + args.steps, shape, n_audio, text_len, text_dim,
+                                  seed=args.seed + rank)
+    build_s = time.perf_counter() - t0
+
+    def step(i):
+        batch = pack_noisy_batch(data[i], device, gens["noise"], gens["sigma"])
+        set_layout(model, batch["layout"])
+        tv, ta = fs.teacher_velocity(model, batch["inputs"], adapters=True)
+        sv, sa = fs.student_forward(model, batch["inputs"], False)
+        loss = F.mse_loss(sv[0].float(), tv) + 0.5 * F.mse_loss(sa[0].float(), ta)
+        loss, _ = fs.finite_or_zero(loss)
+        loss.backward()
+        fs.clip_gradients(trainable, 1.0)
+        optimizer.step()
+        optimizer.zero_grad(set_to_none=True)
+        return loss
+
+    for i in range(args.warmup):
+        step(i)
+    dist.barrier()
+    if cuda:
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+    else:
+        t_start = time.perf_counter()
+    loss = None
+    for i in range(args.steps):
+        loss = step(args.warmup + i)
+    if cuda:
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end)
+    else:
+        ms = (time.perf_counter() - t_start) * 1e3
+    dist.barrier()
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        line = {
+            "metric": "train samples/s (Stage B: LoRA + hybrid branch, FSDP2)",
+            "value": round(world * args.steps / (ms / 1e3), 4), "unit": "samples/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 1), "higher_is_better": True, "scaling": "weak",
+            "dtype": "bf16 params (fp32 master for trainables), fp32 loss",
+            "data": "synthetic (random-normal latents and prompt embeddings; random-init weights)",
+            "config": {"model": "tiny" if args.tiny else "VDN-H3 (50 blocks, hidden 5376, 56x128 heads)",
+                       "per_gpu_batch": 1, "latent_frames": shape[1],
+                       "latent_hw": list(shape[2:]), "lora_rank": args.lora_rank,
+                       "parallelism": f"fsdp2 x{world}" if world > 1 else "single-gpu",
+                       "activation_checkpointing": "per block"},
+            "loss": float(loss.item()) if loss is not None else None,
+            "build_s": round(build_s, 1),
+        }
+        if cuda:
+            line["peak_gib"] = round(torch.cuda.max_memory_allocated() / 2 ** 30, 1)
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
