@@ -187,3 +187,15 @@ def test_stage_a2_fsdp2_two_ranks(tmp_path):
     res = dict(q.get() for _ in range(2))
     assert res == {0: 2, 1: 2}, res
     assert os.path.exists(os.path.join(out, "hybrid_step000002.pt"))
+
+
+def test_step_profiler_env(tmp_path, monkeypatch, capsys):
+    """VDN_PROF_STEP=N (the reference's H3_PROF_STEP) prints a profiler table for step N."""
+    monkeypatch.setenv("H3_PROF_STEP", "1")
+    seed = _seed_checkpoint(str(tmp_path / "seed.pt"))
+    out = str(tmp_path / "a2")
+    argv = [f"initialization.checkpoint={seed}", f"data.index_file={TINY_DATA}",
+            f"checkpoint.output_dir={out}", "training.max_steps=1", "checkpoint.save_every=1",
+            "checkpoint.early_saves=[]", "distributed.offload_activations=false"]
+    assert _run_stage("a2", argv) == 1
+    assert "profile of step 1" in capsys.readouterr().out

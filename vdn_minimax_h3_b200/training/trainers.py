@@ -41,6 +41,7 @@ from vdn_minimax_h3_b200.training import fsdp_stage as fs
 from vdn_minimax_h3_b200.training.batch import PackedPrompt, initial_noise, pack_noisy_batch, sample_paired_timesteps
 from vdn_minimax_h3_b200.utils import run_lock
 from vdn_minimax_h3_b200.utils.lr_schedule import check_schedule_stamp, lr_at, schedule_stamp
+from vdn_minimax_h3_b200.utils.profiling import step_profiler
 
 
 # ----------------------------------------------------------------------------- common
@@ -175,6 +176,8 @@ def _fsdp_stage(cfg, stage):
             it = iter(loader)
             sample = next(it)
         t0 = time.perf_counter()
+        prof_ctx = step_profiler(step + 1, print_fn=lambda m: print(m, flush=True) if fs.rank0() else None)
+        prof_ctx.__enter__()
         with fs.phase("pack"):
             batch = pack_noisy_batch(sample, device, gens["noise"], gens["sigma"])
             set_layout(model, batch["layout"])
@@ -207,6 +210,7 @@ def _fsdp_stage(cfg, stage):
         gnorm = fs.clip_gradients(trainable, opt_cfg.grad_clip)
         optimizer.step()
         optimizer.zero_grad(set_to_none=True)
+        prof_ctx.__exit__(None, None, None)
         step += 1
         m = _reduce_metrics({"loss": loss.item(), "loss_teacher": loss_teacher.item(),
                              "data_video": data_v.item(), "data_audio": data_a.item(),
