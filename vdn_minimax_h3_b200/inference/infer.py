@@ -48,7 +48,7 @@ def assemble(cfg, device):
     return model, engine
 
 
-def render(cfg, model, engine, device, runtime=None, transformer=None):
+def render(cfg, model, engine, device, runtime=None, transformer=None, on_step=None):
     from vdn_minimax_h3_b200.inference.prompt_cache import load_prompt
     from vdn_minimax_h3_b200.inference.render import generate_latents
     from vdn_minimax_h3_b200.models.hybrid_transform import set_layout
@@ -56,7 +56,7 @@ def render(cfg, model, engine, device, runtime=None, transformer=None):
     transformer = transformer or engine
     kw = dict(video_shift=cfg.render.video_shift, audio_shift=cfg.render.audio_shift,
               conditions=conditions, on_layout=lambda lay: set_layout(model, lay),
-              barrier=runtime.barrier if runtime is not None else None)
+              barrier=runtime.barrier if runtime is not None else None, on_step=on_step)
     if cfg.render.warmup_steps:
         generate_latents(transformer, emb, cfg.render.num_frames, cfg.render.warmup_steps,
                          cfg.render.seed, device, model.config, **kw)

@@ -41,8 +41,13 @@ def main(argv=None):
         runtime = init_ulysses(profile=par.profile, softmax_ranks=par.softmax_ranks)
         sp = UlyssesEngine(engine, runtime, exchange=par.exchange)
     runtime.barrier()
+    # host-side liveness: a rank that dies or stalls is reported before the next NFE launches
+    from vdn_minimax_h3_b200.utils.watchdog import Heartbeat
+    hb = Heartbeat(interval_s=1.0, timeout_s=120.0).start()
     t_setup = time.perf_counter() - t_start
-    lat, aud, steps, denoise = render(cfg, model, engine, device, runtime=runtime, transformer=sp)
+    lat, aud, steps, denoise = render(cfg, model, engine, device, runtime=runtime, transformer=sp,
+                                      on_step=lambda i: hb.check())
+    hb.check()
     d = torch.tensor([denoise], device=device)
     dist.all_reduce(d, op=dist.ReduceOp.MAX)
     t_decode = 0.0
@@ -58,6 +63,7 @@ def main(argv=None):
               f"{float(d.item()):.2f}s ({cfg.render.num_steps} NFE), decode+encode {t_decode:.1f}s, "
               f"E2E {time.perf_counter() - t_start:.1f}s" + (f", sections {prof}" if prof else ""),
               flush=True)
+    hb.stop()
     sp.close()   # symmetric-memory heaps are released on every rank before NCCL goes away
     dist.destroy_process_group()
     return 0

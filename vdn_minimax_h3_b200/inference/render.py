@@ -77,13 +77,15 @@ def build_inputs(geo: RenderGeometry, text_len, device, conditions=None):
 def generate_latents(transformer, prompt_embeds, num_frames, num_steps, seed, device,
                      model_config, video_shift=12.0, audio_shift=3.0, step_seconds=None,
                      conditions=None, latent_h=LATENT_H, latent_w=LATENT_W, audio=True,
-                     on_layout=None, barrier=None, initial_noise=None, num_latent_frames=None):
+                     on_layout=None, barrier=None, initial_noise=None, num_latent_frames=None,
+                     on_step=None):
     """The denoising loop. Returns (latents [1, C, F, H, W] fp32, audio [2, 32, A] fp32).
 
     on_layout(layout) is called once before the loop (the hybrid's set_layout);
     barrier() (multi-GPU) runs before and after the loop; `step_seconds` (a list) gets the
     device-synchronised time of every NFE; `initial_noise` (video_rows, audio_rows) replaces
-    the seeded draw (the e2e bench copies it from pinned host memory)."""
+    the seeded draw (the e2e bench copies it from pinned host memory); `on_step(i)` runs on
+    the host before each NFE is launched (the multi-GPU entry's heartbeat check)."""
     geo = render_geometry(model_config, num_frames, latent_h, latent_w, audio, num_latent_frames)
     text_len = prompt_embeds.shape[0]
     packed, layout, idx = build_inputs(geo, text_len, device, conditions)
@@ -116,6 +118,8 @@ def generate_latents(transformer, prompt_embeds, num_frames, num_steps, seed, de
     emb = prompt_embeds.to(device)[None]
     vid_idx, aud_idx = idx["video_indices"], idx["audio_indices"]
     for i in range(num_steps):
+        if on_step is not None:
+            on_step(i)
         t = float(sched.timesteps[i])
         a_t = float(a_sched.timesteps[i])
         started = time.perf_counter()

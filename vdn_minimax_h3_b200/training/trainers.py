@@ -42,6 +42,7 @@ from vdn_minimax_h3_b200.training.batch import PackedPrompt, initial_noise, pack
 from vdn_minimax_h3_b200.utils import run_lock
 from vdn_minimax_h3_b200.utils.lr_schedule import check_schedule_stamp, lr_at, schedule_stamp
 from vdn_minimax_h3_b200.utils.profiling import step_profiler
+from vdn_minimax_h3_b200.utils.watchdog import Heartbeat
 
 
 # ----------------------------------------------------------------------------- common
@@ -166,7 +167,10 @@ def _fsdp_stage(cfg, stage):
     step = resume.step
     objective = getattr(cfg.training, "objective", "teacher")
     it = iter(loader)
+    hb = Heartbeat(interval_s=1.0, timeout_s=120.0).start() if world > 1 else None
     while step < cfg.training.max_steps:
+        if hb is not None:
+            hb.check()      # a dead or stalled peer is reported before this step's collectives
         fs.phase_reset()
         try:
             sample = next(it)
@@ -230,6 +234,8 @@ def _fsdp_stage(cfg, stage):
                                 data_cursor=(step * world) % max(len(dataset), 1) // world,
                                 extra={"schedule": schedule_stamp(sched)},
                                 keep_states=cfg.checkpoint.keep_states)
+    if hb is not None:
+        hb.stop()
     if fs.rank0():
         open(os.path.join(out, "DONE"), "w").close()
         run_lock.release(out)
