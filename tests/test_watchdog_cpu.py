@@ -1,6 +1,7 @@
 """Host-side failure detection on gloo ranks (no GPU): a rank that goes silent, leaves, or
 dies is reported to the others by the heartbeat before their next collective."""
 import os
+import queue
 import socket
 import time
 
@@ -56,6 +57,9 @@ def _worker(rank, world, port, mode, q):
             time.sleep(0.05)
         q.put((rank, "not detected"))
     finally:
+        # os._exit skips the queue's feeder thread: flush the result before leaving
+        q.close()
+        q.join_thread()
         if mode == "healthy":
             dist.destroy_process_group()
         else:
@@ -72,12 +76,17 @@ def test_heartbeat(mode):
     procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
-    for p in procs:
-        p.join(timeout=60)
     res = {}
-    while not q.empty():
-        r, v = q.get()
+    expected = world - 1 if mode == "die" else world
+    deadline = time.monotonic() + 60
+    while len(res) < expected and time.monotonic() < deadline:
+        try:
+            r, v = q.get(timeout=1.0)
+        except queue.Empty:
+            continue
         res[r] = v
+    for p in procs:
+        p.join(timeout=30)
     if mode == "healthy":
         assert res == {0: "ok", 1: "ok", 2: "ok"}, res
         return
