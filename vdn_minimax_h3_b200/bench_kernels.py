@@ -3,6 +3,7 @@
     python -m vdn_minimax_h3_b200.bench_kernels --gemm
     python -m vdn_minimax_h3_b200.bench_kernels --attention
     python -m vdn_minimax_h3_b200.bench_kernels --linear
+    python -m vdn_minimax_h3_b200.bench_kernels --linear-train
 
 Each case runs 3 warm-up launches and times 10 with CUDA events on the launching stream;
 operands are larger than the 126 MB L2 for the full-size shapes. Library baselines
@@ -126,6 +127,48 @@ def bench_norm():
     return rows
 
 
+def bench_linear_train(frames=81, heads=56):
+    """Training stages of the linear branch, forward + backward at the Stage-B training
+    shape (81 latent frames, 56 heads): the SPD factor and the two scans through
+    ops/linear_branch_grad.py (kernels forward, adjoint scan backward) vs autograd through
+    the eager PyTorch ops (Cholesky + triangular solve, one batched product per frame)."""
+    from vdn_minimax_h3_b200.models import scan as scan_ref
+    from vdn_minimax_h3_b200.models.delta_rule import VdnDelta
+    from vdn_minimax_h3_b200.ops import linear_branch_grad as lbg
+    from vdn_minimax_h3_b200.ops._ext import LAUNCHES, check_device_error
+    torch.manual_seed(0)
+    F, H, d = frames, heads, 128
+    k = torch.nn.functional.normalize(torch.randn(F, H, 256, d, device="cuda"), dim=-1)
+    A = torch.matmul(k.transpose(-1, -2), k)
+    del k
+    B = torch.randn(F, H, d, d, device="cuda")
+    alpha = torch.rand(F, H, d, device="cuda") * 0.5 + 0.45
+    start = torch.randn(H, d, d, device="cuda") * 0.1
+    g_pre, g_suf = torch.randn(2, F, H, d, d, device="cuda")
+    backend = VdnDelta()
+    leaves = [t.requires_grad_() for t in (alpha, A, B, start)]
+
+    def step(factor, scan):
+        trans, inj = factor(backend, *leaves[:3])
+        pre, suf = scan(trans, inj, leaves[3])
+        torch.autograd.backward([pre, suf], [g_pre, g_suf])
+        for t in leaves:
+            t.grad = None
+
+    rows = []
+    for name, factor, scan in (
+            ("kernels", lbg.vdn_factor, lbg.scans),
+            ("eager", lambda b, *a: b.factor_apply(*a), scan_ref.run_scans)):
+        n0 = LAUNCHES[0]
+        ms = timed(lambda: step(factor, scan), iters=5, warmup=3)
+        check_device_error()
+        rows.append({"stage": "factor+scans fwd+bwd", "impl": name, "frames": F, "heads": H,
+                     "ms": round(ms, 3), "own_launches_per_iter": (LAUNCHES[0] - n0) // 8})
+    for r in rows:
+        print(json.dumps(r), flush=True)
+    return rows
+
+
 def profile_small():
     """Single launches on small inputs, for a one-pass-per-kernel profiler capture."""
     from vdn_minimax_h3_b200.models.delta_rule import VdnDelta
@@ -171,6 +214,8 @@ def main(argv=None):
     p.add_argument("--linear-heads", type=int, nargs="*", default=[56],
                    help="head counts for --linear (7 = one rank's share at 8-way Ulysses)")
     p.add_argument("--norm", action="store_true")
+    p.add_argument("--linear-train", action="store_true",
+                   help="SPD factor + scans forward and backward at the training shape")
     p.add_argument("--gemm-fp8", action="store_true")
     p.add_argument("--gemm-fp8-trace", action="store_true",
                    help="fp8 GEMM wait-cycle counters (QKV shape)")
@@ -195,6 +240,8 @@ def main(argv=None):
             bench_linear(timed, heads=h)
     if a.norm:
         bench_norm()
+    if a.linear_train:
+        bench_linear_train()
     if a.gemm_fp8:
         bench_gemm_fp8()
     if a.gemm_fp8_trace:

@@ -147,7 +147,7 @@ void launch_lb_spd_factor(const float* A, const float* B, const float* alpha, fl
                           float* inj, int n_mats, float a_scale, float b_scale,
                           cudaStream_t stream);
 void launch_lb_scan(const float* trans, const float* inj, const float* start, int F, int H,
-                    float* prefix, float* suffix, int* err, cudaStream_t stream);
+                    float* prefix, float* suffix, int* err, cudaStream_t stream, int ndir = 2);
 // Scan cluster size: 0 = automatic (by head count), else 1, 2, 4 or 8.
 void lb_scan_set_cluster(int cs);
 void launch_lb_gather(const float* prefix, const float* suffix, const int* idx, const float* ab,

@@ -985,7 +985,8 @@ __global__ void __launch_bounds__(256, NSLOT == 1 ? 2 : 1) lb_scan_rows_kernel(
 
 template <int RS, int NSLOT>
 static void launch_scan_rows(const float* trans, const float* inj, const float* start, int F,
-                             int H, float* prefix, float* suffix, int* err, cudaStream_t stream) {
+                             int H, float* prefix, float* suffix, int* err, int ndir,
+                             cudaStream_t stream) {
   constexpr int smem = (NSLOT * 16384 + (128 / RS) * SC_PITCH) * 4 + 64;
   static bool attr = false;
   if (!attr) {
@@ -996,16 +997,16 @@ static void launch_scan_rows(const float* trans, const float* inj, const float* 
                          cudaSharedmemCarveoutMaxShared);
     attr = true;
   }
-  lb_scan_rows_kernel<RS, NSLOT><<<dim3(H * RS, 2), 256, smem, stream>>>(trans, inj, start, F, H,
-                                                                          prefix, suffix, err);
+  lb_scan_rows_kernel<RS, NSLOT><<<dim3(H * RS, ndir), 256, smem, stream>>>(trans, inj, start, F, H,
+                                                                             prefix, suffix, err);
 }
 
-// Row split for the scan: the largest of 1, 2, 4, 8 that keeps all 2*H*RS CTAs resident
-// (one per SM) on the device.
-static int scan_cluster_size(int H) {
+// Row split for the scan: the largest of 1, 2, 4, 8 that keeps all nrec*RS CTAs resident
+// (one per SM) on the device; nrec = heads x directions.
+static int scan_cluster_size(int nrec) {
   const int sms = num_sms();
   int cs = 1;
-  while (cs < 8 && 2 * H * cs * 2 <= sms) cs *= 2;
+  while (cs < 8 && nrec * cs * 2 <= sms) cs *= 2;
   return cs;
 }
 
@@ -1013,9 +1014,12 @@ static int g_scan_cluster = 0;   // 0: automatic; else forced: 1 (one CTA per re
                                  // 2, 4, 8 (row parts, two slots), -2 (two parts, one slot)
 void lb_scan_set_cluster(int cs) { g_scan_cluster = cs; }
 
+// ndir = 2: both recurrences (prefix and suffix banks); ndir = 1: the prefix recurrence
+// only (grid.y = 1, so every CTA takes direction 0 and `suffix` is never touched).
 void launch_lb_scan(const float* trans, const float* inj, const float* start, int F, int H,
-                    float* prefix, float* suffix, int* err, cudaStream_t stream) {
+                    float* prefix, float* suffix, int* err, cudaStream_t stream, int ndir) {
   if (!F || !H) return;
+  const int nrec = H * ndir;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(lb_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM);
@@ -1023,18 +1027,18 @@ void launch_lb_scan(const float* trans, const float* inj, const float* start, in
   }
   // many heads: two half-row CTAs per recurrence at two CTAs per SM (one transition slot);
   // few heads: 2, 4 or 8 row parts per recurrence, one CTA per SM, two transition slots
-  const int cs = g_scan_cluster ? g_scan_cluster : scan_cluster_size(H);
-  if (cs == -2 || (cs == 1 && !g_scan_cluster && 2 * H * 2 <= 2 * num_sms())) {
-    launch_scan_rows<2, 1>(trans, inj, start, F, H, prefix, suffix, err, stream);
+  const int cs = g_scan_cluster ? g_scan_cluster : scan_cluster_size(nrec);
+  if (cs == -2 || (cs == 1 && !g_scan_cluster && nrec * 2 <= 2 * num_sms())) {
+    launch_scan_rows<2, 1>(trans, inj, start, F, H, prefix, suffix, err, ndir, stream);
     return;
   }
   switch (cs) {
-    case 2: launch_scan_rows<2, 2>(trans, inj, start, F, H, prefix, suffix, err, stream); return;
-    case 4: launch_scan_rows<4, 2>(trans, inj, start, F, H, prefix, suffix, err, stream); return;
-    case 8: launch_scan_rows<8, 2>(trans, inj, start, F, H, prefix, suffix, err, stream); return;
+    case 2: launch_scan_rows<2, 2>(trans, inj, start, F, H, prefix, suffix, err, ndir, stream); return;
+    case 4: launch_scan_rows<4, 2>(trans, inj, start, F, H, prefix, suffix, err, ndir, stream); return;
+    case 8: launch_scan_rows<8, 2>(trans, inj, start, F, H, prefix, suffix, err, ndir, stream); return;
     default: break;
   }
-  lb_scan_kernel<<<dim3(H, 2), 256, SC_SMEM, stream>>>(trans, inj, start, F, H, prefix, suffix);
+  lb_scan_kernel<<<dim3(H, ndir), 256, SC_SMEM, stream>>>(trans, inj, start, F, H, prefix, suffix);
 }
 
 // ----------------------------------------------------------------------------- gather

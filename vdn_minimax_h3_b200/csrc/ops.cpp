@@ -604,14 +604,19 @@ void lb_spd_factor(torch::Tensor A, torch::Tensor B, torch::Tensor alpha, torch:
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// suffix = None runs the prefix recurrence only (one direction).
 void lb_scan(torch::Tensor trans, torch::Tensor inj, c10::optional<torch::Tensor> start,
-             torch::Tensor prefix, torch::Tensor suffix, torch::Tensor err) {
+             torch::Tensor prefix, c10::optional<torch::Tensor> suffix, torch::Tensor err) {
   TORCH_CHECK(trans.dim() == 4 && trans.size(2) == 128 && trans.size(3) == 128, "trans [F,H,128,128]");
   const int64_t F = trans.size(0), H = trans.size(1);
   check_f32(trans, "trans", F * H * 16384);
   check_f32(inj, "inj", F * H * 16384);
   check_f32(prefix, "prefix", F * H * 16384);
-  check_f32(suffix, "suffix", F * H * 16384);
+  float* qp = nullptr;
+  if (suffix) {
+    check_f32(*suffix, "suffix", F * H * 16384);
+    qp = suffix->data_ptr<float>();
+  }
   const float* sp = nullptr;
   if (start) {
     check_f32(*start, "start", H * 16384);
@@ -619,7 +624,7 @@ void lb_scan(torch::Tensor trans, torch::Tensor inj, c10::optional<torch::Tensor
   }
   c10::cuda::CUDAGuard g(trans.device());
   launch_lb_scan(trans.data_ptr<float>(), inj.data_ptr<float>(), sp, (int)F, (int)H,
-                 prefix.data_ptr<float>(), suffix.data_ptr<float>(), err_ptr(err), cur());
+                 prefix.data_ptr<float>(), qp, err_ptr(err), cur(), suffix ? 2 : 1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -12,7 +12,10 @@ Reference parity (src/models/linear_attention/):
 Parameter names and shapes are the reference's, so v2 checkpoints load unchanged.
 
 Two bodies, chosen by the caller (`inference=`), never by ambient grad state:
-  _readout            eager PyTorch, differentiable: the training body and the oracle.
+  _readout            eager PyTorch, differentiable: the training body and the oracle. Its
+                      SPD factor and scans go through ops/linear_branch_grad.py (sm_100a
+                      kernels forward and an adjoint-scan backward on CUDA with d = 128;
+                      linear_branch_grad.USE_KERNELS = False keeps them on PyTorch).
   _readout_inference  forward-only: on CUDA every stage is an sm_100a kernel
                       (ops/linear_branch.py); on CPU the same stages run their oracles.
 """
@@ -24,7 +27,8 @@ from torch import nn
 
 from vdn_minimax_h3_b200.models.delta_rule import DELTA_BACKENDS
 from vdn_minimax_h3_b200.models.scan import (BRIDGE_MODES, frame_statistics,
-                                             gather_linear_state, run_scans)
+                                             gather_linear_state)
+from vdn_minimax_h3_b200.ops.linear_branch_grad import scans, vdn_factor
 
 SHORT_CONV_TARGETS = ("q", "k", "v")
 
@@ -250,8 +254,9 @@ class BidirectionalLinearBranch(nn.Module):
         alpha = self.alpha(xv.view(F_, S, -1).mean(dim=1, dtype=torch.float32))
         text_state = self.text_state(text_x, text_qkv_raw)
         with torch.autocast(device_type=A.device.type, enabled=False):
-            trans, inj = self.backend(S).factor_apply(alpha, A, B)
-            prefix, suffix = run_scans(trans, inj, text_state)
+            # sm_100a SPD-factor and scan kernels forward, adjoint recurrence backward
+            trans, inj = vdn_factor(self.backend(S), alpha, A, B)
+            prefix, suffix = scans(trans, inj, text_state)
         state = gather_linear_state(prefix, suffix, alpha, bounds, bridge=self.bridge,
                                     text_state=text_state).to(xv.dtype)
         readout = torch.einsum("fhvk,fshk->fshv", state, qf)
