@@ -8,12 +8,14 @@ One step on every rank = one synthetic clip (per-GPU batch 1) of the BASELINE tr
 shape: 81 latent frames at the inference spatial latent size (48 x 84 -> 24 x 42 tokens per
 frame), the matching audio latents and an 800 x 5120 prompt; the full VDN-H3 geometry with
 random weights (backbone frozen; trainable: the hybrid branch and a rank-64 LoRA on the DiT
-and refiner attention); FSDP2 with per-block activation checkpointing; the dense teacher
+and refiner attention); FSDP2 with per-block activation checkpointing (checkpointed activations in pinned host
+memory, the Stage B default `distributed.offload_activations=true`); the dense teacher
 forward (no grad), the student forward + backward, gradient clipping and the AdamW step are
 all inside the timed region. Timing: W untimed steps, then K steps between a barrier +
 device synchronisation, CUDA events, max over ranks. Rank 0 prints one JSON line whose
 `value` is the whole job's samples per second. `--tiny` swaps in a two-block model for CPU
-tests (its numbers mean nothing).
+tests (its numbers mean nothing). `VDN_PROF_STEP=n` (or H3_PROF_STEP) runs warm-up step n
+(1-based) under torch.profiler and prints its kernel table; timed steps are never profiled.
 
 Reference parity: the Stage B loop of src/training/train_stage_b.py:175-450 (here through
 vdn_minimax_h3_b200.training: the same batch packing, teacher velocity, student forward,
@@ -44,6 +46,9 @@ def parse(argv=None):
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--latent-frames", type=int, default=81)
     p.add_argument("--lora-rank", type=int, default=64)
+    p.add_argument("--no-offload", dest="offload", action="store_false",
+                   help="keep checkpointed activations on the GPU (the Stage B default, "
+                        "distributed.offload_activations=true, saves them to pinned host memory)")
     p.add_argument("--tiny", action="store_true", help="two-block model (CPU tests only)")
     return p.parse_args(argv)
 
@@ -84,7 +89,8 @@ def main(argv=None):
     for n, p in model.named_parameters():
         p.requires_grad_(select(n, p))
     model.to(device)
-    if world > 1:
+    if world > 1 or cuda:
+        # one GPU is a 1-rank FSDP2 mesh: bf16 compute with fp32 trainables, as on N ranks
         fs.shard_model(model, device, None, activation_checkpointing=True)
     else:
         enable_block_checkpointing(model, split=True)
@@ -106,7 +112,7 @@ def main(argv=None):
         batch = pack_noisy_batch(data[i], device, gens["noise"], gens["sigma"])
         set_layout(model, batch["layout"])
         tv, ta = fs.teacher_velocity(model, batch["inputs"], adapters=True)
-        sv, sa = fs.student_forward(model, batch["inputs"], False)
+        sv, sa = fs.student_forward(model, batch["inputs"], args.offload and cuda)
         loss = F.mse_loss(sv[0].float(), tv) + 0.5 * F.mse_loss(sa[0].float(), ta)
         loss, _ = fs.finite_or_zero(loss)
         loss.backward()
@@ -115,8 +121,10 @@ def main(argv=None):
         optimizer.zero_grad(set_to_none=True)
         return loss
 
+    from vdn_minimax_h3_b200.utils.profiling import step_profiler
     for i in range(args.warmup):
-        step(i)
+        with step_profiler(i + 1, row_limit=40):   # VDN_PROF_STEP=n: warm-up step n only
+            step(i)
     dist.barrier()
     if cuda:
         torch.cuda.synchronize()
@@ -149,7 +157,8 @@ def main(argv=None):
                        "per_gpu_batch": 1, "latent_frames": shape[1],
                        "latent_hw": list(shape[2:]), "lora_rank": args.lora_rank,
                        "parallelism": f"fsdp2 x{world}" if world > 1 else "single-gpu",
-                       "activation_checkpointing": "per block"},
+                       "activation_checkpointing": "per block",
+                       "activation_offload": bool(args.offload and cuda)},
             "loss": float(loss.item()) if loss is not None else None,
             "build_s": round(build_s, 1),
         }

@@ -172,6 +172,24 @@ def _fsdp_worker(rank, world, port, seed, out, q):
         q.put((rank, repr(exc)))
 
 
+def test_debug_mem_lines(tmp_path, monkeypatch, capsys):
+    """H3_DEBUG_MEM (reference train_stage_a1.py:92-94) prints one memory line per aligned block."""
+    monkeypatch.setenv("H3_DEBUG_MEM", "1")
+    out = str(tmp_path / "a1m")
+    cfg = h3_tiny_config().to_dict()
+    argv = ["model.base.source=synthetic", f"data.index_file={TINY_DATA}", f"checkpoint.output_dir={out}",
+            "training.max_steps=1", "checkpoint.save_every=1", "checkpoint.early_saves=[]",
+            "model.architecture.hybrid_attention.softmax_attention.radius=0",
+            "model.architecture.hybrid_attention.softmax_attention.chunk=2",
+            "model.architecture.hybrid_attention.linear_attention.delta_rule=sana_scaled",
+            "model.architecture.hybrid_attention.linear_attention.short_conv.targets=[]",
+            "model.base.dtype=float32", "model.base.config_overrides=" + json.dumps(cfg)]
+    assert _run_stage("a1", argv) == 1
+    lines = [ln for ln in capsys.readouterr().out.splitlines() if "alloc=" in ln]
+    assert any(ln.strip().startswith("block  0: alloc=") for ln in lines), lines
+    assert all("peak=" in ln and ln.endswith("GiB") for ln in lines)
+
+
 @pytest.mark.timeout(300)
 def test_stage_a2_fsdp2_two_ranks(tmp_path):
     seed = _seed_checkpoint(str(tmp_path / "seed.pt"))

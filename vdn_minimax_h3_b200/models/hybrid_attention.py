@@ -20,7 +20,7 @@ from vdn_minimax_h3_b200.models.h3 import apply_rotary_emb
 from vdn_minimax_h3_b200.models.layout import SequenceLayout
 from vdn_minimax_h3_b200.models.linear_branch import BidirectionalLinearBranch, OutputGate
 from vdn_minimax_h3_b200.models.window import (ANCHOR_FRAME_MODES, full_cover, window_bounds,
-                                               window_softmax_reference)
+                                               window_softmax_segments)
 
 SOFTMAX_BACKENDS = ("auto", "kernel", "ref")
 
@@ -82,7 +82,7 @@ class HybridAttention(nn.Module):
                                                   v.transpose(0, 1)[None])[0].transpose(0, 1)
             linear_active = False
         else:
-            soft = window_softmax_reference(q, k, v, layout, bounds, scale, self.anchor_frames)
+            soft = window_softmax_segments(q, k, v, layout, bounds, scale, self.anchor_frames)
             linear_active = True
         del q, k, v
         if self.enable_softmax_gate:

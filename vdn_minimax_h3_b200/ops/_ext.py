@@ -7,12 +7,50 @@ of quietly running some other implementation. CPU tensors never reach it -- the 
 of every op is the fp32 PyTorch oracle the kernels are tested against.
 """
 import importlib
+import os
 
 import torch
 
 _EXT = None
 _ERR = {}
 LAUNCHES = [0]   # kernel launches issued through the extension (bench.py reads this)
+# Checked launches (VDN_CHECKED=1, or set_checked(True)): every extension call is followed by
+# a device synchronise, the CUDA error query and the device error word, and a failure is
+# raised naming the call, so an asynchronous fault or an expired bounded wait is pinned to
+# the launch that caused it instead of surfacing at some later synchronisation. Slow: a
+# debugging mode for small shapes (compute-sanitizer is not available on this hardware pool).
+CHECKED = [os.environ.get("VDN_CHECKED", "0") not in ("", "0")]
+
+
+def set_checked(on=True):
+    CHECKED[0] = bool(on)
+
+
+def _launch_device(args):
+    for a in args:
+        if getattr(a, "is_cuda", False):
+            return a.device
+    return None
+
+
+def _check_args(name, args):
+    devs = {str(a.device) for a in args if isinstance(a, torch.Tensor) and a.is_cuda}
+    if len(devs) > 1:
+        raise ValueError(f"{name}: CUDA tensors on several devices {sorted(devs)}")
+
+
+def _check_after(name, args):
+    device = _launch_device(args)
+    if device is None:
+        return
+    try:
+        torch.cuda.synchronize(device)
+    except RuntimeError as exc:
+        raise KernelError(f"{name}: CUDA error after the launch: {exc}") from exc
+    try:
+        check_device_error(device)
+    except KernelError as exc:
+        raise KernelError(f"{name}: {exc}") from exc
 
 
 class _Counted:
@@ -27,9 +65,14 @@ class _Counted:
         if fn is None:
             raw = getattr(self._mod, name)
 
-            def fn(*args, _raw=raw):
+            def fn(*args, _raw=raw, _name=name):
                 LAUNCHES[0] += 1
-                return _raw(*args)
+                if not CHECKED[0]:
+                    return _raw(*args)
+                _check_args(_name, args)
+                out = _raw(*args)
+                _check_after(_name, args)
+                return out
             self._cache[name] = fn
         return fn
 

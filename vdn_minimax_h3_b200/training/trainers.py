@@ -41,7 +41,7 @@ from vdn_minimax_h3_b200.training import fsdp_stage as fs
 from vdn_minimax_h3_b200.training.batch import PackedPrompt, initial_noise, pack_noisy_batch, sample_paired_timesteps
 from vdn_minimax_h3_b200.utils import run_lock
 from vdn_minimax_h3_b200.utils.lr_schedule import check_schedule_stamp, lr_at, schedule_stamp
-from vdn_minimax_h3_b200.utils.profiling import step_profiler
+from vdn_minimax_h3_b200.utils.profiling import debug_memory_line, step_profiler
 from vdn_minimax_h3_b200.utils.watchdog import Heartbeat
 
 
@@ -148,6 +148,9 @@ def _fsdp_stage(cfg, stage):
     from vdn_minimax_h3_b200.utils.distributed import broadcast_and_verify_init
     if world > 1:
         broadcast_and_verify_init(model, [p for n, p in model.named_parameters() if p.requires_grad], device)
+    if world > 1 or torch.device(device).type == "cuda":
+        # one rank on a GPU is a 1-rank FSDP2 mesh too: its mixed-precision policy is what
+        # runs a bf16 backbone with fp32 trainables (and fp32 alpha modules)
         fs.shard_model(model, device, cfg.distributed.shard_size, cfg.distributed.activation_checkpointing)
     opt_cfg = cfg.optimizer
     big = getattr(opt_cfg, "big_lr_scale", getattr(opt_cfg, "branch_lr_scale", 1.0))
@@ -269,6 +272,8 @@ class AlignHook:
             err = (student.float() - target[0].float()).pow(2).sum() / target.float().pow(2).sum().clamp_min(1e-12)
             err.backward()
         self.losses.append(err.item())
+        if not dist.is_initialized() or dist.get_rank() == 0:
+            debug_memory_line(f"block {self.index:2d}")
         return None
 
 
@@ -411,6 +416,7 @@ def run_stage_dmd(cfg):
     if world > 1:
         from vdn_minimax_h3_b200.utils.distributed import broadcast_and_verify_init
         broadcast_and_verify_init(model, [p for p in model.parameters() if p.requires_grad], device)
+    if world > 1 or torch.device(device).type == "cuda":
         fs.shard_model(model, device, cfg.distributed.shard_size, cfg.distributed.activation_checkpointing)
     gen_params = [p for n, p in model.named_parameters() if p.requires_grad and f".{tb.adapter_name}." in n]
     fake_params = [p for n, p in model.named_parameters() if p.requires_grad and f".{d.fake_adapter_name}." in n]

@@ -77,3 +77,19 @@ def step_profiler(step, row_limit=25, print_fn=print):
             torch.cuda.synchronize()
     key = "cuda_time_total" if torch.cuda.is_available() else "cpu_time_total"
     print_fn(f"profile of step {step}:\n" + prof.key_averages().table(sort_by=key, row_limit=row_limit))
+
+
+def debug_memory_line(label, print_fn=print):
+    """Print `label: alloc=.. peak=..GiB` (this process's CUDA allocator) when VDN_DEBUG_MEM
+    or the reference's H3_DEBUG_MEM is set (reference train_stage_a1.py:92-94: one line per
+    aligned block on rank 0). Returns the line, or None when the switch is off."""
+    if not (os.environ.get("VDN_DEBUG_MEM") or os.environ.get("H3_DEBUG_MEM")):
+        return None
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        alloc = torch.cuda.memory_allocated() / 2 ** 30
+        peak = torch.cuda.max_memory_allocated() / 2 ** 30
+    else:
+        alloc = peak = 0.0
+    line = f"    {label}: alloc={alloc:.1f} peak={peak:.1f}GiB"
+    print_fn(line, flush=True)
+    return line
