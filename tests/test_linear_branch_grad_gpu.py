@@ -106,3 +106,33 @@ def test_branch_training_body_kernels_vs_pytorch():
     assert grads_k.keys() == grads_r.keys() and grads_k
     for name in grads_r:
         assert _rel(grads_k[name], grads_r[name]) < 2e-3, name
+
+
+@pytest.mark.parametrize("F,gh,gw,H,l2", [(6, 5, 7, 2, True), (6, 5, 7, 2, False),
+                                          (3, 24, 42, 1, True), (1, 4, 4, 1, True)])
+def test_conv_features_backward_kernels(F, gh, gw, H, l2):
+    """Short conv forward (two-pass kernels) and backward (conv_bwd.cu) vs fp32 autograd
+    through the eager conv: output, input gradient and both weight gradients."""
+    from vdn_minimax_h3_b200.models.linear_branch import conv_features_reference
+    g = torch.Generator().manual_seed(F * 1000 + gh * 10 + gw)
+    C = H * 128
+    N = F * gh * gw
+    tokens = torch.randn(N, H, 128, generator=g).to(torch.bfloat16).cuda()
+    w_sp = (torch.randn(C, 5, 5, generator=g) * 0.2).cuda()
+    w_tm = (torch.randn(C, 5, generator=g) * 0.45).cuda()
+    up = torch.randn(N, H, 128, generator=g).to(torch.bfloat16).cuda()
+    assert lbg.conv_kernel_ok(tokens, (gh, gw))
+    x = tokens.clone().requires_grad_()
+    ws, wt = w_sp.clone().requires_grad_(), w_tm.clone().requires_grad_()
+    out = lbg.conv_features(x, ws, wt, F, (gh, gw), l2)
+    (out.float() * up.float()).sum().backward()
+    check_device_error()
+    xr = tokens.float().requires_grad_()
+    wsr, wtr = w_sp.clone().requires_grad_(), w_tm.clone().requires_grad_()
+    ref = conv_features_reference(xr, wsr, wtr, F, (gh, gw), l2)
+    (ref * up.float()).sum().backward()
+    assert out.dtype == torch.bfloat16 and x.grad.dtype == torch.bfloat16
+    assert _rel(out, ref) < 1e-2
+    assert _rel(x.grad, xr.grad) < 2e-2
+    assert _rel(ws.grad, wsr.grad) < 2e-2
+    assert _rel(wt.grad, wtr.grad) < 2e-2

@@ -131,7 +131,9 @@ def bench_linear_train(frames=81, heads=56):
     """Training stages of the linear branch, forward + backward at the Stage-B training
     shape (81 latent frames, 56 heads): the SPD factor and the two scans through
     ops/linear_branch_grad.py (kernels forward, adjoint scan backward) vs autograd through
-    the eager PyTorch ops (Cholesky + triangular solve, one batched product per frame)."""
+    the eager PyTorch ops (Cholesky + triangular solve, one batched product per frame); then
+    the short conv of one projection (24 x 42 grid, SiLU + L2), two-pass kernels forward and
+    conv_bwd.cu backward vs autograd through the eager bf16 conv."""
     from vdn_minimax_h3_b200.models import scan as scan_ref
     from vdn_minimax_h3_b200.models.delta_rule import VdnDelta
     from vdn_minimax_h3_b200.ops import linear_branch_grad as lbg
@@ -164,6 +166,30 @@ def bench_linear_train(frames=81, heads=56):
         check_device_error()
         rows.append({"stage": "factor+scans fwd+bwd", "impl": name, "frames": F, "heads": H,
                      "ms": round(ms, 3), "own_launches_per_iter": (LAUNCHES[0] - n0) // 8})
+    del A, B, alpha, start, g_pre, g_suf, leaves
+    # the short conv of one projection (k or v), forward + backward
+    from vdn_minimax_h3_b200.models.linear_branch import conv_features_reference
+    gh, gw = 24, 42
+    N, C = F * gh * gw, H * d
+    tokens = torch.randn(N, H, d, device="cuda", dtype=torch.bfloat16)
+    w_sp = (torch.randn(C, 5, 5, device="cuda") * 0.2).to(torch.bfloat16)
+    w_tm = (torch.randn(C, 5, device="cuda") * 0.45).to(torch.bfloat16)
+    up = torch.randn(N, H, d, device="cuda", dtype=torch.bfloat16)
+    x = tokens.requires_grad_()
+    ws, wt = w_sp.requires_grad_(), w_tm.requires_grad_()
+
+    def conv_step(fn):
+        out = fn(x, ws, wt, F, (gh, gw), True)
+        out.backward(up)
+        x.grad = ws.grad = wt.grad = None
+
+    for name, fn in (("kernels", lbg.conv_features), ("eager", conv_features_reference)):
+        n0 = LAUNCHES[0]
+        ms = timed(lambda: conv_step(fn), iters=5, warmup=3)
+        check_device_error()
+        rows.append({"stage": "short conv fwd+bwd (one projection)", "impl": name, "frames": F,
+                     "heads": H, "grid": [gh, gw], "ms": round(ms, 3),
+                     "own_launches_per_iter": (LAUNCHES[0] - n0) // 8})
     for r in rows:
         print(json.dumps(r), flush=True)
     return rows

@@ -150,6 +150,12 @@ void launch_lb_scan(const float* trans, const float* inj, const float* start, in
                     float* prefix, float* suffix, int* err, cudaStream_t stream, int ndir = 2);
 // Scan cluster size: 0 = automatic (by head count), else 1, 2, 4 or 8.
 void lb_scan_set_cluster(int cs);
+// Backward of the two-pass short conv (conv_bwd.cu): dtmp is fp32 scratch [F*gh*gw, H*128];
+// dwsp [25, H*128] and dwtm [H*128, 5] are accumulated into (the caller zeroes them).
+void launch_lb_conv2_bwd(const void* in, int64_t ldi, const void* tmp, int64_t ldt,
+                         const void* dy, int64_t ldy, const float* wsp, const float* wtm,
+                         float* dtmp, void* dx, int64_t ldx, float* dwsp, float* dwtm, int F,
+                         int gh, int gw, int H, int l2, cudaStream_t stream);
 void launch_lb_gather(const float* prefix, const float* suffix, const int* idx, const float* ab,
                       const float* aa, const float* start, int F, int H, void* out,
                       cudaStream_t stream);

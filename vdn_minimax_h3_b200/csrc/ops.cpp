@@ -569,6 +569,34 @@ void lb_conv_features(torch::Tensor in, torch::Tensor wsp, torch::Tensor wtm, to
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Backward of the two-pass short conv: in / tmp / dy / dx [N, H, 128] bf16 rows (N = F*gh*gw),
+// wsp [25 * C] and wtm [C * 5] fp32 as given to the forward, dtmp fp32 scratch [N * C],
+// dwsp / dwtm fp32 accumulators of the weights' shapes (zeroed by the caller).
+void lb_conv_features_bwd(torch::Tensor in, torch::Tensor tmp, torch::Tensor dy, torch::Tensor wsp,
+                          torch::Tensor wtm, torch::Tensor dtmp, torch::Tensor dx,
+                          torch::Tensor dwsp, torch::Tensor dwtm, int64_t F, int64_t gh,
+                          int64_t gw, bool l2) {
+  check_rows_heads(in, "in");
+  check_rows_heads(tmp, "tmp");
+  check_rows_heads(dy, "dy");
+  check_rows_heads(dx, "dx");
+  const int64_t H = in.size(1), N = in.size(0), C = H * 128;
+  TORCH_CHECK(N == F * gh * gw, "rows != F * gh * gw");
+  TORCH_CHECK(tmp.sizes() == in.sizes() && dy.sizes() == in.sizes() && dx.sizes() == in.sizes(),
+              "in, tmp, dy, dx must have one shape");
+  check_f32(wsp, "w_spatial", C * 25);
+  check_f32(wtm, "w_temporal", C * 5);
+  check_f32(dtmp, "dtmp", N * C);
+  check_f32(dwsp, "dw_spatial", C * 25);
+  check_f32(dwtm, "dw_temporal", C * 5);
+  c10::cuda::CUDAGuard g(in.device());
+  launch_lb_conv2_bwd(in.data_ptr(), in.stride(0), tmp.data_ptr(), tmp.stride(0), dy.data_ptr(),
+                      dy.stride(0), wsp.data_ptr<float>(), wtm.data_ptr<float>(),
+                      dtmp.data_ptr<float>(), dx.data_ptr(), dx.stride(0), dwsp.data_ptr<float>(),
+                      dwtm.data_ptr<float>(), (int)F, (int)gh, (int)gw, (int)H, l2, cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void lb_frame_stats(torch::Tensor k, torch::Tensor v, torch::Tensor beta, torch::Tensor A,
                     torch::Tensor B, torch::Tensor err) {
   // k, v: [F, S, H, 128] views whose (F, S) rows are one row stride apart
@@ -773,6 +801,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gw"), py::arg("l2"), py::arg("err"), py::arg("tmp") = py::none());
   m.def("lb_frame_stats", &vdn::lb_frame_stats, "tcgen05 per-frame delta-rule statistics A, B");
   m.def("lb_spd_factor", &vdn::lb_spd_factor, "batched (I + aA)^-1, transition and injection");
+  m.def("lb_conv_features_bwd", &vdn::lb_conv_features_bwd,
+        "backward of the two-pass short conv (dx, dw_spatial, dw_temporal)");
   m.def("lb_scan", &vdn::lb_scan, "bidirectional serial state recurrences");
   m.def("lb_scan_set_cluster", &vdn::lb_scan_set_cluster,
         "scan cluster size: 0 = by head count, else 1, 2, 4 or 8");

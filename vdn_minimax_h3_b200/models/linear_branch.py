@@ -28,7 +28,8 @@ from torch import nn
 from vdn_minimax_h3_b200.models.delta_rule import DELTA_BACKENDS
 from vdn_minimax_h3_b200.models.scan import (BRIDGE_MODES, frame_statistics,
                                              gather_linear_state)
-from vdn_minimax_h3_b200.ops.linear_branch_grad import scans, vdn_factor
+from vdn_minimax_h3_b200.ops.linear_branch_grad import conv_features as conv_features_grad
+from vdn_minimax_h3_b200.ops.linear_branch_grad import conv_kernel_ok, scans, vdn_factor
 
 SHORT_CONV_TARGETS = ("q", "k", "v")
 
@@ -183,6 +184,9 @@ class BidirectionalLinearBranch(nn.Module):
             if frame_size is None:
                 raise ValueError("short_conv needs the spatial grid; pass frame_size=(H, W)")
             w_sp, w_tm = conv.weights(proj, channels)
+            if conv_kernel_ok(tokens, frame_size):
+                # sm_100a two-pass forward, conv_bwd.cu backward
+                return conv_features_grad(tokens, w_sp, w_tm, num_frames, frame_size, l2)
             return conv_features_reference(tokens, w_sp, w_tm, num_frames, frame_size, l2)
         return activate(tokens, l2)
 

@@ -25,6 +25,13 @@ plus a Cholesky backward per frame. Here both stages are `torch.autograd.Functio
       dX = diag(alpha) dT + b B^T dinj,  dalpha = rowsum(dT * X),  dB = b dinj X,
       dA = -a sym(X dX X)               (X symmetric)
 
+* `conv_features(tokens, w_sp, w_tm, F, frame_size, l2)`: the short conv's forward runs the
+  two-pass kernels (5x5 spatial into a bf16 intermediate, then 5-tap temporal + SiLU [+ L2]),
+  keeping the intermediate; the backward runs conv_bwd.cu (temporal + activation backward
+  with the temporal weight gradient, then the flipped 5x5 stencil with the spatial weight
+  gradient). Needs bf16 [N, H, 128] rows and a grid row of at most 44 positions; anything
+  else, and CPU tensors, runs the eager PyTorch conv through autograd.
+
 On CPU tensors, or a head dim other than 128, the same Functions run the fp32 PyTorch
 recurrences (no kernel), so the adjoint formulas are tested against autograd on CPU.
 """
@@ -188,3 +195,58 @@ def vdn_factor(backend, alpha, A, B):
         return backend.factor_apply(alpha, A, B)
     return _VdnFactor.apply(_f32(alpha), _f32(A).contiguous(), _f32(B).contiguous(),
                             float(backend.a_scale), float(backend.b_scale))
+
+
+# ------------------------------------------------------------------------- short conv
+CONV_MAX_ROW = 44        # widest grid row of the two-pass forward kernels
+
+
+def conv_kernel_ok(tokens, frame_size):
+    """Whether the short conv's training kernels take these rows."""
+    return (USE_KERNELS and tokens.is_cuda and tokens.dtype == torch.bfloat16
+            and tokens.dim() == 3 and tokens.shape[-1] == 128 and tokens.stride(2) == 1
+            and tokens.stride(1) == 128 and (tokens.stride(0) * 2) % 16 == 0
+            and tokens.data_ptr() % 16 == 0 and frame_size[1] <= CONV_MAX_ROW)
+
+
+class _ConvFeatures(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, tokens, w_sp, w_tm, num_frames, gh, gw, l2norm):
+        from vdn_minimax_h3_b200.ops._ext import error_word, ext
+        C = tokens.shape[1] * tokens.shape[2]
+        wsp_t = w_sp.detach().float().reshape(C, 25).t().contiguous()     # taps [25, C]
+        wtm = w_tm.detach().float().reshape(C, 5).contiguous()
+        out = torch.empty(tokens.shape, dtype=torch.bfloat16, device=tokens.device)
+        tmp = torch.empty(tokens.shape, dtype=torch.bfloat16, device=tokens.device)
+        ext().lb_conv_features(tokens, wsp_t.reshape(-1), wtm.reshape(-1), out, num_frames, gh, gw,
+                               bool(l2norm), error_word(tokens.device), tmp)
+        ctx.save_for_backward(tokens, tmp, wsp_t, wtm)
+        ctx.meta = (num_frames, gh, gw, bool(l2norm), w_sp.shape, w_sp.dtype, w_tm.shape,
+                    w_tm.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        from vdn_minimax_h3_b200.ops._ext import ext
+        tokens, tmp, wsp_t, wtm = ctx.saved_tensors
+        num_frames, gh, gw, l2norm, sp_shape, sp_dtype, tm_shape, tm_dtype = ctx.meta
+        C = tokens.shape[1] * tokens.shape[2]
+        d_out = d_out.to(torch.bfloat16).contiguous()
+        dtmp = torch.empty(tokens.shape[0], C, dtype=torch.float32, device=tokens.device)
+        dx = torch.empty(tokens.shape, dtype=torch.bfloat16, device=tokens.device)
+        dwsp = torch.zeros(25, C, dtype=torch.float32, device=tokens.device)
+        dwtm = torch.zeros(C, 5, dtype=torch.float32, device=tokens.device)
+        ext().lb_conv_features_bwd(tokens, tmp, d_out, wsp_t.reshape(-1), wtm.reshape(-1), dtmp, dx,
+                                   dwsp.view(-1), dwtm.view(-1), num_frames, gh, gw, l2norm)
+        del dtmp
+        return (dx, dwsp.t().reshape(sp_shape).to(sp_dtype), dwtm.reshape(tm_shape).to(tm_dtype),
+                None, None, None, None)
+
+
+def conv_features(tokens, w_sp, w_tm, num_frames, frame_size, l2norm):
+    """Differentiable short conv on the kernels; callers check `conv_kernel_ok` first.
+    tokens [F*S, H, 128] bf16, w_sp [C, 5, 5], w_tm [C, 5] -> [F*S, H, 128] bf16."""
+    gh, gw = frame_size
+    return _ConvFeatures.apply(tokens, w_sp, w_tm, int(num_frames), int(gh), int(gw),
+                               bool(l2norm))
+
