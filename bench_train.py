@@ -53,6 +53,18 @@ def parse(argv=None):
     return p.parse_args(argv)
 
 
+def host_available_gib():
+    """MemAvailable of this host in GiB (None where /proc/meminfo is absent)."""
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) / 2 ** 20
+    except OSError:
+        return None
+    return None
+
+
 def main(argv=None):
     args = parse(argv)
     from vdn_minimax_h3_b200.models.factory import RELEASED_HYBRID, TINY_HYBRID, build_model, make_spec
@@ -107,6 +119,17 @@ def main(argv=None):
     data = SyntheticLatentDataset(args.warmup + args.steps, shape, n_audio, text_len, text_dim,
                                   seed=args.seed + rank)
     build_s = time.perf_counter() - t0
+    if args.offload and cuda:
+        # checkpointed block inputs go to pinned host memory: refuse to start on a host that
+        # cannot hold them twice over rather than exhaust the machine's memory
+        rows = shape[1] * (shape[2] // 2) * (shape[3] // 2) + n_audio + text_len
+        # measured on one B200: ~2 block inputs' worth (bf16) saved per block
+        need = 2 * cfg.num_layers * rows * cfg.hidden_size * 2 / 2 ** 30
+        avail = host_available_gib()
+        if avail is not None and avail < 2 * need + 64:
+            raise SystemExit(f"activation offload needs ~{need:.0f} GiB of pinned host memory "
+                             f"(2x + 64 GiB margin); {avail:.0f} GiB available: pass --no-offload "
+                             f"or use more ranks")
 
     def step(i):
         batch = pack_noisy_batch(data[i], device, gens["noise"], gens["sigma"])
