@@ -92,6 +92,10 @@ class KernelsConfig:
 @dataclass
 class RuntimeConfig:
     kernels: KernelsConfig = field(default_factory=KernelsConfig)
+    # single-GPU inference: keep the DiT blocks in pinned host memory and stream each onto
+    # the GPU while it runs (inference/offload.py; the reference's infer_diffusers
+    # --offload_dit)
+    offload_blocks: bool = False
 
 
 @dataclass

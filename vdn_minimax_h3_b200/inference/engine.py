@@ -166,7 +166,9 @@ class InferenceEngine:
     def _plans(self, attn, layout, T):
         key = (layout, attn.radius, attn.chunk, attn.anchor_frames) if attn is not None else (T,)
         if key != self._plan_key:
-            dev = self.blocks[0].w_qkvg.device
+            dev = getattr(self, "compute_device", None)   # set when blocks stream from host
+            if dev is None:
+                dev = self.blocks[0].w_qkvg.device
             if attn is None or layout is None:
                 from vdn_minimax_h3_b200.models.layout import SequenceLayout as SL
                 lay = SL(seq_len=T, video_start=T, num_frames=0, tokens_per_frame=1)

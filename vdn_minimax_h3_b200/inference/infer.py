@@ -45,6 +45,9 @@ def assemble(cfg, device):
                     raise ValueError(f"ablation override {k!r} is not a hybrid attention field")
                 setattr(attn, k, v)
     engine = build_inference_engine(model, fp8=cfg.precision.fp8.enabled)
+    if cfg.runtime.offload_blocks:
+        from vdn_minimax_h3_b200.inference.offload import enable_block_offload
+        enable_block_offload(engine)
     return model, engine
 
 
