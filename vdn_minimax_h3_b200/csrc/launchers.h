@@ -150,6 +150,12 @@ void launch_lb_scan(const float* trans, const float* inj, const float* start, in
                     float* prefix, float* suffix, int* err, cudaStream_t stream, int ndir = 2);
 // Scan cluster size: 0 = automatic (by head count), else 1, 2, 4 or 8.
 void lb_scan_set_cluster(int cs);
+// Backward of the AdaLN-modulated RMSNorm (norm_bwd.cu): dx from x, dy, the norm weight
+// (nullable) and the scale columns of the AdaLN table rows picked by idx.
+void launch_adaln_rmsnorm_bwd(const void* x, int64_t ldx, const void* dy, int64_t ldy,
+                              const float* w, float eps, const void* table, int64_t ldt,
+                              int scale_col, const int* idx, void* dx, int64_t ldo, int T, int D,
+                              cudaStream_t stream);
 // Backward of the two-pass short conv (conv_bwd.cu): dtmp is fp32 scratch [F*gh*gw, H*128];
 // dwsp [25, H*128] and dwtm [H*128, 5] are accumulated into (the caller zeroes them).
 void launch_lb_conv2_bwd(const void* in, int64_t ldi, const void* tmp, int64_t ldt,

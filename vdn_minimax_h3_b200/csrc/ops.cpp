@@ -569,6 +569,39 @@ void lb_conv_features(torch::Tensor in, torch::Tensor wsp, torch::Tensor wtm, to
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Backward of the AdaLN-modulated RMSNorm: x / dy / dx [T, D] bf16 rows (16-byte aligned),
+// w fp32 [D] or None, table bf16 [n, >= scale_col + D] with 16-byte aligned rows, idx int32 [T].
+void adaln_rmsnorm_bwd(torch::Tensor x, torch::Tensor dy, c10::optional<torch::Tensor> w,
+                       double eps, torch::Tensor table, int64_t scale_col, torch::Tensor idx,
+                       torch::Tensor dx) {
+  for (const torch::Tensor* t : {&x, &dy, &dx}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 &&
+                    t->stride(1) == 1 && (t->stride(0) * 2) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+                "x, dy, dx must be bf16 CUDA [T, D] with 16-byte aligned rows");
+    TORCH_CHECK(t->sizes() == x.sizes(), "x, dy, dx must have one shape");
+  }
+  const int64_t T = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % 8 == 0, "D must be a multiple of 8");
+  TORCH_CHECK(table.is_cuda() && table.scalar_type() == at::kBFloat16 && table.dim() == 2 &&
+                  table.stride(1) == 1 && (table.stride(0) * 2) % 16 == 0 && scale_col % 8 == 0 &&
+                  scale_col + D <= table.size(1) &&
+                  reinterpret_cast<uintptr_t>(table.data_ptr()) % 16 == 0,
+              "table must be bf16 CUDA [n, >= scale_col + D], aligned rows and column");
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.is_contiguous() &&
+                  idx.numel() == T, "idx must be int32 CUDA [T]");
+  const float* wp = nullptr;
+  if (w) {
+    check_f32(*w, "w", D);
+    wp = w->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  launch_adaln_rmsnorm_bwd(x.data_ptr(), x.stride(0), dy.data_ptr(), dy.stride(0), wp, (float)eps,
+                           table.data_ptr(), table.stride(0), (int)scale_col, idx.data_ptr<int>(),
+                           dx.data_ptr(), dx.stride(0), (int)T, (int)D, cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Backward of the two-pass short conv: in / tmp / dy / dx [N, H, 128] bf16 rows (N = F*gh*gw),
 // wsp [25 * C] and wtm [C * 5] fp32 as given to the forward, dtmp fp32 scratch [N * C],
 // dwsp / dwtm fp32 accumulators of the weights' shapes (zeroed by the caller).
@@ -801,6 +834,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gw"), py::arg("l2"), py::arg("err"), py::arg("tmp") = py::none());
   m.def("lb_frame_stats", &vdn::lb_frame_stats, "tcgen05 per-frame delta-rule statistics A, B");
   m.def("lb_spd_factor", &vdn::lb_spd_factor, "batched (I + aA)^-1, transition and injection");
+  m.def("adaln_rmsnorm_bwd", &vdn::adaln_rmsnorm_bwd, "backward (dx) of the AdaLN RMSNorm");
   m.def("lb_conv_features_bwd", &vdn::lb_conv_features_bwd,
         "backward of the two-pass short conv (dx, dw_spatial, dw_temporal)");
   m.def("lb_scan", &vdn::lb_scan, "bidirectional serial state recurrences");

@@ -29,6 +29,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from vdn_minimax_h3_b200.models.layout import MODALITY_NUM
+from vdn_minimax_h3_b200.ops.norm_grad import adaln_modulated_norm
 
 
 @dataclass
@@ -281,11 +282,10 @@ class H3Block(nn.Module):
     def forward(self, hidden_states, temb, adaln_indices, rotary_emb, attention_mask=None):
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self.adaln_proj(temb)
         x = hidden_states
-        normed = self.norm1(x) * (1.0 + scale_msa.index_select(0, adaln_indices)) \
-            + shift_msa.index_select(0, adaln_indices)
+        # sm_100a forward + backward kernels for bf16 CUDA rows under autograd, else eager
+        normed = adaln_modulated_norm(self.norm1, x, shift_msa, scale_msa, adaln_indices)
         x = x + gate_msa.index_select(0, adaln_indices) * self.attn(normed, rotary_emb, attention_mask)
-        normed = self.norm2(x) * (1.0 + scale_mlp.index_select(0, adaln_indices)) \
-            + shift_mlp.index_select(0, adaln_indices)
+        normed = adaln_modulated_norm(self.norm2, x, shift_mlp, scale_mlp, adaln_indices)
         return x + gate_mlp.index_select(0, adaln_indices) * self.ff(normed)
 
 
