@@ -1,14 +1,18 @@
-"""ModelSpec: the checkpoint-bound statement of WHAT the model is (base reference,
-structural transforms, adapters). Runtime choices never enter it.
+"""ModelSpec: what a checkpoint's model IS -- the base it starts from, the structural
+transforms applied to it and the adapters it carries. How a run executes it (kernels, fp8,
+parallelism) is runtime configuration and is refused here, so a checkpoint never pins a
+kernel choice.
 
-Reference parity: src/models/model_spec.py:1-179 (same JSON layout, same validator rules:
-every value resolved, runtime keys refused, registries shared with the config schema,
-legacy flat transform configs mapped through key_mapping).
+The JSON layout (format_version 2: `base`, `transforms[]`, `adapters[]` with
+`{type, version, config}` entries) and the base-config hash (sha256 over the canonical
+JSON rendering) are the reference's on-disk format (src/models/model_spec.py:18-95); the
+validation here is table driven: every problem of a spec is collected and reported in one
+error, rather than stopping at the first.
 """
 import hashlib
 import json
 from dataclasses import asdict, dataclass, field
-from typing import Any, Dict, List, Optional
+from typing import Any, Callable, Dict, Iterator, List, NamedTuple, Optional, Tuple
 
 from vdn_minimax_h3_b200.checkpoints.key_mapping import (ANCHOR_FRAME_MODES, DELTA_RULE_VALUES,
                                                          SHORT_CONV_TARGETS, map_config)
@@ -16,13 +20,28 @@ from vdn_minimax_h3_b200.checkpoints.key_mapping import (ANCHOR_FRAME_MODES, DEL
 SPEC_FORMAT_VERSION = 2
 HYBRID_TRANSFORM_VERSION = 2
 BRIDGE_VALUES = ("alpha", "none")
-RUNTIME_KEYS = ("softmax_backend", "rmsnorm_backend", "fp8", "compile", "inference_kernels",
-                "optimized_paths", "w_o_far_scale", "window_decomp", "warmup_steps")
+# Execution knobs, present and retired: a transform config naming any of them is refused,
+# wherever in the nesting the key appears.
+RUNTIME_KEYS = frozenset(("softmax_backend", "rmsnorm_backend", "fp8", "compile",
+                          "inference_kernels", "optimized_paths", "w_o_far_scale",
+                          "window_decomp", "warmup_steps"))
+
+
+def _canonical(obj: Any) -> str:
+    return json.dumps(obj, sort_keys=True, separators=(",", ":"), default=str)
 
 
 def config_hash(resolved_config: Dict[str, Any]) -> str:
-    blob = json.dumps(resolved_config, sort_keys=True, separators=(",", ":"), default=str)
-    return hashlib.sha256(blob.encode()).hexdigest()
+    """Hex sha256 of the canonical JSON text: independent of key order."""
+    return hashlib.sha256(_canonical(resolved_config).encode()).hexdigest()
+
+
+class SpecError(ValueError):
+    """A ModelSpec that cannot be stored or loaded; lists every problem found."""
+
+    def __init__(self, problems: List[str]):
+        self.problems = list(problems)
+        super().__init__("invalid ModelSpec:\n  - " + "\n  - ".join(self.problems))
 
 
 @dataclass
@@ -36,12 +55,11 @@ class BaseSpec:
     config_hash: str = ""
 
     def __post_init__(self):
-        want = config_hash(self.resolved_config)
-        if not self.config_hash:
-            self.config_hash = want
-        elif self.config_hash != want:
-            raise ValueError(f"base.config_hash {self.config_hash[:12]} does not match "
-                             f"resolved_config ({want[:12]})")
+        digest = config_hash(self.resolved_config)
+        if self.config_hash and self.config_hash != digest:
+            raise SpecError([f"base.config_hash {self.config_hash[:12]}... was not computed "
+                             f"from base.resolved_config (hash {digest[:12]}...)"])
+        self.config_hash = digest
 
 
 @dataclass
@@ -65,84 +83,119 @@ class ModelSpec:
     transforms: List[TransformSpec] = field(default_factory=list)
     adapters: List[AdapterSpec] = field(default_factory=list)
 
-    def to_dict(self):
+    def to_dict(self) -> Dict[str, Any]:
         return asdict(self)
 
     @staticmethod
-    def from_dict(payload):
-        spec = ModelSpec(format_version=payload["format_version"],
-                         base=BaseSpec(**payload["base"]),
-                         transforms=[TransformSpec(**t) for t in payload.get("transforms", [])],
-                         adapters=[AdapterSpec(**a) for a in payload.get("adapters", [])])
-        validate_spec(spec)
-        return spec
+    def from_dict(payload: Dict[str, Any]) -> "ModelSpec":
+        entries = lambda kind, cls: [cls(**e) for e in payload.get(kind, [])]  # noqa: E731
+        return validate_spec(ModelSpec(payload["format_version"], BaseSpec(**payload["base"]),
+                                       entries("transforms", TransformSpec),
+                                       entries("adapters", AdapterSpec)))
 
 
-def _flat_keys(config):
-    for k, v in config.items():
-        yield k
-        if isinstance(v, dict):
-            yield from _flat_keys(v)
+def _walk(config: Dict[str, Any], prefix: str) -> Iterator[Tuple[str, str, Any]]:
+    """(dotted path, key, value) for every entry of a nested config, parents first."""
+    for key, value in config.items():
+        path = f"{prefix}.{key}"
+        yield path, key, value
+        if isinstance(value, dict):
+            yield from _walk(value, path)
 
 
-def _require_resolved(config, where):
-    for k, v in config.items():
-        if v is None:
-            raise ValueError(f"{where}.{k} is unresolved (null); a ModelSpec stores the value "
-                             f"the model was built with")
-        if isinstance(v, dict):
-            _require_resolved(v, f"{where}.{k}")
+def _storage_problems(config: Dict[str, Any], where: str, runtime_keys=RUNTIME_KEYS) -> List[str]:
+    out = []
+    for path, key, value in _walk(config, where):
+        if value is None:
+            out.append(f"{path} is null: a spec stores the value the model was built with")
+        if key in runtime_keys:
+            out.append(f"{path} is a runtime setting and never enters a ModelSpec")
+    return out
 
 
-def _validate_hybrid(config):
-    lin = config.get("linear_attention", {})
-    soft = config.get("softmax_attention", {})
-    if lin.get("delta_rule") not in DELTA_RULE_VALUES:
-        raise ValueError(f"delta_rule {lin.get('delta_rule')!r} not in {DELTA_RULE_VALUES}")
-    if lin.get("bridge") not in BRIDGE_VALUES:
-        raise ValueError(f"bridge {lin.get('bridge')!r} not in {BRIDGE_VALUES}")
-    sc = lin.get("short_conv")
-    targets = sc.get("targets") if isinstance(sc, dict) else None
-    if (not isinstance(targets, list) or len(set(targets)) != len(targets)
-            or any(t not in SHORT_CONV_TARGETS for t in targets)):
-        raise ValueError(f"short_conv must be {{'targets': subset of {SHORT_CONV_TARGETS}}}, "
-                         f"got {sc!r}")
-    if config.get("anchor_frames") not in ANCHOR_FRAME_MODES:
-        raise ValueError(f"anchor_frames {config.get('anchor_frames')!r} not in {ANCHOR_FRAME_MODES}")
-    if not isinstance(lin.get("linear_head_dim"), int):
-        raise ValueError(f"linear_head_dim must be a resolved int, got {lin.get('linear_head_dim')!r}")
-    if not isinstance(soft.get("radius"), int):
-        raise ValueError(f"softmax_attention.radius must be a resolved int, got {soft.get('radius')!r}")
-    if not isinstance(config.get("enable_softmax_gate"), bool):
-        raise ValueError("enable_softmax_gate must be a resolved bool")
+class _Rule(NamedTuple):
+    path: Tuple[str, ...]                 # key path inside the hybrid transform's config
+    ok: Callable[[Any], bool]
+    expected: str
 
 
-def validate_spec(spec: ModelSpec):
+def _targets_ok(short_conv: Any) -> bool:
+    if not isinstance(short_conv, dict) or not isinstance(short_conv.get("targets"), list):
+        return False
+    targets = short_conv["targets"]
+    return len(set(targets)) == len(targets) and set(targets) <= set(SHORT_CONV_TARGETS)
+
+
+_HYBRID_RULES = (
+    _Rule(("linear_attention", "delta_rule"), lambda v: v in DELTA_RULE_VALUES,
+          f"one of {DELTA_RULE_VALUES}"),
+    _Rule(("linear_attention", "bridge"), lambda v: v in BRIDGE_VALUES, f"one of {BRIDGE_VALUES}"),
+    _Rule(("linear_attention", "short_conv"), _targets_ok,
+          f"{{'targets': [distinct entries of {SHORT_CONV_TARGETS}]}}"),
+    _Rule(("linear_attention", "linear_head_dim"), lambda v: type(v) is int, "an int"),
+    _Rule(("softmax_attention", "radius"), lambda v: type(v) is int, "an int"),
+    _Rule(("anchor_frames",), lambda v: v in ANCHOR_FRAME_MODES, f"one of {ANCHOR_FRAME_MODES}"),
+    _Rule(("enable_softmax_gate",), lambda v: type(v) is bool, "a bool"),
+)
+_MISSING = object()
+
+
+def _lookup(config: Dict[str, Any], path: Tuple[str, ...]) -> Any:
+    node: Any = config
+    for key in path:
+        node = node.get(key, _MISSING) if isinstance(node, dict) else _MISSING
+    return node
+
+
+def _hybrid_problems(t: TransformSpec) -> List[str]:
+    if t.version != HYBRID_TRANSFORM_VERSION:
+        return [f"hybrid_attention transform version {t.version} is not readable here "
+                f"(this code reads version {HYBRID_TRANSFORM_VERSION})"]
+    out = []
+    for rule in _HYBRID_RULES:
+        value = _lookup(t.config, rule.path)
+        if value is _MISSING or not rule.ok(value):
+            shown = "missing" if value is _MISSING else repr(value)
+            out.append(f"hybrid_attention {'.'.join(rule.path)} = {shown}; expected {rule.expected}")
+    return out
+
+
+def validate_spec(spec: ModelSpec) -> ModelSpec:
+    """Returns the spec when it is storable; raises SpecError listing every problem."""
+    problems = []
     if spec.format_version != SPEC_FORMAT_VERSION:
-        raise ValueError(f"spec format_version {spec.format_version} != {SPEC_FORMAT_VERSION}")
+        problems.append(f"format_version {spec.format_version} (this code reads {SPEC_FORMAT_VERSION})")
     for t in spec.transforms:
-        _require_resolved(t.config, f"transforms[{t.type}]")
-        leaked = sorted(set(_flat_keys(t.config)) & set(RUNTIME_KEYS))
-        if leaked:
-            raise ValueError(f"transforms[{t.type}] carries runtime keys {leaked}")
+        problems += _storage_problems(t.config, f"transforms[{t.type}]")
         if t.type == "hybrid_attention":
-            if t.version != HYBRID_TRANSFORM_VERSION:
-                raise ValueError(f"hybrid_attention transform version {t.version}; this code "
-                                 f"reads version {HYBRID_TRANSFORM_VERSION}")
-            _validate_hybrid(t.config)
+            problems += _hybrid_problems(t)
     for a in spec.adapters:
-        _require_resolved(a.config, f"adapters[{a.type}]")
+        problems += _storage_problems(a.config, f"adapters[{a.type}]", runtime_keys=())
+    if problems:
+        raise SpecError(problems)
     return spec
 
 
-def hybrid_transform_spec(legacy_or_nested):
-    """TransformSpec from either the flat pre-v2 kwargs or the nested v2 layout."""
-    if "softmax_attention" in legacy_or_nested:
-        nested = dict(legacy_or_nested)
-    else:
-        flat = map_config(dict(legacy_or_nested))
-        nested = dict(enable_softmax_gate=flat.pop("enable_softmax_gate", True),
-                      anchor_frames=flat.pop("anchor_frames", "none"),
-                      softmax_attention=dict(radius=flat.pop("radius"), chunk=flat.pop("chunk", 0)),
-                      linear_attention=flat)
+# Flat pre-v2 kwargs that belong outside `linear_attention` in the nested v2 layout:
+# (flat key, nested destination, default when absent).
+_FLAT_TO_NESTED = (("enable_softmax_gate", ("enable_softmax_gate",), True),
+                   ("anchor_frames", ("anchor_frames",), "none"),
+                   ("radius", ("softmax_attention", "radius"), _MISSING),
+                   ("chunk", ("softmax_attention", "chunk"), 0))
+
+
+def hybrid_transform_spec(kwargs: Dict[str, Any]) -> TransformSpec:
+    """The v2 TransformSpec of the hybrid attention from either the nested v2 config or the
+    flat pre-v2 conversion kwargs (renamed through key_mapping.map_config); whatever the
+    flat form does not place elsewhere is the `linear_attention` block."""
+    if "softmax_attention" in kwargs:
+        return TransformSpec("hybrid_attention", HYBRID_TRANSFORM_VERSION, dict(kwargs))
+    rest = map_config(dict(kwargs))
+    nested: Dict[str, Any] = {"softmax_attention": {}}
+    for flat_key, dest, default in _FLAT_TO_NESTED:
+        value = rest.pop(flat_key, default)
+        if value is _MISSING:
+            raise KeyError(f"pre-v2 hybrid kwargs lack {flat_key!r}")
+        (nested if len(dest) == 1 else nested[dest[0]])[dest[-1]] = value
+    nested["linear_attention"] = rest
     return TransformSpec("hybrid_attention", HYBRID_TRANSFORM_VERSION, nested)
