@@ -100,13 +100,14 @@ def test_window_attention_dense_gated_strided():
     assert out_full[:, H * 128:].abs().max().item() == 0
 
 
-@pytest.mark.parametrize("variant,growing", [(1, False), (2, False), (2, True), (3, True),
-                                             (4, False), (5, False), (6, True), (7, False)])
+@pytest.mark.parametrize("variant,growing", [(0, False), (0, True), (1, True), (2, False),
+                                             (3, True), (4, False)])
 def test_window_attention_variants(variant, growing):
-    """Every kernel variant (polynomial share of the exponentials, speculative running max,
-    truncated P pack) matches the oracle like the default instance. `growing` scales the keys up along the
-    sequence so later blocks raise the running max by more than 2^8 and the speculative
-    variants take their redo path."""
+    """Every exponential-pass variant that computes the attention (scalar, packed f32x2, and
+    the packed pass with 2/16, 4/16 or 6/16 of the exponentials on the polynomial) matches
+    the oracle like the default instance. `growing` scales the keys up along the sequence so
+    later blocks raise the running max by more than 2^8 and the O rescale path runs. The
+    timing-only variants 5-7 compute wrong results on purpose and are not checked."""
     from vdn_minimax_h3_b200.ops._ext import ext
     torch.manual_seed(2)
     lay = _layout(40, 30, 12, 100)

@@ -53,3 +53,29 @@ def test_adaln_norm_backward_kernel(T, D, n, grads_all):
         assert _rel(norm.weight.grad, ref_norm.weight.grad) < 1e-2
         assert _rel(sk.grad, sr.grad) < 1e-2
         assert _rel(ck.grad, cr.grad) < 1e-2
+
+
+def test_adaln_norm_same_path_with_and_without_grad():
+    """A no-grad forward (the teacher) and a graph-recording forward (the student) run the
+    same kernel, bit for bit. The kernel rounds once where the eager bf16 expression rounds
+    after every op, so it is checked to be at least as close to the fp32 result as eager is,
+    and close to eager itself."""
+    g = torch.Generator().manual_seed(7)
+    T, D, n = 257, 1024, 3
+    x = torch.randn(1, T, D, generator=g).to(torch.bfloat16).cuda()
+    norm = _Norm((1 + 0.1 * torch.randn(D, generator=g)).cuda(), 1e-6).cuda()
+    shift = (0.3 * torch.randn(n, D, generator=g)).to(torch.bfloat16).cuda()
+    scale = (0.3 * torch.randn(n, D, generator=g)).to(torch.bfloat16).cuda()
+    idx = torch.randint(0, n, (T,), generator=g).cuda()
+    with torch.no_grad():
+        teacher = norm_grad.adaln_modulated_norm(norm, x, shift, scale, idx)
+    student = norm_grad.adaln_modulated_norm(norm, x.clone().requires_grad_(), shift, scale, idx)
+    check_device_error()
+    assert torch.equal(teacher, student.detach())
+    with torch.no_grad():
+        eager = norm(x) * (1.0 + scale.index_select(0, idx)) + shift.index_select(0, idx)
+        xf = x.float()
+        exact = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * norm.weight
+                 * (1.0 + scale.float().index_select(0, idx)) + shift.float().index_select(0, idx))
+    assert _rel(teacher, exact) <= _rel(eager, exact) * 1.05
+    assert _rel(teacher, eager) < 8e-3

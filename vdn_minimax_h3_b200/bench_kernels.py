@@ -236,6 +236,10 @@ def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gemm", action="store_true")
     p.add_argument("--attention", action="store_true")
+    p.add_argument("--attention-ab", action="store_true",
+                   help="window attention against cuDNN / flash SDPA on the same plan segments")
+    p.add_argument("--trace-variant", type=int, default=None,
+                   help="kernel variant for --attention-trace (default: the current one)")
     p.add_argument("--linear", action="store_true")
     p.add_argument("--linear-heads", type=int, nargs="*", default=[56],
                    help="head counts for --linear (7 = one rank's share at 8-way Ulysses)")
@@ -260,6 +264,9 @@ def main(argv=None):
     if a.attention:
         from vdn_minimax_h3_b200.ops.attention import bench_attention
         bench_attention(timed)
+    if a.attention_ab:
+        from vdn_minimax_h3_b200.ops.attention import bench_attention_vs_cudnn
+        bench_attention_vs_cudnn(timed)
     if a.linear:
         from vdn_minimax_h3_b200.ops.linear_branch import bench_linear
         for h in a.linear_heads:
@@ -275,7 +282,7 @@ def main(argv=None):
         trace_gemm_fp8()
     if a.attention_trace:
         from vdn_minimax_h3_b200.ops.attention import trace_attention
-        trace_attention(variant=0)
+        trace_attention(variant=a.trace_variant)
     if a.profile_small:
         profile_small()
     if a.attention_small:

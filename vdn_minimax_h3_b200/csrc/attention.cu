@@ -56,15 +56,17 @@ constexpr int AT_REGS_HIGH = 208;
 static_assert(128 * AT_REGS_LOW + 256 * AT_REGS_HIGH <= AT_THREADS * 168, "register split");
 constexpr int AT_SMEM = 2 * AT_Q_BYTES + (AT_KSTAGES + AT_VSTAGES) * AT_KV_BYTES + 1024 + 384;
 constexpr int AT_MAX_RANGES = 4;
-// Kernel variants (attention_set_variant): bit 0 = one of every 8 exponentials runs as a
-// polynomial on the FMA pipe; bit 1 = speculative running max (the exponentials of block j
-// use the running max of blocks < j and the block's own max is taken in the same pass;
-// only when it exceeds the running max by more than 2^8 is the block redone against the
-// new max); bit 2 = truncated P pack: the bf16 P pairs are assembled with a byte permute
-// (round toward zero) instead of the float->bf16x2 conversion, which issues on the same
-// pipe as the exponentials.
+// Kernel variants (attention_set_variant), for A/B runs of the softmax's exponential pass:
+//   0  the scalar pass (one FFMA, one MUFU ex2 and one FADD per score, cvt pairs)
+//   1  packed pass: scale-and-subtract and the row-sum adds on fma/add.f32x2 (two lanes per
+//      issue slot), MUFU ex2 for every score
+//   2, 3, 4  the packed pass with 1, 2 or 3 of every 8 score pairs exponentiated by the
+//      cubic polynomial on the FMA / integer pipes instead of MUFU (2/16, 4/16, 6/16 of
+//      the scores), trading MUFU cycles (16 per clock per SM) for FMA issue slots
+//   5, 6, 7  timing diagnostics (wrong results): the packed pass without the MUFU ex2, without
+//      the bf16 pack conversion, or without the P store to TMEM
 constexpr int AT_VARIANTS = 8;
-static int g_variant = 0;
+static int g_variant = 1;
 
 struct AttnParams {
   const int* tiles;          // [n_items_per_head, 4] (q0, q_end, segment, kv_len), q_end-q0 <= 256
@@ -100,6 +102,23 @@ __device__ __forceinline__ float ex2_poly(float x) {
                        0.9999195980f);
   const int ni = __float_as_int(j) - 0x4B400000;
   return __int_as_float(__float_as_int(p) + (ni << 23));
+}
+
+// The same polynomial on a pair: n = round(x) through the 1.5 * 2^23 rounding sum, the
+// reduction and the cubic on fma/add.f32x2, the exponent add on the integer pipe.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 j = __fadd2_rn(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 n = __fadd2_rn(j, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
+  float2 q = __ffma2_rn(make_float2(0.0552129932f, 0.0552129932f), f,
+                        make_float2(0.2427141405f, 0.2427141405f));
+  q = __ffma2_rn(q, f, make_float2(0.6932621603f, 0.6932621603f));
+  q = __ffma2_rn(q, f, make_float2(0.9999195980f, 0.9999195980f));
+  // (bits(j) << 23) == n << 23 modulo 2^32: the magic constant's bits shift out
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(j.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(j.y) << 23)));
 }
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -148,6 +167,7 @@ struct KvWalk {
 // Pipeline tracing (diagnostics, off unless p.trace is set): CTA 0 records clock64 at
 // events of its first AT_TRACE_BLOCKS blocks, slot = (event * 2 + tile) * AT_TRACE_BLOCKS + block.
 constexpr int AT_TRACE_BLOCKS = 64;
+constexpr int AT_TRACE_SLOTS = 12 * AT_TRACE_BLOCKS;   // + 4 clock-rate stamps
 enum AtTraceEvent : int {
   TR_S_WAIT = 0, TR_S_READY, TR_LD_DONE, TR_MAX_DONE, TR_EXP_DONE, TR_P_ARRIVE, TR_EVENTS
 };
@@ -220,6 +240,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // trace mode: the SM clock rate seen by CTA 0 (globaltimer ns against clock64 cycles)
+  const bool clock_probe = p.trace && blockIdx.x == 0 && threadIdx.x == 128;
+  if (clock_probe) {
+    p.trace[AT_TRACE_SLOTS] = (long long)globaltimer_ns();
+    p.trace[AT_TRACE_SLOTS + 1] = clock64();
+  }
 
   // The register re-split sits inside each role's branch, so every role's code is
   // dominated by exactly one limit.
@@ -444,6 +470,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const int r = quarter * 32 + lane;        // row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + qt * AT_BN;
+    const uint32_t tP = tS;                   // P (bf16 pairs) over the first 64 columns of S
     const uint32_t tO = tmem + lane_off + 256 + qt * 128;
     uint32_t g = 0;
     int local = 0;
@@ -475,9 +502,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         tmem_wait_ld();
         if (tr) at_trace(p, TR_LD_DONE, qt, g);
-        constexpr int AT_POLY_EVERY = AT_VARIANT & 1;
-        constexpr bool AT_SPEC = (AT_VARIANT & 2) != 0;
-        constexpr bool AT_TRUNC = (AT_VARIANT & 4) != 0;
+        constexpr bool kPacked = AT_VARIANT >= 1;
+        constexpr int kPolyPairs = (AT_VARIANT >= 2 && AT_VARIANT <= 4) ? AT_VARIANT - 1 : 0;
+        constexpr bool kNoMufu = AT_VARIANT == 5, kNoCvt = AT_VARIANT == 6, kNoStore = AT_VARIANT == 7;
         // only a ragged block is masked
         const int valid = w.valid();
         if (valid < AT_BN) {
@@ -486,32 +513,58 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         // p = 2^(s * scale_log2 - m), packed bf16 pairs written over S_t in TMEM
-        auto exp_pass = [&](float neg_m, float* mxv) {
+        auto exp_pass = [&](float neg_m) {
+          if constexpr (!kPacked) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) sums[i] = 0.f;
+            for (int h = 0; h < 2; ++h) {
+              uint32_t pk[32];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t pk[32];
+              for (int c = 0; c < 64; c += 8) {
+                float e[8];
 #pragma unroll
-            for (int c = 0; c < 64; c += 8) {
-              float e[8];
+                for (int i = 0; i < 8; ++i) {
+                  e[i] = ex2(fmaf(s[h * 64 + c + i], p.scale_log2, neg_m));
+                  sums[i] += e[i];
+                }
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float x = fmaf(s[h * 64 + c + i], p.scale_log2, neg_m);
-                if (mxv) mxv[i] = fmaxf(mxv[i], x);
-                e[i] = (i >= 8 - AT_POLY_EVERY) ? ex2_poly(x) : ex2(x);
-                // truncated pack: P is the top half of each fp32 (round toward zero) and the
-                // row sum adds exactly those values, so O / l stays a softmax of the scores
-                if (AT_TRUNC) e[i] = __uint_as_float(__float_as_uint(e[i]) & 0xffff0000u);
-                sums[i] += e[i];
+                for (int i = 0; i < 4; ++i) pk[c / 2 + i] = pack_bf16(e[2 * i], e[2 * i + 1]);
               }
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                pk[c / 2 + i] = AT_TRUNC ? __byte_perm(__float_as_uint(e[2 * i]),
-                                                       __float_as_uint(e[2 * i + 1]), 0x7632)
-                                         : pack_bf16(e[2 * i], e[2 * i + 1]);
+              tmem_st32(tP + h * 32, pk);
             }
-            tmem_st32(tS + h * 32, pk);
+          } else {
+            const float2 sc = make_float2(p.scale_log2, p.scale_log2);
+            const float2 nm = make_float2(neg_m, neg_m);
+            float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                             make_float2(0.f, 0.f)};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t pk[32];
+#pragma unroll
+              for (int c = 0; c < 64; c += 16) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {   // pair i of this 16-score group
+                  const int col = h * 64 + c + 2 * i;
+                  const float2 x = __ffma2_rn(make_float2(s[col], s[col + 1]), sc, nm);
+                  float2 e;
+                  if (i >= 8 - kPolyPairs) {
+                    e = ex2_poly2(x);
+                  } else if (kNoMufu) {
+                    e = x;
+                  } else {
+                    e = make_float2(ex2(x.x), ex2(x.y));
+                  }
+                  acc[i & 3] = __fadd2_rn(acc[i & 3], e);
+                  pk[c / 2 + i] = kNoCvt ? __byte_perm(__float_as_uint(e.x), __float_as_uint(e.y), 0x7632)
+                                         : pack_bf16(e.x, e.y);
+                }
+              }
+              if (!kNoStore) tmem_st32(tP + h * 32, pk);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              sums[2 * i] = acc[i].x;
+              sums[2 * i + 1] = acc[i].y;
+            }
           }
         };
         // O rescale (warp-collective TMEM round trip; rows that keep their max use 1)
@@ -526,33 +579,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             tmem_st32(tO + c, u);
           }
         };
-        const bool spec = AT_SPEC && __all_sync(0xffffffffu, m_ref != -INFINITY);
-        if (spec) {
-          // exponentials against the running max; the block max (relative to it) comes
-          // out of the same pass. P <= 2^8 unless the max grew by more than that.
-          float mxv[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) mxv[i] = -INFINITY;
-          if (tr) at_trace(p, TR_MAX_DONE, qt, g);
-          exp_pass(-m_ref, mxv);
-          const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
-                                 fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7])));
-          const bool need = mx > 8.0f;
-          if (__any_sync(0xffffffffu, need)) {
-            // rare: redo the block against the new max (S_t was issued after the previous
-            // block's P.V, so O is complete and may be rescaled here)
-            float factor = 1.f;
-            if (need) {
-              factor = ex2(-mx);
-              m_ref += mx;
-              l *= factor;
-            }
-            tmem_wait_st();
-            if (j > 0) rescale_o(factor);
-            exp_pass(-m_ref, nullptr);
-          }
-        } else {
-          // row max on the raw scores (8 independent chains)
+        {
+          // row max on the raw scores (8 independent chains of 3-input max)
           float mxv[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) mxv[i] = s[i];
@@ -560,8 +588,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           for (int c = 8; c < AT_BN; c += 16)
 #pragma unroll
             for (int i = 0; i < 8; ++i) mxv[i] = fmax3(mxv[i], s[c + i], s[c + 8 + i]);
-          const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
-                                 fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * p.scale_log2;
+          const float mx = fmax3(fmax3(mxv[0], mxv[1], mxv[2]), fmax3(mxv[3], mxv[4], mxv[5]),
+                                 fmaxf(mxv[6], mxv[7])) * p.scale_log2;
           const float m_new = fmaxf(m_ref, mx);
           const bool need = m_new > m_ref + 8.0f;
           const bool warp_need = __any_sync(0xffffffffu, need);
@@ -572,10 +600,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             m_ref = m_new;
             l *= factor;
           }
-          // S_t was issued after the previous block's P.V, so that P.V is complete: O may
+          // S_t(j) completes after P_t(j-1).V(j-1) (in-order MMAs), so O is complete and may
           // be rescaled before this block's P is published.
           if (j > 0 && warp_need) rescale_o(factor);
-          exp_pass((m_ref == -INFINITY) ? 0.f : -m_ref, nullptr);
+          exp_pass((m_ref == -INFINITY) ? 0.f : -m_ref);
         }
         l += ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
         if (tr) at_trace(p, TR_EXP_DONE, qt, g);
@@ -612,6 +640,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
   }
 
+  if (clock_probe) {
+    p.trace[AT_TRACE_SLOTS + 2] = (long long)globaltimer_ns();
+    p.trace[AT_TRACE_SLOTS + 3] = clock64();
+  }
   __syncthreads();
   if (warp == 1) {
     __syncwarp();
@@ -626,13 +658,13 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              int64_t ldo, float scale, int* err, cudaStream_t stream,
                              const RowScatter* scatter, long long* trace) {
   if (n_tiles == 0 || H == 0) return;
-  static bool attr = false;
+  static std::atomic<uint64_t> attr{0};
   using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, AttnParams);
   static const KernelFn kernels[AT_VARIANTS] = {
       window_attention_kernel<0>, window_attention_kernel<1>, window_attention_kernel<2>,
       window_attention_kernel<3>, window_attention_kernel<4>, window_attention_kernel<5>,
       window_attention_kernel<6>, window_attention_kernel<7>};
-  if (!attr) {
+  if (attr_needed(attr)) {
     // setmaxnreg.inc waits until the registers it asks for are free: refuse to launch if
     // the compiled launch register count cannot fund the split.
     for (auto fn : kernels) {
@@ -643,7 +675,7 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
         throw std::runtime_error("window attention: launch registers cannot fund the "
                                  "warpgroup register split");
     }
-    attr = true;
+    attr_done(attr);
   }
   const uint64_t cols = (uint64_t)H * AT_D;
   CUtensorMap tq = make_tmap_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, T, ldq * 2, 64, AT_BM);

@@ -534,11 +534,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 // ------------------------------------------------------------------------------- host
 template <int EPI>
 static void launch_gemm(const GemmArgs& a, EpiParams p, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
+  static std::atomic<uint64_t> attr_set{0};
+  if (attr_needed(attr_set)) {
     cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          GM_SMEM);
-    attr_set = true;
+    attr_done(attr_set);
   }
   CUtensorMap ta = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M,
                                 a.lda * 2, GM_BK, GM_BM);

@@ -500,14 +500,14 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
 template <int EPI>
 static void launch_fp8(const GemmFp8Args& a, Fp8Params p, cudaStream_t stream) {
   p.trace = g_fp8_trace;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static std::atomic<uint64_t> attr_set{0};
+  if (attr_needed(attr_set)) {
     cudaFuncSetAttribute(gemm_fp8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, F8_SMEM);
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, gemm_fp8_kernel<EPI>) != cudaSuccess ||
         fa.numRegs * F8_THREADS < 128 * F8_REGS_LOW + 256 * F8_REGS_HIGH)
       throw std::runtime_error("fp8 GEMM: launch registers cannot fund the register split");
-    attr_set = true;
+    attr_done(attr_set);
   }
   CUtensorMap ta = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.M, a.lda, F8_BK, F8_BM);
   CUtensorMap tb = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, a.ldb, F8_BK, F8_BN);

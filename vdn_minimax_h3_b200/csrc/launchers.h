@@ -6,7 +6,24 @@
 
 #include <cuda_bf16.h>
 
+#include <atomic>
+
 namespace vdn {
+
+// Kernel attributes (dynamic shared-memory limit, carveout) are per device: a launcher
+// sets them the first time it runs on each device. `attr_needed` is true until
+// `attr_done` has been called for the current device (ordinals 0..63).
+inline int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+inline bool attr_needed(const std::atomic<uint64_t>& done) {
+  return !(done.load(std::memory_order_acquire) & (1ull << (current_device() & 63)));
+}
+inline void attr_done(std::atomic<uint64_t>& done) {
+  done.fetch_or(1ull << (current_device() & 63), std::memory_order_release);
+}
 
 // Row-owner scatter of an epilogue's output rows. Under Ulysses the rows of the packed
 // sequence are owned in contiguous shards of `rows_per_rank`; an epilogue that produced row

@@ -234,10 +234,10 @@ void launch_lb_conv(const void* in, int64_t ldi, const float* wsp, const float* 
                     cudaStream_t stream) {
   if (!F || !gh || !gw) return;
   if (gw > LB_MAXW) throw std::runtime_error("short conv: grid width above 48 is not supported");
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (attr_needed(attr)) {
     cudaFuncSetAttribute(lb_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LB_CONV_SMEM);
-    attr = true;
+    attr_done(attr);
   }
   // rows = packed tokens of the F frames, one 128-channel head per box column
   CUtensorMap tm = make_tmap_2d(in, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * 128,
@@ -439,13 +439,13 @@ void launch_lb_conv2(const void* in, int64_t ldi, const float* wsp, const float*
                      int* err, cudaStream_t stream) {
   if (!F || !gh || !gw) return;
   if (gw > LB_MAXW) throw std::runtime_error("short conv: grid width above 44 is not supported");
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (attr_needed(attr)) {
     cudaFuncSetAttribute(lb_spatial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SP_SMEM);
     // two blocks per SM need the largest shared-memory carveout
     cudaFuncSetAttribute(lb_spatial_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);
-    attr = true;
+    attr_done(attr);
   }
   CUtensorMap tm = make_tmap_2d(in, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * 128,
                                 (uint64_t)F * gh * gw, ldi * 2, SP_CH, gw, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -637,10 +637,10 @@ void launch_lb_frame_stats(const void* k, int64_t ldk, const void* v, int64_t ld
                            int H, const float* beta, float* A, float* B, int* err,
                            cudaStream_t stream) {
   if (!F || !S || !H) return;
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (attr_needed(attr)) {
     cudaFuncSetAttribute(lb_frame_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FS_SMEM);
-    attr = true;
+    attr_done(attr);
   }
   const uint64_t cols = (uint64_t)H * 128, rows = (uint64_t)F * S;
   CUtensorMap tk = make_tmap_2d(k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, ldk * 2, 64, FS_CHUNK);
@@ -806,10 +806,10 @@ void launch_lb_spd_factor(const float* A, const float* B, const float* alpha, fl
                           float* inj, int n_mats, float a_scale, float b_scale,
                           cudaStream_t stream) {
   if (!n_mats) return;
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (attr_needed(attr)) {
     cudaFuncSetAttribute(lb_spd_factor_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SPD_SMEM);
-    attr = true;
+    attr_done(attr);
   }
   lb_spd_factor_kernel<<<n_mats, 256, SPD_SMEM, stream>>>(A, B, alpha, trans, inj, a_scale, b_scale);
 }
@@ -988,14 +988,14 @@ static void launch_scan_rows(const float* trans, const float* inj, const float* 
                              int H, float* prefix, float* suffix, int* err, int ndir,
                              cudaStream_t stream) {
   constexpr int smem = (NSLOT * 16384 + (128 / RS) * SC_PITCH) * 4 + 64;
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (attr_needed(attr)) {
     cudaFuncSetAttribute(lb_scan_rows_kernel<RS, NSLOT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          smem);
     cudaFuncSetAttribute(lb_scan_rows_kernel<RS, NSLOT>,
                          cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);
-    attr = true;
+    attr_done(attr);
   }
   lb_scan_rows_kernel<RS, NSLOT><<<dim3(H * RS, ndir), 256, smem, stream>>>(trans, inj, start, F, H,
                                                                              prefix, suffix, err);
@@ -1020,10 +1020,10 @@ void launch_lb_scan(const float* trans, const float* inj, const float* start, in
                     float* prefix, float* suffix, int* err, cudaStream_t stream, int ndir) {
   if (!F || !H) return;
   const int nrec = H * ndir;
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (attr_needed(attr)) {
     cudaFuncSetAttribute(lb_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM);
-    attr = true;
+    attr_done(attr);
   }
   // many heads: two half-row CTAs per recurrence at two CTAs per SM (one transition slot);
   // few heads: 2, 4 or 8 row parts per recurrence, one CTA per SM, two transition slots
@@ -1195,10 +1195,10 @@ void launch_lb_readout(const void* q, int64_t ldq, const void* state, int F, int
                        int64_t ldo, float eps, int* err, cudaStream_t stream,
                        const RowScatter* scatter) {
   if (!F || !S || !H) return;
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (attr_needed(attr)) {
     cudaFuncSetAttribute(lb_readout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RO_SMEM);
-    attr = true;
+    attr_done(attr);
   }
   CUtensorMap tq = make_tmap_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * 128,
                                 (uint64_t)F * S, ldq * 2, 64, 128);

@@ -57,6 +57,9 @@ extern "C" __attribute__((visibility("default"))) int vdn_delta_stats_factor_noa
   if (!aligned16(k) || !aligned16(v) || !aligned16(trans) || !aligned16(inj) || ldk % 8 ||
       ldv % 8 || ldk < (int64_t)H * 128 || ldv < (int64_t)H * 128)
     return VDN_NOALLOC_BAD_ARGUMENT;
+  // An error already pending on this host thread belongs to the caller: refuse to run
+  // (leaving it pending) rather than report it as ours or clear it.
+  if (cudaPeekAtLastError() != cudaSuccess) return VDN_NOALLOC_CUDA_ERROR;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return VDN_NOALLOC_CUDA_ERROR;
   ScratchAddrs* s = nullptr;
@@ -69,6 +72,7 @@ extern "C" __attribute__((visibility("default"))) int vdn_delta_stats_factor_noa
   } catch (...) {
     return VDN_NOALLOC_CUDA_ERROR;
   }
+  // nothing was pending at entry, so an error here comes from this call's launches
   return cudaGetLastError() == cudaSuccess ? VDN_NOALLOC_OK : VDN_NOALLOC_CUDA_ERROR;
 }
 

@@ -493,8 +493,8 @@ void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
   check_out_or_scatter(out, sc, out.stride(0), T, H * 128);
   if (trace)
     TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous() &&
-                    trace->numel() >= 12 * 64,
-                "trace must be a contiguous int64 CUDA tensor of >= 1152 entries");
+                    trace->numel() >= 12 * 64 + 4,
+                "trace must be a contiguous int64 CUDA tensor of >= 772 entries");
   TORCH_CHECK(tiles.is_cuda() && tiles.scalar_type() == at::kInt && tiles.is_contiguous() &&
                   tiles.dim() == 2 && tiles.size(1) == 4, "tiles must be int32 [n, 4]");
   TORCH_CHECK(kv.is_cuda() && kv.scalar_type() == at::kInt && kv.is_contiguous() &&

@@ -12,8 +12,15 @@
 //   [F*H*128]. Outputs: trans, inj fp32 [F, H, 128, 128].
 //   Limit: F * H <= VDN_NOALLOC_MAX_MATS (the scratch holds that many 128 x 128 pairs,
 //   2 x 64 KB each: 16 MB); larger requests return VDN_NOALLOC_TOO_LARGE and launch nothing.
-//   Nothing in the scratch needs to start at zero: A and B are fully overwritten each call;
-//   the scratch error word is cleared by each call before its kernels run.
+//   Nothing in the scratch needs to start at zero: each call clears the scratch error word
+//   before its kernels run, and the statistics kernel writes all of A and B -- unless it
+//   gives up on a bounded wait. Then it records a code in the error word and skips its
+//   stores, the factor kernel reads the previous call's A / B, and trans / inj are invalid:
+//   after the stream finishes, check vdn_noalloc_read_device_error and discard the outputs
+//   whenever the word is nonzero.
+//   A CUDA error already pending on the calling host thread is left in place and the call
+//   returns VDN_NOALLOC_CUDA_ERROR without launching, so an earlier, unrelated failure is
+//   never reported as this call's nor cleared by it.
 //   The scratch is shared by every call on a device: calls that overlap in time (different
 //   streams, or host threads, without ordering between them) race on it.
 //   The first call on a device resolves the scratch addresses (cudaGetSymbolAddress) and

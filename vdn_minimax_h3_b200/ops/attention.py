@@ -68,7 +68,7 @@ def bench_attention(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
     k, v = torch.randn_like(q), torch.randn_like(q)
     fl = plan.flops(H, d)
     prev = ext().attention_variant()
-    for var in (0, 2, 4):
+    for var in range(8):
         ext().attention_set_variant(var)
         ms = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
         print(json.dumps(dict(case="window_attention_c1_both", T=T, heads=H, variant=var, ms=ms,
@@ -92,7 +92,7 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
     plan = AttentionPlan(lay, window_bounds(frames, 1, 5), "both", device="cuda")
     q = torch.randn(lay.seq_len, heads, 128, device="cuda", dtype=torch.bfloat16)
     k, v = torch.randn_like(q), torch.randn_like(q)
-    tr = torch.zeros(12 * 64, dtype=torch.int64, device="cuda")
+    tr = torch.zeros(12 * 64 + 4, dtype=torch.int64, device="cuda")
     prev = ext().attention_variant()
     if variant is not None:
         ext().attention_set_variant(variant)
@@ -102,7 +102,8 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
         torch.cuda.synchronize()
     finally:
         ext().attention_set_variant(prev)
-    t = tr.view(6, 2, 64).cpu().double()
+    stamps = tr[12 * 64:].cpu().double()
+    t = tr[:12 * 64].view(6, 2, 64).cpu().double()
     a, b = blocks
     ev = {n: t[i] for i, n in enumerate(TRACE_EVENTS)}
     out = {}
@@ -122,6 +123,50 @@ def trace_attention(frames=102, heads=56, blocks=(8, 60), variant=None):  # prag
     for n in ("s_ready", "max_done", "exp_done", "p_arrive"):
         line[n] = [[int(ev[n][tile, i] - t0) for i in range(a, a + 6)] for tile in (0, 1)]
     out["timeline"] = line
+    out["sm_mhz"] = float((stamps[3] - stamps[1]) / (stamps[2] - stamps[0]) * 1e3)
     out["variant"] = ext().attention_variant() if variant is None else variant
     print(json.dumps({"attention_trace_cycles": out}), flush=True)
     return out
+
+
+def bench_attention_vs_cudnn(timed, frames=102, heads=56):  # pragma: no cover - GPU tool
+    """A/B of the window-attention kernel against cuDNN SDPA (and torch's flash backend) on
+    the SAME work: the library runs one dense attention per plan segment over that
+    segment's K/V rows, gathered and laid out [1, H, L, d] before timing (the gather is not
+    charged to it). All numbers are ms per layer, 56 heads, the whole 14.4 s clip."""
+    import json
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from vdn_minimax_h3_b200.models.layout import SequenceLayout
+    from vdn_minimax_h3_b200.models.window import AttentionPlan, window_bounds
+    T_text, T_audio, Fr, S, H, d = 800, 1150, frames, 1008, heads, 128
+    layout = SequenceLayout(seq_len=T_text + T_audio + Fr * S, video_start=T_text + T_audio,
+                            num_frames=Fr, tokens_per_frame=S, frame_height=24, frame_width=42,
+                            text_start=0, text_len=T_text)
+    plan = AttentionPlan(layout, window_bounds(Fr, 1, 5), "both", device="cuda")
+    T = layout.seq_len
+    q = torch.randn(T, H, d, device="cuda", dtype=torch.bfloat16)
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    fl = plan.flops(H, d)
+    ours = timed(lambda: window_attention(q, k, v, plan, d ** -0.5))
+    segs = []
+    for seg in plan.segments:
+        rows = torch.cat([torch.arange(a, b, device="cuda") for a, b in seg.kv])
+        segs.append((q[seg.q_start:seg.q_end].permute(1, 0, 2).unsqueeze(0).contiguous(),
+                     k[rows].permute(1, 0, 2).unsqueeze(0).contiguous(),
+                     v[rows].permute(1, 0, 2).unsqueeze(0).contiguous()))
+    res = dict(case="window_attention_c1_both_ab", T=T, heads=H, segments=len(segs),
+               variant=ext().attention_variant(), ours_ms=ours, ours_tflops=fl / ours / 1e9)
+    for name, backend in (("cudnn", SDPBackend.CUDNN_ATTENTION),
+                          ("flash", SDPBackend.FLASH_ATTENTION)):
+        def run():
+            with sdpa_kernel([backend]):
+                for qs, ks, vs in segs:
+                    F.scaled_dot_product_attention(qs, ks, vs, scale=d ** -0.5)
+        try:
+            ms = timed(run)
+            res[f"{name}_ms"] = ms
+            res[f"{name}_tflops"] = fl / ms / 1e9
+        except RuntimeError as e:  # backend not available for this shape / GPU
+            res[f"{name}_error"] = str(e).splitlines()[0][:200]
+    print(json.dumps(res), flush=True)
+    return res

@@ -7,8 +7,15 @@ Forward: the inference kernel `adaln_rmsnorm` (csrc/norm.cu; one read of x, one 
 per-row modulation gathered in registers). Backward: `adaln_rmsnorm_bwd` (csrc/norm_bwd.cu)
 for dx = r g - (r^3 / D) x sum(g x), g = dy * w * (1 + scale[idx]); the gradients of w, shift
 and scale (all frozen in the shipped training stages) only when they are required, in
-PyTorch. `adaln_modulated_norm` takes the kernels for bf16 CUDA rows under autograd and the
-eager expression otherwise.
+PyTorch. `adaln_modulated_norm` takes the kernels for every bf16 CUDA row set -- with or
+without autograd -- and the eager expression otherwise.
+
+The kernel keeps the normalisation and the affine chain in fp32 and rounds once, where the
+eager expression rounds to bf16 after each op, so the two differ by up to about two bf16
+ulps. The choice is therefore made by the module flag `NORM_KERNELS` and the tensors' dtype
+and layout only, never by whether a graph is being recorded: a no-grad teacher forward and
+the student forward it is compared with (Stage A2 / B losses, the DMD real score) always
+run the same norm implementation, so no loss carries a difference between two norms.
 """
 import torch
 
@@ -63,7 +70,7 @@ def adaln_modulated_norm(norm, x, shift, scale, idx):
     x [..., T, D], shift / scale [n, D], idx [T]."""
     D = x.shape[-1]
     x2 = x.reshape(-1, D)
-    if (NORM_KERNELS and x.is_cuda and torch.is_grad_enabled() and x.dtype == torch.bfloat16
+    if (NORM_KERNELS and x.is_cuda and x.dtype == torch.bfloat16
             and shift.dtype == torch.bfloat16 and scale.dtype == torch.bfloat16
             and D % 8 == 0 and D <= MAX_DIM and x2.shape[0] == idx.numel()
             and x2.stride(1) == 1 and (x2.stride(0) * 2) % 16 == 0 and x2.data_ptr() % 16 == 0):
