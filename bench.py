@@ -28,7 +28,7 @@ import time
 
 import torch
 
-BASELINE = {1: 47.6, 2: 25.9, 4: 13.1, 8: 6.9}     # published denoise s, 8 NFE
+BASELINE = {1: 47.6, 2: 25.9, 4: 13.1, 8: 6.9}     # published SGLang MXFP8 denoise s, 8 NFE, B200 (reference README.md:133)
 METRIC = "denoise s per 14.4s clip, 8 steps (e2e s alongside)"
 NUM_FRAMES, TEXT_LEN, NFE = 345, 800, 8
 

@@ -103,4 +103,10 @@ def test_engine_fp8_close_to_bf16():
         out_v, _ = InferenceEngine(gm, fp8=True)(**kwg, layout=layout)
     torch.cuda.synchronize()
     check_device_error()
-    assert _rel(out_v, ref_v) < 0.08
+    err = _rel(out_v, ref_v)
+    print(f"fp8 engine vs bf16 engine: {err:.3e}")
+    # budget: an E4M3 operand carries a relative rounding error of RMS 2^-3 / sqrt(12) =
+    # 3.6e-2; a GEMM with both operands quantised, ~5.1e-2 on its output. The block output
+    # adds that error to a residual stream that carries most of the signal, so the whole
+    # engine must stay well under one GEMM's error.
+    assert err < 3.0e-2

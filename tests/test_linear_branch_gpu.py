@@ -152,9 +152,19 @@ def test_engine_gpu_matches_cpu_eager():
     gmodel.time_embedder.float()
     for blk in gmodel.transformer_blocks:
         blk.attn.linear_attention.alpha.float()
+    eager = copy.deepcopy(gmodel)
     eng = InferenceEngine(gmodel)
     kwg = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in kw.items()}
     out_v, out_a = eng(**kwg, layout=layout)
     check_device_error()
-    assert _rel(out_v, ref_v) < 6e-2
-    assert _rel(out_a, ref_a) < 6e-2
+    # budget: the round-off of the same model run eagerly in bf16 on this GPU (every op
+    # rounds to bf16 there too); the fused kernels keep more of each chain in fp32, so they
+    # must land within a small multiple of it
+    set_layout(eager, layout)
+    bf_v, bf_a = eager(**kwg)
+    budget_v = 1.5 * _rel(bf_v, ref_v) + 2e-3
+    budget_a = 1.5 * _rel(bf_a, ref_a) + 2e-3
+    print(f"engine vs fp32: video {_rel(out_v, ref_v):.2e} (budget {budget_v:.2e}), "
+          f"audio {_rel(out_a, ref_a):.2e} (budget {budget_a:.2e})")
+    assert _rel(out_v, ref_v) < budget_v
+    assert _rel(out_a, ref_a) < budget_a

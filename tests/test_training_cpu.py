@@ -217,3 +217,42 @@ def test_step_profiler_env(tmp_path, monkeypatch, capsys):
             "checkpoint.early_saves=[]", "distributed.offload_activations=false"]
     assert _run_stage("a2", argv) == 1
     assert "profile of step 1" in capsys.readouterr().out
+
+
+def _bucket_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from vdn_minimax_h3_b200.training.trainers import _bucketed
+        g = torch.Generator().manual_seed(rank)
+        ts = [torch.randn(3, 5, generator=g), torch.randn(7, generator=g).bfloat16(),
+              torch.randn(2, 2, generator=g)]
+        want = [t.clone() for t in ts]
+        for t in want:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        _bucketed(ts, lambda flat: dist.all_reduce(flat, op=dist.ReduceOp.SUM))
+        same = all(torch.equal(a, b) for a, b in zip(ts, want))
+        params = [torch.full((4,), float(rank)), torch.full((2, 3), float(rank)).bfloat16()]
+        _bucketed(params, lambda flat: dist.broadcast(flat, src=1))
+        q.put((rank, same and all(bool((p == 1).all()) for p in params)))
+        dist.destroy_process_group()
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, repr(exc)))
+
+
+@pytest.mark.timeout(120)
+def test_a1_bucketed_collectives_two_ranks():
+    """Stage A1's per-layer buckets (one collective per dtype over a flat buffer) give the
+    same all-reduce sums as per-tensor calls, and the broadcast leaves every rank with the
+    owner's values, on 2 gloo ranks with mixed fp32 / bf16 tensors."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_bucket_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=100) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+    assert res == {0: True, 1: True}

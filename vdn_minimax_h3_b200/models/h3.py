@@ -15,7 +15,7 @@ Parameter NAMES follow the diffusers module tree those call sites use, so LoRA t
 (`transformer_blocks.N.attn.to_q`, `token_refiner.refiner_blocks.N.attn.to_q`, ...) and the
 hybrid transform's `.attn.orig.` re-rooting resolve the same way.
 
-Assumed where the reference is silent (fixed in H3Config, documented in DESIGN.md):
+Assumed where the reference is silent (fixed in H3Config):
 time_embed_dim 3072 (this reproduces the ~33B parameter count), MODALITY_NUM 3, the rotary
 split 32/48/48 channels over (t, h, w) with theta 10000, biases on every projection, a
 two-block unconditioned self-attention token refiner, and LayerNorm-free RMS norm_out.

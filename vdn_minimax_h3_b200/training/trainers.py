@@ -277,6 +277,21 @@ class AlignHook:
         return None
 
 
+def _bucketed(tensors, collective):
+    """Runs `collective` once per dtype on one flat buffer holding all of `tensors`, then
+    copies the result back (one NCCL call per layer instead of one per parameter)."""
+    by_dtype = {}
+    for t in tensors:
+        by_dtype.setdefault(t.dtype, []).append(t)
+    for group in by_dtype.values():
+        flat = torch.cat([t.reshape(-1) for t in group])
+        collective(flat)
+        offset = 0
+        for t in group:
+            t.copy_(flat[offset:offset + t.numel()].view_as(t))
+            offset += t.numel()
+
+
 def run_stage_a1(cfg):
     out = cfg.checkpoint.output_dir
     fs.refuse_if_guarded(out, os.path.join(out, "DONE"))
@@ -353,7 +368,8 @@ def run_stage_a1(cfg):
                 for p in params:
                     if p.grad is None:
                         p.grad = torch.zeros_like(p)
-                    dist.all_reduce(p.grad, op=dist.ReduceOp.AVG)
+                _bucketed([p.grad for p in params],
+                          lambda flat: dist.all_reduce(flat, op=dist.ReduceOp.AVG))
             norms[idx] = fs.clip_gradients(params, opt_cfg.grad_clip)
             if idx in optimizers:
                 fs.set_group_lrs(optimizers[idx], lr)
@@ -361,8 +377,7 @@ def run_stage_a1(cfg):
             for p in params:
                 p.grad = None
             if world > 1:
-                for p in params:
-                    dist.broadcast(p.data, src=idx % world)
+                _bucketed([p.data for p in params], lambda flat, src=idx % world: dist.broadcast(flat, src=src))
         step += 1
         rel = _reduce_metrics({f"rel_{h.index}": (h.losses[-1] if h.losses else 0.0) for h in hooks}, device)
         write({"step": step, "lr": lr, "rel_mean": sum(rel.values()) / max(len(rel), 1),
