@@ -38,7 +38,8 @@ def _worker(rank, world, port, q, exchange, softmax_ranks=0):
         from vdn_minimax_h3_b200.models.hybrid_transform import set_layout
         from vdn_minimax_h3_b200.ops._ext import check_device_error
         from vdn_minimax_h3_b200.parallel.ulysses import UlyssesEngine, init_ulysses
-        cfg = H3Config(hidden_size=256, num_layers=2, num_attention_heads=4, attention_head_dim=128,
+        cfg = H3Config(hidden_size=256, num_layers=2, num_attention_heads=max(4, world),
+                       attention_head_dim=128,
                        in_channels=8, text_dim=96, time_embed_dim=64, time_freq_dim=32,
                        ff_inner_dim=512, num_refiner_layers=1, rope_axes_dim=(32, 48, 48))
         model = tiny_model(RELEASED_HYBRID, cfg)
@@ -127,10 +128,12 @@ def test_symmetric_heap_two_gpus():
 
 @pytest.mark.timeout(300)
 @pytest.mark.parametrize("world,exchange,softmax_ranks", [
-    (2, "nccl", 0), (2, "p2p", 0), (2, "nccl", 1), (2, "p2p", 1), (4, "p2p", 3), (4, "nccl", 1)])
+    (2, "nccl", 0), (2, "p2p", 0), (2, "nccl", 1), (2, "p2p", 1), (4, "p2p", 3), (4, "nccl", 1),
+    (8, "p2p", 0), (8, "p2p", 5), (8, "nccl", 5)])
 def test_ulysses_match_single(world, exchange, softmax_ranks):
     """Plain Ulysses (softmax_ranks 0) and branch parallel: with 4 heads on 4 GPUs,
-    3 softmax ranks hold 2 + 1 + 1 heads and 1 linear rank all 4 (uneven splits)."""
+    3 softmax ranks hold 2 + 1 + 1 heads and 1 linear rank all 4 (uneven splits); on 8 GPUs
+    (8 heads) the shipped B200 layout 5 + 3 (softmax heads 2,2,2,1,1; linear 3,3,2)."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     res = _spawn(_worker, world, exchange, softmax_ranks)
@@ -188,7 +191,7 @@ def _hybrid_worker(rank, world, port, q, tp, fp8):
 
 
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("world,tp,fp8", [(2, 2, False), (2, 2, True), (4, 2, True)])
+@pytest.mark.parametrize("world,tp,fp8", [(2, 2, False), (2, 2, True), (4, 2, True), (8, 2, True)])
 def test_tp_ulysses_match_single(world, tp, fp8):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")

@@ -124,8 +124,15 @@ void launch_adaln_rmsnorm(const void* x, int64_t ldx, const float* w, float eps,
                           int64_t ldt, int shift_col, int scale_col, const int* idx, void* out,
                           int64_t ldo, int T, int D, cudaStream_t stream, void* q = nullptr,
                           int64_t ldq = 0, void* qsf = nullptr);
+// Destinations of the frame sums in peers' memory (see frame_sums_kernel); n == 0: `out`.
+struct FrameSumDst {
+  float* base[kMaxScatterRanks];
+  int64_t offset;
+  int n;
+};
 void launch_frame_sums(const void* x, int64_t ldx, int64_t row0, int64_t nrows, int64_t vs,
-                       int F, int S, int D, float* out, cudaStream_t stream);
+                       int F, int S, int D, float* out, cudaStream_t stream,
+                       const FrameSumDst* dst = nullptr);
 void launch_qk_prep(const void* src, int64_t lds, int T, int H, int d, const float* w, float eps,
                     const float* cosv, const float* sinv, int rot, void* out, int64_t ldo,
                     cudaStream_t stream);

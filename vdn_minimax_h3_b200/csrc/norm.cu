@@ -144,10 +144,14 @@ void launch_adaln_rmsnorm_dst(const void* x, int64_t ldx, const float* w, float 
 // Column sums of video rows grouped by frame: out[f, c] = sum over the rows of frame f that
 // lie in x (x[0] is packed row `row0`, x holds `nrows` rows; frame f is packed rows
 // [vs + f*S, vs + (f+1)*S)). grid (F, ceil(D/256)); lane = 8 columns, warps stride rows.
+// With dst.n > 0 the partial sums go to dst.n destinations instead of `out` (the peers'
+// slots in symmetric memory, plain stores over NVLink): frame f's sums land at
+// dst.base[p] + dst.offset + f * D, and only frames this shard touches are stored -- the
+// slots of the others stay at the zero they were cleared to, so a receiver may sum all slots.
 __global__ void __launch_bounds__(256) frame_sums_kernel(const __nv_bfloat16* __restrict__ x,
                                                          int64_t ldx, int64_t row0, int64_t nrows,
                                                          int64_t vs, int S, int D,
-                                                         float* __restrict__ out) {
+                                                         float* __restrict__ out, FrameSumDst dst) {
   __shared__ float red[8][256];
   const int f = blockIdx.x;
   const int c0 = blockIdx.y * 256;
@@ -175,16 +179,23 @@ __global__ void __launch_bounds__(256) frame_sums_kernel(const __nv_bfloat16* __
     float s = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) s += red[w][t];
-    out[(int64_t)f * D + c0 + t] = s;
+    if (dst.n == 0) {
+      out[(int64_t)f * D + c0 + t] = s;
+    } else if (b > a) {
+      for (int p = 0; p < dst.n; ++p) dst.base[p][dst.offset + (int64_t)f * D + c0 + t] = s;
+    }
   }
 }
 
 void launch_frame_sums(const void* x, int64_t ldx, int64_t row0, int64_t nrows, int64_t vs,
-                       int F, int S, int D, float* out, cudaStream_t stream) {
+                       int F, int S, int D, float* out, cudaStream_t stream,
+                       const FrameSumDst* dst) {
   if (F == 0) return;
   dim3 grid(F, (D + 255) / 256);
+  FrameSumDst d{};
+  if (dst) d = *dst;
   frame_sums_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                              row0, nrows, vs, S, D, out);
+                                              row0, nrows, vs, S, D, out, d);
 }
 
 // One warp per (row, head). Generic head_dim <= 256 (multiple of 2), rotary_dim <= head_dim.

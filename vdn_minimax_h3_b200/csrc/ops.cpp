@@ -402,16 +402,23 @@ void residual_combine(torch::Tensor x, torch::Tensor a, torch::Tensor b,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// peers: optional addresses (int64) of the peers' fp32 slot arrays; the sums go to
+// peers[p] + slot_offset (elements) instead of `out`, frames outside this shard skipped.
 void frame_sums(torch::Tensor x, int64_t row0, int64_t video_start, int64_t F, int64_t S,
-                torch::Tensor out) {
+                torch::Tensor out, std::vector<int64_t> peers, int64_t slot_offset) {
   check_2d_bf16(x, "x");
   const int D = x.size(1);
   TORCH_CHECK(D % 8 == 0, "D must be a multiple of 8");
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() &&
                   out.numel() == F * D, "out must be contiguous fp32 [F, D]");
+  TORCH_CHECK((int)peers.size() <= kMaxScatterRanks, "at most 8 peer destinations");
+  FrameSumDst dst{};
+  dst.n = (int)peers.size();
+  dst.offset = slot_offset;
+  for (int p = 0; p < dst.n; ++p) dst.base[p] = reinterpret_cast<float*>(peers[p]);
   c10::cuda::CUDAGuard g(x.device());
   launch_frame_sums(x.data_ptr(), x.stride(0), row0, x.size(0), video_start, (int)F, (int)S, D,
-                    out.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
+                    out.data_ptr<float>(), at::cuda::getCurrentCUDAStream(), &dst);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -816,7 +823,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("residual_combine", &vdn::residual_combine,
         "x += gate[idx] * (partial_a + partial_b + bias)");
   m.def("adaln_rmsnorm", &vdn::adaln_rmsnorm, "RMSNorm * w * (1 + scale[idx]) + shift[idx]");
-  m.def("frame_sums", &vdn::frame_sums, "per-frame fp32 column sums of video rows");
+  m.def("frame_sums", &vdn::frame_sums, "per-frame fp32 column sums of video rows",
+        py::arg("x"), py::arg("row0"), py::arg("video_start"), py::arg("F"), py::arg("S"),
+        py::arg("out"), py::arg("peers") = std::vector<int64_t>{}, py::arg("slot_offset") = 0);
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");
   m.def("window_attention", &vdn::window_attention,
         "tcgen05 window softmax attention over an AttentionPlan (gated epilogue)");

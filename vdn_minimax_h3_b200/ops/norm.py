@@ -52,11 +52,15 @@ def adaln_rmsnorm(x, weight, eps, table, shift_col, scale_col, idx, out=None, fp
     return fp8_out if out is False else out
 
 
-def frame_sums(rows, num_frames, tokens_per_frame, row0=0, video_start=0):
+def frame_sums(rows, num_frames, tokens_per_frame, row0=0, video_start=0, peers=None,
+               slot_offset=0, out=None):
     """fp32 [F, D] per-frame column sums of the video rows found in `rows`.
 
     rows[0] is packed row `row0`; frame f spans packed rows [video_start + f*S, ... + S).
-    A shard that holds part of a frame contributes its part (sum the shards' results)."""
+    A shard that holds part of a frame contributes its part (sum the shards' results).
+    With `peers` (CUDA only: addresses of fp32 arrays, e.g. the ranks' copies of a
+    symmetric-memory buffer) the sums are stored at peers[p] + slot_offset instead, only
+    for the frames this shard touches; `out` is then not written."""
     F_, S = num_frames, tokens_per_frame
     if not rows.is_cuda:
         out = torch.zeros(F_, rows.shape[1], dtype=torch.float32)
@@ -66,8 +70,10 @@ def frame_sums(rows, num_frames, tokens_per_frame, row0=0, video_start=0):
             if b > a:
                 out[f] = rows[a:b].float().sum(0)
         return out
-    out = torch.empty(F_, rows.shape[1], dtype=torch.float32, device=rows.device)
-    ext().frame_sums(rows, int(row0), int(video_start), int(F_), int(S), out)
+    if out is None:
+        out = torch.empty(F_, rows.shape[1], dtype=torch.float32, device=rows.device)
+    ext().frame_sums(rows, int(row0), int(video_start), int(F_), int(S), out,
+                     [int(a) for a in (peers or [])], int(slot_offset))
     return out
 
 

@@ -33,6 +33,7 @@ from vdn_minimax_h3_b200.ops import attention as attn_ops
 from vdn_minimax_h3_b200.ops import gemm
 from vdn_minimax_h3_b200.ops import norm as norm_ops
 from vdn_minimax_h3_b200.ops._ext import error_word, ext
+from vdn_minimax_h3_b200.parallel.head import ShardedHead
 from vdn_minimax_h3_b200.parallel.symmetric import SymmetricHeap
 from vdn_minimax_h3_b200.utils.profiling import SectionTimer
 
@@ -161,6 +162,7 @@ class HybridEngine:
         self.tp_heap = None
         self.sp_heap = None
         self._heap_key = None
+        self.head = ShardedHead()
 
     def _buf(self, name, shape, dtype, device):
         b = self._bufs.get(name)
@@ -419,10 +421,10 @@ class HybridEngine:
         temb_act = torch.nn.functional.silu(temb.float()).to(x.dtype).contiguous()
         for i in range(len(self.engine.blocks)):
             self.block_forward(i, x, temb_act, idx, rope, rope_shard, layout)
-        full = self._buf("gather", (rt.world * rt.C, x.shape[1]), x.dtype, x.device)
-        local = self._buf("gather_local", (rt.C, x.shape[1]), x.dtype, x.device)
-        local[:x.shape[0]].copy_(x)
-        dist.all_gather_into_tensor(full, local)
-        return m.head(full[:T].unsqueeze(0), temb, timestep_indices, video_indices, audio_indices)
+        # N6: the head on this rank's own video / audio rows, outputs gathered
+        bounds = [(min(T, p * rt.C), min(T, (p + 1) * rt.C)) for p in range(rt.world)]
+        with rt.timer.section("head"):
+            return self.head(m, x, bounds, rt.rank, temb, timestep_indices, video_indices,
+                             audio_indices)
 
     __call__ = forward

@@ -6,9 +6,12 @@ is sharded by packed-sequence row (ceil(T/P) rows per rank, the short shard last
 "all rows x local heads" (seq -> heads), every rank runs the window softmax and the linear
 branch over the WHOLE sequence for its H/P heads, and a second all-to-all brings both
 branches' outputs back to the row owners (heads -> seq). The per-frame means the linear
-branch's alpha needs are partial sums per shard, all-reduced (N7 in the reference's
-collective inventory). Embedding, token refiner and the output head run replicated, the
-block residual is all-gathered once at the end.
+branch's alpha needs are partial sums per shard: with exchange="p2p" the frame-sum kernel
+stores each rank's partials straight into every peer's symmetric-memory slot and the
+barrier that already closes the QKV exchange orders them (N7 without a collective); with
+"nccl" they are all-reduced. Embedding and token refiner run replicated; the output head
+runs on each rank's own video / audio rows and only its outputs are gathered
+(parallel/head.py).
 
 `exchange` selects the transport: "nccl" (torch.distributed all_to_all_single, the
 reference's own path, fed by the routed QKV GEMM that packs the send buffer in its
@@ -25,6 +28,7 @@ from vdn_minimax_h3_b200.inference.engine import (InferenceEngine, fused_qk_ok,
 from vdn_minimax_h3_b200.ops import attention as attn_ops
 from vdn_minimax_h3_b200.ops import gemm
 from vdn_minimax_h3_b200.ops import norm as norm_ops
+from vdn_minimax_h3_b200.parallel.head import ShardedHead
 from vdn_minimax_h3_b200.utils.profiling import SectionTimer
 
 
@@ -158,6 +162,8 @@ class UlyssesEngine:
         self._bufs = {}
         self._routes = {}
         self.heap = None
+        self._heap_key = self._fsum_key = None
+        self.head = ShardedHead(runtime.group)
 
     def _buf(self, name, shape, dtype, device):
         b = self._bufs.get(name)
@@ -232,20 +238,35 @@ class UlyssesEngine:
                     route.place(lo_c, slab[:, offs[name][0]:offs[name][0] + width], plane=plane)
         return route
 
-    def _ensure_heap(self, dev, C, W, kcat, dtype):
-        key = (C, W, kcat, dtype)
-        if self.heap is not None and self._heap_key == key:
-            return
-        if self.heap is not None:
-            self.heap.close()
-        from vdn_minimax_h3_b200.parallel.symmetric import SymmetricHeap
-        P = self.rt.world_size
-        specs = [((P, C, W), dtype), ((C, kcat), dtype)]
-        self.heap = SymmetricHeap(SymmetricHeap.required_bytes(specs), self.rt.group, dev)
-        self.heap.alloc("recv", (P, C, W), dtype)
-        self.heap.alloc("cat", (C, kcat), dtype)
-        self._heap_key = key
-        self._routes.clear()
+    def _ensure_heap(self, dev, C, W, kcat, dtype, frames=None):
+        """Symmetric buffers of the fused exchanges: `recv` (seq -> heads slabs), `cat` (the
+        O-projection input the attention / readout epilogues scatter into) and, when
+        `frames` = (F, D, geometry key) is given, `fsum`: [P, F, D] fp32 slots, slot p
+        holding rank p's per-frame partial sums (zeroed whenever the frame geometry
+        changes; a rank only stores the frames its shard touches)."""
+        fshape = None if frames is None else tuple(frames[:2])
+        key = (C, W, kcat, dtype, fshape)
+        if self.heap is None or self._heap_key != key:
+            if self.heap is not None:
+                self.heap.close()
+            from vdn_minimax_h3_b200.parallel.symmetric import SymmetricHeap
+            P = self.rt.world_size
+            specs = [((P, C, W), dtype), ((C, kcat), dtype)]
+            if fshape is not None:
+                specs.append(((P,) + fshape, torch.float32))
+            self.heap = SymmetricHeap(SymmetricHeap.required_bytes(specs), self.rt.group, dev)
+            self.heap.alloc("recv", (P, C, W), dtype)
+            self.heap.alloc("cat", (C, kcat), dtype)
+            if fshape is not None:
+                self.heap.alloc("fsum", (P,) + fshape, torch.float32)
+            self._heap_key = key
+            self._fsum_key = None
+            self._routes.clear()
+        if frames is not None and self._fsum_key != frames:
+            # every rank clears its own slots; the barrier keeps peers' stores after that
+            self.heap.local("fsum").zero_()
+            self.heap.barrier()
+            self._fsum_key = frames
 
     def close(self):
         if self.heap is not None:
@@ -287,11 +308,6 @@ class UlyssesEngine:
             norm_ops.adaln_rmsnorm(x, pb.norm1, pb.eps, table, 0, D, adaln_idx,
                                    out=n1 if (linear_on or not f8) else False,
                                    fp8_out=(nq, nsf) if f8 else None)
-        work = None
-        if linear_on:
-            fsum = norm_ops.frame_sums(n1, layout.num_frames, layout.tokens_per_frame, a0,
-                                       layout.video_start)
-            work = rt.all_reduce(fsum, async_op=True)
         c = pb.cols
         cos, sin = rope
         layouts, W = self._layouts(pb)
@@ -299,9 +315,27 @@ class UlyssesEngine:
         kind, h0, h1 = rt.branch_of(r)
         run_softmax, run_linear = kind != "linear", kind != "softmax"
         kcat_max = 2 * H * d
+        if p2p:
+            F_ = layout.num_frames if layout is not None else 0
+            frames = ((F_, D, layout.tokens_per_frame, layout.video_start, T)
+                      if layout is not None else None)
+            self._ensure_heap(dev, C, W, kcat_max, x.dtype, frames)
+        work = fsum = None
+        if linear_on:
+            if p2p:
+                # N7 over peer memory: this shard's partials go straight into slot r of
+                # every rank's `fsum`; the dispatch barrier below orders them
+                F_, S_ = layout.num_frames, layout.tokens_per_frame
+                norm_ops.frame_sums(n1, F_, S_, a0, layout.video_start,
+                                    peers=[self.heap.peer("fsum", p).data_ptr() for p in range(P)],
+                                    slot_offset=r * F_ * D,
+                                    out=self._buf("fsum_unused", (F_, D), torch.float32, dev))
+            else:
+                fsum = norm_ops.frame_sums(n1, layout.num_frames, layout.tokens_per_frame, a0,
+                                           layout.video_start)
+                work = rt.all_reduce(fsum, async_op=True)
         # ---- seq -> heads, fused into the QKV GEMM epilogue
         if p2p:
-            self._ensure_heap(dev, C, W, kcat_max, x.dtype)
             recv = self.heap.local("recv")
             key = ("p2p", tuple(sorted(c.items())), rows)
             route = self._routes.get(key)
@@ -361,7 +395,10 @@ class UlyssesEngine:
                     d ** -0.5, gate_logits=fv("sgate", h0, Hp) if pb.has_sgate else None,
                     out=attn_out, scatter=scat(h0 * d, 0) if p2p else None)
         if linear_on:
-            work.wait()
+            if not p2p:
+                work.wait()
+            elif run_linear:
+                fsum = self.heap.local("fsum").sum(0)     # ordered by the dispatch barrier
         if pb.hybrid and run_linear:
             if linear_on:
                 if not p2p:
@@ -455,10 +492,11 @@ class UlyssesEngine:
         temb_act = torch.nn.functional.silu(temb.float()).to(x.dtype).contiguous()
         for i in range(len(self.engine.blocks)):
             self.block_forward(i, x, temb_act, idx, rope_l, layout)
-        full = self._buf("gather", (rt.world_size * rt.rows, x.shape[1]), x.dtype, x.device)
-        local = self._buf("gather_local", (rt.rows, x.shape[1]), x.dtype, x.device)
-        local[:x.shape[0]].copy_(x)
-        rt.all_gather_rows(local, full)
-        return m.head(full[:T].unsqueeze(0), temb, timestep_indices, video_indices, audio_indices)
+        # N6: the head on this rank's own video / audio rows, outputs gathered
+        starts = [sum(rt.splits[:p]) for p in range(rt.world_size)]
+        bounds = [(s0, s0 + n) for s0, n in zip(starts, rt.splits)]
+        with rt.timer.section("head"):
+            return self.head(m, x, bounds, rt.rank, temb, timestep_indices, video_indices,
+                             audio_indices)
 
     __call__ = forward
