@@ -49,6 +49,12 @@ def parse(argv=None):
     p.add_argument("--no-offload", dest="offload", action="store_false",
                    help="keep checkpointed activations on the GPU (the Stage B default, "
                         "distributed.offload_activations=true, saves them to pinned host memory)")
+    p.add_argument("--ac", choices=("block", "two-level"), default="block",
+                   help="activation checkpointing: per block (BASELINE config 4), or per block "
+                        "with the attention and feed-forward as inner regions")
+    p.add_argument("--num-layers", type=int, default=None,
+                   help="diagnostic only: fewer DiT blocks (the printed number is then not the "
+                        "benchmark's)")
     p.add_argument("--tiny", action="store_true", help="two-block model (CPU tests only)")
     return p.parse_args(argv)
 
@@ -92,6 +98,8 @@ def main(argv=None):
     torch.manual_seed(args.seed)
 
     cfg = h3_tiny_config() if args.tiny else h3_full_config()
+    if args.num_layers:
+        cfg.num_layers = args.num_layers
     hybrid = TINY_HYBRID if args.tiny else RELEASED_HYBRID
     t0 = time.perf_counter()
     spec = make_spec(cfg, hybrid, dtype="float32" if args.tiny else "bfloat16")
@@ -103,9 +111,10 @@ def main(argv=None):
     model.to(device)
     if world > 1 or cuda:
         # one GPU is a 1-rank FSDP2 mesh: bf16 compute with fp32 trainables, as on N ranks
-        fs.shard_model(model, device, None, activation_checkpointing=True)
+        fs.shard_model(model, device, None, activation_checkpointing=True,
+                       split_ac=args.ac == "two-level")
     else:
-        enable_block_checkpointing(model, split=True)
+        enable_block_checkpointing(model, split=args.ac == "two-level")
     groups = fs.build_param_groups(model, 1e-4, big_scale=0.4, small_scale=2.0, lora_scale=1.0)
     optimizer = torch.optim.AdamW(groups, lr=1e-4, weight_decay=0.0)
     trainable = [p for p in model.parameters() if p.requires_grad]
@@ -131,11 +140,18 @@ def main(argv=None):
                              f"(2x + 64 GiB margin); {avail:.0f} GiB available: pass --no-offload "
                              f"or use more ranks")
 
+    saved = {}
+
     def step(i):
         batch = pack_noisy_batch(data[i], device, gens["noise"], gens["sigma"])
         set_layout(model, batch["layout"])
         tv, ta = fs.teacher_velocity(model, batch["inputs"], adapters=True)
+        before = torch.cuda.memory_allocated() if cuda else 0
         sv, sa = fs.student_forward(model, batch["inputs"], args.offload and cuda)
+        if cuda and "per_block_gib" not in saved:
+            # device memory the graph keeps between forward and backward, per block
+            saved["per_block_gib"] = round((torch.cuda.memory_allocated() - before)
+                                           / cfg.num_layers / 2 ** 30, 3)
         loss = F.mse_loss(sv[0].float(), tv) + 0.5 * F.mse_loss(sa[0].float(), ta)
         loss, _ = fs.finite_or_zero(loss)
         loss.backward()
@@ -180,13 +196,16 @@ def main(argv=None):
                        "per_gpu_batch": 1, "latent_frames": shape[1],
                        "latent_hw": list(shape[2:]), "lora_rank": args.lora_rank,
                        "parallelism": f"fsdp2 x{world}" if world > 1 else "single-gpu",
-                       "activation_checkpointing": "per block",
+                       "activation_checkpointing": "per block" if args.ac == "block"
+                       else "per block + attn/ff regions",
+                       "num_layers": cfg.num_layers,
                        "activation_offload": bool(args.offload and cuda)},
             "loss": float(loss.item()) if loss is not None else None,
             "build_s": round(build_s, 1),
         }
         if cuda:
             line["peak_gib"] = round(torch.cuda.max_memory_allocated() / 2 ** 30, 1)
+            line["saved_per_block_gib"] = saved.get("per_block_gib")
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
     return 0

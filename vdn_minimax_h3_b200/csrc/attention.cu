@@ -78,6 +78,7 @@ struct AttnParams {
   int64_t ldo;
   RowScatter scatter;        // optional: rows to their Ulysses owners
   long long* trace;          // optional: clock64 stamps of CTA 0's pipeline events
+  float* lse;                // optional [H, T]: log2-sum-exp of each row's scores (training)
   float scale_log2;          // softmax scale * log2(e)
   int* err;
 };
@@ -619,6 +620,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       const int row = t[0] + qt * AT_BM + r;
       const bool row_ok = row < t[1];
       float gscale = j > 0 ? 1.f / l : 0.f;   // an item without K/V writes zeros
+      // the softmax denominator in the exp2 domain, for the backward: p = 2^(s*c - lse)
+      if (p.lse && row_ok) p.lse[(int64_t)head * p.T + row] = j > 0 ? m_ref + log2f(l) : 0.f;
       if (p.gate && row_ok) gscale *= sigmoidf_(__bfloat162float(p.gate[(int64_t)row * p.ldg + head]));
 #pragma unroll 1
       for (int c = 0; c < AT_D; c += 32) {
@@ -656,7 +659,7 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              int64_t ldv, int T, int H, const int* tiles, int n_tiles,
                              const int* kv, const void* gate, int64_t ldg, void* out,
                              int64_t ldo, float scale, int* err, cudaStream_t stream,
-                             const RowScatter* scatter, long long* trace) {
+                             const RowScatter* scatter, long long* trace, float* lse) {
   if (n_tiles == 0 || H == 0) return;
   static std::atomic<uint64_t> attr{0};
   using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, AttnParams);
@@ -694,6 +697,7 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
   p.scatter = RowScatter{};
   if (scatter) p.scatter = *scatter;
   p.trace = trace;
+  p.lse = lse;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
   const int items = n_tiles * H;

@@ -141,9 +141,33 @@ void launch_window_attention(const void* q, int64_t ldq, const void* k, int64_t 
                              int64_t ldv, int T, int H, const int* tiles, int n_tiles,
                              const int* kv, const void* gate, int64_t ldg, void* out,
                              int64_t ldo, float scale, int* err, cudaStream_t stream,
-                             const RowScatter* scatter = nullptr, long long* trace = nullptr);
+                             const RowScatter* scatter = nullptr, long long* trace = nullptr,
+                             float* lse = nullptr);
 
 void attention_set_variant(int v);
+
+// Training backward of the window attention (attention_bwd.cu). q/k/v/dout/o and the
+// gradients are [T, H*128] bf16 row views; lse (log2 domain, from the forward) and delta
+// (written by the dq pass) are fp32 [H, T]. q_tiles/kv_ranges: the forward plan (query
+// tiles of <= 128 rows here); k_tiles/q_ranges: the transposed plan (key tiles).
+struct AttnBwdArgs {
+  const void *q, *k, *v, *o, *dout;
+  int64_t ldq, ldk, ldv, ldo, lddo;
+  void *dq, *dk, *dv;
+  int64_t lddq, lddk, lddv;
+  const float* lse;
+  float* delta;
+  int T, H;
+  const int* q_tiles;
+  int n_q_tiles;
+  const int* kv_ranges;
+  const int* k_tiles;
+  int n_k_tiles;
+  const int* q_ranges;
+  float scale;
+  int* err;
+};
+void launch_attention_bwd(const AttnBwdArgs& a, cudaStream_t stream);
 int attention_variant();
 
 // Symmetric memory (symmetric.cu): IPC-exported regions and the peer flag barrier.

@@ -491,8 +491,11 @@ void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
                       torch::Tensor kv, c10::optional<torch::Tensor> gate, torch::Tensor out,
                       double scale, torch::Tensor err, std::vector<int64_t> scatter_base,
                       int64_t scatter_row0, int64_t scatter_rows,
-                      c10::optional<torch::Tensor> trace) {
+                      c10::optional<torch::Tensor> trace, c10::optional<torch::Tensor> lse) {
   const int64_t T = q.size(0), H = q.size(1);
+  if (lse)
+    TORCH_CHECK(lse->is_cuda() && lse->scalar_type() == at::kFloat && lse->is_contiguous() &&
+                    lse->numel() == H * T, "lse must be contiguous fp32 [H, T]");
   check_heads(q, "q", T, H);
   check_heads(k, "k", T, H);
   check_heads(v, "v", T, H);
@@ -520,7 +523,49 @@ void window_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
                           v.stride(0), (int)T, (int)H, tiles.data_ptr<int>(), (int)tiles.size(0),
                           kv.data_ptr<int>(), gp, ldg, out.data_ptr(), out.stride(0),
                           (float)scale, err_ptr(err), at::cuda::getCurrentCUDAStream(), &sc,
-                          trace ? reinterpret_cast<long long*>(trace->data_ptr<int64_t>()) : nullptr);
+                          trace ? reinterpret_cast<long long*>(trace->data_ptr<int64_t>()) : nullptr,
+                          lse ? lse->data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Window-attention backward: gradients of q, k, v (ungated attention) from dout, the
+// forward output o and its lse; delta [H, T] is scratch the dq pass fills for the dkv pass.
+void window_attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+                          torch::Tensor dout, torch::Tensor lse, torch::Tensor delta,
+                          torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
+                          torch::Tensor q_tiles, torch::Tensor kv_ranges, torch::Tensor k_tiles,
+                          torch::Tensor q_ranges, double scale, torch::Tensor err) {
+  const int64_t T = q.size(0), H = q.size(1);
+  for (auto* t : {&q, &k, &v, &o, &dout, &dq, &dk, &dv}) check_heads(*t, "attention tensor", T, H);
+  TORCH_CHECK(lse.is_cuda() && lse.scalar_type() == at::kFloat && lse.is_contiguous() &&
+                  lse.numel() == H * T, "lse must be contiguous fp32 [H, T]");
+  TORCH_CHECK(delta.is_cuda() && delta.scalar_type() == at::kFloat && delta.is_contiguous() &&
+                  delta.numel() == H * T, "delta must be contiguous fp32 [H, T]");
+  for (auto* t : {&q_tiles, &k_tiles})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kInt && t->is_contiguous() && t->dim() == 2 &&
+                    t->size(1) == 4, "tiles must be int32 [n, 4]");
+  for (auto* t : {&kv_ranges, &q_ranges})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kInt && t->is_contiguous() && t->dim() == 2 &&
+                    t->size(1) == 8, "ranges must be int32 [n_seg, 8]");
+  AttnBwdArgs a{};
+  a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.o = o.data_ptr(); a.dout = dout.data_ptr();
+  a.ldq = q.stride(0); a.ldk = k.stride(0); a.ldv = v.stride(0); a.ldo = o.stride(0); a.lddo = dout.stride(0);
+  a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr();
+  a.lddq = dq.stride(0); a.lddk = dk.stride(0); a.lddv = dv.stride(0);
+  a.lse = lse.data_ptr<float>();
+  a.delta = delta.data_ptr<float>();
+  a.T = (int)T;
+  a.H = (int)H;
+  a.q_tiles = q_tiles.data_ptr<int>();
+  a.n_q_tiles = (int)q_tiles.size(0);
+  a.kv_ranges = kv_ranges.data_ptr<int>();
+  a.k_tiles = k_tiles.data_ptr<int>();
+  a.n_k_tiles = (int)k_tiles.size(0);
+  a.q_ranges = q_ranges.data_ptr<int>();
+  a.scale = (float)scale;
+  a.err = err_ptr(err);
+  c10::cuda::CUDAGuard g(q.device());
+  launch_attention_bwd(a, at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -829,9 +874,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");
   m.def("window_attention", &vdn::window_attention,
         "tcgen05 window softmax attention over an AttentionPlan (gated epilogue)");
+  m.def("window_attention_bwd", &vdn::window_attention_bwd,
+        "tcgen05 window attention backward (dq pass over the plan, dk/dv pass over the "
+        "transposed plan)");
   m.def("attention_set_variant", &vdn::attention_set_variant,
-        "window attention kernel variant: bits 0-1 = polynomial exps per 8, bit 2 = "
-        "speculative running max");
+        "window attention exponential-pass variant 0..7 (1: packed f32x2, the default; 2-4: "
+        "polynomial share; 5-7: timing diagnostics)");
   m.def("attention_variant", &vdn::attention_variant, "current window attention variant");
   m.def("gemm_fp8_set_trace", [](c10::optional<torch::Tensor> t) {
     vdn::gemm_fp8_set_trace(t ? reinterpret_cast<long long*>(t->data_ptr()) : nullptr);

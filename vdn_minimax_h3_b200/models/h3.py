@@ -189,9 +189,15 @@ class H3Attention(nn.Module):
     def forward(self, hidden_states, rotary_emb=None, attention_mask=None):
         x = hidden_states[0]
         q, k, v, _ = self.project(x, rotary_emb)
-        o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
-                                           v.transpose(0, 1)[None], attn_mask=attention_mask)
-        o = o[0].transpose(0, 1).reshape(x.shape[0], -1)
+        from vdn_minimax_h3_b200.ops import attention_grad as ag
+        if attention_mask is None and ag.ATTENTION_KERNELS and ag.kernel_path_ok(q, k, v):
+            # dense attention (the teacher trunk, the refiner) on the sm_100a kernels
+            o = ag.window_attention_train(q, k, v, ag.dense_plan(x.shape[0], x.device),
+                                          q.shape[-1] ** -0.5).reshape(x.shape[0], -1)
+        else:
+            o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                               v.transpose(0, 1)[None], attn_mask=attention_mask)
+            o = o[0].transpose(0, 1).reshape(x.shape[0], -1)
         return self.to_out[1](self.to_out[0](o)).unsqueeze(0)
 
 

@@ -76,7 +76,14 @@ class HybridAttention(nn.Module):
         covered = layout is None or full_cover(bounds, layout.num_frames)
         scale = self.head_dim ** -0.5
         q, k, v, raw = self.orig.project(x, rotary_emb)
-        if covered:
+        from vdn_minimax_h3_b200.ops import attention_grad as ag
+        if ag.ATTENTION_KERNELS and ag.kernel_path_ok(q, k, v):
+            # sm_100a forward + backward kernels over the analytic plan (dense when covered)
+            plan = (ag.dense_plan(x.shape[0], x.device) if covered
+                    else ag.window_plan(layout, bounds, self.anchor_frames, x.device))
+            soft = ag.window_attention_train(q, k, v, plan, scale)
+            linear_active = not covered
+        elif covered:
             import torch.nn.functional as F
             soft = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
                                                   v.transpose(0, 1)[None])[0].transpose(0, 1)

@@ -162,8 +162,9 @@ class AttentionPlan:
     """
 
     def __init__(self, layout, bounds, anchor_frames="none", device="cpu", block_q=256,
-                 dense=False):
-        self.segments = plan_segments(layout, bounds, anchor_frames, dense=dense)
+                 dense=False, segments=None):
+        self.segments = (segments if segments is not None
+                         else plan_segments(layout, bounds, anchor_frames, dense=dense))
         kv = torch.zeros(len(self.segments), 2 * MAX_KV_RANGES, dtype=torch.int32)
         tiles, cost = [], []
         for i, seg in enumerate(self.segments):
@@ -174,11 +175,58 @@ class AttentionPlan:
                 tiles.append((q0, min(q0 + block_q, seg.q_end), i, kv_len))
                 cost.append(kv_len)
         order = sorted(range(len(tiles)), key=lambda t: -cost[t])
-        self.tiles = torch.tensor([tiles[t] for t in order], dtype=torch.int32).to(device)
+        self.tiles = torch.tensor([tiles[t] for t in order], dtype=torch.int32).view(-1, 4).to(device)
         self.kv = kv.to(device)
         self.num_tiles = len(tiles)
         self.kv_rows_total = sum((t[1] - t[0]) * t[3] for t in tiles)
 
+    @classmethod
+    def dense_rows(cls, T, device="cpu", block_q=256):
+        """Every row attends to every row (the dense teacher) -- no layout needed."""
+        return cls(None, None, device=device, block_q=block_q, segments=[Segment(0, T, [(0, T)])])
+
     def flops(self, heads, head_dim):
         """Useful attention FLOPs (QK^T and PV) of the plan."""
         return 4.0 * self.kv_rows_total * heads * head_dim
+
+
+def transpose_segments(segments: List[Segment]) -> List[Segment]:
+    """The same attention pattern seen from the keys: for every maximal run of key rows
+    attended by the same query rows, a Segment(k_start, k_end, query ranges) (the `kv`
+    field then holds the <= MAX_KV_RANGES merged QUERY ranges)."""
+    cuts = sorted({x for seg in segments for a, b in seg.kv for x in (a, b)})
+    runs = []
+    for lo, hi in zip(cuts[:-1], cuts[1:]):
+        qs = _merge([(seg.q_start, seg.q_end) for seg in segments
+                     if any(a <= lo and hi <= b for a, b in seg.kv)])
+        if not qs:
+            continue
+        if runs and runs[-1].q_end == lo and runs[-1].kv == qs:
+            runs[-1] = Segment(runs[-1].q_start, hi, qs)
+        else:
+            runs.append(Segment(lo, hi, qs))
+    for r in runs:
+        if len(r.kv) > MAX_KV_RANGES:
+            raise ValueError(f"keys {r.q_start}:{r.q_end} are read by {len(r.kv)} query ranges "
+                             f"> {MAX_KV_RANGES}")
+    return runs
+
+
+class TrainingAttentionPlan:
+    """The three tables the training attention needs for one (layout, bounds): the forward
+    plan (256-row items), the dq-pass plan (the same segments in 128-row query tiles) and
+    the dk/dv-pass plan (128-row key tiles over the transposed segments)."""
+
+    def __init__(self, segments: List[Segment], device):
+        self.forward = AttentionPlan(None, None, device=device, segments=segments)
+        self.dq = AttentionPlan(None, None, device=device, block_q=128, segments=segments)
+        self.dkv = AttentionPlan(None, None, device=device, block_q=128,
+                                 segments=transpose_segments(segments))
+
+    @classmethod
+    def for_layout(cls, layout, bounds, anchor_frames, device, dense=False):
+        return cls(plan_segments(layout, bounds, anchor_frames, dense=dense), device)
+
+    @classmethod
+    def dense_rows(cls, T, device):
+        return cls([Segment(0, T, [(0, T)])], device)

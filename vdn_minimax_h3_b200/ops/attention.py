@@ -31,12 +31,14 @@ def window_attention_reference(q, k, v, plan, scale, gate_logits=None):
     return out.reshape(T, H * d).to(q.dtype)
 
 
-def window_attention(q, k, v, plan, scale, gate_logits=None, out=None, scatter=None, trace=None):
+def window_attention(q, k, v, plan, scale, gate_logits=None, out=None, scatter=None, trace=None,
+                     lse=None):
     """q, k, v: [T, H, d] views (row stride allowed, d contiguous). out: [T, H*d] view.
 
     scatter = (bases, row0, rows_per_rank) sends output row t to its Ulysses owner
     r = (row0 + t) // rows_per_rank instead: bases[r] is the address of that owner's
-    destination at shard row 0 (this rank's first column), rows keep `out`'s row stride."""
+    destination at shard row 0 (this rank's first column), rows keep `out`'s row stride.
+    lse: optional fp32 [H, T] receiving each row's log2-sum-exp (training forward)."""
     if scatter is not None and not q.is_cuda:
         raise ValueError("row-owner scatter needs CUDA tensors")
     if not q.is_cuda:
@@ -50,7 +52,7 @@ def window_attention(q, k, v, plan, scale, gate_logits=None, out=None, scatter=N
         out = torch.empty(T, H * d, dtype=q.dtype, device=q.device)
     bases, row0, rows = scatter if scatter is not None else ([], 0, 0)
     ext().window_attention(q, k, v, plan.tiles, plan.kv, gate_logits, out, float(scale),
-                           error_word(q.device), list(bases), int(row0), int(rows), trace)
+                           error_word(q.device), list(bases), int(row0), int(rows), trace, lse)
     return out
 
 
