@@ -1,8 +1,22 @@
-"""Training throughput: Stage B (LoRA `default` + linear branch against the dense teacher).
+"""Training throughput: Stage B (LoRA `default` + linear branch against the dense teacher)
+or Stage DMD (few-step generator, frozen real score, trainable fake score on one model).
 
-    python bench_train.py [--steps K --warmup W]                                  # 1 GPU
+    python bench_train.py [--stage b|dmd] [--steps K --warmup W] [--kernels on|off]   # 1 GPU
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench_train.py --gpus N --steps K --warmup W            # N GPUs, FSDP2
+
+`--kernels off` is the labelled baseline arm: the same model and loop with every sm_100a
+training kernel switched off (attention through PyTorch SDPA, the linear branch's scans /
+SPD factor / short conv and the AdaLN norm in eager PyTorch), i.e. PyTorch FSDP2 + NCCL +
+cuBLAS / cuDNN.
+
+Stage DMD (`--stage dmd`): each step is one DMD2 sub-iteration on every rank -- the
+generator's own rollout of k grid steps (k the rank-shared index of that iteration, 8-step
+grid), then on a generator turn the DM-loss update of `turbo` (generator x0 with a graph,
+real and fake score x0) and on every turn the fake score's flow-matching update
+(training.trainers.dmd_sub_iteration). Timed steps follow the 1 : 5 turn schedule from the
+first generator turn; the line reports each turn kind's time and the whole-cycle rate
+(1 generator + 5 fake sub-iterations).
 
 One step on every rank = one synthetic clip (per-GPU batch 1) of the BASELINE training
 shape: 81 latent frames at the inference spatial latent size (48 x 84 -> 24 x 42 tokens per
@@ -55,6 +69,9 @@ def parse(argv=None):
     p.add_argument("--num-layers", type=int, default=None,
                    help="diagnostic only: fewer DiT blocks (the printed number is then not the "
                         "benchmark's)")
+    p.add_argument("--stage", choices=("b", "dmd"), default="b")
+    p.add_argument("--kernels", choices=("on", "off"), default="on",
+                   help="off: the labelled baseline (PyTorch / cuBLAS / cuDNN for every op)")
     p.add_argument("--tiny", action="store_true", help="two-block model (CPU tests only)")
     return p.parse_args(argv)
 
@@ -82,6 +99,11 @@ def main(argv=None):
     from vdn_minimax_h3_b200.training.dataset import SyntheticLatentDataset
     from vdn_minimax_h3_b200.utils.activation_checkpointing import enable_block_checkpointing
 
+    if args.kernels == "off":
+        from vdn_minimax_h3_b200.ops import attention_grad, linear_branch_grad, norm_grad
+        attention_grad.ATTENTION_KERNELS = False
+        linear_branch_grad.USE_KERNELS = False
+        norm_grad.NORM_KERNELS = False
     cuda = torch.cuda.is_available()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local) if cuda else torch.device("cpu")
@@ -105,7 +127,15 @@ def main(argv=None):
     spec = make_spec(cfg, hybrid, dtype="float32" if args.tiny else "bfloat16")
     model = build_model(spec, device="cpu" if args.tiny else device, init="random", seed=args.seed)
     inject_lora(model, "default", args.lora_rank, args.lora_rank, LORA_TARGETS)
-    select = fs.trainable_select(include_lora=True)
+    if args.stage == "dmd":
+        # generator adapter `turbo` (trainable), fake-score adapter `fake` (trainable, B = 0);
+        # the backbone, the hybrid branch and `default` are frozen (the Stage DMD trainables)
+        inject_lora(model, "turbo", args.lora_rank, args.lora_rank, LORA_TARGETS, init_b_zero=False)
+        inject_lora(model, "fake", 128, 128, LORA_TARGETS, init_b_zero=True)
+        select = lambda n, p: ".lora_A.turbo." in n or ".lora_B.turbo." in n or \
+            ".lora_A.fake." in n or ".lora_B.fake." in n  # noqa: E731
+    else:
+        select = fs.trainable_select(include_lora=True)
     for n, p in model.named_parameters():
         p.requires_grad_(select(n, p))
     model.to(device)
@@ -115,8 +145,14 @@ def main(argv=None):
                        split_ac=args.ac == "two-level")
     else:
         enable_block_checkpointing(model, split=args.ac == "two-level")
-    groups = fs.build_param_groups(model, 1e-4, big_scale=0.4, small_scale=2.0, lora_scale=1.0)
-    optimizer = torch.optim.AdamW(groups, lr=1e-4, weight_decay=0.0)
+    if args.stage == "dmd":
+        gen_params = [p for n, p in model.named_parameters() if p.requires_grad and ".turbo." in n]
+        fake_params = [p for n, p in model.named_parameters() if p.requires_grad and ".fake." in n]
+        optimizer = torch.optim.AdamW([{"params": gen_params}, {"params": fake_params}], lr=1e-5,
+                                      weight_decay=0.0)
+    else:
+        groups = fs.build_param_groups(model, 1e-4, big_scale=0.4, small_scale=2.0, lora_scale=1.0)
+        optimizer = torch.optim.AdamW(groups, lr=1e-4, weight_decay=0.0)
     trainable = [p for p in model.parameters() if p.requires_grad]
     gens = fs.make_generators(args.seed, rank, device)
     if args.tiny:
@@ -160,33 +196,71 @@ def main(argv=None):
         optimizer.zero_grad(set_to_none=True)
         return loss
 
+    kinds = {}
+    if args.stage == "dmd":
+        from vdn_minimax_h3_b200.training import dmd as dmd_lib
+        from vdn_minimax_h3_b200.training.batch import PackedPrompt, initial_noise
+        from vdn_minimax_h3_b200.training.trainers import dmd_sub_iteration
+        roles = dmd_lib.Roles(model, "vdn", "default", "turbo", "fake")
+        schedule = dmd_lib.FewStepSchedule(8, 12.0, 3.0)
+        video_shape = shape
+
+        def turn_of(i):
+            # warm-up: one generator and one fake turn (when W >= 2), then the 1:5 schedule
+            # from its first generator turn
+            if i < args.warmup:
+                return dmd_lib.GENERATOR_TURN if i == 0 else dmd_lib.FAKE_TURN
+            return dmd_lib.turn(i - args.warmup, 0, 5)
+
+        def step(i):
+            packed = PackedPrompt(data[i]["prompt_embeds"], video_shape, n_audio, device)
+            set_layout(model, packed.layout)
+            k = dmd_lib.shared_rollout_index(args.seed, i, schedule.num_steps)
+            v0, a0 = initial_noise(video_shape, n_audio, gens["noise"], device)
+            xv, xa = dmd_lib.rollout(model, roles, schedule, packed, v0, a0, k)
+            rec = dmd_sub_iteration(model, roles, schedule, packed, xv, xa, k, turn_of(i), gens,
+                                    optimizer, gen_params, fake_params, gen_lr=1e-5, fake_lr=1e-5,
+                                    u_range=(0.02, 0.98), shifts=(12.0, 3.0), audio_weight=0.5,
+                                    clips=(1.0, 1.0))
+            kinds.setdefault("rollout_k", []).append(k)
+            return torch.tensor(rec["fake_loss"])
+
     from vdn_minimax_h3_b200.utils.profiling import step_profiler
     for i in range(args.warmup):
         with step_profiler(i + 1, row_limit=40):   # VDN_PROF_STEP=n: warm-up step n only
             step(i)
+    kinds.clear()
     dist.barrier()
+    per_step = []
     if cuda:
         torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        events[0].record()
     else:
         t_start = time.perf_counter()
     loss = None
     for i in range(args.steps):
+        t_i = time.perf_counter()
         loss = step(args.warmup + i)
+        if cuda:
+            events[i + 1].record()
+        else:
+            per_step.append((time.perf_counter() - t_i) * 1e3)
     if cuda:
-        end.record()
         torch.cuda.synchronize()
-        ms = start.elapsed_time(end)
+        per_step = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
+        ms = events[0].elapsed_time(events[-1])
     else:
         ms = (time.perf_counter() - t_start) * 1e3
     dist.barrier()
-    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    t = torch.tensor([ms] + per_step, dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms, per_step = float(t[0].item()), [float(x) for x in t[1:].tolist()]
     if rank == 0:
+        stage_name = ("Stage DMD: DMD2 sub-iterations, generator:fake 1:5, 8-step grid"
+                      if args.stage == "dmd" else "Stage B: LoRA + hybrid branch")
         line = {
-            "metric": "train samples/s (Stage B: LoRA + hybrid branch, FSDP2)",
+            "metric": f"train samples/s ({stage_name}, FSDP2)",
             "value": round(world * args.steps / (ms / 1e3), 4), "unit": "samples/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 1), "higher_is_better": True, "scaling": "weak",
@@ -201,8 +275,20 @@ def main(argv=None):
                        "num_layers": cfg.num_layers,
                        "activation_offload": bool(args.offload and cuda)},
             "loss": float(loss.item()) if loss is not None else None,
+            "kernels": args.kernels,
+            "step_ms": [round(x, 1) for x in per_step],
             "build_s": round(build_s, 1),
         }
+        if args.stage == "dmd" and per_step:
+            from vdn_minimax_h3_b200.training import dmd as dmd_lib
+            gen = [ms_i for j, ms_i in enumerate(per_step) if dmd_lib.turn(j, 0, 5) == dmd_lib.GENERATOR_TURN]
+            fake = [ms_i for j, ms_i in enumerate(per_step) if dmd_lib.turn(j, 0, 5) != dmd_lib.GENERATOR_TURN]
+            if gen and fake:
+                tg, tf = sum(gen) / len(gen), sum(fake) / len(fake)
+                line["generator_turn_ms"], line["fake_turn_ms"] = round(tg, 1), round(tf, 1)
+                # one 1:5 cycle = 1 generator + 5 fake sub-iterations, one clip per rank each
+                line["cycle_samples_per_s"] = round(world * 6 / ((tg + 5 * tf) / 1e3), 4)
+            line["rollout_k"] = kinds.get("rollout_k")
         if cuda:
             line["peak_gib"] = round(torch.cuda.max_memory_allocated() / 2 ** 30, 1)
             line["saved_per_block_gib"] = saved.get("per_block_gib")

@@ -33,3 +33,21 @@ def test_bench_train_tiny(world):
     out = json.loads(lines[0])
     assert out["n_gpus"] == world and out["steps"] == 1 and out["value"] > 0
     assert out["higher_is_better"] is True and out["loss"] == out["loss"]
+
+
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("world,kernels", [(1, "on"), (2, "off")])
+def test_bench_train_dmd_tiny(world, kernels):
+    """--stage dmd times DMD2 sub-iterations on the 1:5 turn schedule and reports each turn
+    kind and the cycle rate; --kernels off (the labelled baseline arm) runs the same loop."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(_port()), "bench_train.py",
+           "--tiny", "--stage", "dmd", "--steps", "2", "--warmup", "2", "--gpus", str(world),
+           "--kernels", kernels]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=580)
+    assert r.returncode == 0, r.stderr[-3000:]
+    out = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][0])
+    assert "Stage DMD" in out["metric"] and out["kernels"] == kernels
+    assert len(out["step_ms"]) == 2 and out["generator_turn_ms"] > 0 and out["fake_turn_ms"] > 0
+    assert out["cycle_samples_per_s"] > 0 and len(out["rollout_k"]) == 2

@@ -236,6 +236,8 @@ def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gemm", action="store_true")
     p.add_argument("--attention", action="store_true")
+    p.add_argument("--attention-train", action="store_true",
+                   help="training attention forward + backward at the Stage-B shape vs SDPA")
     p.add_argument("--attention-ab", action="store_true",
                    help="window attention against cuDNN / flash SDPA on the same plan segments")
     p.add_argument("--trace-variant", type=int, default=None,
@@ -264,6 +266,9 @@ def main(argv=None):
     if a.attention:
         from vdn_minimax_h3_b200.ops.attention import bench_attention
         bench_attention(timed)
+    if a.attention_train:
+        from vdn_minimax_h3_b200.ops.attention_grad import bench_attention_train
+        bench_attention_train(timed)
     if a.attention_ab:
         from vdn_minimax_h3_b200.ops.attention import bench_attention_vs_cudnn
         bench_attention_vs_cudnn(timed)

@@ -97,3 +97,66 @@ def dense_plan(T, device):
     """TrainingAttentionPlan of T rows that all attend to each other (dense teacher)."""
     from vdn_minimax_h3_b200.models.window import TrainingAttentionPlan
     return _cached(("dense", int(T), str(device)), lambda: TrainingAttentionPlan.dense_rows(T, device))
+
+
+def bench_attention_train(timed, frames=81, heads=56):  # pragma: no cover - GPU tool
+    """Training attention at the Stage-B shape (81 latent frames, 56 heads, c1 window with
+    anchors): forward + backward of the kernels against autograd of the per-segment SDPA
+    path under cuDNN and flash, and the dense teacher forward against cuDNN SDPA. ms per
+    layer; FLOPs counted as 4 * pairs * d (forward) and 2.5x that (backward)."""
+    import json
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from vdn_minimax_h3_b200.models.layout import SequenceLayout
+    from vdn_minimax_h3_b200.models.window import window_bounds, window_softmax_segments
+    text, audio, S, d = 800, frames * 455 // 102, 1008, HEAD_DIM
+    lay = SequenceLayout(seq_len=text + audio + frames * S, video_start=text + audio,
+                         num_frames=frames, tokens_per_frame=S, frame_height=24, frame_width=42,
+                         text_start=0, text_len=text)
+    T = lay.seq_len
+    bounds = window_bounds(frames, 1, 5)
+    plan = window_plan(lay, bounds, "both", "cuda")
+    fl = plan.forward.flops(heads, d)
+    q, k, v = (torch.randn(T, heads, d, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    up = torch.randn_like(q)
+    qg, kg, vg = (t.clone().requires_grad_() for t in (q, k, v))
+    res = dict(case="attention_train_c1_both", T=T, heads=heads)
+
+    def ours_fwd():
+        with torch.no_grad():
+            window_attention_train(q, k, v, plan, d ** -0.5)
+
+    def ours_fb():
+        window_attention_train(qg, kg, vg, plan, d ** -0.5).backward(up)
+
+    res["ours_fwd_ms"] = timed(ours_fwd)
+    res["ours_fwd_bwd_ms"] = timed(ours_fb)
+    res["ours_bwd_ms"] = res["ours_fwd_bwd_ms"] - res["ours_fwd_ms"]
+    res["ours_bwd_tflops"] = 2.5 * fl / res["ours_bwd_ms"] / 1e9
+    for name, backend in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION)):
+        def lib_fb():
+            with sdpa_kernel([backend]):
+                window_softmax_segments(qg, kg, vg, lay, bounds, d ** -0.5, "both").backward(up)
+        try:
+            res[f"{name}_segments_fwd_bwd_ms"] = timed(lib_fb)
+        except RuntimeError as e:
+            res[f"{name}_error"] = str(e).splitlines()[0][:160]
+    dplan = dense_plan(T, "cuda")
+    dfl = dplan.forward.flops(heads, d)
+
+    def dense_ours():
+        with torch.no_grad():
+            window_attention_train(q, k, v, dplan, d ** -0.5)
+
+    res["dense_ours_ms"] = timed(dense_ours, iters=3, warmup=1)
+    res["dense_ours_tflops"] = dfl / res["dense_ours_ms"] / 1e9
+    qt, kt, vt = (t.transpose(0, 1)[None] for t in (q, k, v))
+    for name, backend in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION)):
+        def dense_lib():
+            with torch.no_grad(), sdpa_kernel([backend]):
+                torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, scale=d ** -0.5)
+        try:
+            res[f"dense_{name}_ms"] = timed(dense_lib, iters=3, warmup=1)
+        except RuntimeError as e:
+            res[f"dense_{name}_error"] = str(e).splitlines()[0][:160]
+    print(json.dumps(res), flush=True)
+    return res

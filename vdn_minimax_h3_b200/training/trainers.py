@@ -394,6 +394,60 @@ def run_stage_a1(cfg):
 
 
 # ------------------------------------------------------------------------------- DMD
+def dmd_sub_iteration(model, roles, schedule, packed, xv, xa, k, kind, gens, optimizer,
+                      gen_params, fake_params, gen_lr, fake_lr, u_range, shifts, audio_weight,
+                      clips):
+    """One Stage-DMD sub-iteration after the rollout (xv, xa at grid step k): on a generator
+    turn the DM-loss update of `turbo` (generator x0 with a graph, real and fake score x0 at a
+    fresh (x_t, t), the distribution-matching gradient); on every turn the fake score's
+    flow-matching update on the detached generator sample. Optimizer group 0 is the
+    generator's, group 1 the fake score's. Returns the turn's metrics."""
+    rec = {}
+    dev = xv.device
+    if kind == dmd_lib.GENERATOR_TURN:
+        x0v, x0a = dmd_lib.generator_x0(model, roles, schedule, packed, xv, xa, k, build_graph=True)
+        t_v, t_a, _ = sample_paired_timesteps(gens["sigma"], *u_range, *shifts)
+        nv = torch.randn(x0v.shape, generator=gens["noise"], device=dev)
+        na = torch.randn(x0a.shape, generator=gens["noise"], device=dev)
+        xt_v, xt_a = dmd_lib.noised(x0v.detach(), t_v, nv), dmd_lib.noised(x0a.detach(), t_a, na)
+        rv, ra = dmd_lib.score_x0(model, roles, dmd_lib.REAL, packed, xt_v, xt_a, t_v, t_a)
+        fv, fa = dmd_lib.score_x0(model, roles, dmd_lib.FAKE, packed, xt_v, xt_a, t_v, t_a)
+        lv, normv, gapv = dmd_lib.distribution_matching_loss(x0v, rv, fv)
+        la, _, _ = dmd_lib.distribution_matching_loss(x0a, ra, fa)
+        loss, _ = fs.finite_or_zero(lv + audio_weight * la)
+        dmd_lib.require_role(roles, dmd_lib.GENERATOR, "generator backward")
+        loss.backward()
+        for p in fake_params:
+            p.grad = None
+        optimizer.param_groups[0]["lr"] = gen_lr
+        optimizer.param_groups[1]["lr"] = 0.0
+        rec.update(dm_loss=loss.item(), dm_norm_video=normv.item(), dm_gap_video=gapv.item(),
+                   grad_norm_turbo=fs.clip_gradients(gen_params, clips[0]))
+        optimizer.step()
+        optimizer.zero_grad(set_to_none=True)
+        x0v, x0a = x0v.detach(), x0a.detach()
+    else:
+        x0v, x0a = dmd_lib.generator_x0(model, roles, schedule, packed, xv, xa, k, build_graph=False)
+    # fake-score flow-matching update on the (detached) generator sample
+    roles.set(dmd_lib.FAKE)
+    t_v, t_a, _ = sample_paired_timesteps(gens["sigma"], *u_range, *shifts)
+    nv = torch.randn(x0v.shape, generator=gens["noise"], device=dev)
+    na = torch.randn(x0a.shape, generator=gens["noise"], device=dev)
+    vel_v, vel_a = model(**packed.inputs(dmd_lib.noised(x0v, t_v, nv), dmd_lib.noised(x0a, t_a, na), t_v, t_a))
+    floss = dmd_lib.fake_regression_loss(vel_v[0].float(), x0v, nv) + \
+        audio_weight * dmd_lib.fake_regression_loss(vel_a[0].float(), x0a, na)
+    floss, _ = fs.finite_or_zero(floss)
+    floss.backward()
+    for p in gen_params:
+        p.grad = None
+    optimizer.param_groups[0]["lr"] = 0.0
+    optimizer.param_groups[1]["lr"] = fake_lr
+    rec.update(fake_loss=floss.item(), grad_norm_fake=fs.clip_gradients(fake_params, clips[1]))
+    optimizer.step()
+    optimizer.zero_grad(set_to_none=True)
+    return rec
+
+
 def run_stage_dmd(cfg):
     out = cfg.checkpoint.output_dir
     fs.refuse_if_guarded(out, os.path.join(out, "DONE"), cfg.training.ignore_stopped)
@@ -467,49 +521,13 @@ def run_stage_dmd(cfg):
         v0, a0 = initial_noise(video_shape, n_audio, gens["noise"], device)
         xv, xa = dmd_lib.rollout(model, roles, schedule, packed, v0, a0, k)
         rec = {"iteration": iteration, "turn": kind, "rollout_k": k}
+        rec.update(dmd_sub_iteration(
+            model, roles, schedule, packed, xv, xa, k, kind, gens, optimizer, gen_params, fake_params,
+            gen_lr=lr_at(gen_step, gen_sched), fake_lr=lr_at(fake_step, fake_sched),
+            u_range=(d.u_min, d.u_max), shifts=(tb.video_shift, tb.audio_shift),
+            audio_weight=cfg.training.audio_loss_weight, clips=(o.grad_clip, o.fake_grad_clip)))
         if kind == dmd_lib.GENERATOR_TURN:
-            x0v, x0a = dmd_lib.generator_x0(model, roles, schedule, packed, xv, xa, k, build_graph=True)
-            t_v, t_a, u = sample_paired_timesteps(gens["sigma"], d.u_min, d.u_max, tb.video_shift, tb.audio_shift)
-            nv = torch.randn(x0v.shape, generator=gens["noise"], device=device)
-            na = torch.randn(x0a.shape, generator=gens["noise"], device=device)
-            xt_v, xt_a = dmd_lib.noised(x0v.detach(), t_v, nv), dmd_lib.noised(x0a.detach(), t_a, na)
-            rv, ra = dmd_lib.score_x0(model, roles, dmd_lib.REAL, packed, xt_v, xt_a, t_v, t_a)
-            fv, fa = dmd_lib.score_x0(model, roles, dmd_lib.FAKE, packed, xt_v, xt_a, t_v, t_a)
-            lv, normv, gapv = dmd_lib.distribution_matching_loss(x0v, rv, fv)
-            la, norma, gapa = dmd_lib.distribution_matching_loss(x0a, ra, fa)
-            loss = lv + cfg.training.audio_loss_weight * la
-            loss, _ = fs.finite_or_zero(loss)
-            dmd_lib.require_role(roles, dmd_lib.GENERATOR, "generator backward")
-            loss.backward()
-            for p in fake_params:
-                p.grad = None
-            optimizer.param_groups[0]["lr"] = lr_at(gen_step, gen_sched)
-            optimizer.param_groups[1]["lr"] = 0.0
-            rec.update(dm_loss=loss.item(), dm_norm_video=normv.item(), dm_gap_video=gapv.item(),
-                       grad_norm_turbo=fs.clip_gradients(gen_params, o.grad_clip))
-            optimizer.step()
-            optimizer.zero_grad(set_to_none=True)
             gen_step += 1
-            x0v, x0a = x0v.detach(), x0a.detach()
-        else:
-            x0v, x0a = dmd_lib.generator_x0(model, roles, schedule, packed, xv, xa, k, build_graph=False)
-        # fake-score flow-matching update on the (detached) generator sample
-        roles.set(dmd_lib.FAKE)
-        t_v, t_a, _ = sample_paired_timesteps(gens["sigma"], d.u_min, d.u_max, tb.video_shift, tb.audio_shift)
-        nv = torch.randn(x0v.shape, generator=gens["noise"], device=device)
-        na = torch.randn(x0a.shape, generator=gens["noise"], device=device)
-        vel_v, vel_a = model(**packed.inputs(dmd_lib.noised(x0v, t_v, nv), dmd_lib.noised(x0a, t_a, na), t_v, t_a))
-        floss = dmd_lib.fake_regression_loss(vel_v[0].float(), x0v, nv) + \
-            cfg.training.audio_loss_weight * dmd_lib.fake_regression_loss(vel_a[0].float(), x0a, na)
-        floss, _ = fs.finite_or_zero(floss)
-        floss.backward()
-        for p in gen_params:
-            p.grad = None
-        optimizer.param_groups[0]["lr"] = 0.0
-        optimizer.param_groups[1]["lr"] = lr_at(fake_step, fake_sched)
-        rec.update(fake_loss=floss.item(), grad_norm_fake=fs.clip_gradients(fake_params, o.fake_grad_clip))
-        optimizer.step()
-        optimizer.zero_grad(set_to_none=True)
         fake_step += 1
         iteration += 1
         rec.update(gen_step=gen_step, fake_step=fake_step)
