@@ -99,6 +99,13 @@ def main(argv=None):
     from vdn_minimax_h3_b200.training.dataset import SyntheticLatentDataset
     from vdn_minimax_h3_b200.utils.activation_checkpointing import enable_block_checkpointing
 
+    timing_phases = [False]
+
+    def phase(name):
+        """fs.phase when the step is being broken down, else a no-op context."""
+        import contextlib
+        return fs.phase(name) if timing_phases[0] else contextlib.nullcontext()
+
     if args.kernels == "off":
         from vdn_minimax_h3_b200.ops import attention_grad, linear_branch_grad, norm_grad
         attention_grad.ATTENTION_KERNELS = False
@@ -179,21 +186,26 @@ def main(argv=None):
     saved = {}
 
     def step(i):
-        batch = pack_noisy_batch(data[i], device, gens["noise"], gens["sigma"])
-        set_layout(model, batch["layout"])
-        tv, ta = fs.teacher_velocity(model, batch["inputs"], adapters=True)
+        with phase("pack"):
+            batch = pack_noisy_batch(data[i], device, gens["noise"], gens["sigma"])
+            set_layout(model, batch["layout"])
+        with phase("teacher"):
+            tv, ta = fs.teacher_velocity(model, batch["inputs"], adapters=True)
         before = torch.cuda.memory_allocated() if cuda else 0
-        sv, sa = fs.student_forward(model, batch["inputs"], args.offload and cuda)
+        with phase("student_forward"):
+            sv, sa = fs.student_forward(model, batch["inputs"], args.offload and cuda)
         if cuda and "per_block_gib" not in saved:
             # device memory the graph keeps between forward and backward, per block
             saved["per_block_gib"] = round((torch.cuda.memory_allocated() - before)
                                            / cfg.num_layers / 2 ** 30, 3)
         loss = F.mse_loss(sv[0].float(), tv) + 0.5 * F.mse_loss(sa[0].float(), ta)
         loss, _ = fs.finite_or_zero(loss)
-        loss.backward()
-        fs.clip_gradients(trainable, 1.0)
-        optimizer.step()
-        optimizer.zero_grad(set_to_none=True)
+        with phase("backward"):
+            loss.backward()
+        with phase("optimizer"):
+            fs.clip_gradients(trainable, 1.0)
+            optimizer.step()
+            optimizer.zero_grad(set_to_none=True)
         return loss
 
     kinds = {}
@@ -217,8 +229,10 @@ def main(argv=None):
             set_layout(model, packed.layout)
             k = dmd_lib.shared_rollout_index(args.seed, i, schedule.num_steps)
             v0, a0 = initial_noise(video_shape, n_audio, gens["noise"], device)
-            xv, xa = dmd_lib.rollout(model, roles, schedule, packed, v0, a0, k)
-            rec = dmd_sub_iteration(model, roles, schedule, packed, xv, xa, k, turn_of(i), gens,
+            with phase("rollout"):
+                xv, xa = dmd_lib.rollout(model, roles, schedule, packed, v0, a0, k)
+            with phase(f"{turn_of(i)}_turn"):
+                rec = dmd_sub_iteration(model, roles, schedule, packed, xv, xa, k, turn_of(i), gens,
                                     optimizer, gen_params, fake_params, gen_lr=1e-5, fake_lr=1e-5,
                                     u_range=(0.02, 0.98), shifts=(12.0, 3.0), audio_weight=0.5,
                                     clips=(1.0, 1.0))
@@ -226,10 +240,20 @@ def main(argv=None):
             return torch.tensor(rec["fake_loss"])
 
     from vdn_minimax_h3_b200.utils.profiling import step_profiler
+    phases = {}
     for i in range(args.warmup):
+        timing_phases[0] = i == args.warmup - 1    # the last warm-up step is broken down
+        fs.phase_reset()
         with step_profiler(i + 1, row_limit=40):   # VDN_PROF_STEP=n: warm-up step n only
             step(i)
+        phases = fs.phase_fields("")
+    timing_phases[0] = False
     kinds.clear()
+    clocks = None
+    if cuda:
+        from bench import ClockSampler
+        clocks = ClockSampler(device)
+        clocks.start()
     dist.barrier()
     per_step = []
     if cuda:
@@ -250,6 +274,7 @@ def main(argv=None):
         torch.cuda.synchronize()
         per_step = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
         ms = events[0].elapsed_time(events[-1])
+        clock_info = clocks.stop()
     else:
         ms = (time.perf_counter() - t_start) * 1e3
     dist.barrier()
@@ -276,6 +301,8 @@ def main(argv=None):
                        "activation_offload": bool(args.offload and cuda)},
             "loss": float(loss.item()) if loss is not None else None,
             "kernels": args.kernels,
+            "phases_s": phases,
+            "phases_note": "wall seconds of the last warm-up step (synchronising timers, not in the timed steps)",
             "step_ms": [round(x, 1) for x in per_step],
             "build_s": round(build_s, 1),
         }
@@ -290,6 +317,7 @@ def main(argv=None):
                 line["cycle_samples_per_s"] = round(world * 6 / ((tg + 5 * tf) / 1e3), 4)
             line["rollout_k"] = kinds.get("rollout_k")
         if cuda:
+            line["clocks"] = clock_info
             line["peak_gib"] = round(torch.cuda.max_memory_allocated() / 2 ** 30, 1)
             line["saved_per_block_gib"] = saved.get("per_block_gib")
         print(json.dumps(line), flush=True)
