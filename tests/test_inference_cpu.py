@@ -58,8 +58,28 @@ def test_lora_merge_reroot_and_translation():
 
 
 def test_decode_and_save(tmp_path):
+    """17n+5 pixel frames at 16x the latent size, written as one mp4 whose second track is
+    the 48 kHz stereo PCM soundtrack (muxed here, no external muxer)."""
+    import cv2
+    from vdn_minimax_h3_b200.inference.mp4mux import boxes, track_handlers
+    from vdn_minimax_h3_b200.inference.vae import AudioDecoderStandIn, VideoDecoderStandIn
     lat = torch.randn(1, 24, 7, 4, 6)
     aud = torch.randn(2, 32, 5)
-    out = decode_and_save(lat, aud, str(tmp_path / "clip.mp4"))
-    assert os.path.getsize(out) > 0 and os.path.exists(str(tmp_path / "clip.wav"))
+    dec = VideoDecoderStandIn(24, widths=(16, 16, 8, 8), chunk_frames=5)
+    timings = {}
+    out = decode_and_save(lat, aud, str(tmp_path / "clip.mp4"), dec, AudioDecoderStandIn(32),
+                          timings=timings)
     assert not os.path.exists(str(tmp_path / "clip.partial.mp4"))
+    assert timings["frames"] == 22 and timings["decode_s"] > 0
+    data = open(out, "rb").read()
+    assert track_handlers(data) == [b"vide", b"soun"]
+    assert [k for k, _, _ in boxes(data)][-2:] == [b"mdat", b"moov"]
+    cap = cv2.VideoCapture(out)
+    n = 0
+    while True:
+        ok, frame = cap.read()
+        if not ok:
+            break
+        assert frame.shape == (64, 96, 3)
+        n += 1
+    assert n == 22

@@ -1,0 +1,62 @@
+"""The MP4 muxer: the PCM track added to OpenCV's video-only mp4 points at exactly the
+samples given (chunk offset, sample count, sample size, rate), the movie header's next
+track id and duration are updated, and the video track still decodes."""
+import struct
+
+import numpy as np
+import pytest
+
+from vdn_minimax_h3_b200.inference.mp4mux import add_pcm_track, boxes, track_handlers
+
+
+def _find(data, path, start=0, end=None):
+    """Offset and size of the first box along a path of box types."""
+    for kind in path:
+        hit = next(((o, s) for k, o, s in boxes(data, start, end) if k == kind), None)
+        if hit is None:
+            return None
+        start, end = hit[0] + 8, hit[0] + hit[1]
+    return hit
+
+
+def test_pcm_track_round_trip(tmp_path):
+    cv2 = pytest.importorskip("cv2")
+    path = str(tmp_path / "v.mp4")
+    w = cv2.VideoWriter(path, cv2.VideoWriter_fourcc(*"mp4v"), 24, (64, 48))
+    for i in range(10):
+        w.write(np.full((48, 64, 3), 20 * i, np.uint8))
+    w.release()
+    video = open(path, "rb").read()
+    rng = np.random.default_rng(0)
+    pcm = rng.integers(-30000, 30000, size=(20000, 2), dtype=np.int16)
+    out = add_pcm_track(video, pcm, 48000)
+    assert out[:len(video) - (len(video) - [o for k, o, s in boxes(video) if k == b"moov"][0])] == \
+        video[:[o for k, o, s in boxes(video) if k == b"moov"][0]]
+    assert track_handlers(out) == [b"vide", b"soun"]
+    moov = _find(out, [b"moov"])
+    traks = [(o, s) for k, o, s in boxes(out, moov[0] + 8, moov[0] + moov[1]) if k == b"trak"]
+    o, s = traks[1]
+    stbl = _find(out, [b"mdia", b"minf", b"stbl"], o + 8, o + s)
+    so, ss = _find(out, [b"stco"], stbl[0] + 8, stbl[0] + stbl[1])
+    count, offset = struct.unpack(">II", out[so + 12:so + 20])
+    zo, zs = _find(out, [b"stsz"], stbl[0] + 8, stbl[0] + stbl[1])
+    size, n = struct.unpack(">II", out[zo + 12:zo + 20])
+    assert count == 1 and size == 4 and n == 20000
+    assert np.array_equal(np.frombuffer(out[offset:offset + 4 * n], dtype="<i2").reshape(-1, 2), pcm)
+    mdhd = _find(out, [b"mdia", b"mdhd"], o + 8, o + s)
+    rate, dur = struct.unpack(">II", out[mdhd[0] + 20:mdhd[0] + 28])
+    assert (rate, dur) == (48000, 20000)
+    mvhd = _find(out, [b"moov", b"mvhd"])
+    assert struct.unpack(">I", out[mvhd[0] + mvhd[1] - 4:mvhd[0] + mvhd[1]])[0] == 3
+    open(path, "wb").write(out)
+    cap = cv2.VideoCapture(path)
+    frames = 0
+    while cap.read()[0]:
+        frames += 1
+    assert frames == 10
+
+
+def test_refuses_moov_first():
+    with pytest.raises(ValueError):
+        add_pcm_track(struct.pack(">I4s", 8, b"moov") + struct.pack(">I4s", 8, b"mdat"),
+                      np.zeros((4, 2), np.int16), 48000)

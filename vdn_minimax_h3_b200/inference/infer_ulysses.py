@@ -50,12 +50,11 @@ def main(argv=None):
     hb.check()
     d = torch.tensor([denoise], device=device)
     dist.all_reduce(d, op=dist.ReduceOp.MAX)
-    t_decode = 0.0
-    if dist.get_rank() == 0:
-        from vdn_minimax_h3_b200.inference.vae import decode_and_save
-        t0 = time.perf_counter()
-        decode_and_save(lat, aud, cfg.render.out)
-        t_decode = time.perf_counter() - t0
+    # every rank decodes a share of the frames; rank 0 gathers them and writes the mp4
+    from vdn_minimax_h3_b200.inference.vae import decode_and_save
+    t0 = time.perf_counter()
+    decode_and_save(lat, aud, cfg.render.out)
+    t_decode = time.perf_counter() - t0
     runtime.barrier()
     if dist.get_rank() == 0:
         prof = runtime.timer.report() if cfg.parallel.profile else {}
