@@ -218,10 +218,10 @@ def main(argv=None):
         video_shape = shape
 
         def turn_of(i):
-            # warm-up: one generator and one fake turn (when W >= 2), then the 1:5 schedule
-            # from its first generator turn
+            # warm-up: a generator turn then fake turns when W >= 2, one fake turn when W == 1;
+            # then the 1:5 schedule from its first generator turn
             if i < args.warmup:
-                return dmd_lib.GENERATOR_TURN if i == 0 else dmd_lib.FAKE_TURN
+                return dmd_lib.GENERATOR_TURN if (i == 0 and args.warmup >= 2) else dmd_lib.FAKE_TURN
             return dmd_lib.turn(i - args.warmup, 0, 5)
 
         def step(i):
