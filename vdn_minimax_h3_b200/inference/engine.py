@@ -22,8 +22,11 @@ allocation-neutral: the packed buffers are built block by block and every origin
 parameter is re-pointed at a view of them, so the module tree (and LoRA/state-dict names)
 keeps working and nothing is held twice.
 """
+import types
+
 import torch
 import torch.nn.functional as F
+from torch import nn
 
 from vdn_minimax_h3_b200.models.h3 import H3Transformer
 from vdn_minimax_h3_b200.models.hybrid_attention import HybridAttention
@@ -137,6 +140,37 @@ class PackedBlock:
             self.gate_up_b = _f32(br.output_gate.up.bias)
 
 
+def _kernel_linear_forward(self, x):
+    """nn.Linear.forward on the package's bf16 tcgen05 GEMM for bf16 CUDA rows (K a multiple
+    of 8, 16-byte aligned rows), PyTorch otherwise."""
+    w = self.weight
+    if (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+            and x.shape[-1] % 8 == 0 and w.is_contiguous() and w.data_ptr() % 16 == 0):
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(-1) == 1 and (x2.stride(0) * 2) % 16 == 0 and x2.data_ptr() % 16 == 0:
+            return gemm.linear(x2, w, self.bias).view(*x.shape[:-1], w.shape[0])
+    return F.linear(x, w, self.bias)
+
+
+def route_outer_linears(model):
+    """The Linears outside the block stack -- patch / audio / text embedders, the token
+    refiner's projections and feed-forward, the video and audio output heads -- run on the
+    bf16 GEMM kernel (instance-level forwards; parameters and their names are untouched).
+    The refiner's attention already runs the dense plan of the attention kernel
+    (models/h3.py: H3Attention). Returns the number of Linears routed."""
+    names = ["proj_in", "audio_proj_in", "context_embedder", "proj_out", "audio_proj_out"]
+    mods = [getattr(model, n) for n in names if hasattr(model, n)]
+    for blk in model.token_refiner.refiner_blocks:
+        mods += [m for m in blk.modules() if type(m) is nn.Linear]
+    n = 0
+    for m in mods:
+        if type(m) is nn.Linear and not getattr(m, "_vdn_kernel_linear", False):
+            m.forward = types.MethodType(_kernel_linear_forward, m)
+            m._vdn_kernel_linear = True
+            n += 1
+    return n
+
+
 class InferenceEngine:
     """Runs an H3Transformer (dense or hybrid) forward through the fused kernels."""
 
@@ -148,6 +182,7 @@ class InferenceEngine:
         self.model = model
         self.cfg = model.config
         self.fp8 = fp8
+        self.outer_linears = route_outer_linears(model)
         self.blocks = []
         with torch.no_grad():
             for block in model.transformer_blocks:

@@ -23,6 +23,9 @@ def main(argv=None):
     p.add_argument("--fp8", action="store_true")
     p.add_argument("--tp", type=int, default=1)
     p.add_argument("--softmax-ranks", type=int, default=0)
+    p.add_argument("--kernel-table", action="store_true",
+                   help="also run one NFE under torch.profiler and print its device-time table "
+                        "(kernels, copies) and the host calls that synchronise")
     a = p.parse_args(argv)
     import bench  # noqa: F401  (same synthetic request as the headline bench)
     from vdn_minimax_h3_b200.inference.assemble import build_inference_engine, build_synthetic_model
@@ -57,6 +60,21 @@ def main(argv=None):
     timer.enabled = True
     generate_latents(transformer, emb, 345, a.nfe, 0, dev, cfg, on_layout=on_layout)
     rep = timer.report()
+    if a.kernel_table and (world == 1 or torch.distributed.get_rank() == 0):
+        from torch.profiler import ProfilerActivity, profile
+        timer.enabled = False
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+            generate_latents(transformer, emb, 345, 1, 0, dev, cfg, on_layout=on_layout)
+            torch.cuda.synchronize()
+        ka = prof.key_averages()
+        print(ka.table(sort_by="cuda_time_total", row_limit=45, max_name_column_width=70),
+              flush=True)
+        syncs = [e for e in ka if any(s in e.key for s in ("Synchronize", "Memcpy", "item",
+                                                           "_local_scalar_dense", "nonzero"))]
+        for e in syncs:
+            print(json.dumps({"host_call": e.key, "count": e.count,
+                              "cpu_ms": round(e.cpu_time_total / 1e3, 3)}), flush=True)
+        timer.enabled = True
     per_nfe = {k: round(v / a.nfe, 2) for k, v in rep.items()}
     line = {"ms_per_nfe_by_section": per_nfe, "total_ms_per_nfe": round(sum(per_nfe.values()), 1),
             "num_layers": a.num_layers, "world": world, "fp8": a.fp8, "tp": a.tp}
