@@ -198,3 +198,66 @@ def test_tp_ulysses_match_single(world, tp, fp8):
     res = _spawn(_hybrid_worker, world, tp, fp8)
     tol = 4e-2 if fp8 else 2e-2
     assert all(isinstance(v, float) and v < tol for v in res.values()), res
+
+
+def _fsdp_rs_worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from torch.distributed.fsdp import fully_shard
+        from vdn_minimax_h3_b200.ops._ext import check_device_error
+        from vdn_minimax_h3_b200.parallel.fsdp_comm import SymmetricReduceScatter, trainable_reduce_numel
+
+        def grads(custom, steps=3):
+            torch.manual_seed(0)
+            m = torch.nn.Sequential(torch.nn.Linear(256, 512), torch.nn.GELU(),
+                                    torch.nn.Linear(512, 256), torch.nn.GELU(),
+                                    torch.nn.Linear(256, 40)).to(dev)
+            for i in (0, 2, 4):
+                fully_shard(m[i])
+            fully_shard(m)
+            comm = None
+            if custom:
+                groups = [list(m[i].parameters()) for i in (0, 2, 4)]
+                comm = SymmetricReduceScatter(dist.group.WORLD, dev,
+                                              trainable_reduce_numel(groups, world), slots=2)
+                for u in (m[0], m[2], m[4], m):
+                    u.set_custom_reduce_scatter(comm)
+            out = []
+            for s in range(steps):     # more steps than slots: the slot ring is reused
+                torch.manual_seed(100 * s + rank)
+                m(torch.randn(64, 256, device=dev)).square().mean().backward()
+                out.append({n: p.grad.full_tensor().clone() for n, p in m.named_parameters()})
+                m.zero_grad(set_to_none=True)
+            torch.cuda.synchronize()
+            return out, comm
+
+        ref, _ = grads(False)
+        got, comm = grads(True)
+        check_device_error()
+        err = max(((a[k] - b[k]).norm() / b[k].norm()).item() for a, b in zip(got, ref) for k in b)
+        res = err if (comm.calls > 0 and comm.fallbacks == 0) else f"calls {comm.calls} fallbacks {comm.fallbacks}"
+        comm.close()
+        q.put((rank, res))
+    except Exception as exc:  # noqa: BLE001
+        import traceback
+        q.put((rank, repr(exc) + traceback.format_exc()[-1500:]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("world", [2, 4])
+def test_fsdp_symmetric_reduce_scatter(world):
+    """FSDP2 with its gradient reduce-scatter over symmetric memory (the owner pulls its shard
+    from every rank and sums; parallel/fsdp_comm.py) gives the stock NCCL gradients, over
+    three backward passes that reuse the slot ring."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _spawn(_fsdp_rs_worker, world)
+    assert all(isinstance(v, float) and v < 1e-5 for v in res.values()), res

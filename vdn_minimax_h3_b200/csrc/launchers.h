@@ -175,6 +175,8 @@ void* symm_malloc(size_t nbytes, void* handle_out);
 void* symm_open(const void* handle);
 void symm_close(void* peer_ptr);
 void symm_free(void* p);
+void launch_symm_reduce_scatter(const float* const* srcs, int P, int64_t offset, int64_t n,
+                                float scale, float* out, cudaStream_t stream);
 void launch_symm_barrier(unsigned long long* counter, unsigned long long* local_flags,
                          unsigned long long* const* peer_flags, int rank, int P,
                          long long timeout_ns, int* err, cudaStream_t stream);

@@ -822,6 +822,20 @@ torch::Tensor bytes_at(int64_t ptr, int64_t nbytes, int64_t device) {
   return torch::from_blob(reinterpret_cast<void*>(ptr), {nbytes}, [](void*) {}, opts);
 }
 
+// out = scale * sum_p srcs[p][offset : offset + out.numel()] (fp32; srcs are the ranks'
+// copies of one symmetric buffer, as int64 addresses on out's device).
+void symm_reduce_scatter(std::vector<int64_t> srcs, int64_t offset, torch::Tensor out,
+                         double scale) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous(),
+              "out must be a contiguous fp32 CUDA tensor");
+  std::vector<const float*> p;
+  for (auto a : srcs) p.push_back(reinterpret_cast<const float*>(a));
+  c10::cuda::CUDAGuard g(out.device());
+  launch_symm_reduce_scatter(p.data(), (int)p.size(), offset, out.numel(), (float)scale,
+                             out.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void symm_barrier(int64_t counter, int64_t local_flags, torch::Tensor peer_flags, int64_t rank,
                   int64_t timeout_ns, torch::Tensor err) {
   TORCH_CHECK(peer_flags.is_cuda() && peer_flags.scalar_type() == at::kLong &&
@@ -874,6 +888,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");
   m.def("window_attention", &vdn::window_attention,
         "tcgen05 window softmax attention over an AttentionPlan (gated epilogue)");
+  m.def("symm_reduce_scatter", &vdn::symm_reduce_scatter,
+        "reduce-scatter by peer loads over a symmetric buffer (fp32 sum, scaled)");
   m.def("window_attention_bwd", &vdn::window_attention_bwd,
         "tcgen05 window attention backward (dq pass over the plan, dk/dv pass over the "
         "transposed plan)");

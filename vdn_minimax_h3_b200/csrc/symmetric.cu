@@ -81,6 +81,65 @@ void symm_close(void* peer_ptr) { ck(cudaIpcCloseMemHandle(peer_ptr), "cudaIpcCl
 
 void symm_free(void* p) { ck(cudaFree(p), "cudaFree (symmetric region)"); }
 
+// Reduce-scatter by peer loads (the owner pulls): out[i] = scale * sum_p src_p[offset + i],
+// fp32, for i < n; src_p is rank p's copy of the same symmetric buffer (this GPU's own copy
+// among them). 16-byte vector loads over NVLink, one pass, no staging. Called between two
+// flag barriers: the first makes every peer's input visible, the second keeps the peers
+// from rewriting their inputs while this rank still reads them.
+constexpr int kMaxReducePeers = 8;
+struct ReduceSrc {
+  const float* p[kMaxReducePeers];
+};
+
+__global__ void __launch_bounds__(256) symm_reduce_scatter_kernel(ReduceSrc src, int P,
+                                                                  int64_t offset, int64_t n,
+                                                                  float scale, float* __restrict__ out) {
+  const int64_t nvec = n >> 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < kMaxReducePeers; ++q) {
+      if (q < P) {
+        const float4 x = *reinterpret_cast<const float4*>(src.p[q] + offset + 4 * v);
+        acc.x += x.x;
+        acc.y += x.y;
+        acc.z += x.z;
+        acc.w += x.w;
+      }
+    }
+    acc.x *= scale;
+    acc.y *= scale;
+    acc.z *= scale;
+    acc.w *= scale;
+    reinterpret_cast<float4*>(out)[v] = acc;
+  }
+  // ragged tail (n % 4)
+  const int64_t t = (nvec << 2) + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (blockIdx.x == 0 && t < n) {
+    float acc = 0.f;
+    for (int q = 0; q < P; ++q) acc += src.p[q][offset + t];
+    out[t] = acc * scale;
+  }
+}
+
+void launch_symm_reduce_scatter(const float* const* srcs, int P, int64_t offset, int64_t n,
+                                float scale, float* out, cudaStream_t stream) {
+  if (P < 1 || P > kMaxReducePeers) throw std::runtime_error("symm_reduce_scatter: 1..8 ranks");
+  if (offset % 4 || reinterpret_cast<uintptr_t>(out) % 16)
+    throw std::runtime_error("symm_reduce_scatter: offset and output must be 16-byte aligned");
+  ReduceSrc s{};
+  for (int q = 0; q < P; ++q) {
+    if (reinterpret_cast<uintptr_t>(srcs[q]) % 16)
+      throw std::runtime_error("symm_reduce_scatter: sources must be 16-byte aligned");
+    s.p[q] = srcs[q];
+  }
+  if (n <= 0) return;
+  int blocks = (int)((n / 4 + 255) / 256);
+  blocks = blocks < 1 ? 1 : (blocks > 4 * 148 ? 4 * 148 : blocks);
+  symm_reduce_scatter_kernel<<<blocks, 256, 0, stream>>>(s, P, offset, n, scale, out);
+}
+
 void launch_symm_barrier(unsigned long long* counter, unsigned long long* local_flags,
                          unsigned long long* const* peer_flags, int rank, int P,
                          long long timeout_ns, int* err, cudaStream_t stream) {

@@ -268,9 +268,12 @@ def restore_optimizer_and_rng(resume, model, optimizer, generators):
 
 # ------------------------------------------------------------------------- sharding
 def shard_model(model, device, shard_size=None, activation_checkpointing=True, split_ac=True,
-                param_dtype=torch.bfloat16, reduce_dtype=torch.float32):
+                param_dtype=torch.bfloat16, reduce_dtype=torch.float32, symmetric_reduce=None):
     """fully_shard each refiner block and DiT block (alpha modules first, in fp32), then the
-    root; HSDP when the world is larger than `shard_size`."""
+    root; HSDP when the world is larger than `shard_size`. With `symmetric_reduce` (default:
+    on for CUDA shard groups of 2-8 ranks) the gradient reduce-scatter of every unit runs over
+    symmetric memory (parallel/fsdp_comm.py) instead of NCCL; the comm object is returned as
+    `model._vdn_reduce_comm` (close() it before destroying the process group)."""
     from torch.distributed.device_mesh import init_device_mesh
     from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
     from vdn_minimax_h3_b200.utils.activation_checkpointing import enable_block_checkpointing
@@ -295,6 +298,22 @@ def shard_model(model, device, shard_size=None, activation_checkpointing=True, s
     for blk in model.token_refiner.refiner_blocks:
         fully_shard(blk, mesh=mesh, mp_policy=mp)
     fully_shard(model, mesh=mesh, mp_policy=mp)
+    if symmetric_reduce is None:
+        symmetric_reduce = dev_type == "cuda" and 1 < shard <= 8
+    if symmetric_reduce:
+        from torch.distributed.fsdp import FSDPModule
+        from vdn_minimax_h3_b200.parallel.fsdp_comm import SymmetricReduceScatter, trainable_reduce_numel
+        units = [m for m in model.modules() if isinstance(m, FSDPModule)]
+        blocks = list(model.transformer_blocks) + list(model.token_refiner.refiner_blocks)
+        in_blocks = {id(p) for b in blocks for p in b.parameters()}
+        groups = [list(b.parameters()) for b in blocks]      # (a block's alpha unit included)
+        groups.append([p for p in model.parameters() if id(p) not in in_blocks])
+        shard_group = mesh.get_group("shard")
+        comm = SymmetricReduceScatter(shard_group, device, trainable_reduce_numel(groups, shard))
+        if comm.enabled():
+            for u in units:
+                u.set_custom_reduce_scatter(comm)
+        model._vdn_reduce_comm = comm
     return model
 
 
