@@ -189,8 +189,8 @@ class H3Attention(nn.Module):
     def forward(self, hidden_states, rotary_emb=None, attention_mask=None):
         x = hidden_states[0]
         q, k, v, _ = self.project(x, rotary_emb)
-        from vdn_minimax_h3_b200.ops import attention_grad as ag
-        if attention_mask is None and ag.ATTENTION_KERNELS and ag.kernel_path_ok(q, k, v):
+        ag = _attention_kernels()
+        if ag is not None and attention_mask is None and ag.kernel_path_ok(q, k, v):
             # dense attention (the teacher trunk, the refiner) on the sm_100a kernels
             o = ag.window_attention_train(q, k, v, ag.dense_plan(x.shape[0], x.device),
                                           q.shape[-1] ** -0.5).reshape(x.shape[0], -1)
@@ -199,6 +199,16 @@ class H3Attention(nn.Module):
                                                v.transpose(0, 1)[None], attn_mask=attention_mask)
             o = o[0].transpose(0, 1).reshape(x.shape[0], -1)
         return self.to_out[1](self.to_out[0](o)).unsqueeze(0)
+
+
+def _attention_kernels():
+    """ops.attention_grad when it is importable and switched on, else None (the exported
+    single-file component, which carries no kernels, takes the SDPA path)."""
+    try:
+        from vdn_minimax_h3_b200.ops import attention_grad
+    except ImportError:
+        return None
+    return attention_grad if attention_grad.ATTENTION_KERNELS else None
 
 
 class SwiGLU(nn.Module):

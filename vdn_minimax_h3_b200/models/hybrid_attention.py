@@ -16,7 +16,7 @@ kernel over the AttentionPlan -- is inference/engine.py, which reads the same pa
 import torch
 from torch import nn
 
-from vdn_minimax_h3_b200.models.h3 import apply_rotary_emb
+from vdn_minimax_h3_b200.models.h3 import _attention_kernels, apply_rotary_emb
 from vdn_minimax_h3_b200.models.layout import SequenceLayout
 from vdn_minimax_h3_b200.models.linear_branch import BidirectionalLinearBranch, OutputGate
 from vdn_minimax_h3_b200.models.window import (ANCHOR_FRAME_MODES, full_cover, window_bounds,
@@ -76,8 +76,8 @@ class HybridAttention(nn.Module):
         covered = layout is None or full_cover(bounds, layout.num_frames)
         scale = self.head_dim ** -0.5
         q, k, v, raw = self.orig.project(x, rotary_emb)
-        from vdn_minimax_h3_b200.ops import attention_grad as ag
-        if ag.ATTENTION_KERNELS and ag.kernel_path_ok(q, k, v):
+        ag = _attention_kernels()
+        if ag is not None and ag.kernel_path_ok(q, k, v):
             # sm_100a forward + backward kernels over the analytic plan (dense when covered)
             plan = (ag.dense_plan(x.shape[0], x.device) if covered
                     else ag.window_plan(layout, bounds, self.anchor_frames, x.device))
