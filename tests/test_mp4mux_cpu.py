@@ -60,3 +60,44 @@ def test_refuses_moov_first():
     with pytest.raises(ValueError):
         add_pcm_track(struct.pack(">I4s", 8, b"moov") + struct.pack(">I4s", 8, b"mdat"),
                       np.zeros((4, 2), np.int16), 48000)
+
+
+def test_concat_segments_decodes_like_its_parts(tmp_path):
+    """Segments encoded separately and joined into one track decode, frame for frame, to
+    exactly what each segment decodes to on its own (the samples are copied verbatim), with
+    one sync sample per segment start at least, and the soundtrack can still be muxed."""
+    cv2 = pytest.importorskip("cv2")
+    from vdn_minimax_h3_b200.inference.mp4mux import concat_video_segments
+
+    def frame(i):
+        y, x = np.mgrid[0:48, 0:64]
+        return np.stack([(x * 4 + i * 7) % 256, (y * 5 + i * 3) % 256,
+                         np.full_like(x, 10 * i % 256)], -1).astype(np.uint8)
+
+    def encode(idx, path):
+        w = cv2.VideoWriter(path, cv2.VideoWriter_fourcc(*"mp4v"), 24, (64, 48))
+        for i in idx:
+            w.write(frame(i))
+        w.release()
+        return open(path, "rb").read()
+
+    def decode(path):
+        cap, out = cv2.VideoCapture(path), []
+        while True:
+            ok, f = cap.read()
+            if not ok:
+                return out
+            out.append(f)
+
+    parts = [range(0, 9), range(9, 20), range(20, 30)]
+    segs = [encode(r, str(tmp_path / f"s{i}.mp4")) for i, r in enumerate(parts)]
+    joined = concat_video_segments(segs)
+    path = str(tmp_path / "joined.mp4")
+    open(path, "wb").write(joined)
+    got = decode(path)
+    want = [f for i in range(3) for f in decode(str(tmp_path / f"s{i}.mp4"))]
+    assert len(got) == 30 and all(np.array_equal(a, b) for a, b in zip(got, want))
+    muxed = add_pcm_track(joined, np.zeros((4800, 2), np.int16), 48000)
+    assert track_handlers(muxed) == [b"vide", b"soun"]
+    open(path, "wb").write(muxed)
+    assert len(decode(path)) == 30

@@ -115,3 +115,183 @@ def track_handlers(mp4: bytes) -> List[bytes]:
         hdlr = next((ho, hs) for k, ho, hs in boxes(mp4, mdia[0] + 8, mdia[0] + mdia[1]) if k == b"hdlr")
         out.append(mp4[hdlr[0] + 16:hdlr[0] + 20])
     return out
+
+
+# ------------------------------------------------------------------ segment concatenation
+# Video tracks encoded in parallel (one encoder per frame range, each starting with a key
+# frame) are joined into one track: every segment's samples are copied, in order, into one
+# mdat; the first segment's sample entry (the codec configuration, identical for segments
+# written by the same encoder settings) describes them all; the sample tables are rebuilt
+# with one chunk per segment and the sync-sample numbers shifted; edit lists are dropped.
+_CONTAINERS = {b"moov", b"trak", b"mdia", b"minf", b"stbl", b"dinf"}
+
+
+def _children(data: bytes, off: int, size: int):
+    return boxes(data, off + 8, off + size)
+
+
+def _find_child(data, off, size, kind):
+    return next(((o, s) for k, o, s in _children(data, off, size) if k == kind), None)
+
+
+def _u32s(b: bytes, n: int, at: int):
+    return list(struct.unpack(f">{n}I", b[at:at + 4 * n]))
+
+
+def _video_samples(data: bytes):
+    """(sample byte ranges, per-sample durations, sync sample numbers, ctts offsets or
+    None, media timescale) of the first video track of an MP4."""
+    moov = next((o, s) for k, o, s in boxes(data) if k == b"moov")
+    for kind, to, ts in _children(data, *moov):
+        if kind != b"trak":
+            continue
+        mdia = _find_child(data, to, ts, b"mdia")
+        hdlr = _find_child(data, *mdia, b"hdlr")
+        if data[hdlr[0] + 16:hdlr[0] + 20] != b"vide":
+            continue
+        mdhd = _find_child(data, *mdia, b"mdhd")
+        version = data[mdhd[0] + 8]
+        at = mdhd[0] + (28 if version == 1 else 20)
+        timescale = struct.unpack(">I", data[at:at + 4])[0]
+        stbl = _find_child(data, *_find_child(data, *mdia, b"minf"), b"stbl")
+        tab = {k: (o, s) for k, o, s in _children(data, *stbl)}
+        o = tab[b"stts"][0]
+        n = _u32s(data, 1, o + 12)[0]
+        runs = _u32s(data, 2 * n, o + 16)
+        durations = [d for c, d in zip(runs[::2], runs[1::2]) for _ in range(c)]
+        o = tab[b"stsz"][0]
+        fixed, count = _u32s(data, 2, o + 12)
+        sizes = [fixed] * count if fixed else _u32s(data, count, o + 20)
+        o = tab[b"stsc"][0]
+        n = _u32s(data, 1, o + 12)[0]
+        stsc = _u32s(data, 3 * n, o + 16)
+        if b"stco" in tab:
+            o = tab[b"stco"][0]
+            n = _u32s(data, 1, o + 12)[0]
+            chunks = _u32s(data, n, o + 16)
+        else:
+            o = tab[b"co64"][0]
+            n = _u32s(data, 1, o + 12)[0]
+            chunks = list(struct.unpack(f">{n}Q", data[o + 16:o + 16 + 8 * n]))
+        ranges, sample = [], 0
+        for c, base in enumerate(chunks, start=1):
+            per = next(stsc[3 * i + 1] for i in range(len(stsc) // 3 - 1, -1, -1) if stsc[3 * i] <= c)
+            pos = base
+            for _ in range(per):
+                ranges.append((pos, sizes[sample]))
+                pos += sizes[sample]
+                sample += 1
+        sync = None
+        if b"stss" in tab:
+            o = tab[b"stss"][0]
+            n = _u32s(data, 1, o + 12)[0]
+            sync = _u32s(data, n, o + 16)
+        ctts = None
+        if b"ctts" in tab:
+            o = tab[b"ctts"][0]
+            n = _u32s(data, 1, o + 12)[0]
+            vals = list(struct.unpack(f">{2 * n}i", data[o + 16:o + 16 + 8 * n]))
+            ctts = [v for c, v in zip(vals[::2], vals[1::2]) for _ in range(c)]
+        return ranges, durations, sync, ctts, timescale
+    raise ValueError("no video track")
+
+
+def _runs(values):
+    out = []
+    for v in values:
+        if out and out[-1][1] == v:
+            out[-1][0] += 1
+        else:
+            out.append([1, v])
+    return out
+
+
+def concat_video_segments(segments: List[bytes]) -> bytes:
+    """One video-only MP4 from MP4 segments encoded with identical settings (moov last in
+    each, a key frame first in each)."""
+    if len(segments) == 1:
+        return segments[0]
+    first = segments[0]
+    parsed = [_video_samples(s) for s in segments]
+    timescale = parsed[0][4]
+    if any(p[4] != timescale for p in parsed):
+        raise ValueError("segments use different media timescales")
+    ftyp = next((first[o:o + s] for k, o, s in boxes(first) if k == b"ftyp"), b"")
+    payload, chunk_starts, counts = bytearray(), [], []
+    durations, sync, ctts = [], [], []
+    header = 16                                    # 64-bit mdat header: offsets known now
+    for (ranges, dur, sy, ct, _), seg in zip(parsed, segments):
+        chunk_starts.append(len(ftyp) + header + len(payload))
+        for pos, size in ranges:
+            payload += seg[pos:pos + size]
+        base = len(durations)
+        counts.append(len(ranges))
+        durations += dur
+        sync += [base + x for x in sy] if sy is not None else [base + i + 1 for i in range(len(ranges))]
+        ctts += ct if ct is not None else [0] * len(ranges)
+    total = sum(durations)
+    mdat = struct.pack(">I4sQ", 1, b"mdat", header + len(payload)) + bytes(payload)
+    sizes = [s for p in parsed for _, s in p[0]]
+    stts = _full(b"stts", 0, 0, struct.pack(">I", len(_runs(durations)))
+                 + b"".join(struct.pack(">II", c, d) for c, d in _runs(durations)))
+    stsz = _full(b"stsz", 0, 0, struct.pack(">II", 0, len(sizes)) + struct.pack(f">{len(sizes)}I", *sizes))
+    stsc = _full(b"stsc", 0, 0, struct.pack(">I", len(counts))
+                 + b"".join(struct.pack(">III", i + 1, n, 1) for i, n in enumerate(counts)))
+    co64 = _full(b"co64", 0, 0, struct.pack(">I", len(chunk_starts))
+                 + struct.pack(f">{len(chunk_starts)}Q", *chunk_starts))
+    stss = _full(b"stss", 0, 0, struct.pack(">I", len(sync)) + struct.pack(f">{len(sync)}I", *sync))
+    new_ctts = b""
+    if any(ctts):
+        r = _runs(ctts)
+        new_ctts = _full(b"ctts", 1, 0, struct.pack(">I", len(r))
+                         + b"".join(struct.pack(">Ii", c, v) for c, v in r))
+    tables = {b"stts": stts, b"stsz": stsz, b"stsc": stsc, b"stss": stss}
+
+    def rebuild(off, size, movie_ts):
+        """The box at off with its subtree rewritten for the joined video track."""
+        kind = first[off + 4:off + 8]
+        if kind == b"trak":
+            mdia = _find_child(first, off, size, b"mdia")
+            hdlr = _find_child(first, *mdia, b"hdlr")
+            if first[hdlr[0] + 16:hdlr[0] + 20] != b"vide":
+                raise ValueError("segments must be video-only")
+        if kind in _CONTAINERS:
+            parts = []
+            for k, o, s in _children(first, off, size):
+                if k == b"edts":
+                    continue                        # the edit list described one segment
+                if k == b"stbl":
+                    sub = []
+                    for kk, oo, ss in _children(first, o, s):
+                        if kk in tables:
+                            sub.append(tables[kk])
+                        elif kk in (b"stco", b"co64"):
+                            sub.append(co64)
+                        elif kk == b"ctts":
+                            sub.append(new_ctts)
+                        else:
+                            sub.append(first[oo:oo + ss])
+                    if b"stss" not in {kk for kk, _, _ in _children(first, o, s)}:
+                        sub.append(stss)
+                    parts.append(_box(b"stbl", b"".join(sub)))
+                else:
+                    parts.append(rebuild(o, s, movie_ts))
+            return _box(kind, b"".join(parts))
+        raw = bytearray(first[off:off + size])
+        v = raw[8]
+        if kind == b"mvhd":
+            at, fmt = (32, ">Q") if v == 1 else (24, ">I")
+            raw[at:at + struct.calcsize(fmt)] = struct.pack(fmt, total * movie_ts // timescale)
+        elif kind == b"tkhd":
+            at, fmt = (36, ">Q") if v == 1 else (28, ">I")
+            raw[at:at + struct.calcsize(fmt)] = struct.pack(fmt, total * movie_ts // timescale)
+        elif kind == b"mdhd":
+            at, fmt = (32, ">Q") if v == 1 else (24, ">I")
+            raw[at:at + struct.calcsize(fmt)] = struct.pack(fmt, total)
+        return bytes(raw)
+
+    moov = next((o, s) for k, o, s in boxes(first) if k == b"moov")
+    mvhd = _find_child(first, *moov, b"mvhd")
+    at = mvhd[0] + (28 if first[mvhd[0] + 8] == 1 else 20)
+    movie_ts = struct.unpack(">I", first[at:at + 4])[0]
+    return ftyp + mdat + rebuild(*moov, movie_ts)

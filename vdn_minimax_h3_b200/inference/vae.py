@@ -17,7 +17,8 @@ output is not a picture or a sound of anything.
 
 decode_and_save follows reference src/inference/render.py:166-198: decode, pixel
 de-normalisation, uint8 frames, atomic `.partial.mp4` -> rename; the soundtrack is muxed into
-the same mp4 as 16-bit PCM (inference/mp4mux.py) after OpenCV encodes the video track.
+the same mp4 as 16-bit PCM (inference/mp4mux.py) after OpenCV encodes the video track --
+frame ranges in parallel threads, joined into one track by the same muxer.
 """
 import os
 import time
@@ -184,15 +185,34 @@ def write_mp4(frames, path, fps=FPS):
     writer.release()
 
 
-def mux_pcm(path, audio, rate=AUDIO_SAMPLE_RATE):
-    """Rewrites the video-only mp4 at `path` with `audio` ([channels, samples] in [-1, 1])
-    as a 16-bit PCM track."""
+def encode_mp4(frames, fps=FPS, workers=None, min_frames=8):
+    """The bytes of a video-only mp4 of `frames` ([P, H, W, 3] uint8): contiguous frame
+    ranges are encoded by parallel OpenCV writers (the encoder releases the GIL), each range
+    starting on a key frame, and joined into one track (mp4mux.concat_video_segments)."""
+    import tempfile
+    from concurrent.futures import ThreadPoolExecutor
+    from vdn_minimax_h3_b200.inference.mp4mux import concat_video_segments
+    P = frames.shape[0]
+    workers = workers or min(16, os.cpu_count() or 1)
+    k = max(1, min(workers, P // max(min_frames, 1)))
+    cuts = [round(i * P / k) for i in range(k + 1)]
+    with tempfile.TemporaryDirectory(prefix="vdn_mp4_") as tmp:
+        paths = [os.path.join(tmp, f"seg{i}.mp4") for i in range(k)]
+        with ThreadPoolExecutor(k) as pool:
+            list(pool.map(lambda i: write_mp4(frames[cuts[i]:cuts[i + 1]], paths[i], fps), range(k)))
+        segments = []
+        for path in paths:
+            with open(path, "rb") as f:
+                segments.append(f.read())
+    return concat_video_segments(segments)
+
+
+def mux_pcm(video_mp4, audio, rate=AUDIO_SAMPLE_RATE):
+    """The mp4 bytes `video_mp4` with `audio` ([channels, samples] in [-1, 1]) added as a
+    16-bit PCM track."""
     from vdn_minimax_h3_b200.inference.mp4mux import add_pcm_track
     pcm = (audio.clamp(-1, 1).numpy().T * 32767).astype(np.int16)
-    with open(path, "rb") as f:
-        data = f.read()
-    with open(path, "wb") as f:
-        f.write(add_pcm_track(data, pcm, rate))
+    return add_pcm_track(video_mp4, pcm, rate)
 
 
 @torch.no_grad()
@@ -214,9 +234,10 @@ def decode_and_save(latents, audio_latents, out_path, video_decoder=None, audio_
     os.makedirs(os.path.dirname(os.path.abspath(out_path)) or ".", exist_ok=True)
     stem, ext = os.path.splitext(out_path)
     partial = f"{stem}.partial{ext}"
-    write_mp4(frames, partial)
+    video = encode_mp4(frames)
     t2 = time.perf_counter()
-    mux_pcm(partial, audio)
+    with open(partial, "wb") as f:
+        f.write(mux_pcm(video, audio))
     os.replace(partial, out_path)
     if timings is not None:
         timings.update(decode_s=t1 - t0, encode_s=t2 - t1, mux_s=time.perf_counter() - t2,
