@@ -237,7 +237,7 @@ def main(argv=None):
     p.add_argument("--gemm", action="store_true")
     p.add_argument("--attention", action="store_true")
     p.add_argument("--attention-train-small", action="store_true",
-                   help="training attention forward + backward on 10 frames x 8 heads (ncu-sized)")
+                   help="training attention forward + backward on 20 frames x 16 heads (ncu-sized, tensors above L2)")
     p.add_argument("--attention-train", action="store_true",
                    help="training attention forward + backward at the Stage-B shape vs SDPA")
     p.add_argument("--attention-ab", action="store_true",
@@ -273,7 +273,7 @@ def main(argv=None):
         bench_attention_train(timed)
     if a.attention_train_small:
         from vdn_minimax_h3_b200.ops.attention_grad import bench_attention_train
-        bench_attention_train(timed, frames=10, heads=8)
+        bench_attention_train(timed, frames=20, heads=16)
     if a.attention_ab:
         from vdn_minimax_h3_b200.ops.attention import bench_attention_vs_cudnn
         bench_attention_vs_cudnn(timed)
