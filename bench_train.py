@@ -7,8 +7,9 @@ or Stage DMD (few-step generator, frozen real score, trainable fake score on one
 
 `--kernels off` is the labelled baseline arm: the same model and loop with every sm_100a
 training kernel switched off (attention through PyTorch SDPA, the linear branch's scans /
-SPD factor / short conv and the AdaLN norm in eager PyTorch), i.e. PyTorch FSDP2 + NCCL +
-cuBLAS / cuDNN.
+SPD factor / short conv and the AdaLN norm in eager PyTorch, every Linear's forward, dgrad
+and wgrad through cuBLAS), i.e. PyTorch FSDP2 + NCCL + cuBLAS / cuDNN. With `--kernels on`
+the Linears run on the package's tcgen05 GEMM (ops/linear_grad.py).
 
 Stage DMD (`--stage dmd`): each step is one DMD2 sub-iteration on every rank -- the
 generator's own rollout of k grid steps (k the rank-shared index of that iteration, 8-step
@@ -88,6 +89,12 @@ def host_available_gib():
     return None
 
 
+def _linear_calls():
+    """Linear forwards issued so far on the GEMM kernel vs on F.linear (ops/linear_grad.py)."""
+    from vdn_minimax_h3_b200.ops import linear_grad
+    return dict(linear_grad.STATS)
+
+
 def main(argv=None):
     args = parse(argv)
     from vdn_minimax_h3_b200.models.factory import RELEASED_HYBRID, TINY_HYBRID, build_model, make_spec
@@ -107,9 +114,10 @@ def main(argv=None):
         return fs.phase(name) if timing_phases[0] else contextlib.nullcontext()
 
     if args.kernels == "off":
-        from vdn_minimax_h3_b200.ops import attention_grad, linear_branch_grad, norm_grad
+        from vdn_minimax_h3_b200.ops import attention_grad, linear_branch_grad, linear_grad, norm_grad
         attention_grad.ATTENTION_KERNELS = False
         linear_branch_grad.USE_KERNELS = False
+        linear_grad.LINEAR_KERNELS = False
         norm_grad.NORM_KERNELS = False
     cuda = torch.cuda.is_available()
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -301,6 +309,7 @@ def main(argv=None):
                        "activation_offload": bool(args.offload and cuda)},
             "loss": float(loss.item()) if loss is not None else None,
             "kernels": args.kernels,
+            "linear_calls": _linear_calls(),
             "reduce_scatter": ("symmetric memory (own kernel)" if getattr(
                 getattr(model, "_vdn_reduce_comm", None), "calls", 0) else "nccl"),
             "phases_s": phases,

@@ -4,6 +4,7 @@
     python -m vdn_minimax_h3_b200.bench_kernels --attention
     python -m vdn_minimax_h3_b200.bench_kernels --linear
     python -m vdn_minimax_h3_b200.bench_kernels --linear-train
+    python -m vdn_minimax_h3_b200.bench_kernels --gemm-train
 
 Each case runs 3 warm-up launches and times 10 with CUDA events on the launching stream;
 operands are larger than the 126 MB L2 for the full-size shapes. Library baselines
@@ -52,6 +53,43 @@ def bench_gemm():
         rows.append(row)
         print(json.dumps(row), flush=True)
         del x, w, out
+        torch.cuda.empty_cache()
+    return rows
+
+
+def bench_gemm_train(rows_t=82809):
+    """The three products of each training Linear at the Stage-B shape (81 latent frames:
+    82,809 packed rows): forward x W^T, dgrad dy W (W read MN-major) and wgrad dy^T x (both
+    read MN-major, contraction over the rows), the package's GEMM against cuBLAS
+    (torch.matmul on the same stored tensors)."""
+    from vdn_minimax_h3_b200.ops import gemm
+    from vdn_minimax_h3_b200.ops._ext import check_device_error
+    rows = []
+    for name, n, k in [("q_k_v", 7168, 5376), ("o_proj", 5376, 7168), ("ff_up", 28672, 5376),
+                       ("ff_down", 5376, 14336)]:
+        m = rows_t
+        x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) / k ** 0.5
+        dy = torch.randn(m, n, device="cuda", dtype=torch.bfloat16)
+        y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        dx = torch.empty(m, k, device="cuda", dtype=torch.bfloat16)
+        dw = torch.empty(n, k, device="cuda", dtype=torch.bfloat16)
+        flop = 2.0 * m * n * k
+        row = dict(case=name, T=m, out=n, inp=k)
+        for prod, ours, lib in (
+                ("fwd", lambda: gemm.linear(x, w, out=y), lambda: torch.matmul(x, w.t(), out=y)),
+                ("dgrad", lambda: gemm.linear_dgrad(dy, w, out=dx), lambda: torch.matmul(dy, w, out=dx)),
+                ("wgrad", lambda: gemm.linear_wgrad(dy, x, out=dw), lambda: torch.matmul(dy.t(), x, out=dw))):
+            t_ours = timed(ours)
+            check_device_error()
+            t_lib = timed(lib)
+            row[f"{prod}_ms"] = round(t_ours, 3)
+            row[f"{prod}_tflops"] = round(flop / t_ours / 1e9, 1)
+            row[f"{prod}_cublas_ms"] = round(t_lib, 3)
+            row[f"{prod}_cublas_tflops"] = round(flop / t_lib / 1e9, 1)
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+        del x, w, dy, y, dx, dw
         torch.cuda.empty_cache()
     return rows
 
@@ -236,6 +274,10 @@ def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gemm", action="store_true")
     p.add_argument("--attention", action="store_true")
+    p.add_argument("--gemm-train", action="store_true",
+                   help="training Linear products (forward, dgrad, wgrad) vs cuBLAS at the Stage-B shape")
+    p.add_argument("--gemm-train-small", action="store_true",
+                   help="the same products at 8,192 rows (ncu-sized)")
     p.add_argument("--attention-train-small", action="store_true",
                    help="training attention forward + backward on 20 frames x 16 heads (ncu-sized, tensors above L2)")
     p.add_argument("--attention-train", action="store_true",
@@ -271,6 +313,10 @@ def main(argv=None):
     if a.attention_train:
         from vdn_minimax_h3_b200.ops.attention_grad import bench_attention_train
         bench_attention_train(timed)
+    if a.gemm_train:
+        bench_gemm_train()
+    if a.gemm_train_small:
+        bench_gemm_train(8192)
     if a.attention_train_small:
         from vdn_minimax_h3_b200.ops.attention_grad import bench_attention_train
         bench_attention_train(timed, frames=20, heads=16)

@@ -2,6 +2,14 @@
 //
 //   C[M, N] = A[M, K] @ B[N, K]^T      (both operands K-major, i.e. nn.Linear layout)
 //
+// or, for the two products of a Linear's backward, with either operand stored MN-major
+// (template LAYOUT: bit 0 = A held as [K, M], bit 1 = B held as [K, N], rows contiguous):
+//   dgrad  dX = dY W        A = dY [T, out] K-major, B = W [out, in] read as [K, N]
+//   wgrad  dW = dY^T X      A = dY read as [K=T, M=out], B = X [T, in] read as [K, N]
+// An MN-major operand arrives as 64-column boxes (64 K-rows x 128 B each, 128-byte swizzle)
+// and is described to tcgen05.mma as MN-major with the box size as the stride between the
+// 64-wide MN atoms, so neither backward product needs a transposed copy.
+//
 // One CTA per SM, 128x256 output tiles, 64-deep K blocks:
 //   warp 0      TMA producer: A and B tiles into a 4-stage shared-memory ring
 //               (128-byte swizzle), completion counted by mbarrier transaction bytes.
@@ -377,7 +385,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, uint32_t tacc,
   }
 }
 
-template <int EPI>
+template <int EPI, int LAYOUT>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, EpiParams p, int M, int N,
@@ -441,9 +449,31 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           }
           uint8_t* sA = smem + stage * GM_STAGE_BYTES;
           uint8_t* sB = sA + GM_A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], GM_STAGE_BYTES);
-          tma_load_2d(sA, &tmA, &full[stage], kb * GM_BK, mb * GM_BM);
-          tma_load_2d(sB, &tmB, &full[stage], kb * GM_BK, nb * GM_BN);
+          if constexpr (LAYOUT == 0) {
+            mbar_arrive_expect_tx(&full[stage], GM_STAGE_BYTES);
+            tma_load_2d(sA, &tmA, &full[stage], kb * GM_BK, mb * GM_BM);
+            tma_load_2d(sB, &tmB, &full[stage], kb * GM_BK, nb * GM_BN);
+          } else {
+            // MN-major boxes that start past the edge are not loaded: they would only
+            // feed accumulator rows / columns the epilogue never stores.
+            const int na = (LAYOUT & 1) ? min(GM_BM / 64, (M - mb * GM_BM + 63) / 64) : 1;
+            const int nbx = (LAYOUT & 2) ? min(GM_BN / 64, (N - nb * GM_BN + 63) / 64) : 1;
+            const uint32_t bytes = ((LAYOUT & 1) ? na * (GM_A_BYTES / 2) : GM_A_BYTES) +
+                                   ((LAYOUT & 2) ? nbx * (GM_B_BYTES / 4) : GM_B_BYTES);
+            mbar_arrive_expect_tx(&full[stage], bytes);
+            if constexpr ((LAYOUT & 1) != 0) {
+              for (int i = 0; i < na; ++i)
+                tma_load_2d(sA + i * (GM_A_BYTES / 2), &tmA, &full[stage], mb * GM_BM + 64 * i, kb * GM_BK);
+            } else {
+              tma_load_2d(sA, &tmA, &full[stage], kb * GM_BK, mb * GM_BM);
+            }
+            if constexpr ((LAYOUT & 2) != 0) {
+              for (int i = 0; i < nbx; ++i)
+                tma_load_2d(sB + i * (GM_B_BYTES / 4), &tmB, &full[stage], nb * GM_BN + 64 * i, kb * GM_BK);
+            } else {
+              tma_load_2d(sB, &tmB, &full[stage], kb * GM_BK, nb * GM_BN);
+            }
+          }
           issued_mask |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           if (++stage == GM_STAGES) {
@@ -465,7 +495,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(GM_BM, GM_BN, false, false);
+      constexpr uint32_t idesc = umma_idesc_bf16(GM_BM, GM_BN, (LAYOUT & 1) != 0, (LAYOUT & 2) != 0);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -489,8 +519,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           const uint32_t baddr = aaddr + GM_A_BYTES;
 #pragma unroll
           for (int k = 0; k < GM_BK / 16; ++k) {
-            umma_f16_ss(tacc, umma_desc_kmajor_sw128(aaddr + k * 32),
-                        umma_desc_kmajor_sw128(baddr + k * 32), idesc, (kb | k) != 0);
+            // K-major: 16 K-elements = 32 B into the swizzled row; MN-major: 16 K-rows of
+            // 128 B = 2048 B down the box, 64-wide MN atoms one box apart.
+            const uint64_t da = (LAYOUT & 1) ? umma_desc_mnmajor_sw128(aaddr + k * 2048, GM_A_BYTES / 2)
+                                             : umma_desc_kmajor_sw128(aaddr + k * 32);
+            const uint64_t db = (LAYOUT & 2) ? umma_desc_mnmajor_sw128(baddr + k * 2048, GM_B_BYTES / 4)
+                                             : umma_desc_kmajor_sw128(baddr + k * 32);
+            umma_f16_ss(tacc, da, db, idesc, (kb | k) != 0);
           }
           umma_commit(&empty[stage]);
           if (++stage == GM_STAGES) {
@@ -532,21 +567,22 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------- host
-template <int EPI>
+template <int EPI, int LAYOUT = 0>
 static void launch_gemm(const GemmArgs& a, EpiParams p, cudaStream_t stream) {
   static std::atomic<uint64_t> attr_set{0};
   if (attr_needed(attr_set)) {
-    cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemm_bf16_kernel<EPI, LAYOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          GM_SMEM);
     attr_done(attr_set);
   }
-  CUtensorMap ta = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M,
-                                a.lda * 2, GM_BK, GM_BM);
-  CUtensorMap tb = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N,
-                                a.ldb * 2, GM_BK, GM_BN);
+  constexpr auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta = (LAYOUT & 1) ? make_tmap_2d(a.A, BF16, 2, a.M, a.K, a.lda * 2, 64, GM_BK)
+                                : make_tmap_2d(a.A, BF16, 2, a.K, a.M, a.lda * 2, GM_BK, GM_BM);
+  CUtensorMap tb = (LAYOUT & 2) ? make_tmap_2d(a.B, BF16, 2, a.N, a.K, a.ldb * 2, 64, GM_BK)
+                                : make_tmap_2d(a.B, BF16, 2, a.K, a.N, a.ldb * 2, GM_BK, GM_BN);
   const int tiles = ((a.M + GM_BM - 1) / GM_BM) * ((a.N + GM_BN - 1) / GM_BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_bf16_kernel<EPI><<<grid, GM_THREADS, GM_SMEM, stream>>>(ta, tb, p, a.M, a.N, a.K);
+  gemm_bf16_kernel<EPI, LAYOUT><<<grid, GM_THREADS, GM_SMEM, stream>>>(ta, tb, p, a.M, a.N, a.K);
 }
 
 void launch_gemm_bf16_routed(const GemmArgs& a, const GemmRoute& r, const float* bias, int* err,
@@ -602,6 +638,26 @@ void launch_gemm_bf16(const GemmArgs& a, int mode, void* out, int64_t ldo, const
     case EPI_SWIGLU: launch_gemm<EPI_SWIGLU>(a, p, stream); break;
     case EPI_ADD: launch_gemm<EPI_ADD>(a, p, stream); break;
     default: throw std::runtime_error("unknown GEMM epilogue mode");
+  }
+}
+
+void launch_gemm_bf16_layout(const GemmArgs& a, bool a_mn, bool b_mn, bool accumulate, void* out,
+                             int64_t ldo, int* err, cudaStream_t stream) {
+  if (a.M == 0 || a.N == 0) return;
+  EpiParams p{};
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.err = err;
+  const int layout = (a_mn ? 1 : 0) | (b_mn ? 2 : 0);
+  switch (layout * 2 + (accumulate ? 1 : 0)) {
+    case 0: launch_gemm<EPI_STORE, 0>(a, p, stream); break;
+    case 1: launch_gemm<EPI_ADD, 0>(a, p, stream); break;
+    case 2: launch_gemm<EPI_STORE, 1>(a, p, stream); break;
+    case 3: launch_gemm<EPI_ADD, 1>(a, p, stream); break;
+    case 4: launch_gemm<EPI_STORE, 2>(a, p, stream); break;
+    case 5: launch_gemm<EPI_ADD, 2>(a, p, stream); break;
+    case 6: launch_gemm<EPI_STORE, 3>(a, p, stream); break;
+    default: launch_gemm<EPI_ADD, 3>(a, p, stream); break;
   }
 }
 

@@ -60,6 +60,12 @@ void launch_gemm_bf16(const GemmArgs& a, int mode, void* out, int64_t ldo, const
                       const void* gate, int64_t ldg, const int* gate_idx, int* err,
                       cudaStream_t stream);
 
+// C (+)= A @ B^T with either operand stored MN-major: a_mn = A held as [K, M] (row stride
+// lda), b_mn = B held as [K, N] (row stride ldb); GemmArgs' M, N, K are the product's.
+// The input and weight gradients of a Linear (gemm.cu, LAYOUT).
+void launch_gemm_bf16_layout(const GemmArgs& a, bool a_mn, bool b_mn, bool accumulate, void* out,
+                             int64_t ldo, int* err, cudaStream_t stream);
+
 // Routed epilogue (see gemm.cu, EPI_ROUTE). `route` holds `planes` tables of N/8 addresses;
 // every column group is stored to each plane that has an address for it, except the
 // 128-wide q/k heads in [q0,q1) and [k0,k1): raw values to plane 0, normalised + rotated

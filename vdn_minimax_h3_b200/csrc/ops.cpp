@@ -76,6 +76,38 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// out (+)= op(A) @ op(B)^T where a_mn means A is held as [K, M] and b_mn means B is held as
+// [K, N] (the input / weight gradients of a Linear without transposed copies).
+void gemm_bf16_layout(torch::Tensor A, torch::Tensor B, torch::Tensor out, bool a_mn, bool b_mn,
+                      bool accumulate, torch::Tensor err) {
+  check_2d_bf16(A, "A");
+  check_2d_bf16(B, "B");
+  check_2d_bf16(out, "out");
+  GemmArgs a;
+  a.A = A.data_ptr();
+  a.B = B.data_ptr();
+  a.lda = A.stride(0);
+  a.ldb = B.stride(0);
+  const int64_t M = a_mn ? A.size(1) : A.size(0), ka = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0), kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(ka == kb, "K mismatch: A ", A.sizes(), " B ", B.sizes(), " (a_mn ", a_mn,
+              ", b_mn ", b_mn, ")");
+  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && ka < (1ll << 31), "GEMM extent too large");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "out must be [", M, ", ", N, "], got ",
+              out.sizes());
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)ka;
+  if (a.K == 0) {
+    if (!accumulate) out.zero_();
+    return;
+  }
+  c10::cuda::CUDAGuard g(A.device());
+  launch_gemm_bf16_layout(a, a_mn, b_mn, accumulate, out.data_ptr(), out.stride(0), err_ptr(err),
+                          at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void gemm_bf16_residual(torch::Tensor A, torch::Tensor B, torch::Tensor X,
                         c10::optional<torch::Tensor> bias, torch::Tensor gate,
                         torch::Tensor gate_idx, torch::Tensor err) {
@@ -862,6 +894,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_barrier", &vdn::symm_barrier, "bounded all-ranks flag barrier over peer memory");
   m.doc() = "VDN-H3 sm_100a kernels";
   m.def("gemm_bf16", &vdn::gemm_bf16, "bf16 tcgen05 GEMM: out (+)= A @ B^T (+ bias)");
+  m.def("gemm_bf16_layout", &vdn::gemm_bf16_layout,
+        "bf16 tcgen05 GEMM with MN-major operands: out (+)= op(A) @ op(B)^T",
+        py::arg("A"), py::arg("B"), py::arg("out"), py::arg("a_mn"), py::arg("b_mn"),
+        py::arg("accumulate"), py::arg("err"));
   m.def("gemm_bf16_residual", &vdn::gemm_bf16_residual,
         "bf16 tcgen05 GEMM with gated-residual epilogue: X += gate[idx] * (A @ B^T + bias)");
   m.def("gemm_bf16_swiglu", &vdn::gemm_bf16_swiglu,

@@ -36,6 +36,39 @@ def linear(x, weight, bias=None, out=None, accumulate=False):
     return out
 
 
+def matmul_layout(a, b, a_mn=False, b_mn=False, out=None, accumulate=False):
+    """out (+)= op(a) @ op(b)^T on the tcgen05 GEMM, where op(a) = a.T when `a_mn` (a held as
+    [K, M]) and op(b)^T = b when `b_mn` (b held as [K, N]); otherwise a is [M, K] and b is
+    [N, K] as in `linear`. No transposed copy is made: the kernel reads the MN-major operand
+    in its stored layout. CPU tensors take the fp32 oracle."""
+    am = a.t() if a_mn else a
+    bm = b if b_mn else b.t()
+    M, N = am.shape[0], bm.shape[1]
+    if not a.is_cuda:
+        y = am.float() @ bm.float()
+        if out is None:
+            return y.to(a.dtype)
+        out.copy_(((out.float() + y) if accumulate else y).to(out.dtype))
+        return out
+    if out is None:
+        assert not accumulate
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    ext().gemm_bf16_layout(a, b, out, bool(a_mn), bool(b_mn), bool(accumulate), error_word(a.device))
+    return out
+
+
+def linear_dgrad(dy, weight, out=None):
+    """Input gradient of y = x W^T: dx = dy @ W, with W [out, in] read as the MN-major
+    [K=out, N=in] operand."""
+    return matmul_layout(dy, weight, a_mn=False, b_mn=True, out=out)
+
+
+def linear_wgrad(dy, x, out=None, accumulate=False):
+    """Weight gradient of y = x W^T: dW = dy^T @ x [out, in], contracting over the rows (T):
+    dy read as the MN-major [K=T, M=out] operand, x as [K=T, N=in]."""
+    return matmul_layout(dy, x, a_mn=True, b_mn=True, out=out, accumulate=accumulate)
+
+
 def linear_gated_residual(x, weight, bias, residual, gate_table, gate_index):
     """residual += gate_table[gate_index] * (x @ weight.T + bias), in place; returns residual.
     The fused `post` of the block (reference fused_block.py:47-49)."""

@@ -268,9 +268,12 @@ def restore_optimizer_and_rng(resume, model, optimizer, generators):
 
 # ------------------------------------------------------------------------- sharding
 def shard_model(model, device, shard_size=None, activation_checkpointing=True, split_ac=True,
-                param_dtype=torch.bfloat16, reduce_dtype=torch.float32, symmetric_reduce=None):
+                param_dtype=torch.bfloat16, reduce_dtype=torch.float32, symmetric_reduce=None,
+                kernel_linears=True):
     """fully_shard each refiner block and DiT block (alpha modules first, in fp32), then the
-    root; HSDP when the world is larger than `shard_size`. With `symmetric_reduce` (default:
+    root; HSDP when the world is larger than `shard_size`. On CUDA every nn.Linear first gets
+    the GEMM-kernel forward / dgrad / wgrad of ops/linear_grad.py (`kernel_linears`; the
+    module switch linear_grad.LINEAR_KERNELS turns it off at run time). With `symmetric_reduce` (default:
     on for CUDA shard groups of 2-8 ranks) the gradient reduce-scatter of every unit runs over
     symmetric memory (parallel/fsdp_comm.py) instead of NCCL; the comm object is returned as
     `model._vdn_reduce_comm` (close() it before destroying the process group)."""
@@ -282,6 +285,9 @@ def shard_model(model, device, shard_size=None, activation_checkpointing=True, s
     if world % shard:
         raise ValueError(f"world {world} is not a multiple of shard_size {shard}")
     dev_type = torch.device(device).type
+    if kernel_linears and dev_type == "cuda":
+        from vdn_minimax_h3_b200.ops.linear_grad import route_training_linears
+        route_training_linears(model)
     if world // shard > 1:
         mesh = init_device_mesh(dev_type, (world // shard, shard), mesh_dim_names=("replicate", "shard"))
     else:

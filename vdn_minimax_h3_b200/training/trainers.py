@@ -322,6 +322,9 @@ def run_stage_a1(cfg):
             if attn.enable_softmax_gate:
                 attn.softmax_gate.requires_grad_(False)
     model.to(device)
+    if torch.device(device).type == "cuda":
+        from vdn_minimax_h3_b200.ops.linear_grad import route_training_linears
+        route_training_linears(model)
     if world > 1:
         from vdn_minimax_h3_b200.utils.distributed import broadcast_and_verify_init
         broadcast_and_verify_init(model, [p for p in model.parameters() if p.requires_grad], device)
