@@ -14,7 +14,23 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
                                   CUtensorMapFloatOOBfill);
 
+// The encode call is a driver API call: it needs a current context on the calling thread.
+// A thread whose first CUDA work is a tensor-map encode (autograd's backward threads, where
+// PyTorch skips cudaSetDevice when the device already matches) has none and the encode
+// fails with CUDA_ERROR_INVALID_CONTEXT; binding the device's primary context once per
+// thread and device fixes that.
+inline void bind_current_context() {
+  thread_local int bound = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  if (bound != dev) {
+    cudaSetDevice(dev);
+    bound = dev;
+  }
+}
+
 inline EncodeTiledFn encode_tiled_fn() {
+  bind_current_context();
   static EncodeTiledFn fn = nullptr;
   if (!fn) {
     void* p = nullptr;
