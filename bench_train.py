@@ -73,6 +73,9 @@ def parse(argv=None):
     p.add_argument("--stage", choices=("b", "dmd"), default="b")
     p.add_argument("--kernels", choices=("on", "off"), default="on",
                    help="off: the labelled baseline (PyTorch / cuBLAS / cuDNN for every op)")
+    p.add_argument("--linears", choices=("kernel", "cublas"), default="kernel",
+                   help="with --kernels on: the Linears' forward / dgrad / wgrad on the package's "
+                        "GEMM (default) or on cuBLAS (isolates the GEMM's share of the step)")
     p.add_argument("--tiny", action="store_true", help="two-block model (CPU tests only)")
     return p.parse_args(argv)
 
@@ -113,6 +116,9 @@ def main(argv=None):
         import contextlib
         return fs.phase(name) if timing_phases[0] else contextlib.nullcontext()
 
+    if args.linears == "cublas":
+        from vdn_minimax_h3_b200.ops import linear_grad
+        linear_grad.LINEAR_KERNELS = False
     if args.kernels == "off":
         from vdn_minimax_h3_b200.ops import attention_grad, linear_branch_grad, linear_grad, norm_grad
         attention_grad.ATTENTION_KERNELS = False
@@ -309,6 +315,7 @@ def main(argv=None):
                        "activation_offload": bool(args.offload and cuda)},
             "loss": float(loss.item()) if loss is not None else None,
             "kernels": args.kernels,
+            "linears": "cublas" if args.kernels == "off" else args.linears,
             "linear_calls": _linear_calls(),
             "reduce_scatter": ("symmetric memory (own kernel)" if getattr(
                 getattr(model, "_vdn_reduce_comm", None), "calls", 0) else "nccl"),
