@@ -103,13 +103,11 @@ class _Block:
 
 
 class BlockStreamer:
-    """Keeps an InferenceEngine's block weights on the host and streams them per block."""
+    """Keeps a sequence of blocks' weights on the host and streams them per block.
+    `per_block[i]` lists every tensor block i reads."""
 
-    def __init__(self, engine, device):
-        self.engine = engine
+    def __init__(self, per_block, device):
         self.device = torch.device(device)
-        n = len(engine.blocks)
-        per_block = [_refs(engine.blocks[i], engine.model.transformer_blocks[i]) for i in range(n)]
         owners = {}
         for i, ts in enumerate(per_block):
             for t in ts:
@@ -165,7 +163,9 @@ def enable_block_offload(engine, device=None):
         return engine.offload
     if device is None:
         device = engine.blocks[0].w_qkvg.device
-    streamer = BlockStreamer(engine, device)
+    per_block = [_refs(engine.blocks[i], engine.model.transformer_blocks[i])
+                 for i in range(len(engine.blocks))]
+    streamer = BlockStreamer(per_block, device)
     engine.offload = streamer
     engine.compute_device = torch.device(device)
     resident_forward = engine.block_forward
@@ -178,4 +178,28 @@ def enable_block_offload(engine, device=None):
             streamer.release(i)
 
     engine.block_forward = block_forward
+    return streamer
+
+
+def enable_module_offload(model, device):
+    """Stream an eager H3Transformer's DiT blocks (its `transformer_blocks`, parameters and
+    buffers) from pinned host memory through forward hooks, the same way as
+    `enable_block_offload` does for the fused engine; everything outside the blocks must
+    already be on `device`. Returns the BlockStreamer (also `model._vdn_offload`)."""
+    if getattr(model, "_vdn_offload", None) is not None:
+        return model._vdn_offload
+    blocks = list(model.transformer_blocks)
+    per_block = []
+    for blk in blocks:
+        seen, ts = set(), []
+        for t in list(blk.parameters()) + list(blk.buffers()):
+            if id(t) not in seen:
+                seen.add(id(t))
+                ts.append(t)
+        per_block.append(ts)
+    streamer = BlockStreamer(per_block, device)
+    for i, blk in enumerate(blocks):
+        blk.register_forward_pre_hook(lambda mod, args, i=i: streamer.acquire(i))
+        blk.register_forward_hook(lambda mod, args, out, i=i: streamer.release(i))
+    model._vdn_offload = streamer
     return streamer
