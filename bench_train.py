@@ -319,6 +319,8 @@ def main(argv=None):
             "linear_calls": _linear_calls(),
             "reduce_scatter": ("symmetric memory (own kernel)" if getattr(
                 getattr(model, "_vdn_reduce_comm", None), "calls", 0) else "nccl"),
+            "all_gather": ("symmetric memory (own kernel)" if getattr(
+                getattr(model, "_vdn_gather_comm", None), "calls", 0) else "nccl"),
             "phases_s": phases,
             "phases_note": "wall seconds of the last warm-up step (synchronising timers, not in the timed steps)",
             "step_ms": [round(x, 1) for x in per_step],
@@ -339,9 +341,7 @@ def main(argv=None):
             line["peak_gib"] = round(torch.cuda.max_memory_allocated() / 2 ** 30, 1)
             line["saved_per_block_gib"] = saved.get("per_block_gib")
         print(json.dumps(line), flush=True)
-    comm = getattr(model, "_vdn_reduce_comm", None)
-    if comm is not None:
-        comm.close()
+    fs.close_comms(model)
     dist.destroy_process_group()
     return 0
 

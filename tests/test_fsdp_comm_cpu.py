@@ -1,7 +1,7 @@
-"""The FSDP2 reduce-scatter comm on CPU: its allocate() hands out one buffer per call in
-FSDP's input / output order (only inputs may ever come from a slot), and set on every
-fully_shard unit it leaves the gradients of 2 gloo ranks exactly as stock FSDP2 makes them
-(on CPU every call takes the torch.distributed fallback)."""
+"""The FSDP2 reduce-scatter and all-gather comms on CPU: the reduce-scatter's allocate() hands
+out one buffer per call in FSDP's input / output order (only inputs may ever come from a
+slot), and set on every fully_shard unit the two comms leave the gradients of 2 gloo ranks
+exactly as stock FSDP2 makes them (on CPU every call takes the torch.distributed fallback)."""
 import os
 import socket
 
@@ -26,7 +26,7 @@ def _model():
 
 def _grads(custom):
     from torch.distributed.fsdp import fully_shard
-    from vdn_minimax_h3_b200.parallel.fsdp_comm import SymmetricReduceScatter
+    from vdn_minimax_h3_b200.parallel.fsdp_comm import SymmetricAllGather, SymmetricReduceScatter
     m = _model()
     fully_shard(m[0])
     fully_shard(m[2])
@@ -34,8 +34,10 @@ def _grads(custom):
     comm = None
     if custom:
         comm = SymmetricReduceScatter(dist.group.WORLD, "cpu", 1024)
+        comm.gather = SymmetricAllGather(dist.group.WORLD, "cpu", 4096)
         for u in (m[0], m[2], m):
             u.set_custom_reduce_scatter(comm)
+            u.set_custom_all_gather(comm.gather)
     torch.manual_seed(10 + dist.get_rank())
     x = torch.randn(5, 16)
     m(x).square().sum().backward()
@@ -50,7 +52,8 @@ def _worker(rank, world, port, q):
         ref, _ = _grads(False)
         got, comm = _grads(True)
         same = all(torch.equal(ref[k], got[k]) for k in ref)
-        q.put((rank, same and comm.fallbacks > 0 and not comm.enabled()))
+        q.put((rank, same and comm.fallbacks > 0 and not comm.enabled()
+               and comm.gather.fallbacks > 0 and not comm.gather.enabled()))
     except Exception as exc:  # noqa: BLE001
         q.put((rank, repr(exc)))
     finally:

@@ -200,7 +200,7 @@ def test_tp_ulysses_match_single(world, tp, fp8):
     assert all(isinstance(v, float) and v < tol for v in res.values()), res
 
 
-def _fsdp_rs_worker(rank, world, port, q):
+def _fsdp_comm_worker(rank, world, port, q, gather):
     import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -209,40 +209,56 @@ def _fsdp_rs_worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=120))
     try:
-        from torch.distributed.fsdp import fully_shard
+        from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
         from vdn_minimax_h3_b200.ops._ext import check_device_error
-        from vdn_minimax_h3_b200.parallel.fsdp_comm import SymmetricReduceScatter, trainable_reduce_numel
+        from vdn_minimax_h3_b200.parallel.fsdp_comm import (SymmetricAllGather, SymmetricReduceScatter,
+                                                            gather_shard_bytes, trainable_reduce_numel)
 
         def grads(custom, steps=3):
             torch.manual_seed(0)
             m = torch.nn.Sequential(torch.nn.Linear(256, 512), torch.nn.GELU(),
                                     torch.nn.Linear(512, 256), torch.nn.GELU(),
                                     torch.nn.Linear(256, 40)).to(dev)
+            mp = MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32) \
+                if gather else None
+            kw = {"mp_policy": mp} if mp is not None else {}
             for i in (0, 2, 4):
-                fully_shard(m[i])
-            fully_shard(m)
-            comm = None
+                fully_shard(m[i], **kw)
+            fully_shard(m, **kw)
+            comms = []
             if custom:
                 groups = [list(m[i].parameters()) for i in (0, 2, 4)]
-                comm = SymmetricReduceScatter(dist.group.WORLD, dev,
-                                              trainable_reduce_numel(groups, world), slots=2)
+                rs = SymmetricReduceScatter(dist.group.WORLD, dev,
+                                            trainable_reduce_numel(groups, world), slots=2)
+                comms.append(rs)
                 for u in (m[0], m[2], m[4], m):
-                    u.set_custom_reduce_scatter(comm)
+                    u.set_custom_reduce_scatter(rs)
+                if gather:
+                    ag = SymmetricAllGather(dist.group.WORLD, dev, gather_shard_bytes(groups, world))
+                    comms.append(ag)
+                    for u in (m[0], m[2], m[4], m):
+                        u.set_custom_all_gather(ag)
             out = []
-            for s in range(steps):     # more steps than slots: the slot ring is reused
+            for s in range(steps):     # more steps than slots: the slot rings are reused
                 torch.manual_seed(100 * s + rank)
-                m(torch.randn(64, 256, device=dev)).square().mean().backward()
-                out.append({n: p.grad.full_tensor().clone() for n, p in m.named_parameters()})
+                loss = m(torch.randn(64, 256, device=dev)).float().square().mean()
+                loss.backward()
+                g = {n: p.grad.full_tensor().clone() for n, p in m.named_parameters()}
+                g["loss"] = loss.detach().reshape(1)
+                out.append(g)
                 m.zero_grad(set_to_none=True)
             torch.cuda.synchronize()
-            return out, comm
+            return out, comms
 
         ref, _ = grads(False)
-        got, comm = grads(True)
+        got, comms = grads(True)
         check_device_error()
         err = max(((a[k] - b[k]).norm() / b[k].norm()).item() for a, b in zip(got, ref) for k in b)
-        res = err if (comm.calls > 0 and comm.fallbacks == 0) else f"calls {comm.calls} fallbacks {comm.fallbacks}"
-        comm.close()
+        bad = [f"{type(c).__name__} calls {c.calls} fallbacks {c.fallbacks}" for c in comms
+               if c.calls == 0 or c.fallbacks]
+        res = err if not bad else "; ".join(bad)
+        for c in comms:
+            c.close()
         q.put((rank, res))
     except Exception as exc:  # noqa: BLE001
         import traceback
@@ -260,4 +276,25 @@ def test_fsdp_symmetric_reduce_scatter(world):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     res = _spawn(_fsdp_rs_worker, world)
+    assert all(isinstance(v, float) and v < 1e-5 for v in res.values()), res
+
+
+def _fsdp_rs_worker(rank, world, port, q):
+    _fsdp_comm_worker(rank, world, port, q, gather=False)
+
+
+def _fsdp_ag_worker(rank, world, port, q):
+    _fsdp_comm_worker(rank, world, port, q, gather=True)
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("world", [2, 4])
+def test_fsdp_symmetric_all_gather(world):
+    """FSDP2 (bf16 parameters) with both its parameter all-gather (shard -> symmetric slot,
+    flag barrier, peer-pull kernel) and its gradient reduce-scatter over symmetric memory
+    gives the stock NCCL losses and gradients -- the gather moves bytes, so they match
+    exactly -- over three steps that reuse both slot rings."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _spawn(_fsdp_ag_worker, world)
     assert all(isinstance(v, float) and v < 1e-5 for v in res.values()), res

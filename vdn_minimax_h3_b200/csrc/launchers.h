@@ -183,6 +183,11 @@ void symm_close(void* peer_ptr);
 void symm_free(void* p);
 void launch_symm_reduce_scatter(const float* const* srcs, int P, int64_t offset, int64_t n,
                                 float scale, float* out, cudaStream_t stream);
+
+// out[q * shard_bytes ...] = srcs[q][0 .. shard_bytes) for every rank q != rank (the FSDP2
+// parameter all-gather over symmetric memory; this rank's shard is already in `out`).
+void launch_symm_all_gather(const void* const* srcs, int P, int rank, int64_t shard_bytes, void* out,
+                            cudaStream_t stream);
 void launch_symm_barrier(unsigned long long* counter, unsigned long long* local_flags,
                          unsigned long long* const* peer_flags, int rank, int P,
                          long long timeout_ns, int* err, cudaStream_t stream);

@@ -868,6 +868,20 @@ void symm_reduce_scatter(std::vector<int64_t> srcs, int64_t offset, torch::Tenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// out[q * shard_bytes, (q + 1) * shard_bytes) = the shard at srcs[q], for every rank q != rank.
+void symm_all_gather(std::vector<int64_t> srcs, int64_t rank, torch::Tensor out, int64_t shard_bytes) {
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous(), "out must be a contiguous CUDA tensor");
+  const int P = (int)srcs.size();
+  TORCH_CHECK((int64_t)out.numel() * out.element_size() >= (int64_t)P * shard_bytes,
+              "out is smaller than ranks x shard_bytes");
+  std::vector<const void*> p;
+  for (auto a : srcs) p.push_back(reinterpret_cast<const void*>(a));
+  c10::cuda::CUDAGuard g(out.device());
+  launch_symm_all_gather(p.data(), P, (int)rank, shard_bytes, out.data_ptr(),
+                         at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void symm_barrier(int64_t counter, int64_t local_flags, torch::Tensor peer_flags, int64_t rank,
                   int64_t timeout_ns, torch::Tensor err) {
   TORCH_CHECK(peer_flags.is_cuda() && peer_flags.scalar_type() == at::kLong &&
@@ -924,6 +938,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_prep", &vdn::qk_prep, "per-head RMSNorm + rotate-half RoPE");
   m.def("window_attention", &vdn::window_attention,
         "tcgen05 window softmax attention over an AttentionPlan (gated epilogue)");
+  m.def("symm_all_gather", &vdn::symm_all_gather,
+        "all-gather of equal shards read from peers' symmetric memory",
+        py::arg("srcs"), py::arg("rank"), py::arg("out"), py::arg("shard_bytes"));
   m.def("symm_reduce_scatter", &vdn::symm_reduce_scatter,
         "reduce-scatter by peer loads over a symmetric buffer (fp32 sum, scaled)");
   m.def("window_attention_bwd", &vdn::window_attention_bwd,

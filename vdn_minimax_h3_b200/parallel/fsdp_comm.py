@@ -1,4 +1,5 @@
-"""FSDP2 gradient reduce-scatter over symmetric memory instead of NCCL.
+"""FSDP2 gradient reduce-scatter and parameter all-gather over symmetric memory instead of
+NCCL.
 
 FSDP2 (torch.distributed.fsdp.fully_shard) lets a module replace its reduce-scatter with a
 `ReduceScatter` comm object that also allocates the buffers. `SymmetricReduceScatter`
@@ -12,8 +13,17 @@ AVG) as it stores -- no NCCL, no intermediate buffer -- between two device flag 
 while peers still read it). It runs on FSDP's reduce-scatter stream, so it overlaps the
 backward of the next block like the NCCL call it replaces.
 
-Reference: the implicit reduce-scatter of FSDP2 in src/training/fsdp_stage.py:392-451
-(NCCL). What is NOT done here: the all-gather fused into the first consuming GEMM.
+`SymmetricAllGather` is the parameter all-gather: FSDP keeps its own output buffer (its
+copy-in already put this rank's shard at the rank's slice); the comm copies that shard into
+a slot of a symmetric heap, passes one device flag barrier, and one kernel
+(csrc/symmetric.cu: symm_all_gather) pulls every peer's shard over NVLink into the output,
+all on FSDP's all-gather stream. Two slots suffice without a closing barrier: a rank writes
+slot k again only after passing the barrier of the gather after k, which every rank reaches
+only once its pull of gather k is done (stream order).
+
+Reference: the implicit all-gather / reduce-scatter of FSDP2 in
+src/training/fsdp_stage.py:392-451 (NCCL). What is NOT done here: the all-gather fused into
+the first consuming GEMM (the gathered parameters still land in FSDP's unsharded buffer).
 
 A slot is reused only after the event recorded behind its closing barrier, waited on by the
 stream that allocates it again. Anything the kernel does not take (non-fp32 dtype, an op
@@ -24,7 +34,7 @@ import math
 
 import torch
 import torch.distributed as dist
-from torch.distributed.fsdp._fully_shard._fsdp_collectives import ReduceScatter
+from torch.distributed.fsdp._fully_shard._fsdp_collectives import AllGather, ReduceScatter
 
 
 class SymmetricReduceScatter(ReduceScatter):
@@ -116,4 +126,83 @@ def trainable_reduce_numel(param_groups, world):
                 d0 = p.shape[0] if p.dim() else 1
                 total += math.ceil(d0 / world) * world * (p.numel() // max(d0, 1))
         best = max(best, total)
+    return best
+
+
+class SymmetricAllGather(AllGather):
+    """FSDP2 parameter all-gather: shard -> symmetric slot, flag barrier, peer-pull kernel."""
+
+    def __init__(self, group, device, slot_bytes, slots=2):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        self.slots = max(2, int(slots))
+        self.slot_bytes = int(math.ceil(slot_bytes / 256) * 256)
+        self.heap = None
+        self._next = 0
+        self._srcs = {}
+        self.calls = self.fallbacks = 0
+        if self.enabled():
+            from vdn_minimax_h3_b200.parallel.symmetric import SymmetricHeap
+            specs = [((self.slot_bytes,), torch.uint8)] * self.slots
+            self.heap = SymmetricHeap(SymmetricHeap.required_bytes(specs), group, self.device,
+                                      timeout_s=120.0)
+            for i in range(self.slots):
+                self.heap.alloc(f"ag{i}", (self.slot_bytes,), torch.uint8)
+
+    def enabled(self):
+        return self.device.type == "cuda" and 1 < self.world <= 8 and self.slot_bytes > 0
+
+    def allocate(self, size, *, dtype, device):
+        return torch.empty(*size, dtype=dtype, device=device)
+
+    def _same_group(self, group):
+        if group is self.group:
+            return True
+        return dist.get_process_group_ranks(group) == dist.get_process_group_ranks(self.group)
+
+    def close(self):
+        if self.heap is not None:
+            torch.cuda.synchronize(self.device)
+            self.heap.check()
+            self.heap.close()
+            self.heap = None
+
+    def __call__(self, output_tensor, input_tensor, group, async_op=False):
+        shard = input_tensor.numel() * input_tensor.element_size()
+        in_place = (output_tensor.is_contiguous() and input_tensor.is_contiguous()
+                    and output_tensor.numel() == input_tensor.numel() * self.world
+                    and input_tensor.data_ptr() == output_tensor.data_ptr() + self.rank * shard)
+        if (self.heap is None or async_op or not in_place or not self._same_group(group)
+                or shard > self.slot_bytes or shard % 16 or output_tensor.data_ptr() % 16):
+            self.fallbacks += 1
+            return dist.all_gather_into_tensor(output_tensor, input_tensor, group=group,
+                                               async_op=async_op)
+        from vdn_minimax_h3_b200.ops._ext import ext
+        slot = self._next
+        self._next = (self._next + 1) % self.slots
+        local = self.heap.local(f"ag{slot}")[:shard]
+        local.copy_(input_tensor.view(-1).view(torch.uint8))
+        srcs = self._srcs.get(slot)
+        if srcs is None:
+            srcs = self._srcs[slot] = [self.heap.peer(f"ag{slot}", p).data_ptr()
+                                       for p in range(self.world)]
+        self.heap.barrier()                      # every rank's shard is in its slot
+        ext().symm_all_gather(srcs, self.rank, output_tensor, shard)
+        self.calls += 1
+        return None
+
+
+def gather_shard_bytes(param_groups, world, elem_bytes=4):
+    """Largest per-rank all-gather shard (bytes) FSDP will form for one of the parameter
+    groups: the dim-0-padded shard of every parameter, at `elem_bytes` per element (an upper
+    bound for the bf16 / fp32 mixed-precision gathers)."""
+    best = 0
+    for params in param_groups:
+        total = 0
+        for p in params:
+            d0 = p.shape[0] if p.dim() else 1
+            total += math.ceil(d0 / world) * (p.numel() // max(d0, 1))
+        best = max(best, total * elem_bytes)
     return best

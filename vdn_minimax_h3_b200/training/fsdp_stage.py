@@ -269,14 +269,16 @@ def restore_optimizer_and_rng(resume, model, optimizer, generators):
 # ------------------------------------------------------------------------- sharding
 def shard_model(model, device, shard_size=None, activation_checkpointing=True, split_ac=True,
                 param_dtype=torch.bfloat16, reduce_dtype=torch.float32, symmetric_reduce=None,
-                kernel_linears=True):
+                kernel_linears=True, symmetric_gather=None):
     """fully_shard each refiner block and DiT block (alpha modules first, in fp32), then the
     root; HSDP when the world is larger than `shard_size`. On CUDA every nn.Linear first gets
     the GEMM-kernel forward / dgrad / wgrad of ops/linear_grad.py (`kernel_linears`; the
     module switch linear_grad.LINEAR_KERNELS turns it off at run time). With `symmetric_reduce` (default:
     on for CUDA shard groups of 2-8 ranks) the gradient reduce-scatter of every unit runs over
-    symmetric memory (parallel/fsdp_comm.py) instead of NCCL; the comm object is returned as
-    `model._vdn_reduce_comm` (close() it before destroying the process group)."""
+    symmetric memory (parallel/fsdp_comm.py) instead of NCCL, and with `symmetric_gather`
+    (same default) the parameter all-gather as well; the comm objects are kept as
+    `model._vdn_reduce_comm` / `model._vdn_gather_comm` (`close_comms(model)` before
+    destroying the process group)."""
     from torch.distributed.device_mesh import init_device_mesh
     from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
     from vdn_minimax_h3_b200.utils.activation_checkpointing import enable_block_checkpointing
@@ -320,7 +322,30 @@ def shard_model(model, device, shard_size=None, activation_checkpointing=True, s
             for u in units:
                 u.set_custom_reduce_scatter(comm)
         model._vdn_reduce_comm = comm
+    if symmetric_gather is None:
+        symmetric_gather = dev_type == "cuda" and 1 < shard <= 8
+    if symmetric_gather:
+        from torch.distributed.fsdp import FSDPModule
+        from vdn_minimax_h3_b200.parallel.fsdp_comm import SymmetricAllGather, gather_shard_bytes
+        units = [m for m in model.modules() if isinstance(m, FSDPModule)]
+        blocks = list(model.transformer_blocks) + list(model.token_refiner.refiner_blocks)
+        in_blocks = {id(p) for b in blocks for p in b.parameters()}
+        groups = [list(b.parameters()) for b in blocks]
+        groups.append([p for p in model.parameters() if id(p) not in in_blocks])
+        comm = SymmetricAllGather(mesh.get_group("shard"), device, gather_shard_bytes(groups, shard))
+        if comm.enabled():
+            for u in units:
+                u.set_custom_all_gather(comm)
+        model._vdn_gather_comm = comm
     return model
+
+
+def close_comms(model):
+    """Release the symmetric heaps of the FSDP comms `shard_model` installed."""
+    for name in ("_vdn_reduce_comm", "_vdn_gather_comm"):
+        comm = getattr(model, name, None)
+        if comm is not None:
+            comm.close()
 
 
 def trainable_select(include_lora=True, adapter_names=None):

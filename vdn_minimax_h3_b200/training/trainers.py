@@ -239,9 +239,7 @@ def _fsdp_stage(cfg, stage):
                                 keep_states=cfg.checkpoint.keep_states)
     if hb is not None:
         hb.stop()
-    comm = getattr(model, "_vdn_reduce_comm", None)
-    if comm is not None:
-        comm.close()
+    fs.close_comms(model)
     if fs.rank0():
         open(os.path.join(out, "DONE"), "w").close()
         run_lock.release(out)
