@@ -256,7 +256,7 @@ def _fsdp_comm_worker(rank, world, port, q, gather):
         err = max(((a[k] - b[k]).norm() / b[k].norm()).item() for a, b in zip(got, ref) for k in b)
         bad = [f"{type(c).__name__} calls {c.calls} fallbacks {c.fallbacks}" for c in comms
                if c.calls == 0 or c.fallbacks]
-        res = err if not bad else "; ".join(bad)
+        res = err if not bad else f"err {err}; " + "; ".join(bad)
         for c in comms:
             c.close()
         q.put((rank, res))

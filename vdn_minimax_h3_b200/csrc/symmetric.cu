@@ -91,6 +91,11 @@ struct ReduceSrc {
   const float* p[kMaxReducePeers];
 };
 
+template <typename V>
+struct GatherSrcT {
+  const V* p[kMaxReducePeers];
+};
+
 __global__ void __launch_bounds__(256) symm_reduce_scatter_kernel(ReduceSrc src, int P,
                                                                   int64_t offset, int64_t n,
                                                                   float scale, float* __restrict__ out) {
@@ -142,42 +147,49 @@ void launch_symm_reduce_scatter(const float* const* srcs, int P, int64_t offset,
 
 // All-gather of equal shards held in symmetric memory: out[q * shard + i] = src[q][i] for every
 // rank q other than `rank` (this rank's shard is already in place). Consecutive threads read
-// different peers, so every NVLink peer is streamed from at once; 16-byte loads and stores.
-struct GatherSrc {
-  const uint4* p[kMaxReducePeers];
-};
-
-__global__ void __launch_bounds__(256) symm_all_gather_kernel(GatherSrc src, int P, int rank,
-                                                              int64_t shard_vec,
-                                                              uint4* __restrict__ out) {
+// different peers, so every NVLink peer is streamed from at once. The copy unit V is the
+// widest of 16 / 8 / 4 / 2 / 1 bytes that divides the shard size (FSDP pads each parameter's
+// dim 0, not the shard total, so a shard need not be a multiple of 16 bytes).
+template <typename V>
+__global__ void __launch_bounds__(256) symm_all_gather_kernel(GatherSrcT<V> src, int P, int rank,
+                                                              int64_t shard_units, V* __restrict__ out) {
   const int others = P - 1;
-  const int64_t total = (int64_t)others * shard_vec;
+  const int64_t total = (int64_t)others * shard_units;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int64_t w = i / others;
     const int j = (int)(i - w * others);
     const int q = j + (j >= rank ? 1 : 0);
-    out[(int64_t)q * shard_vec + w] = src.p[q][w];
+    out[(int64_t)q * shard_units + w] = src.p[q][w];
   }
+}
+
+template <typename V>
+static void launch_gather(const void* const* srcs, int P, int rank, int64_t shard_bytes, void* out,
+                          cudaStream_t stream) {
+  GatherSrcT<V> s{};
+  for (int q = 0; q < P; ++q) s.p[q] = reinterpret_cast<const V*>(srcs[q]);
+  const int64_t units = shard_bytes / (int64_t)sizeof(V);
+  int64_t blocks = ((P - 1) * units + 255) / 256;
+  blocks = blocks < 1 ? 1 : (blocks > 8 * 148 ? 8 * 148 : blocks);
+  symm_all_gather_kernel<V><<<(int)blocks, 256, 0, stream>>>(s, P, rank, units, reinterpret_cast<V*>(out));
 }
 
 void launch_symm_all_gather(const void* const* srcs, int P, int rank, int64_t shard_bytes, void* out,
                             cudaStream_t stream) {
   if (P < 1 || P > kMaxReducePeers) throw std::runtime_error("symm_all_gather: 1..8 ranks");
   if (rank < 0 || rank >= P) throw std::runtime_error("symm_all_gather: rank out of range");
-  if (shard_bytes % 16 || reinterpret_cast<uintptr_t>(out) % 16)
-    throw std::runtime_error("symm_all_gather: shard size and output must be 16-byte aligned");
-  GatherSrc s{};
-  for (int q = 0; q < P; ++q) {
+  if (reinterpret_cast<uintptr_t>(out) % 16)
+    throw std::runtime_error("symm_all_gather: output must be 16-byte aligned");
+  for (int q = 0; q < P; ++q)
     if (reinterpret_cast<uintptr_t>(srcs[q]) % 16)
       throw std::runtime_error("symm_all_gather: sources must be 16-byte aligned");
-    s.p[q] = reinterpret_cast<const uint4*>(srcs[q]);
-  }
-  const int64_t vec = shard_bytes / 16;
-  if (P == 1 || vec == 0) return;
-  int64_t blocks = ((P - 1) * vec + 255) / 256;
-  blocks = blocks < 1 ? 1 : (blocks > 8 * 148 ? 8 * 148 : blocks);
-  symm_all_gather_kernel<<<(int)blocks, 256, 0, stream>>>(s, P, rank, vec, reinterpret_cast<uint4*>(out));
+  if (P == 1 || shard_bytes <= 0) return;
+  if (shard_bytes % 16 == 0) launch_gather<uint4>(srcs, P, rank, shard_bytes, out, stream);
+  else if (shard_bytes % 8 == 0) launch_gather<uint2>(srcs, P, rank, shard_bytes, out, stream);
+  else if (shard_bytes % 4 == 0) launch_gather<uint32_t>(srcs, P, rank, shard_bytes, out, stream);
+  else if (shard_bytes % 2 == 0) launch_gather<uint16_t>(srcs, P, rank, shard_bytes, out, stream);
+  else launch_gather<uint8_t>(srcs, P, rank, shard_bytes, out, stream);
 }
 
 void launch_symm_barrier(unsigned long long* counter, unsigned long long* local_flags,

@@ -175,7 +175,7 @@ class SymmetricAllGather(AllGather):
                     and output_tensor.numel() == input_tensor.numel() * self.world
                     and input_tensor.data_ptr() == output_tensor.data_ptr() + self.rank * shard)
         if (self.heap is None or async_op or not in_place or not self._same_group(group)
-                or shard > self.slot_bytes or shard % 16 or output_tensor.data_ptr() % 16):
+                or shard > self.slot_bytes or output_tensor.data_ptr() % 16):
             self.fallbacks += 1
             return dist.all_gather_into_tensor(output_tensor, input_tensor, group=group,
                                                async_op=async_op)
