@@ -2,6 +2,7 @@
 LoRA merge semantics, decode-and-save stand-ins."""
 import os
 
+import pytest
 import torch
 
 from vdn_minimax_h3_b200.inference.lora import merge_lora_state, random_lora_state, translate_original_layout
@@ -83,3 +84,72 @@ def test_decode_and_save(tmp_path):
         assert frame.shape == (64, 96, 3)
         n += 1
     assert n == 22
+
+
+def _decode_rank(rank, world, port, out_dir, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from vdn_minimax_h3_b200.inference.vae import (AudioDecoderStandIn, VideoDecoderStandIn,
+                                                       decode_and_save)
+        torch.manual_seed(0)
+        lat = torch.randn(1, 24, 7, 4, 6)
+        aud = torch.randn(2, 32, 5)
+        dec = VideoDecoderStandIn(24, widths=(16, 16, 8, 8), chunk_frames=5)
+        timings = {}
+        out = decode_and_save(lat, aud, os.path.join(out_dir, "dist.mp4"), dec,
+                              AudioDecoderStandIn(32), timings=timings)
+        q.put((rank, (out, sorted(timings))))
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(240)
+def test_decode_and_save_split_over_ranks(tmp_path):
+    """Two gloo ranks each decode and encode half of the frames; rank 0 joins the two
+    encoded segments: one mp4 with every frame (each within the codec's error of the
+    single-process encode) and the soundtrack; the other rank returns None."""
+    import socket
+    import cv2
+    import torch.multiprocessing as mp
+    from vdn_minimax_h3_b200.inference.mp4mux import track_handlers
+    from vdn_minimax_h3_b200.inference.vae import AudioDecoderStandIn, VideoDecoderStandIn
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_decode_rank, args=(r, 2, port, str(tmp_path), q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=200) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+    assert res[1] == (None, ["decode_s", "encode_s"]), res
+    out, keys = res[0]
+    assert keys == ["decode_s", "encode_s", "frames", "mux_s"], res
+    data = open(out, "rb").read()
+    assert track_handlers(data) == [b"vide", b"soun"]
+    torch.manual_seed(0)
+    lat = torch.randn(1, 24, 7, 4, 6)
+    aud = torch.randn(2, 32, 5)
+    single = decode_and_save(lat, aud, str(tmp_path / "single.mp4"),
+                             VideoDecoderStandIn(24, widths=(16, 16, 8, 8), chunk_frames=5),
+                             AudioDecoderStandIn(32))
+
+    def frames(path):
+        cap, got = cv2.VideoCapture(path), []
+        while True:
+            ok, f = cap.read()
+            if not ok:
+                return got
+            got.append(f.astype("float32"))
+
+    a, b = frames(out), frames(single)
+    assert len(a) == len(b) == 22
+    for x, y in zip(a, b):
+        assert abs(x - y).mean() < 8.0

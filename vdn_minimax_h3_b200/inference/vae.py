@@ -137,17 +137,19 @@ def _to_uint8(video):
     return (pix * 255).round().to(torch.uint8).permute(0, 2, 3, 1)
 
 
-@torch.no_grad()
-def decode_frames(latents, video_decoder, group=None, single=False):
-    """uint8 frames [P, H, W, 3] on the host of rank 0 (None elsewhere). Under an initialised
-    process group (unless `single`) every rank decodes a contiguous share of the pixel frames
-    and rank 0 gathers them."""
+def _ranks(group, single=False):
     import torch.distributed as dist
-    dev = latents.device
-    dec = video_decoder.prepare(dev)
     on = not single and dist.is_available() and dist.is_initialized()
     world = dist.get_world_size(group) if on else 1
-    rank = dist.get_rank(group) if world > 1 else 0
+    return (dist.get_rank(group) if world > 1 else 0), world
+
+
+@torch.no_grad()
+def decode_share(latents, video_decoder, rank=0, world=1):
+    """This rank's contiguous share of the pixel frames, uint8 [n, H, W, 3] on the latents'
+    device, and the total pixel frame count P (shares of ceil(P / world) frames)."""
+    dev = latents.device
+    dec = video_decoder.prepare(dev)
     z = dec.latent_stage(latents)
     P = pixel_frames(latents.shape[2])
     share = -(-P // world)
@@ -156,6 +158,20 @@ def decode_frames(latents, video_decoder, group=None, single=False):
              for a in range(p0, p1, dec.chunk_frames)]
     H, W = latents.shape[3] * dec.spatial, latents.shape[4] * dec.spatial
     mine = torch.cat(parts) if parts else torch.empty(0, H, W, 3, dtype=torch.uint8, device=dev)
+    return mine, P
+
+
+@torch.no_grad()
+def decode_frames(latents, video_decoder, group=None, single=False):
+    """uint8 frames [P, H, W, 3] on the host of rank 0 (None elsewhere). Under an initialised
+    process group (unless `single`) every rank decodes a contiguous share of the pixel frames
+    and rank 0 gathers them."""
+    import torch.distributed as dist
+    rank, world = _ranks(group, single)
+    mine, P = decode_share(latents, video_decoder, rank, world)
+    dev = mine.device
+    H, W = mine.shape[1], mine.shape[2]
+    share = -(-P // world)
     if world == 1:
         return mine.cpu()
     pad = torch.zeros(share, H, W, 3, dtype=torch.uint8, device=dev)
@@ -218,28 +234,44 @@ def mux_pcm(video_mp4, audio, rate=AUDIO_SAMPLE_RATE):
 @torch.no_grad()
 def decode_and_save(latents, audio_latents, out_path, video_decoder=None, audio_decoder=None,
                     group=None, timings=None):
-    """Decodes (every rank of `group` takes a share of the frames) and writes one mp4 with
-    sound on rank 0; returns the path there and None on the other ranks. `timings` (a dict)
-    receives the seconds spent decoding, encoding and muxing on this rank."""
+    """Decodes and writes one mp4 with sound on rank 0; returns the path there and None on
+    the other ranks. Under an initialised process group every rank of `group` decodes a
+    contiguous share of the frames, copies only that share to its host and encodes it there
+    (its own key frame first); rank 0 gathers the encoded segments -- a few MB instead of
+    the raw frames -- and joins them into one track (mp4mux.concat_video_segments).
+    `timings` (a dict) receives the seconds spent decoding (to host), encoding (with the
+    segment gather and join) and muxing on this rank."""
     video_decoder = video_decoder or VideoDecoderStandIn(latents.shape[1])
     audio_decoder = audio_decoder or AudioDecoderStandIn(audio_latents.shape[1])
+    rank, world = _ranks(group)
     t0 = time.perf_counter()
-    frames = decode_frames(latents, video_decoder, group)
-    audio = audio_decoder.to(latents.device)(audio_latents.float()).clamp(-1, 1).cpu()
+    mine, P = decode_share(latents, video_decoder, rank, world)
+    frames = mine.cpu()
+    audio = audio_decoder.to(latents.device)(audio_latents.float()).clamp(-1, 1).cpu() \
+        if rank == 0 else None
     t1 = time.perf_counter()
-    if frames is None:
-        if timings is not None:
-            timings.update(decode_s=t1 - t0)
-        return None
+    if world == 1:
+        video = encode_mp4(frames)
+    else:
+        import torch.distributed as dist
+        from vdn_minimax_h3_b200.inference.mp4mux import concat_video_segments
+        threads = max(1, (os.cpu_count() or 1) // world)
+        seg = encode_mp4(frames, workers=threads) if frames.shape[0] else b""
+        segs = [None] * world
+        dist.all_gather_object(segs, seg, group=group)
+        if rank != 0:
+            if timings is not None:
+                timings.update(decode_s=t1 - t0, encode_s=time.perf_counter() - t1)
+            return None
+        video = concat_video_segments([x for x in segs if x])
     os.makedirs(os.path.dirname(os.path.abspath(out_path)) or ".", exist_ok=True)
     stem, ext = os.path.splitext(out_path)
     partial = f"{stem}.partial{ext}"
-    video = encode_mp4(frames)
     t2 = time.perf_counter()
     with open(partial, "wb") as f:
         f.write(mux_pcm(video, audio))
     os.replace(partial, out_path)
     if timings is not None:
         timings.update(decode_s=t1 - t0, encode_s=t2 - t1, mux_s=time.perf_counter() - t2,
-                       frames=int(frames.shape[0]))
+                       frames=int(P))
     return out_path
