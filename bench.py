@@ -241,8 +241,10 @@ def main(argv=None):
         # The public API end to end: inputs from pinned host memory, the 8-NFE render
         # (inference.render.generate_latents), then inference.vae.decode_and_save -- the
         # video decoder stand-in (the VAE's geometry and ~700 TFLOP of convolutions, frames
-        # split across the ranks), OpenCV's mp4 encode and the PCM soundtrack muxed into
-        # the same file on rank 0. Wall clock, both ends synchronised, max over ranks.
+        # split across the ranks), OpenCV's mp4 encode (each rank encodes its own frames,
+        # rank 0 joins the segments) and the PCM soundtrack muxed into the same file on
+        # rank 0. Wall clock, both ends synchronised, max over ranks. d2h counts every
+        # frame of the clip once (each rank copies its share).
         from vdn_minimax_h3_b200.inference.vae import (AudioDecoderStandIn, VideoDecoderStandIn,
                                                        decode_and_save, decode_frames)
         vdec, adec = VideoDecoderStandIn(geo.channels), AudioDecoderStandIn(32)
@@ -285,7 +287,8 @@ def main(argv=None):
                "note": "one clip through inference.render.generate_latents and "
                        "inference.vae.decode_and_save: H2D of the inputs, 8 NFE, decode by the "
                        "VAE-geometry decoder STAND-IN (random weights, ~700 TFLOP), uint8 "
-                       "frames to the host, OpenCV mp4v encode, PCM audio muxed into the mp4"}
+                       "frames to the host (each rank its share), OpenCV mp4v encode per rank, "
+                       "segments joined and PCM audio muxed into the mp4 on rank 0"}
         _ext.check_device_error(dev)
 
     if rank == 0:
