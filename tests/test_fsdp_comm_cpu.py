@@ -83,3 +83,38 @@ def test_allocate_alternates_input_and_output():
         shapes.append(tuple(c.allocate((64,), dtype=torch.float32, device="cpu").shape))
         shapes.append(tuple(c.allocate((32,), dtype=torch.float32, device="cpu").shape))
     assert shapes == [(64,), (32,)] * 3 and c._expect_output is False
+
+
+def test_shard_sizing_helpers():
+    """The slot sizes cover FSDP's dim-0-padded shards: reduce-scatter inputs count only
+    parameters that take gradients (fp32 elements), all-gather shards count every parameter
+    (bytes at the given element size)."""
+    from vdn_minimax_h3_b200.parallel.fsdp_comm import gather_shard_bytes, trainable_reduce_numel
+    w = torch.nn.Parameter(torch.zeros(40, 256))          # 40 rows over 3 ranks -> 14 per rank
+    b = torch.nn.Parameter(torch.zeros(40))
+    frozen = torch.nn.Parameter(torch.zeros(9, 16), requires_grad=False)
+    groups = [[w, b, frozen], [torch.nn.Parameter(torch.zeros(8, 8))]]
+    assert trainable_reduce_numel(groups, 3) == 14 * 3 * 256 + 14 * 3
+    assert gather_shard_bytes(groups, 3, elem_bytes=2) == (14 * 256 + 14 + 3 * 16) * 2
+    assert gather_shard_bytes(groups, 3) == (14 * 256 + 14 + 3 * 16) * 4
+
+
+def test_all_gather_falls_back_when_not_in_place():
+    """Without a heap (CPU) or when FSDP's input is not the output's own rank slice, the
+    gather goes to torch.distributed and is counted as a fallback."""
+    from vdn_minimax_h3_b200.parallel import fsdp_comm
+    c = fsdp_comm.SymmetricAllGather.__new__(fsdp_comm.SymmetricAllGather)
+    c.heap, c.world, c.rank, c.group, c.slot_bytes = None, 2, 1, None, 1 << 20
+    c.calls = c.fallbacks = 0
+    seen = []
+    orig = fsdp_comm.dist.all_gather_into_tensor
+    fsdp_comm.dist.all_gather_into_tensor = lambda out, inp, group=None, async_op=False: seen.append(
+        (out.shape, inp.shape)) or None
+    try:
+        out = torch.zeros(8)
+        assert c(out, out[4:], None) is None
+        assert c(out, torch.zeros(4), None) is None      # not in place
+    finally:
+        fsdp_comm.dist.all_gather_into_tensor = orig
+    assert c.fallbacks == 2 and c.calls == 0 and len(seen) == 2
+    assert c.allocate((3, 5), dtype=torch.bfloat16, device="cpu").shape == (3, 5)
