@@ -19,7 +19,7 @@ real and fake score x0) and on every turn the fake score's flow-matching update
 first generator turn; the line reports each turn kind's time and the whole-cycle rate
 (1 generator + 5 fake sub-iterations).
 
-One step on every rank = one synthetic clip (per-GPU batch 1) of the BASELINE training
+One step on every rank = one synthetic clip (per-GPU batch 1) of the headline training
 shape: 81 latent frames at the inference spatial latent size (48 x 84 -> 24 x 42 tokens per
 frame), the matching audio latents and an 800 x 5120 prompt; the full VDN-H3 geometry with
 random weights (backbone frozen; trainable: the hybrid branch and a rank-64 LoRA on the DiT
@@ -65,7 +65,7 @@ def parse(argv=None):
                    help="keep checkpointed activations on the GPU (the Stage B default, "
                         "distributed.offload_activations=true, saves them to pinned host memory)")
     p.add_argument("--ac", choices=("block", "two-level"), default="block",
-                   help="activation checkpointing: per block (BASELINE config 4), or per block "
+                   help="activation checkpointing: per block (the headline training setup), or per block "
                         "with the attention and feed-forward as inner regions")
     p.add_argument("--num-layers", type=int, default=None,
                    help="diagnostic only: fewer DiT blocks (the printed number is then not the "

@@ -1,5 +1,5 @@
 """CPU: the inference engine's packed/fused block equals the eager reference forward, the
-tiny golden sampling run, and the full-cover == dense-teacher rule."""
+tiny golden sampling run (the 2-block CPU configuration), and the full-cover == dense-teacher rule."""
 import copy
 
 import pytest
@@ -94,7 +94,7 @@ def test_full_cover_hybrid_equals_teacher():
 
 @torch.no_grad()
 def test_tiny_golden_two_euler_steps():
-    """latent [1,16,4,16,16], text [1,32,256], 2 Euler steps at sigma
+    """The tiny CPU configuration: latent [1,16,4,16,16], text [1,32,256], 2 Euler steps at sigma
     1.0 and 0.5 (shift 1); engine and eager agree and the run is deterministic."""
     cfg = h3_tiny_config()
     model = tiny_model()

@@ -184,5 +184,5 @@ TINY_HYBRID = dict(
     softmax_attention=dict(radius=0, chunk=2),
     linear_attention=dict(delta_rule="sana_scaled", linear_head_dim=None, bridge="alpha",
                           short_conv=dict(targets=[]), enable_text_state=False, a_fp32=True))
-"""BASELINE config 1's transform: a 2-frame window (chunk 2, radius 0), chunk-64 delta rule
+"""The tiny CPU configuration's transform: a 2-frame window (chunk 2, radius 0), chunk-64 delta rule
 (one 8x8 frame), beta = sigmoid(linear)."""

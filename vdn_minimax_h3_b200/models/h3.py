@@ -86,7 +86,7 @@ def h3_full_config():
 
 
 def h3_tiny_config():
-    """2 blocks, hidden 256, 4 heads of 64, GELU MLP 4x, 16 channels."""
+    """The tiny CPU configuration: 2 blocks, hidden 256, 4 heads of 64, GELU MLP 4x, 16 channels."""
     return H3Config(hidden_size=256, num_layers=2, num_attention_heads=4,
                     attention_head_dim=64, in_channels=16, audio_in_channels=32,
                     text_dim=256, time_embed_dim=256, time_freq_dim=64, ff_inner_dim=1024,
