@@ -14,10 +14,10 @@ keys and FSDP2 sharding are unchanged); a Linear whose tensors the kernel does n
 CPU tensors) runs F.linear. The module switch `LINEAR_KERNELS = False` sends every routed
 Linear back to F.linear (the labelled library baseline of the training bench).
 
-Reference parity: the reference trains every projection through nn.Linear / cuBLAS
-(src/training/fsdp_stage.py:392-451 wraps the stock modules; src/models/hybrid_attention.py
-projections); the math is the same product, the rounding is one bf16 rounding of an fp32
-accumulator as in cuBLAS.
+Reference parity: the reference trains every projection as a stock nn.Linear on cuBLAS
+(e.g. src/models/hybrid_attention.py:100, `to_out_linear`), sharded by
+src/training/fsdp_stage.py:392-451; the math is the same product, rounded once to bf16 from
+an fp32 accumulator as cuBLAS does.
 """
 import types
 
