@@ -209,6 +209,11 @@ def validate_ablation(cfg):
 def validate_kernels(cfg):
     if cfg.kernels.softmax_backend not in SOFTMAX_BACKENDS:
         raise ValueError(f"kernels.softmax_backend {cfg.kernels.softmax_backend!r} not in {SOFTMAX_BACKENDS}")
+    if cfg.kernels.inference_kernels and cfg.kernels.softmax_backend == "ref":
+        raise ValueError("kernels.softmax_backend=ref is the eager oracle: it needs "
+                         "kernels.inference_kernels=false (the fused engine runs the window kernel)")
+    if not cfg.kernels.inference_kernels and cfg.precision.fp8.enabled:
+        raise ValueError("precision.fp8 runs on the fused engine: it needs kernels.inference_kernels=true")
     if cfg.render.warmup_steps < 0:
         raise ValueError("render.warmup_steps must be >= 0")
     if cfg.precision.fp8.skip_end_blocks < 0:

@@ -1,11 +1,16 @@
 """Single-GPU render entry point.
 
-    python -m vdn_minimax_h3_b200.inference.infer --config configs/inference/8nfe.yaml \
+    python -m vdn_minimax_h3_b200.inference.infer --config configs/inference/8nfe_tuned_fp8.yaml \
         checkpoint=... render.prompt_file=... render.out=clip.mp4 [synthetic_base=true]
 
 config -> assemble (checkpoint + base, or the synthetic random-init model) -> warm-up NFEs
 -> timed render (device-synchronised per-NFE times) -> decode (stand-in decoders) -> mp4
-(+ wav) -> optional record JSON. Reference parity: src/inference/infer.py:28-73.
+with the soundtrack muxed in -> optional record JSON. `kernels.inference_kernels=false`
+(the configs' rung 0, 8nfe.yaml / 50nfe.yaml) renders with the eager model -- the released
+arithmetic, `kernels.softmax_backend` choosing the window path -- instead of the fused
+engine; `true` (the `_tuned` rungs) runs the fused sm_100a engine, in fp8 when
+`precision.fp8.enabled`. Reference parity: src/inference/infer.py:28-73 and the config
+ladder of configs/inference/8nfe*.yaml.
 """
 import json
 import os
@@ -37,6 +42,8 @@ def assemble(cfg, device):
         merge_lora_state(model, state, scale)
     if cfg.behavior.teacher_mode:
         set_teacher_mode(model, True)
+    from vdn_minimax_h3_b200.models.hybrid_transform import set_softmax_backend
+    set_softmax_backend(model, cfg.kernels.softmax_backend)
     if cfg.ablation.enabled:
         from vdn_minimax_h3_b200.models.hybrid_transform import iter_hybrids
         for attn in iter_hybrids(model):
@@ -44,6 +51,12 @@ def assemble(cfg, device):
                 if not hasattr(attn, k):
                     raise ValueError(f"ablation override {k!r} is not a hybrid attention field")
                 setattr(attn, k, v)
+    if not cfg.kernels.inference_kernels:
+        # rung 0: the eager model itself (returned as the engine, so callers run it)
+        if cfg.runtime.offload_blocks:
+            from vdn_minimax_h3_b200.inference.offload import enable_module_offload
+            enable_module_offload(model, device)
+        return model, model
     engine = build_inference_engine(model, fp8=cfg.precision.fp8.enabled)
     if cfg.runtime.offload_blocks:
         from vdn_minimax_h3_b200.inference.offload import enable_block_offload
@@ -97,7 +110,9 @@ def main(argv=None):
             commit = None
         rec = {"config": resolved_dict(cfg), "step_seconds": steps, "denoise_s": denoise,
                "setup_s": t_setup, "decode_s": t_decode, "git_commit": commit,
-               "fp8": cfg.precision.fp8.enabled, "engine": "fused sm_100a kernels"}
+               "fp8": cfg.precision.fp8.enabled,
+               "engine": ("fused sm_100a kernels" if cfg.kernels.inference_kernels
+                          else f"eager model (softmax_backend={cfg.kernels.softmax_backend})")}
         with open(cfg.render.out + ".inference.json", "w") as f:
             json.dump(rec, f, indent=2)
     return 0

@@ -1,7 +1,7 @@
 """Multi-GPU render entry point (one process per GPU, Ulysses sequence parallel).
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m vdn_minimax_h3_b200.inference.infer_ulysses \
-        --config configs/inference/8nfe_ulysses_b200.yaml render.prompt_file=... render.out=...
+        --config configs/inference/8nfe_tuned_fp8_ulysses_b200.yaml render.prompt_file=... render.out=...
 
 init NCCL -> assemble on every rank -> UlyssesEngine -> barrier -> warm-up -> timed render
 (device-synchronised, max over ranks) -> rank-0 decode + save -> timing line.
@@ -23,6 +23,9 @@ from vdn_minimax_h3_b200.config.schemas import (InferenceConfig, validate_ablati
 def main(argv=None):
     t_start = time.perf_counter()
     cfg = load_config(InferenceConfig, argv, (validate_kernels, validate_ablation, validate_parallel))
+    if not cfg.kernels.inference_kernels:
+        raise ValueError("the sequence / tensor parallel engines run the fused kernels: "
+                         "kernels.inference_kernels=false is a single-GPU (infer.py) setting")
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)

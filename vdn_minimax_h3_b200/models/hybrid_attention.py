@@ -76,8 +76,12 @@ class HybridAttention(nn.Module):
         covered = layout is None or full_cover(bounds, layout.num_frames)
         scale = self.head_dim ** -0.5
         q, k, v, raw = self.orig.project(x, rotary_emb)
-        ag = _attention_kernels()
-        if ag is not None and ag.kernel_path_ok(q, k, v):
+        ag = _attention_kernels() if self.softmax_impl != "ref" else None
+        use_kernel = ag is not None and ag.kernel_path_ok(q, k, v)
+        if self.softmax_impl == "kernel" and q.is_cuda and not use_kernel:
+            raise RuntimeError("softmax_backend=kernel: the window kernel does not take these "
+                               f"tensors (q {tuple(q.shape)} {q.dtype}); use auto or ref")
+        if use_kernel:
             # sm_100a forward + backward kernels over the analytic plan (dense when covered)
             plan = (ag.dense_plan(x.shape[0], x.device) if covered
                     else ag.window_plan(layout, bounds, self.anchor_frames, x.device))

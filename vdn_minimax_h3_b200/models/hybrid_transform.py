@@ -49,13 +49,22 @@ def set_teacher_mode(model, enabled: bool):
         attn.teacher_mode = enabled
 
 
+# The reference's backend names: `flex` (FlexAttention / FA4) and `decomposed` (FA4 varlen
+# + cuDNN legs) are both its GPU window paths; here both are the sm_100a window kernel.
+BACKEND_ALIASES = {"auto": "auto", "kernel": "kernel", "flex": "kernel", "decomposed": "kernel",
+                   "ref": "ref"}
+
+
 def set_softmax_backend(model, backend: str) -> str:
-    """auto | kernel (the sm_100a window kernel; what auto is on CUDA) | ref (eager oracle)."""
-    if backend not in SOFTMAX_BACKENDS:
-        raise ValueError(f"softmax_backend={backend!r}; expected one of {SOFTMAX_BACKENDS}")
+    """auto (the sm_100a window kernel where its tensors qualify, else the oracle) | kernel
+    (the kernel required on CUDA; `flex` and `decomposed` mean the same) | ref (the eager
+    per-segment oracle even on CUDA). Returns the backend the hybrids now use."""
+    impl = BACKEND_ALIASES.get(backend)
+    if impl is None or impl not in SOFTMAX_BACKENDS:
+        raise ValueError(f"softmax_backend={backend!r}; expected one of {sorted(BACKEND_ALIASES)}")
     for attn in iter_hybrids(model):
-        attn.softmax_impl = backend
-    return backend
+        attn.softmax_impl = impl
+    return impl
 
 
 def set_inference_mode(model, enabled: bool):
