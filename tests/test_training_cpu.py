@@ -256,3 +256,42 @@ def test_a1_bucketed_collectives_two_ranks():
     for p in procs:
         p.join(timeout=30)
     assert res == {0: True, 1: True}
+
+
+def test_train_cli_validates_every_stage():
+    """`python -m vdn_minimax_h3_b200.training.train <stage> --config ... --validate-only`
+    loads and validates each shipped stage config and exits 0; an unknown stage is refused."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cases = {"a1": ["configs/training/stage_a1_c1_vdn_anchor.yaml", "data.index_file=i"],
+             "a2": ["configs/training/stage_a2_c1_vdn_anchor.yaml", "data.index_file=i"],
+             "b": ["configs/training/stage_b_c1_vdn_anchor.yaml", "data.index_file=i"],
+             "dmd": ["configs/training/stage_dmd_vdn.yaml", "data.index_file=i", "turbo.checkpoint=t"]}
+    for stage, (cfg, *over) in cases.items():
+        r = subprocess.run([sys.executable, "-m", "vdn_minimax_h3_b200.training.train", stage,
+                            "--config", cfg, *over, "--validate-only"], cwd=root,
+                           capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0 and "config ok" in r.stderr, (stage, r.stderr[-1500:])
+    r = subprocess.run([sys.executable, "-m", "vdn_minimax_h3_b200.training.train", "c"], cwd=root,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0 and "usage" in r.stderr
+
+
+@pytest.mark.timeout(300)
+def test_train_cli_runs_stage_a1(tmp_path):
+    from vdn_minimax_h3_b200.training import train
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_port()), WORLD_SIZE="1", RANK="0",
+                      LOCAL_RANK="0")
+    out = str(tmp_path / "a1")
+    cfg = h3_tiny_config().to_dict()
+    argv = ["a1", "model.base.source=synthetic", f"data.index_file={TINY_DATA}",
+            f"checkpoint.output_dir={out}", "training.max_steps=1", "checkpoint.save_every=1",
+            "checkpoint.early_saves=[]",
+            "model.architecture.hybrid_attention.softmax_attention.radius=0",
+            "model.architecture.hybrid_attention.softmax_attention.chunk=2",
+            "model.architecture.hybrid_attention.linear_attention.delta_rule=sana_scaled",
+            "model.architecture.hybrid_attention.linear_attention.short_conv.targets=[]",
+            "model.base.dtype=float32", "model.base.config_overrides=" + json.dumps(cfg)]
+    assert train.main(argv) == 1
+    assert os.path.exists(os.path.join(out, "DONE"))
