@@ -395,12 +395,22 @@ def clip_gradients(params, grad_clip):
     return float(_full(norm)) if torch.is_tensor(norm) else float(norm)
 
 
-def make_loader(dataset, world, rank, seed, num_workers=0):
+def make_loader(dataset, world, rank, seed, num_workers=0, pin_memory=None):
+    """One clip per rank per step (DistributedSampler behind SkipFirst for resumes).
+    `num_workers` reader processes (the config's data.num_workers) keep the next clips'
+    latents loading while the step runs; on CUDA the batches land in pinned host memory so
+    the copies to the GPU are DMA transfers."""
     from torch.utils.data import DataLoader, DistributedSampler
     from vdn_minimax_h3_b200.training.dataset import collate_single
+    if pin_memory is None:
+        pin_memory = torch.cuda.is_available()
     sampler = SkipFirst(DistributedSampler(dataset, num_replicas=world, rank=rank, shuffle=True, seed=seed))
+    # workers come from a forkserver, not a fork of this (multi-threaded: NCCL, heartbeat)
+    # process, which can leave a lock held in the child
+    extra = ({"persistent_workers": True, "prefetch_factor": 2,
+              "multiprocessing_context": "forkserver"} if num_workers > 0 else {})
     loader = DataLoader(dataset, batch_size=1, sampler=sampler, num_workers=num_workers,
-                        collate_fn=collate_single)
+                        collate_fn=collate_single, pin_memory=pin_memory, **extra)
     return loader, sampler
 
 

@@ -163,7 +163,8 @@ def _fsdp_stage(cfg, stage):
     if resume.artifact is not None and resume.artifact.resolved_training_config:
         check_schedule_stamp(resume.artifact.metadata.get("schedule"), sched, rank, resume.step)
     dataset = _load_dataset(cfg)
-    loader, sampler = fs.make_loader(dataset, world, rank, cfg.training.seed)
+    loader, sampler = fs.make_loader(dataset, world, rank, cfg.training.seed,
+                                      getattr(cfg.data, "num_workers", 0))
     sampler.skip = cursor
     write = _metrics_writer(out)
     trainable = [p for p in model.parameters() if p.requires_grad]
@@ -348,7 +349,8 @@ def run_stage_a1(cfg):
     sched = _sched_args(opt_cfg, cfg.training.max_steps)
     gens = fs.make_generators(cfg.training.seed, rank, device)
     dataset = _load_dataset(cfg)
-    loader, sampler = fs.make_loader(dataset, world, rank, cfg.training.seed)
+    loader, sampler = fs.make_loader(dataset, world, rank, cfg.training.seed,
+                                      getattr(cfg.data, "num_workers", 0))
     write = _metrics_writer(out)
     step = 0
     it = iter(loader)
@@ -500,7 +502,8 @@ def run_stage_dmd(cfg):
     schedule = dmd_lib.FewStepSchedule(tb.num_steps, tb.video_shift, tb.audio_shift)
     gens = fs.make_generators(cfg.training.seed, rank, device)
     dataset = _load_dataset(cfg, text_only=True)
-    loader, sampler = fs.make_loader(dataset, world, rank, cfg.training.seed)
+    loader, sampler = fs.make_loader(dataset, world, rank, cfg.training.seed,
+                                      getattr(cfg.data, "num_workers", 0))
     g = cfg.generation
     from vdn_minimax_h3_b200.models.layout import align_num_frames, audio_latent_num_frames, video_latent_num_frames
     nf = align_num_frames(g.num_frames)
