@@ -85,7 +85,7 @@ class PackedPrompt:
     """One prompt's packed geometry, built once per iteration and reused by every forward."""
 
     def __init__(self, prompt_embeds, video_shape, num_audio_latents, device):
-        self.prompt_embeds = prompt_embeds.to(device, torch.bfloat16)[None]
+        self.prompt_embeds = prompt_embeds.to(device, torch.bfloat16, non_blocking=True)[None]
         self.video_shape = tuple(video_shape)
         self.num_audio_latents = int(num_audio_latents)
         self.device = device
@@ -117,8 +117,9 @@ class PackedPrompt:
 
 def pack_noisy_batch(sample, device, noise_generator, sigma_generator, fixed_timesteps=None):
     """Dataset sample -> model inputs, fp32 velocity targets, the two timesteps, the layout."""
-    video = sample["video_latents"].to(device, torch.float32)[None]
-    audio = sample["audio_latents"].to(device, torch.float32)               # (2, 32, A)
+    # from the loader's pinned buffers these are asynchronous DMA copies
+    video = sample["video_latents"].to(device, torch.float32, non_blocking=True)[None]
+    audio = sample["audio_latents"].to(device, torch.float32, non_blocking=True)   # (2, 32, A)
     emb = sample["prompt_embeds"]
     audio_rows = audio.permute(0, 2, 1).reshape(-1, audio.shape[1])
     pp = PackedPrompt(emb, tuple(video.shape[1:]), audio.shape[-1], device)
