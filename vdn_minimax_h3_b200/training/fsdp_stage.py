@@ -276,7 +276,8 @@ def shard_model(model, device, shard_size=None, activation_checkpointing=True, s
     module switch linear_grad.LINEAR_KERNELS turns it off at run time). With `symmetric_reduce` (default:
     on for CUDA shard groups of 2-8 ranks) the gradient reduce-scatter of every unit runs over
     symmetric memory (parallel/fsdp_comm.py) instead of NCCL, and with `symmetric_gather`
-    (same default) the parameter all-gather as well; the comm objects are kept as
+    (same default) the parameter all-gather as well -- both only when the shard group's ranks
+    share one host (CUDA IPC); the comm objects are kept as
     `model._vdn_reduce_comm` / `model._vdn_gather_comm` (`close_comms(model)` before
     destroying the process group)."""
     from torch.distributed.device_mesh import init_device_mesh
@@ -306,8 +307,9 @@ def shard_model(model, device, shard_size=None, activation_checkpointing=True, s
     for blk in model.token_refiner.refiner_blocks:
         fully_shard(blk, mesh=mesh, mp_policy=mp)
     fully_shard(model, mesh=mesh, mp_policy=mp)
+    one_host = dev_type == "cuda" and 1 < shard <= 8 and _group_on_one_host(mesh.get_group("shard"))
     if symmetric_reduce is None:
-        symmetric_reduce = dev_type == "cuda" and 1 < shard <= 8
+        symmetric_reduce = one_host
     if symmetric_reduce:
         from torch.distributed.fsdp import FSDPModule
         from vdn_minimax_h3_b200.parallel.fsdp_comm import SymmetricReduceScatter, trainable_reduce_numel
@@ -323,7 +325,7 @@ def shard_model(model, device, shard_size=None, activation_checkpointing=True, s
                 u.set_custom_reduce_scatter(comm)
         model._vdn_reduce_comm = comm
     if symmetric_gather is None:
-        symmetric_gather = dev_type == "cuda" and 1 < shard <= 8
+        symmetric_gather = one_host
     if symmetric_gather:
         from torch.distributed.fsdp import FSDPModule
         from vdn_minimax_h3_b200.parallel.fsdp_comm import SymmetricAllGather, gather_shard_bytes
@@ -338,6 +340,15 @@ def shard_model(model, device, shard_size=None, activation_checkpointing=True, s
                 u.set_custom_all_gather(comm)
         model._vdn_gather_comm = comm
     return model
+
+
+def _group_on_one_host(group):
+    """True when every rank of `group` runs on this host (the symmetric heaps map peers'
+    memory through CUDA IPC, which does not cross nodes)."""
+    import socket
+    names = [None] * dist.get_world_size(group)
+    dist.all_gather_object(names, socket.gethostname(), group=group)
+    return len(set(names)) == 1
 
 
 def close_comms(model):
