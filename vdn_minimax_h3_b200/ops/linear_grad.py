@@ -76,7 +76,7 @@ def kernel_linear(x, weight, bias=None):
     """F.linear(x, weight, bias) for x [..., in] on the GEMM kernel (forward and backward)
     when `kernel_path_ok`, else F.linear."""
     x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
-    if x2.is_cuda and not _rows_ok(x2):
+    if x2.is_cuda and x2.dtype == torch.bfloat16 and not _rows_ok(x2):
         x2 = x2.contiguous()
     if not kernel_path_ok(x2, weight):
         STATS["fallback"] += 1
