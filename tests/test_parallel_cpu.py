@@ -81,3 +81,21 @@ def test_ulysses_matches_single_process(world, softmax_ranks):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert len(results) == world
     assert max(results.values()) < 1e-4, results
+
+
+def test_sharded_head_plan_cache_follows_the_tensor():
+    """The head's row cuts are cached per index tensor: the same tensor hits the cache, an
+    in-place change or a new tensor with other rows (even one of the same size) is re-cut."""
+    import torch
+    from vdn_minimax_h3_b200.parallel.head import ShardedHead
+    head = ShardedHead()
+    bounds = [(0, 10), (10, 20), (20, 30)]
+    a = torch.tensor([2, 3, 11, 12, 13, 25])
+    assert head._plan(a, bounds) == [(0, 2), (2, 5), (5, 6)]
+    assert head._plan(a, bounds) is head._plan(a, bounds)
+    a[2:] = torch.tensor([21, 22, 23, 24])                  # in place: version changes
+    assert head._plan(a, bounds) == [(0, 2), (2, 2), (2, 6)]
+    del a
+    b = torch.tensor([0, 1, 2, 3, 4, 29])                   # same size, other rows
+    assert head._plan(b, bounds) == [(0, 5), (5, 5), (5, 6)]
+    assert head._plan(b, [(0, 3), (3, 30)]) == [(0, 3), (3, 6)]

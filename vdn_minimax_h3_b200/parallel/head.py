@@ -8,6 +8,7 @@ model's norm_out / proj_out). The head is row-wise, so the same result comes fro
 projecting its own rows: the gathered bytes drop from T x 5376 bf16 (1.1 GB at H3 scale) to
 the video and audio output channels (~20 MB), and no rank projects text rows.
 """
+import weakref
 from typing import List, Sequence, Tuple
 
 import torch
@@ -22,15 +23,22 @@ class ShardedHead:
         self._plans = {}
 
     def _plan(self, indices: torch.Tensor, bounds: Sequence[Tuple[int, int]]):
-        key = (indices.data_ptr(), indices.numel(), tuple(bounds))
-        plan = self._plans.get(key)
-        if plan is None:
-            if indices.numel() > 1 and not bool((indices[1:] > indices[:-1]).all()):
-                raise ValueError("sharded head needs ascending output row indices")
-            edges = torch.tensor([b[0] for b in bounds] + [bounds[-1][1]], device=indices.device,
-                                 dtype=indices.dtype)
-            cuts = torch.searchsorted(indices, edges).tolist()        # one small D2H, cached
-            plan = self._plans[key] = [(cuts[p], cuts[p + 1]) for p in range(len(bounds))]
+        """Per-rank (first, end) positions in `indices` of the rows each rank owns. Cached
+        per index TENSOR (held weakly, checked against its in-place version counter), so a
+        later request whose indices reuse the same memory is never served stale cuts."""
+        bounds = tuple(tuple(b) for b in bounds)
+        entry = self._plans.get(id(indices))
+        if (entry is not None and entry[0]() is indices and entry[1] == indices._version
+                and entry[2] == bounds):
+            return entry[3]
+        if indices.numel() > 1 and not bool((indices[1:] > indices[:-1]).all()):
+            raise ValueError("sharded head needs ascending output row indices")
+        edges = torch.tensor([b[0] for b in bounds] + [bounds[-1][1]], device=indices.device,
+                             dtype=indices.dtype)
+        cuts = torch.searchsorted(indices, edges).tolist()        # one small D2H per new tensor
+        plan = [(cuts[p], cuts[p + 1]) for p in range(len(bounds))]
+        self._plans = {k: v for k, v in self._plans.items() if v[0]() is not None}
+        self._plans[id(indices)] = (weakref.ref(indices), indices._version, bounds, plan)
         return plan
 
     def _gather(self, local: torch.Tensor, spans: List[Tuple[int, int]]) -> torch.Tensor:
