@@ -258,24 +258,29 @@ def test_a1_bucketed_collectives_two_ranks():
     assert res == {0: True, 1: True}
 
 
-def test_train_cli_validates_every_stage():
-    """`python -m vdn_minimax_h3_b200.training.train <stage> --config ... --validate-only`
-    loads and validates each shipped stage config and exits 0; an unknown stage is refused."""
+def test_train_cli_validates_every_stage(capsys):
+    """`train <stage> --config ... --validate-only` loads and validates each shipped stage
+    config and exits 0; an unknown stage is refused (the module entry checked once through
+    `python -m`)."""
     import subprocess
     import sys
+    from vdn_minimax_h3_b200.training import train
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     cases = {"a1": ["configs/training/stage_a1_c1_vdn_anchor.yaml", "data.index_file=i"],
              "a2": ["configs/training/stage_a2_c1_vdn_anchor.yaml", "data.index_file=i"],
              "b": ["configs/training/stage_b_c1_vdn_anchor.yaml", "data.index_file=i"],
              "dmd": ["configs/training/stage_dmd_vdn.yaml", "data.index_file=i", "turbo.checkpoint=t"]}
     for stage, (cfg, *over) in cases.items():
-        r = subprocess.run([sys.executable, "-m", "vdn_minimax_h3_b200.training.train", stage,
-                            "--config", cfg, *over, "--validate-only"], cwd=root,
-                           capture_output=True, text=True, timeout=300)
-        assert r.returncode == 0 and "config ok" in r.stderr, (stage, r.stderr[-1500:])
-    r = subprocess.run([sys.executable, "-m", "vdn_minimax_h3_b200.training.train", "c"], cwd=root,
-                       capture_output=True, text=True, timeout=300)
-    assert r.returncode != 0 and "usage" in r.stderr
+        with pytest.raises(SystemExit) as ex:
+            train.main([stage, "--config", os.path.join(root, cfg), *over, "--validate-only"])
+        assert ex.value.code == 0 and "config ok" in capsys.readouterr().err, stage
+    with pytest.raises(SystemExit) as ex:
+        train.main(["c"])
+    assert "usage" in str(ex.value.code)
+    r = subprocess.run([sys.executable, "-m", "vdn_minimax_h3_b200.training.train", "b", "--config",
+                        "configs/training/stage_b_c1_vdn_anchor.yaml", "data.index_file=i",
+                        "--print-config"], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "index_file: i" in r.stdout, r.stderr[-1500:]
 
 
 @pytest.mark.timeout(300)
