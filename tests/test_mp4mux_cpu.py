@@ -101,3 +101,44 @@ def test_concat_segments_decodes_like_its_parts(tmp_path):
     assert track_handlers(muxed) == [b"vide", b"soun"]
     open(path, "wb").write(muxed)
     assert len(decode(path)) == 30
+
+
+def test_concat_many_small_segments(tmp_path):
+    """The split encode of 8 ranks x several writers hands the join up to ~40 segments, some
+    of a single frame: all of them join into one track that decodes like its parts."""
+    cv2 = pytest.importorskip("cv2")
+    from vdn_minimax_h3_b200.inference.mp4mux import concat_video_segments
+    from vdn_minimax_h3_b200.inference.vae import encode_mp4
+
+    rng = np.random.default_rng(0)
+    frames = rng.integers(0, 255, size=(61, 32, 48, 3), dtype=np.uint8)
+    frames[:, :16] = 40                                   # some structure for the codec
+    cuts = [0, 1, 3, 4, 8, 9, 15, 16, 17, 25, 26, 27, 40, 41, 55, 60, 61]
+    segs = []
+    for i in range(len(cuts) - 1):
+        path = str(tmp_path / f"s{i}.mp4")
+        w = cv2.VideoWriter(path, cv2.VideoWriter_fourcc(*"mp4v"), 24, (48, 32))
+        for f in frames[cuts[i]:cuts[i + 1]]:
+            w.write(np.ascontiguousarray(f[:, :, ::-1]))
+        w.release()
+        segs.append(open(path, "rb").read())
+    joined = str(tmp_path / "joined.mp4")
+    open(joined, "wb").write(concat_video_segments(segs))
+
+    def decode(path):
+        cap, out = cv2.VideoCapture(path), []
+        while True:
+            ok, f = cap.read()
+            if not ok:
+                return out
+            out.append(f)
+
+    got = decode(joined)
+    want = [f for i in range(len(segs)) for f in decode(str(tmp_path / f"s{i}.mp4"))]
+    assert len(got) == 61 and all(np.array_equal(a, b) for a, b in zip(got, want))
+    # and the encoder's own split (ranges of >= 8 frames on several writers) gives every frame
+    import torch
+    data = encode_mp4(torch.from_numpy(frames), workers=6)
+    path = str(tmp_path / "split.mp4")
+    open(path, "wb").write(data)
+    assert len(decode(path)) == 61
