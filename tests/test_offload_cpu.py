@@ -44,3 +44,39 @@ def test_block_offload_matches_resident_engine():
     assert seen and all(seen)
     # only block 0 stays resident: prefetched for the next model evaluation
     assert [b.resident for b in streamer.blocks] == [True] + [False] * (len(streamer.blocks) - 1)
+
+
+def test_module_offload_keeps_tied_tensors_and_outputs():
+    """Eager block streaming (forward hooks): a parameter tied between two blocks stays
+    resident (never re-pointed), every other block tensor lives on its host copy between
+    forwards, and the outputs equal the resident model's."""
+    import torch
+    import torch.nn as nn
+    from vdn_minimax_h3_b200.inference.offload import enable_module_offload
+
+    class Blocks(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.transformer_blocks = nn.ModuleList(nn.Linear(8, 8) for _ in range(3))
+            self.transformer_blocks[2].weight = self.transformer_blocks[0].weight   # tied
+
+        def forward(self, x):
+            for b in self.transformer_blocks:
+                x = torch.tanh(b(x))
+            return x
+
+    torch.manual_seed(0)
+    m = Blocks()
+    x = torch.randn(4, 8)
+    want = m(x)
+    tied = m.transformer_blocks[0].weight
+    streamer = enable_module_offload(m, torch.device("cpu"))
+    assert enable_module_offload(m, torch.device("cpu")) is streamer           # idempotent
+    for _ in range(2):
+        torch.testing.assert_close(m(x), want, rtol=0, atol=0)
+    assert m.transformer_blocks[0].weight is tied
+    assert streamer.host_bytes() == sum(b.nbytes() for b in streamer.blocks) > 0
+    # the tied weight is in no block's streamed groups
+    key = tied.untyped_storage().data_ptr()
+    for b in streamer.blocks:
+        assert all(k[2] != key for k in b.groups)
